@@ -1,0 +1,318 @@
+"""The CPU oracle against the reference's own known-answer tests.
+
+Each test restates one unit test of zealot-rl (file:line given) and runs it
+on the C restatement, which pins the oracle before it is used as the
+checker for the CUDA library.  Further self-consistency checks (a float64
+finite-difference check of the whole PPO gradient, and the multi-threaded
+fold against the sequential one) follow.
+"""
+import math
+
+import numpy as np
+import pytest
+
+import oracle as O
+from zealot_b200 import synth
+
+
+def test_lcg_deterministic_unit():
+    # rng.rs:39-46
+    a, b = O.Lcg(9), O.Lcg(9)
+    for _ in range(100):
+        assert a.unit() == b.unit()
+
+
+def test_lcg_first_values_match_definition():
+    # rng.rs:14-26 restated with Python integers: x = x*a + c mod 2^64,
+    # unit = (x >> 40) / 2^24 in f32.
+    x = 9 | 1
+    lcg = O.Lcg(9)
+    for _ in range(50):
+        x = (x * 6364136223846793005 + 1442695040888963407) % (1 << 64)
+        want = np.float32(np.float32(x >> 40) / np.float32(1 << 24))
+        assert np.float32(lcg.unit()) == want
+
+
+def test_lcg_seed_or_one_collision():
+    # Lcg::new(s) ORs 1 (rng.rs:14-16): seeds 2 and 3 give one stream.
+    a, b = O.Lcg(2), O.Lcg(3)
+    assert [a.unit() for _ in range(8)] == [b.unit() for _ in range(8)]
+
+
+def test_gauss_moments():
+    g = O.Lcg(5).gausses(200_000)
+    assert abs(float(g.mean())) < 0.01
+    assert abs(float(g.std()) - 1.0) < 0.01
+
+
+def test_shuffle_is_permutation_and_matches_python():
+    n = 1000
+    order = O.shuffle(7, n)
+    assert sorted(order.tolist()) == list(range(n))
+    # ppo.rs:357-363 in pure Python (f32 product, truncation, min(j, i)).
+    x = 7 | 1
+    ref = list(range(n))
+    for i in range(n - 1, 0, -1):
+        x = (x * 6364136223846793005 + 1442695040888963407) % (1 << 64)
+        u = np.float32(np.float32(x >> 40) / np.float32(1 << 24))
+        j = int(np.float32(u * np.float32(i + 1)))
+        j = min(j, i)
+        ref[i], ref[j] = ref[j], ref[i]
+    assert order.tolist() == ref
+
+
+def test_gae_matches_hand_computation():
+    # ppo.rs:709-721
+    adv, ret = O.gae([1.0, 2.0], [0.0, 0.0], [0, 0], 0.0, 1.0, 1.0)
+    assert abs(ret[1] - 2.0) < 1e-6 and abs(ret[0] - 3.0) < 1e-6
+    assert abs(adv[0] - 3.0) < 1e-6 and abs(adv[1] - 2.0) < 1e-6
+
+
+def test_gae_respects_done_boundary():
+    # ppo.rs:760-768
+    adv, _ = O.gae([1.0, 1.0], [5.0, 5.0], [1, 0], 0.0, 0.99, 0.95)
+    assert abs(adv[0] - (-4.0)) < 1e-6
+
+
+def test_elu_and_grad():
+    # net.rs:258-265 through a [1,1,1] net: hidden ELU with w=1, b=0, linear
+    # output with w=1, b=0, so the output is elu(x) and the input gradient
+    # of a unit output gradient is elu'(x).
+    m = O.Mlp([1, 1, 1], np.array([1, 0, 1, 0], np.float32))
+    for x, want in [(2.0, 2.0), (0.0, 0.0), (-1.0, math.exp(-1.0) - 1.0)]:
+        acts = m.forward([x])
+        assert abs(float(m.output(acts)[0]) - want) < 1e-6
+    acts = m.forward([2.0])
+    g = np.zeros(4, np.float32)
+    assert m.backward(acts, [1.0], g)[0] == 1.0
+    acts = m.forward([-1.0])
+    g = np.zeros(4, np.float32)
+    assert abs(float(m.backward(acts, [1.0], g)[0]) - math.exp(-1.0)) < 1e-6
+
+
+def test_backward_matches_finite_difference():
+    # net.rs:267-307
+    rng = O.Lcg(123)
+    dims = [4, 6, 5, 3]
+    net = O.Mlp.new(dims, 1.0, rng)
+    x = np.array([0.3, -0.7, 0.1, 0.9], np.float32)
+    target = np.array([0.2, -0.4, 0.6], np.float32)
+
+    def loss():
+        o = net.output(net.forward(x))
+        return 0.5 * float(np.sum((o - target) ** 2, dtype=np.float32))
+
+    acts = net.forward(x)
+    g = np.zeros_like(net.params)
+    net.backward(acts, net.output(acts) - target, g)
+    eps = 1e-3
+    off = 0
+    for l in range(len(dims) - 1):
+        nw = dims[l + 1] * dims[l]
+        for idx in (0, nw // 2, nw - 1):
+            k = off + idx
+            orig = net.params[k]
+            net.params[k] = orig + eps
+            lp = loss()
+            net.params[k] = orig - eps
+            lm = loss()
+            net.params[k] = orig
+            fd = (lp - lm) / (2 * eps)
+            assert abs(fd - g[k]) < 1e-2, (l, idx, fd, g[k])
+        off += nw + dims[l + 1]
+
+
+def test_adam_minimizes_quadratic():
+    # net.rs:309-328
+    rng = O.Lcg(7)
+    net = O.Mlp.new([2, 1], 1.0, rng)
+    m = np.zeros_like(net.params)
+    v = np.zeros_like(net.params)
+    x = np.array([1.0, -2.0], np.float32)
+    target = 0.5
+
+    def loss():
+        return float((net.output(net.forward(x))[0] - target) ** 2)
+
+    l0 = loss()
+    t = 0
+    for _ in range(500):
+        acts = net.forward(x)
+        g = np.zeros_like(net.params)
+        net.backward(acts, [2.0 * (net.output(acts)[0] - target)], g)
+        t = O.adam_step(net.params, g, m, v, t, 1e-2)
+    assert loss() < l0 * 1e-3
+
+
+def test_grad_clip_caps_norm():
+    # net.rs:330-338
+    net = O.Mlp.new([3, 4, 2], 1.0, O.Lcg(1))
+    g = np.zeros_like(net.params)
+    g[3 * 4] = 100.0  # b_0[0]
+    O.grad_clip(g, 1.0)
+    assert abs(O.grad_l2_norm(g) - 1.0) < 1e-4
+
+
+def test_powi_is_square_and_multiply():
+    for t in range(1, 60):
+        r = np.float32(1.0)
+        a = np.float32(0.999)
+        b = t
+        while True:
+            if b & 1:
+                r = np.float32(r * a)
+            b //= 2
+            if b == 0:
+                break
+            a = np.float32(a * a)
+        assert np.float32(O.powi(0.999, t)) == r
+        assert abs(O.powi(0.9, t) - 0.9 ** t) < 1e-6
+
+
+def _bandit_sample(ac: O.ActorCritic, obs, rng: O.Lcg):
+    mean, _ = ac.forward(obs[None, :], obs[None, :])
+    mean = mean[0]
+    ls = ac.params[-len(mean):]
+    action = np.array([mean[k] + np.float32(math.exp(ls[k])) * np.float32(rng.gauss())
+                       for k in range(len(mean))], np.float32)
+    return action, ac.logp(action, mean), mean
+
+
+@pytest.mark.slow
+def test_ppo_improves_on_bandit():
+    # ppo.rs:770-845
+    rng = O.Lcg(2024)
+    target = np.array([0.7, -0.4], np.float32)
+    ac = O.ActorCritic.new([3, 32, 2], [3, 32, 1], 0.6, 3e-3, rng)
+    cfg = O.PpoConfig(entropy_coef=0.0, minibatches=4, epochs=4)
+    obs = np.array([0.5, -0.2, 0.1], np.float32)
+
+    def mean_reward():
+        m, _ = ac.forward(obs[None, :], obs[None, :])
+        return -float(np.sum((m[0] - target) ** 2))
+
+    r0 = mean_reward()
+    n = 256
+    for _ in range(120):
+        rows = {f: [] for f in O.SoaBatch.FIELDS}
+        for _ in range(n):
+            action, logp, mean_old = _bandit_sample(ac, obs, rng)
+            r = -float(np.sum((action - target) ** 2, dtype=np.float32))
+            _, v = ac.forward(obs[None, :], obs[None, :])
+            adv, ret = O.gae([r], [v[0]], [1], 0.0, cfg.gamma, cfg.lam)
+            for f, val in (("obs", obs), ("critic_obs", obs), ("action", action),
+                           ("mean_old", mean_old), ("logp_old", logp),
+                           ("value_old", v[0]), ("adv", adv[0]), ("ret", ret[0])):
+                rows[f].append(val)
+        batch = O.SoaBatch(**{f: np.array(v, np.float32) for f, v in rows.items()})
+        ac.update(batch, cfg)
+    r1 = mean_reward()
+    assert r1 > r0 + 0.2, (r0, r1)
+    m, _ = ac.forward(obs[None, :], obs[None, :])
+    assert abs(m[0][0] - target[0]) < 0.25 and abs(m[0][1] - target[1]) < 0.25
+
+
+# ------------------------------------------------------------------ extras
+
+def _small_rollout(seed=3, n_envs=6, T=8, adims=(7, 16, 12, 3), cdims=(5, 16, 12, 1),
+                   fresh=True):
+    def fwd(params, obs, cobs):
+        ac = O.ActorCritic(adims, cdims)
+        ac.params = params
+        return ac.forward(obs, cobs)
+
+    ro = synth.make_rollout(seed, n_envs, T, adims, cdims, fwd)
+    adv, ret = O.gae_batch(ro.rewards, ro.value_old.reshape(n_envs, T), ro.dones,
+                           ro.last_values, 0.99, 0.95)
+    batch = O.SoaBatch(obs=ro.obs, critic_obs=ro.critic_obs, action=ro.action,
+                       mean_old=ro.mean_old, logp_old=ro.logp_old,
+                       value_old=ro.value_old, adv=adv.reshape(-1),
+                       ret=ret.reshape(-1))
+    return ro, batch
+
+
+def _ppo_loss64(params, adims, cdims, batch, idx, cfg):
+    """float64 PPO objective whose gradient minibatch_step accumulates
+    (unclipped regime): mean(-ratio*A + value_coef*(v-R)^2) - ent*entropy."""
+    A = adims[-1]
+
+    def mlp(dims, p, x):
+        off = 0
+        a = x
+        for l in range(len(dims) - 1):
+            fi, fo = dims[l], dims[l + 1]
+            w = p[off:off + fo * fi].reshape(fo, fi)
+            off += fo * fi
+            b = p[off:off + fo]
+            off += fo
+            z = a @ w.T + b
+            a = z if l == len(dims) - 2 else np.where(z > 0, z, np.exp(z) - 1)
+        return a, off
+
+    na = O.lib().orc_mlp_param_count(np.asarray(adims, np.int32), len(adims))
+    mean, _ = mlp(adims, params[:na], batch.obs[idx].astype(np.float64))
+    v, nc = mlp(cdims, params[na:], batch.critic_obs[idx].astype(np.float64))
+    ls = params[na + nc:]
+    d = (batch.action[idx] - mean) / np.exp(ls)
+    logp = np.sum(-0.5 * d * d - ls - 0.9189385, axis=1)
+    ratio = np.exp(logp - batch.logp_old[idx])
+    surr = ratio * batch.adv[idx]
+    vl = (v[:, 0] - batch.ret[idx]) ** 2
+    ent = np.sum(ls + 0.5 + 0.9189385)
+    return np.mean(-surr + cfg.value_coef * vl) - cfg.entropy_coef * ent
+
+
+def test_minibatch_grads_match_float64_finite_difference():
+    adims, cdims = (7, 16, 12, 3), (5, 16, 12, 1)
+    ro, batch = _small_rollout(adims=adims, cdims=cdims)
+    ac = O.ActorCritic(adims, cdims)
+    ac.params = ro.params
+    cfg = O.PpoConfig()
+    idx = np.arange(0, batch.n, 2)
+    # identity normalizers: the oracle whitens with mean 0 / var 1 and
+    # clamps to +-5, which N(0,1) inputs essentially never reach.
+    assert np.abs(batch.obs).max() < 5 and np.abs(batch.critic_obs).max() < 5
+    g, sums = ac.minibatch_grads(batch, idx, cfg)
+    p64 = ro.params.astype(np.float64)
+    rng = np.random.default_rng(0)
+    picks = rng.choice(len(p64), size=60, replace=False)
+    # fresh rollout: mean_old == current mean, v_old == current v -> ratio 1,
+    # nothing clipped, so the f64 objective is exactly what is differentiated
+    h = 1e-5
+    for k in picks:
+        pp = p64.copy()
+        pp[k] += h
+        lp = _ppo_loss64(pp, adims, cdims, batch, idx, cfg)
+        pp[k] -= 2 * h
+        lm = _ppo_loss64(pp, adims, cdims, batch, idx, cfg)
+        fd = (lp - lm) / (2 * h)
+        assert abs(fd - g[k]) < 2e-4 + 2e-3 * abs(fd), (k, fd, g[k])
+    assert abs(sums[2]) < 1e-6  # KL of a fresh rollout is 0
+
+
+def test_parallel_fold_matches_sequential():
+    ro, batch = _small_rollout()
+    ac = O.ActorCritic((7, 16, 12, 3), (5, 16, 12, 1))
+    ac.params = ro.params
+    cfg = O.PpoConfig()
+    idx = O.shuffle(1, batch.n)
+    g1, s1 = ac.minibatch_grads(batch, idx, cfg, n_threads=1)
+    g4, s4 = ac.minibatch_grads(batch, idx, cfg, n_threads=4)
+    scale = np.abs(g1).max()
+    assert np.abs(g1 - g4).max() <= 1e-5 * scale
+    assert np.allclose(s1, s4, rtol=1e-5, atol=1e-7)
+
+
+def test_update_is_deterministic_and_moves_params():
+    ro, batch = _small_rollout()
+    cfg = O.PpoConfig(epochs=2, minibatches=3)
+    outs = []
+    for _ in range(2):
+        ac = O.ActorCritic((7, 16, 12, 3), (5, 16, 12, 1))
+        ac.params = ro.params
+        st = ac.update(batch.copy(), cfg)
+        outs.append((ac.params, st, ac.adam_state()[0]))
+    assert np.array_equal(outs[0][0], outs[1][0])
+    assert outs[0][1] == outs[1][1]
+    assert outs[0][2].tolist() == [6, 6, 6]
+    assert not np.array_equal(outs[0][0], ro.params)
