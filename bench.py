@@ -1,0 +1,453 @@
+"""PPO-update benchmark (BASELINE metric: PPO-update samples/s).
+
+One step = one full zealot-rl update of a synthetic rollout: GAE over every
+env, advantage normalization, then epochs x minibatches of shuffled
+minibatch steps (forward and backward of actor and critic, PPO losses,
+per-net gradient clip, adaptive LR, Adam).  At N=1 the workload is
+BASELINE configs[1] (N=4096 envs x T=24, 5 epochs x 4 minibatches, tf32
+GEMMs); with --gpus N every rank runs that per-GPU workload on its own envs
+(weak scaling; the global minibatch is N times larger) and the gradient is
+allreduced over NCCL once per minibatch.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--config c2|c4|c5] [--precision tf32|fp32|bf16]
+
+Timing: CUDA events on the library's stream around each update; an L2
+flush (a 512 MiB write) runs between timed updates, outside the events;
+ms_per_step is the max over ranks of the mean.  `e2e` times the same
+update through the host-pointer API (pinned host buffers, H2D copies of the
+whole rollout and the D2H of the statistics inside the timed region).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "PPO-update samples/s (fwd+bwd+GAE+Adam)"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--config", default=None, choices=["c1", "c2", "c4", "c5"])
+    p.add_argument("--precision", default=None, choices=["tf32", "fp32", "bf16"])
+    p.add_argument("--envs-per-gpu", type=int, default=None)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--profile-only", action="store_true",
+                   help="run warmup+steps without clocks/baselines (for ncu)")
+    return p.parse_args()
+
+
+def workload(args, world):
+    from zealot_b200 import synth
+    name = args.config or "c2"
+    w = synth.WORKLOADS[name]
+    if name == "c4":
+        n_envs_local = w.n_envs // world  # the 65,536-env job split over ranks
+        scaling = "strong"
+    else:
+        n_envs_local = args.envs_per_gpu or w.n_envs
+        scaling = "weak"
+    precision = args.precision or w.precision
+    return w, n_envs_local, precision, scaling
+
+
+def flops_per_sample_pass(adims, cdims):
+    """Algorithmic GEMM FLOPs per sample per epoch: forward, weight gradient
+    (every layer) and input gradient (every layer but the first)."""
+    f = 0
+    for d in (adims, cdims):
+        macs = [d[l] * d[l + 1] for l in range(len(d) - 1)]
+        f += 2 * sum(macs) * 2 + 2 * sum(macs[1:])
+    return f
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except OSError:
+        return {}
+
+
+def tf32_peak(torch, dev):
+    """cuBLAS tf32 GEMM (8192^3) throughput, the tensor-core denominator for
+    a tf32 kernel (MEASURED_PEAKS has bf16 only).  Best of 10, burst."""
+    torch.backends.cuda.matmul.allow_tf32 = True
+    a = torch.randn(8192, 8192, device=dev)
+    b = torch.randn(8192, 8192, device=dev)
+    for _ in range(3):
+        a @ b
+    torch.cuda.synchronize()
+    best = 1e9
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        a @ b
+        e1.record()
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    torch.backends.cuda.matmul.allow_tf32 = False
+    del a, b
+    return 2 * 8192 ** 3 / (best * 1e-3) / 1e12
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu
+    summary (a `traffic_bytes_per_launch:` line), else None."""
+    d = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(d):
+        return None
+    for fn in sorted(os.listdir(d)):
+        if not fn.endswith((".md", ".txt")):
+            continue
+        for ln in open(os.path.join(d, fn)):
+            if ln.strip().startswith("traffic_bytes_per_launch:"):
+                try:
+                    return float(ln.split(":", 1)[1].split()[0])
+                except ValueError:
+                    return None
+    return None
+
+
+# ------------------------------------------------------------- CPU legs
+
+def cpu_minibatch_sample(w, seed=0):
+    """Oracle (C restatement of zealot-rl) timing of one minibatch step on
+    all host cores.  Returns (seconds per minibatch step, threads, rows)."""
+    import oracle as O
+    from zealot_b200 import synth
+
+    mb = w.n // w.minibatches
+    # a bounded sample: the minibatch rows, drawn as a full rollout would be
+    n_envs = max(1, (mb + w.T - 1) // w.T)
+    rng = np.random.default_rng(seed)
+    params = synth.xavier_params(rng, w.actor_dims, w.critic_dims)
+    n = n_envs * w.T
+    od, cd, A = w.actor_dims[0], w.critic_dims[0], w.actor_dims[-1]
+    b = O.SoaBatch(obs=rng.standard_normal((n, od), dtype=np.float32),
+                   critic_obs=rng.standard_normal((n, cd), dtype=np.float32),
+                   action=rng.standard_normal((n, A), dtype=np.float32) * 0.1,
+                   mean_old=np.zeros((n, A), np.float32),
+                   logp_old=np.full(n, -26.0, np.float32),
+                   value_old=np.zeros(n, np.float32),
+                   adv=rng.standard_normal(n, dtype=np.float32),
+                   ret=rng.standard_normal(n, dtype=np.float32) * 0.1)
+    ac = O.ActorCritic(w.actor_dims, w.critic_dims)
+    ac.params = params
+    threads = os.cpu_count() or 1
+    idx = np.arange(mb, dtype=np.int64)
+    cfg = O.PpoConfig()
+    t0 = time.perf_counter()
+    g, sums = ac.minibatch_grads(b, idx, cfg, n_threads=threads)
+    ac.apply(cfg, g, float(sums[2]))
+    dt = time.perf_counter() - t0
+    return dt, threads, mb
+
+
+def cpu_baseline(w):
+    dt, threads, mb = cpu_minibatch_sample(w)
+    steps = w.epochs * w.minibatches
+    value = w.n / (dt * steps)
+    return {"value": value, "unit": "samples/s", "cores": threads, "kind": "port",
+            "sample": f"1 of {steps} minibatch steps ({mb} samples fwd+bwd+clip+Adam) "
+                      f"of {w.name}, {dt:.2f} s, scaled x{steps}; GAE/adv-norm omitted (<1%)"}
+
+
+def run_reference(args):
+    """The reference's CPU path (zealot-rl restated in C, the oracle port):
+    each step is a bounded sample of the update (one minibatch step), scaled
+    to the whole update's samples/s."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    w, _, precision, scaling = workload(args, 1)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        dt, threads, mb = cpu_minibatch_sample(w, seed=i)
+        if i >= args.warmup:
+            vals.append(dt)
+    dt = statistics.median(vals)
+    steps = w.epochs * w.minibatches
+    value = w.n / (dt * steps)
+    line = {"metric": METRIC, "value": value, "unit": "samples/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt * steps * 1e3, "higher_is_better": True, "scaling": scaling,
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": w.name, "n_envs": w.n_envs, "T": w.T,
+                       "epochs": w.epochs, "minibatches": w.minibatches,
+                       "actor": list(w.actor_dims), "critic": list(w.critic_dims)},
+            "cpu_baseline": {"value": value, "unit": "samples/s", "cores": threads,
+                             "kind": "port",
+                             "sample": f"per step 1 of {steps} minibatch steps "
+                                       f"({mb} samples), scaled x{steps}"},
+            "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------- GPU leg
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+    from zealot_b200 import native as N
+    from zealot_b200 import synth
+    from zealot_b200 import zealot_rl as Z
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("gloo", timeout=timedelta(seconds=120))
+
+    w, n_envs, precision, scaling = workload(args, world)
+    comm = None
+    if world > 1:
+        idb = torch.zeros(128, dtype=torch.uint8)
+        if rank == 0:
+            import ctypes
+            buf = (ctypes.c_uint8 * 128)()
+            N.check(N.lib().zrl_nccl_unique_id(buf))
+            idb = torch.tensor(list(buf), dtype=torch.uint8)
+        dist.broadcast(idb, 0)
+        comm = N.CommC()
+        comm.rank, comm.world_size, comm.timeout_ms = rank, world, 120000
+        for i, v in enumerate(idb.tolist()):
+            comm.nccl_id[i] = v
+
+    ac = Z.ActorCritic(w.actor_dims, w.critic_dims, precision=precision, device=local,
+                       comm=comm)
+    # identical parameters on every rank; per-rank rollouts of its own envs
+    params = synth.xavier_params(np.random.default_rng(1234), w.actor_dims, w.critic_dims)
+    ac.params = params
+    ac.lr = w.lr
+
+    def gpu_forward(p, obs, cobs):
+        return ac.forward(obs, cobs)
+
+    ro = synth.make_rollout(1000 + rank, n_envs, w.T, w.actor_dims, w.critic_dims,
+                            gpu_forward, params=params)
+    n_local = ro.n
+    n_global = n_local * world
+    row_off = rank * n_local
+    cfg = Z.PpoConfig(epochs=w.epochs, minibatches=w.minibatches, adaptive_lr=True)
+
+    # device-resident copies
+    def dt_(a, dtype=torch.float32):
+        return torch.from_numpy(np.ascontiguousarray(a)).to(dev, dtype)
+
+    d = {f: dt_(getattr(ro, f)) for f in ("obs", "critic_obs", "action", "mean_old",
+                                          "logp_old", "value_old")}
+    d_rew = dt_(ro.rewards)
+    d_val = dt_(ro.value_old.reshape(ro.n_envs, ro.T))
+    d_done = dt_(ro.dones, torch.uint8)
+    d_lv = dt_(ro.last_values)
+    d_adv = torch.zeros(n_local, device=dev)
+    d_ret = torch.zeros(n_local, device=dev)
+    dbatch = Z.SoaBatch(adv=d_adv, ret=d_ret, **d)
+    # pinned host copies for the e2e leg
+    def pin(a, dtype=torch.float32):
+        t = torch.from_numpy(np.ascontiguousarray(a)).to(dtype).pin_memory()
+        return t.numpy()
+
+    h = {f: pin(getattr(ro, f)) for f in ("obs", "critic_obs", "action", "mean_old",
+                                          "logp_old", "value_old")}
+    h_rew, h_val = pin(ro.rewards), pin(ro.value_old.reshape(ro.n_envs, ro.T))
+    h_done = pin(ro.dones, torch.uint8)
+    h_lv = pin(ro.last_values)
+    hbatch = Z.SoaBatch(adv=pin(np.zeros(n_local, np.float32)),
+                        ret=pin(np.zeros(n_local, np.float32)), **h)
+    h2d_bytes = sum(a.nbytes for a in h.values()) + h_rew.nbytes + h_val.nbytes + \
+        h_done.nbytes + h_lv.nbytes
+    d2h_bytes = 5 * 4  # PpoStats
+
+    stream = torch.cuda.ExternalStream(N.lib().zrl_stream(ac.ctx.h), device=dev)
+    flush = torch.empty(512 * 1024 * 1024 // 4, device=dev)
+
+    def step_device():
+        return ac.gae_update(d_rew, d_val, d_done, d_lv, dbatch, cfg, n_global, row_off)
+
+    def step_host():
+        return ac.gae_update(h_rew, h_val, h_done, h_lv, hbatch, cfg, n_global, row_off)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def timed(fn, k):
+        times = []
+        for _ in range(k):
+            with torch.cuda.stream(stream):
+                flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            st = fn()
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        return times, st
+
+    for _ in range(args.warmup):
+        step_device()
+    barrier()
+    torch.cuda.synchronize()
+    if args.profile_only:
+        for _ in range(args.steps):
+            step_device()
+        torch.cuda.synchronize()
+        return
+
+    clocks = Clocks(local)
+    clocks.start()
+    l0 = ac.kernel_launches()
+    barrier()
+    torch.cuda.synchronize()
+    times, st = timed(step_device, args.steps)
+    torch.cuda.synchronize()
+    barrier()
+    launches = (ac.kernel_launches() - l0) // args.steps
+    clk = clocks.stop()
+    ms = sum(times) / len(times)
+    # e2e through the host-pointer API
+    for _ in range(max(1, args.warmup // 2)):
+        step_host()
+    e2e_times, _ = timed(step_host, max(3, args.steps // 2))
+    e2e_ms = sum(e2e_times) / len(e2e_times)
+    # profiling pass: GEMM device time via events around each GEMM launch
+    N.check(N.lib().zrl_set_profiling(ac.ctx.h, 1), ac.ctx.h)
+    step_device()
+    import ctypes as C
+    g_ms, u_ms, g_n = C.c_float(), C.c_float(), C.c_int64()
+    N.lib().zrl_get_profile(ac.ctx.h, C.byref(g_ms), C.byref(u_ms), C.byref(g_n))
+    N.lib().zrl_set_profiling(ac.ctx.h, 0)
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = t.tolist()
+
+    value = n_global / (ms * 1e-3)
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        ac.close()
+        return
+    peaks = measured_peaks()
+    fl = flops_per_sample_pass(w.actor_dims, w.critic_dims) * n_local * w.epochs
+    if precision == "bf16":
+        peak, peak_src = peaks.get("bf16_tflops", 1590.0), "MEASURED_PEAKS bf16_tflops (burst)"
+    elif precision == "tf32":
+        peak, peak_src = tf32_peak(torch, dev), "cuBLAS tf32 8192^3 measured in this run (burst)"
+    else:
+        peak, peak_src = 75.0, "nominal fp32 CUDA-core peak (no measured figure)"
+    achieved = fl / (g_ms.value * 1e-3) / 1e12 if g_ms.value > 0 else None
+    roof = {"bound": "tensor", "kernel": "mlp gemm (all GEMM launches of one update)",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": (achieved / peak) if achieved else None,
+            "traffic": profile_traffic(), "peak_source": peak_src,
+            "gemm_ms_per_update": g_ms.value, "gemm_launches_per_update": g_n.value,
+            "gemm_share_of_update": g_ms.value / u_ms.value if u_ms.value else None,
+            "algorithmic_gflop_per_update": fl / 1e9}
+    cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline(w)
+    line = {"metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+            "dtype": precision, "data": "synthetic (seeded rollouts, Xavier-uniform init)",
+            "config": {"workload": w.name, "n_envs_per_gpu": n_envs, "n_envs_total": n_envs * world,
+                       "T": w.T, "samples_per_update": n_global, "epochs": w.epochs,
+                       "minibatches": w.minibatches,
+                       "minibatch_size": n_global // w.minibatches,
+                       "actor": list(w.actor_dims), "critic": list(w.critic_dims),
+                       "parallelism": f"dp{world}", "l2": "512 MiB flush between timed updates"},
+            "e2e": {"value": n_global / (e2e_ms * 1e-3), "unit": "samples/s",
+                    "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes},
+            "gpu_launches": int(launches),
+            "roofline": roof, "clocks": clk, "cpu_baseline": cpu,
+            "stats_last": {"kl": st.kl, "surrogate": st.surrogate,
+                           "value_loss": st.value_loss, "entropy": st.entropy, "lr": st.lr}}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    ac.close()
+
+
+if __name__ == "__main__":
+    main()

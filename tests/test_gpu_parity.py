@@ -1,0 +1,289 @@
+"""Parity of the CUDA library with the CPU oracle, called through the C ABI.
+
+Tolerances (written in each test):
+* integer / index work (permutations) and the recurrences the reference
+  evaluates in plain f32 with a fixed order (GAE, Welford, Adam given the
+  same gradient): bit-exact;
+* fp32 CUDA-core GEMM mode: the reference's sums in another order,
+  1e-4 relative (norm-wise per tensor) for gradients, 1e-5 for forwards;
+* tf32 tensor-core mode: 2e-3 relative for GEMM outputs, gradients and
+  losses (the BASELINE tolerance).
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from helpers import C_A, C_C, SMALL_A, SMALL_C, Case, rel, tensor_rel
+from zealot_b200 import native as N
+from zealot_b200 import zealot_rl as Z
+
+pytestmark = pytest.mark.gpu
+
+TOL_FWD = {"fp32": 1e-5, "tf32": 2e-3}
+TOL_GRAD = {"fp32": 1e-4, "tf32": 2e-3}
+PRECISIONS = ["fp32", "tf32"]
+
+
+def test_gae_bit_exact():
+    rng = np.random.default_rng(3)
+    n_envs, T = 37, 24
+    r = rng.standard_normal((n_envs, T), dtype=np.float32)
+    v = rng.standard_normal((n_envs, T), dtype=np.float32)
+    d = (rng.random((n_envs, T)) < 0.1).astype(np.uint8)
+    lv = rng.standard_normal(n_envs, dtype=np.float32)
+    ctx = Z.Context((4, 4), (4, 1), precision="fp32")
+    adv = np.empty_like(r)
+    ret = np.empty_like(r)
+    ctx.call("zrl_gae", N.ptr(r), N.ptr(v), N.ptr(d), N.ptr(lv), n_envs, T, 0.99, 0.95,
+             N.ptr(adv), N.ptr(ret), 0)
+    a2, r2 = O.gae_batch(r, v, d, lv, 0.99, 0.95)
+    assert np.array_equal(adv, a2) and np.array_equal(ret, r2)
+
+
+def test_gae_reference_known_answers():
+    # ppo.rs:709-721 and 760-768 through the GPU kernel
+    adv, ret = Z.gae([1.0, 2.0], [0.0, 0.0], [0, 0], 0.0, 1.0, 1.0)
+    assert abs(ret[1] - 2) < 1e-6 and abs(ret[0] - 3) < 1e-6 and abs(adv[0] - 3) < 1e-6
+    adv, _ = Z.gae([1.0, 1.0], [5.0, 5.0], [1, 0], 0.0, 0.99, 0.95)
+    assert abs(adv[0] + 4.0) < 1e-6
+
+
+@pytest.mark.parametrize("precision", PRECISIONS)
+@pytest.mark.parametrize("dims", [(SMALL_A, SMALL_C), (C_A, C_C)])
+def test_forward_matches_oracle(precision, dims):
+    case = Case(*dims, n_envs=9, T=29, seed=4, perturb=0.02, norm_stats=True)
+    gpu = case.gpu_ac(precision)
+    orc = case.oracle_ac()
+    m, v = gpu.forward(case.ro.obs, case.ro.critic_obs)
+    m2, v2 = orc.forward(case.ro.obs, case.ro.critic_obs)
+    assert rel(m, m2) < TOL_FWD[precision]
+    assert rel(v, v2) < TOL_FWD[precision]
+
+
+@pytest.mark.parametrize("precision", PRECISIONS)
+@pytest.mark.parametrize("dims,n_envs,T", [((SMALL_A, SMALL_C), 8, 12),
+                                           ((C_A, C_C), 64, 24)])
+def test_minibatch_grads_match_oracle(precision, dims, n_envs, T):
+    case = Case(*dims, n_envs=n_envs, T=T, seed=5, perturb=0.03, norm_stats=True)
+    gpu = case.gpu_ac(precision)
+    orc = case.oracle_ac()
+    cfg = Z.PpoConfig()
+    idx = O.shuffle(11, case.ro.n)[: case.ro.n * 3 // 4]
+    g, s = gpu.minibatch_grads(case.soa(), idx, cfg)
+    g2, s2 = orc.minibatch_grads(case.oracle_batch(), idx, O.PpoConfig(), n_threads=8)
+    errs = tensor_rel(g, g2, case.adims, case.cdims)
+    bad = {k: v for k, v in errs.items() if v > TOL_GRAD[precision]}
+    assert not bad, bad
+    # surrogate / value loss / kl sums
+    for a, b in zip(s, s2):
+        assert abs(a - b) <= TOL_GRAD[precision] * max(abs(b), 1e-3), (s, s2)
+
+
+@pytest.mark.parametrize("clip", [1e6, 1e-3])
+@pytest.mark.parametrize("kl", [0.0, 0.001, 0.05])
+def test_apply_grads_matches_oracle(clip, kl):
+    case = Case(seed=6)
+    rng = np.random.default_rng(7)
+    gpu = case.gpu_ac("fp32", lr=3e-3)
+    orc = case.oracle_ac(lr=3e-3)
+    npar = len(case.params)
+    t3 = np.array([4, 4, 4], np.int32)
+    m = (0.01 * rng.standard_normal(npar)).astype(np.float32)
+    v = (1e-4 * rng.random(npar)).astype(np.float32)
+    gpu.set_adam_state(t3, m, v)
+    orc.set_adam_state(t3, m, v)
+    grads = (0.05 * rng.standard_normal(npar)).astype(np.float32)
+    cfg = Z.PpoConfig(max_grad_norm=clip)
+    for _ in range(3):
+        gpu.apply_grads(cfg, grads, kl)
+        orc.apply(O.PpoConfig(max_grad_norm=clip), grads, kl)
+    assert gpu.lr == orc.lr
+    p, p2 = gpu.params, orc.params
+    (tg, mg, vg), (to, mo, vo) = gpu.adam_state(), orc.adam_state()
+    assert tg.tolist() == to.tolist() == [7, 7, 7]
+    if clip > 1e5:
+        # no clipping: the same f32 operations in the same order -> bit-exact
+        assert np.array_equal(p, p2) and np.array_equal(mg, mo) and np.array_equal(vg, vo)
+    else:
+        # the norm is summed in another order: the clip scale may differ by
+        # an ulp (net.rs:181-202), which the 1e-5 Adam tolerance covers
+        assert rel(p - case.params, p2 - case.params) < 1e-5
+        assert rel(mg, mo) < 1e-5 and rel(vg, vo) < 1e-5
+
+
+@pytest.mark.parametrize("adaptive", [False, True])
+@pytest.mark.parametrize("epochs,minibatches", [(1, 1), (3, 2), (2, 5)])
+def test_update_matches_oracle_fp32(adaptive, epochs, minibatches):
+    case = Case(n_envs=10, T=16, seed=8, perturb=0.03, norm_stats=True)
+    cfg = Z.PpoConfig(epochs=epochs, minibatches=minibatches, adaptive_lr=adaptive)
+    ocfg = O.PpoConfig(epochs=epochs, minibatches=minibatches, adaptive_lr=adaptive)
+    gpu = case.gpu_ac("fp32")
+    orc = case.oracle_ac()
+    st = gpu.update(case.soa(), cfg)
+    st2 = orc.update(case.oracle_batch(), ocfg)
+    errs = tensor_rel(gpu.params - case.params, orc.params - case.params,
+                      case.adims, case.cdims)
+    bad = {k: v for k, v in errs.items() if v > 1e-3}
+    assert not bad, bad
+    assert abs(st.lr - st2["lr"]) <= 1e-6 * st2["lr"]
+    for k in ("kl", "surrogate", "value_loss", "entropy"):
+        assert abs(getattr(st, k) - st2[k]) <= 1e-4 * max(abs(st2[k]), 1e-3), (k, st, st2)
+    assert gpu.adam_state()[0].tolist() == [epochs * minibatches] * 3
+
+
+def test_update_c1_matches_oracle_fp32():
+    # N=64 x T=24, 1 epoch x 1 minibatch, lr 1e-3
+    case = Case(C_A, C_C, n_envs=64, T=24, seed=0)
+    for adaptive in (False, True):
+        cfg = Z.PpoConfig(epochs=1, minibatches=1, adaptive_lr=adaptive)
+        gpu = case.gpu_ac("fp32")
+        orc = case.oracle_ac()
+        st = gpu.update(case.soa(), cfg)
+        st2 = orc.update(case.oracle_batch(),
+                         O.PpoConfig(epochs=1, minibatches=1, adaptive_lr=adaptive),
+                         n_threads=8)
+        errs = tensor_rel(gpu.params - case.params, orc.params - case.params,
+                          case.adims, case.cdims)
+        bad = {k: v for k, v in errs.items() if v > 1e-3}
+        assert not bad, bad
+        assert abs(st.value_loss - st2["value_loss"]) <= 1e-4 * abs(st2["value_loss"])
+        assert abs(st.surrogate - st2["surrogate"]) <= 1e-4 * max(abs(st2["surrogate"]), 1e-3)
+
+
+def test_update_edge_cases():
+    case = Case(n_envs=3, T=5, seed=9)
+    gpu = case.gpu_ac("fp32")
+    # fewer samples than minibatches: the reference panics (ppo.rs:340)
+    with pytest.raises(N.ZrlError):
+        gpu.update(case.soa(), Z.PpoConfig(minibatches=16))
+    # epochs = 0: stats are {0, 0, 0, 0, lr} and nothing moves
+    st = gpu.update(case.soa(), Z.PpoConfig(epochs=0))
+    assert (st.kl, st.surrogate, st.value_loss, st.entropy) == (0, 0, 0, 0)
+    assert np.array_equal(gpu.params, case.params)
+    # n == minibatches (one sample per minibatch) and a ragged tail
+    for mbs in (15, 4):
+        g2 = case.gpu_ac("fp32")
+        o2 = case.oracle_ac()
+        st = g2.update(case.soa(), Z.PpoConfig(epochs=2, minibatches=mbs))
+        st2 = o2.update(case.oracle_batch(), O.PpoConfig(epochs=2, minibatches=mbs))
+        assert rel(g2.params - case.params, o2.params - case.params) < 1e-3
+        assert abs(st.value_loss - st2["value_loss"]) <= 1e-4 * abs(st2["value_loss"])
+
+
+def test_update_from_samples_normalizes_adv_in_place():
+    case = Case(n_envs=4, T=6, seed=10)
+    b = case.soa()
+    samples = [Z.Sample(obs=b.obs[i], critic_obs=b.critic_obs[i], action=b.action[i],
+                        mean_old=b.mean_old[i], logp_old=b.logp_old[i],
+                        value_old=b.value_old[i], adv=b.adv[i], ret=b.ret[i])
+               for i in range(b.n)]
+    gpu = case.gpu_ac("fp32")
+    gpu.update(samples, Z.PpoConfig(epochs=1, minibatches=2))
+    ob = case.oracle_batch()
+    case.oracle_ac().update(ob, O.PpoConfig(epochs=1, minibatches=2))
+    assert rel([s.adv for s in samples], ob.adv) < 1e-6
+
+
+def test_gae_update_equals_gae_then_update():
+    case = Case(n_envs=12, T=10, seed=12, perturb=0.02)
+    cfg = Z.PpoConfig(epochs=2, minibatches=3)
+    a = case.gpu_ac("fp32")
+    ro = case.ro
+    st = a.gae_update(ro.rewards, ro.value_old.reshape(ro.n_envs, ro.T), ro.dones,
+                      ro.last_values, case.soa(), cfg)
+    b = case.gpu_ac("fp32")
+    st2 = b.update(case.soa(), cfg)
+    assert np.array_equal(a.params, b.params)
+    assert st == st2
+
+
+def test_record_obs_bit_exact():
+    rng = np.random.default_rng(13)
+    gpu = Z.ActorCritic(SMALL_A, SMALL_C, precision="fp32")
+    obs = rng.standard_normal((300, SMALL_A[0]), dtype=np.float32) * 3 + 1
+    cobs = rng.standard_normal((300, SMALL_C[0]), dtype=np.float32)
+    gpu.record_obs(obs, cobs)
+    om, om2, oc, cm, cm2, cc = gpu.normalizers()
+    mean = np.zeros(SMALL_A[0], np.float32)
+    m2 = np.ones(SMALL_A[0], np.float32)
+    import ctypes as C
+    count = C.c_float(1.0)
+    for r in obs:
+        O.lib().orc_norm_update(mean, m2, C.byref(count), np.ascontiguousarray(r), len(r))
+    assert np.array_equal(om, mean) and np.array_equal(om2, m2) and oc == count.value
+
+
+def _philox_ref(ctr, key):
+    """Philox4x32-10 restated in Python integers (Salmon et al., SC'11)."""
+    M0, M1, W0, W1 = 0xD2511F53, 0xCD9E8D57, 0x9E3779B9, 0xBB67AE85
+    c = list(ctr)
+    k0, k1 = key
+    for _ in range(10):
+        p0 = M0 * c[0]
+        p1 = M1 * c[2]
+        hi0, lo0 = p0 >> 32, p0 & 0xFFFFFFFF
+        hi1, lo1 = p1 >> 32, p1 & 0xFFFFFFFF
+        c = [hi1 ^ c[1] ^ k0, lo1, hi0 ^ c[3] ^ k1, lo0]
+        k0 = (k0 + W0) & 0xFFFFFFFF
+        k1 = (k1 + W1) & 0xFFFFFFFF
+    return c
+
+
+def test_policy_step_philox_sampling():
+    case = Case(n_envs=3, T=7, seed=14, perturb=0.05)
+    gpu = case.gpu_ac("fp32")
+    seed, counter = 0x1234_5678_9ABC, 77
+    act, lp, mean, val = gpu.policy_step(case.ro.obs, case.ro.critic_obs, seed, counter)
+    m2, v2 = gpu.forward(case.ro.obs, case.ro.critic_obs)
+    assert np.array_equal(mean, m2) and np.array_equal(val, v2)
+    ls = gpu.log_std
+    A = len(ls)
+    for row in range(case.ro.n):
+        for g in range((A + 3) // 4):
+            r = _philox_ref((g, row, counter & 0xFFFFFFFF, (counter >> 32) ^ (row >> 32)),
+                            (seed & 0xFFFFFFFF, seed >> 32))
+            u = [((x >> 8) + 0.5) / 16777216.0 for x in r]
+            ra, rb = np.sqrt(-2 * np.log(u[0])), np.sqrt(-2 * np.log(u[2]))
+            z = [ra * np.cos(2 * np.pi * u[1]), ra * np.sin(2 * np.pi * u[1]),
+                 rb * np.cos(2 * np.pi * u[3]), rb * np.sin(2 * np.pi * u[3])]
+            for j in range(4):
+                k = 4 * g + j
+                if k < A:
+                    want = mean[row, k] + np.exp(ls[k]) * z[j]
+                    assert abs(act[row, k] - want) < 1e-4 * max(1.0, abs(want))
+        lp_ref = O.ActorCritic(case.adims, case.cdims)
+        lp_ref.params = gpu.params
+        assert abs(lp[row] - lp_ref.logp(act[row], mean[row])) < 1e-4 * max(1, abs(lp[row]))
+    # a different counter gives different draws; the same one repeats them
+    act2, *_ = gpu.policy_step(case.ro.obs, case.ro.critic_obs, seed, counter + 1)
+    act3, *_ = gpu.policy_step(case.ro.obs, case.ro.critic_obs, seed, counter)
+    assert not np.array_equal(act, act2) and np.array_equal(act, act3)
+
+
+def test_save_load_roundtrip(tmp_path):
+    # ppo.rs:723-758 on the GPU backend
+    rng = Z.Lcg(7)
+    ac = Z.ActorCritic.new([4, 8, 8, 2], [6, 8, 1], 0.3, 1e-3, rng, precision="fp32")
+    for k in range(20):
+        obs = np.sin(np.arange(k, k + 4, dtype=np.float32))
+        cobs = np.cos(np.arange(3 * k, 3 * k + 6, dtype=np.float32))
+        ac.record_obs(obs[None], cobs[None])
+    probes = np.tanh(np.array([[k * 7 + j for j in range(4)] for k in range(3)], np.float32))
+    before, _ = ac.forward(probes)
+    path = str(tmp_path / "rt.safetensors")
+    ac.save(path)
+    ac2 = Z.ActorCritic.load(path, precision="fp32")
+    after, _ = ac2.forward(probes)
+    assert np.max(np.abs(after - before)) < 1e-9
+    assert np.array_equal(ac.log_std, ac2.log_std) and ac.lr == ac2.lr
+    assert np.array_equal(ac.params, ac2.params)
+    data = open(path, "rb").read()
+    ac3 = Z.ActorCritic.load_from_bytes(data, precision="fp32")
+    assert np.array_equal(ac3.params, ac.params)
+
+
+def test_reference_init_matches_oracle():
+    g = Z.ActorCritic.new(SMALL_A, SMALL_C, 0.6, 3e-3, Z.Lcg(2024), precision="fp32")
+    o = O.ActorCritic.new(SMALL_A, SMALL_C, 0.6, 3e-3, O.Lcg(2024))
+    assert np.array_equal(g.params, o.params)
+    assert g.lr == o.lr

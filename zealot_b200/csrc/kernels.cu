@@ -1,0 +1,790 @@
+// kernels.cu -- the bandwidth-bound kernels of the PPO update.
+//
+// Arithmetic that the reference does in plain f32 and that has to match it
+// bit for bit (GAE, the normalizers, Adam) uses the explicitly rounded
+// intrinsics (__fadd_rn, __fmul_rn, ...) so that the compiler cannot fuse a
+// multiply and an add into one FMA.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "zrl_internal.h"
+
+namespace zrl {
+
+namespace {
+
+constexpr float kLogSqrt2Pi = 0.9189385f;  // ppo.rs:18
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide sum in a fixed order (warp shuffles, then warp 0 over warps).
+template <typename T>
+__device__ T block_sum(T v, T *sh) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if constexpr (sizeof(T) == 8)
+    v = warp_sum_d(v);
+  else
+    v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) sh[w] = v;
+  __syncthreads();
+  T r = 0;
+  if (w == 0) {
+    const int nw = (blockDim.x + 31) >> 5;
+    r = lane < nw ? sh[lane] : T(0);
+    if constexpr (sizeof(T) == 8)
+      r = warp_sum_d(r);
+    else
+      r = warp_sum(r);
+  }
+  return r;  // valid in thread 0
+}
+
+// ---------------------------------------------------------------- GAE
+
+// One block handles kEnvs consecutive environments: their [kEnvs*T] slices
+// of rewards/values/dones are contiguous, so they are staged through shared
+// memory with coalesced loads; one thread per env runs the reverse scan
+// (ppo.rs:689-702); results go back through shared memory.
+constexpr int kGaeEnvs = 32;
+constexpr int kGaeThreads = 128;
+
+// Shared memory per block when staged: kGaeEnvs * T * (4 floats + 1 byte).
+// Longer horizons read global memory directly (same arithmetic).
+constexpr int kGaeMaxStagedT = 48 * 1024 / (kGaeEnvs * 17);
+
+template <bool STAGED>
+__global__ void __launch_bounds__(kGaeThreads)
+gae_kernel(GaeArgs a, double *partials) {
+  extern __shared__ float sm[];
+  const int64_t e0 = (int64_t)blockIdx.x * kGaeEnvs;
+  const int ne = (int)(a.n_envs - e0 < kGaeEnvs ? a.n_envs - e0 : kGaeEnvs);
+  const int T = (int)a.T;
+  const int cnt = ne * T;
+  const int64_t base = e0 * T;
+  const float *r_ = a.rewards + base;
+  const float *v_ = a.values + base;
+  const uint8_t *d_ = a.dones + base;
+  float *adv_ = a.adv + base;
+  float *ret_ = a.ret + base;
+  if (STAGED) {
+    float *s_r = sm;
+    float *s_v = s_r + kGaeEnvs * T;
+    float *s_adv = s_v + kGaeEnvs * T;
+    float *s_ret = s_adv + kGaeEnvs * T;
+    uint8_t *s_d = reinterpret_cast<uint8_t *>(s_ret + kGaeEnvs * T);
+    for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
+      s_r[i] = r_[i];
+      s_v[i] = v_[i];
+      s_d[i] = d_[i];
+    }
+    __syncthreads();
+    r_ = s_r;
+    v_ = s_v;
+    d_ = s_d;
+    adv_ = s_adv;
+    ret_ = s_ret;
+  }
+  if (threadIdx.x < ne) {
+    const int e = threadIdx.x;
+    const float gl = __fmul_rn(a.gamma, a.lam);
+    float acc = 0.0f;
+    float next_v = a.last_values[e0 + e];
+    for (int t = T - 1; t >= 0; --t) {
+      const int i = e * T + t;
+      const float nt = d_[i] ? 0.0f : 1.0f;
+      // delta = r + gamma * next_v * nt - v   (left to right, ppo.rs:696)
+      const float delta =
+          __fsub_rn(__fadd_rn(r_[i], __fmul_rn(__fmul_rn(a.gamma, next_v), nt)), v_[i]);
+      // gae = delta + gamma * lam * nt * gae   (ppo.rs:697)
+      acc = __fadd_rn(delta, __fmul_rn(__fmul_rn(gl, nt), acc));
+      adv_[i] = acc;
+      ret_[i] = __fadd_rn(acc, v_[i]);
+      next_v = v_[i];
+    }
+  }
+  __syncthreads();
+  double part = 0.0;
+  for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
+    const float av = adv_[i];  // shared (staged) or global, written above
+    if (STAGED) {
+      a.adv[base + i] = av;
+      a.ret[base + i] = ret_[i];
+    }
+    part += (double)av;
+  }
+  __shared__ double sh[32];
+  double tot = block_sum(part, sh);
+  if (threadIdx.x == 0 && partials) partials[blockIdx.x] = tot;
+}
+
+// ------------------------------------------------------- advantage moments
+
+constexpr int kAdvThreads = 256;
+
+__global__ void adv_sum_kernel(const float *adv, int64_t n, double *partials) {
+  double s = 0.0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    s += (double)adv[i];
+  __shared__ double sh[32];
+  double t = block_sum(s, sh);
+  if (threadIdx.x == 0) partials[blockIdx.x] = t;
+}
+
+// One block: moments[slot] = sum of partials (fixed order).
+__global__ void reduce_partials_kernel(const double *partials, int nblk,
+                                       double *moments, int slot) {
+  double s = 0.0;
+  for (int i = threadIdx.x; i < nblk; i += blockDim.x) s += partials[i];
+  __shared__ double sh[32];
+  double t = block_sum(s, sh);
+  if (threadIdx.x == 0) moments[slot] = t;
+}
+
+__device__ __forceinline__ float adv_mean_from(const double *moments,
+                                               int64_t n_global) {
+  return (float)(moments[0] / (double)n_global);
+}
+
+__global__ void adv_sqdev_kernel(const float *adv, int64_t n,
+                                 const double *moments, int64_t n_global,
+                                 double *partials) {
+  const float mean = adv_mean_from(moments, n_global);
+  double s = 0.0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float d = __fsub_rn(adv[i], mean);
+    s += (double)d * (double)d;
+  }
+  __shared__ double sh[32];
+  double t = block_sum(s, sh);
+  if (threadIdx.x == 0) partials[blockIdx.x] = t;
+}
+
+__global__ void adv_finalize_kernel(const double *moments, int64_t n_global,
+                                    DevState *st) {
+  const float mean = adv_mean_from(moments, n_global);
+  const float var = (float)(moments[1] / (double)n_global);
+  float sd = __fsqrt_rn(var);
+  if (sd < 1e-6f) sd = 1e-6f;  // ppo.rs:345
+  st->adv_mean = mean;
+  st->adv_sd = sd;
+}
+
+// ------------------------------------------------------------ gather
+
+// One warp per output position: copies row order[p] of every batch array,
+// applying Normalizer::normalize (ppo.rs:198-205) to the two observation
+// rows and the advantage normalization (ppo.rs:346-348) to adv.
+__global__ void gather_kernel(GatherArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const float am = a.st->adv_mean, asd = a.st->adv_sd;
+  for (int64_t p = warp; p < a.n_used; p += nwarps) {
+    const int64_t r = a.order[p];
+    const float *o = a.obs + r * a.od;
+    float *xo = a.x_a + p * a.odp;
+    for (int i = lane; i < a.odp; i += 32) {
+      float y = 0.0f;
+      if (i < a.od) {
+        y = __fdiv_rn(__fsub_rn(o[i], a.obs_mean[i]), a.obs_sd[i]);
+        y = fminf(fmaxf(y, -5.0f), 5.0f);
+      }
+      xo[i] = y;
+    }
+    const float *c = a.cobs + r * a.cd;
+    float *xc = a.x_c + p * a.cdp;
+    for (int i = lane; i < a.cdp; i += 32) {
+      float y = 0.0f;
+      if (i < a.cd) {
+        y = __fdiv_rn(__fsub_rn(c[i], a.crit_mean[i]), a.crit_sd[i]);
+        y = fminf(fmaxf(y, -5.0f), 5.0f);
+      }
+      xc[i] = y;
+    }
+    for (int k = lane; k < a.A; k += 32) {
+      a.g_action[p * a.A + k] = a.action[r * a.A + k];
+      a.g_mean_old[p * a.A + k] = a.mean_old[r * a.A + k];
+    }
+    if (lane == 0) {
+      a.g_logp_old[p] = a.logp_old[r];
+      a.g_value_old[p] = a.value_old[r];
+      float ad = a.adv[r];
+      if (a.apply_adv_norm) ad = __fdiv_rn(__fsub_rn(ad, am), asd);
+      a.g_adv[p] = ad;
+      a.g_ret[p] = a.ret[r];
+    }
+  }
+}
+
+// sd[i] = sqrt(max(m2[i]/count, 1e-8)) in f32, the divisor of
+// Normalizer::normalize.
+__global__ void norm_prepare_kernel(const float *m2, float count, int dim,
+                                    float *sd) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < dim) {
+    float var = __fdiv_rn(m2[i], count);
+    if (var < 1e-8f) var = 1e-8f;
+    sd[i] = __fsqrt_rn(var);
+  }
+}
+
+__global__ void normalize_rows_kernel(const float *x, int64_t n, int dim,
+                                      int pitch, const float *mean,
+                                      const float *sd, float *out) {
+  const int64_t total = n * pitch;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = e / pitch;
+    const int i = (int)(e - r * pitch);
+    float y = 0.0f;
+    if (i < dim) {
+      y = __fdiv_rn(__fsub_rn(x[r * dim + i], mean[i]), sd[i]);
+      y = fminf(fmaxf(y, -5.0f), 5.0f);
+    }
+    out[e] = y;
+  }
+}
+
+// ------------------------------------------------------------ PPO loss
+
+constexpr int kLossThreads = 256;
+constexpr int kLossMaxA = 128;  // 4 action dims per lane
+
+// One warp per sample (ppo.rs:410-452).  Lane k holds action dims k,
+// k+32, ...; log-prob and KL are warp sums.  Per-block partials of the
+// log_std gradient and of the three statistics are written to scratch; the
+// last block to finish adds the partials in block order (deterministic).
+__global__ void __launch_bounds__(kLossThreads)
+loss_kernel(LossArgs a, float *partials, unsigned int *ticket) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nwb = blockDim.x >> 5;
+  const int64_t gw = (int64_t)blockIdx.x * nwb + wid;
+  const int64_t nw = (int64_t)gridDim.x * nwb;
+  const int A = a.A;
+  const int width = A + 3;
+  float ls[4], sd[4], inv_var[4], inv_sd[4], gls[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int k = lane + 32 * j;
+    ls[j] = k < A ? a.log_std[k] : 0.0f;
+    sd[j] = expf(ls[j]);
+    inv_var[j] = expf(-2.0f * ls[j]);
+    inv_sd[j] = expf(-ls[j]);
+    gls[j] = 0.0f;
+  }
+  float acc_surr = 0.0f, acc_vloss = 0.0f, acc_kl = 0.0f;
+  const float lo = 1.0f - a.clip, hi = 1.0f + a.clip;
+  const float ent_term = -a.entropy_coef * a.scale;
+  for (int64_t s = gw; s < a.mb; s += nw) {
+    const float *mu = a.mean + s * a.Ap;
+    const float *ac = a.action + s * A;
+    const float *mo = a.mean_old + s * A;
+    float mu_r[4], d_r[4];
+    float lp = 0.0f, kl = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int k = lane + 32 * j;
+      mu_r[j] = 0.0f;
+      d_r[j] = 0.0f;
+      if (k < A) {
+        mu_r[j] = mu[k];
+        d_r[j] = ac[k] - mu_r[j];
+        const float z = d_r[j] / sd[j];
+        lp += -0.5f * z * z - ls[j] - kLogSqrt2Pi;
+        const float dk = (mu_r[j] - mo[k]) * inv_sd[j];
+        kl += 0.5f * (dk * dk);
+      }
+    }
+    lp = warp_sum(lp);
+    kl = warp_sum(kl);
+    const float ratio = expf(lp - a.logp_old[s]);
+    const float adv = a.adv[s];
+    const float rc = fminf(fmaxf(ratio, lo), hi);
+    const float surr = fminf(ratio * adv, rc * adv);
+    const bool clipped = (adv >= 0.0f && ratio > hi) || (adv < 0.0f && ratio < lo);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int k = lane + 32 * j;
+      float g = 0.0f;
+      if (k < A) {
+        if (!clipped) {
+          const float d = d_r[j];
+          g = -(adv * ratio * d * inv_var[j]) * a.scale;
+          const float dls = adv * ratio * ((d * d) * inv_var[j] - 1.0f);
+          gls[j] += -dls * a.scale;
+        }
+        gls[j] += ent_term;
+      }
+      if (k < a.Ap) a.d_actor[s * a.Ap + k] = g;
+    }
+    if (lane == 0) {
+      acc_surr += surr * a.scale;
+      acc_kl += kl * a.scale;
+      // clipped value loss, ppo.rs:439-449
+      const float v = a.value[s * a.cp];
+      const float vo = a.value_old[s];
+      const float R = a.ret[s];
+      const float vc = vo + fminf(fmaxf(v - vo, -a.clip), a.clip);
+      const float eu = v - R, ec = vc - R;
+      const float lu = eu * eu, lc = ec * ec;
+      float vloss, dv;
+      if (lc > lu) {
+        vloss = lc;
+        dv = 2.0f * ec;
+      } else {
+        vloss = lu;
+        dv = 2.0f * eu;
+      }
+      acc_vloss += vloss * a.scale;
+      a.d_critic[s * a.cp] = a.value_coef * dv * a.scale;
+    }
+  }
+  // ---- block partials: warp values into shared memory, summed in order
+  __shared__ float sh[kLossThreads / 32][kLossMaxA + 3];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int k = lane + 32 * j;
+    if (k < A) sh[wid][k] = gls[j];
+  }
+  if (lane == 0) {
+    sh[wid][A] = acc_surr;
+    sh[wid][A + 1] = acc_vloss;
+    sh[wid][A + 2] = acc_kl;
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < width; c += blockDim.x) {
+    float t = 0.0f;
+    for (int w = 0; w < nwb; ++w) t += sh[w][c];
+    partials[(int64_t)blockIdx.x * width + c] = t;
+  }
+  // ---- last block adds the block partials in block order
+  __threadfence();
+  __shared__ bool last;
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  for (int c = threadIdx.x; c < width; c += blockDim.x) {
+    float t = 0.0f;
+    for (int b = 0; b < (int)gridDim.x; ++b)
+      t += __ldcg(&partials[(int64_t)b * width + c]);
+    if (c < A)
+      a.g_logstd[c] = t;
+    else
+      a.sums3[c - A] = t;
+  }
+  if (threadIdx.x == 0) *ticket = 0u;
+}
+
+// ------------------------------------------------------------ colsum
+
+__global__ void colsum_kernel(const float *x, int64_t rows, int cols, int ld,
+                              float *partials, int splits) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int z = blockIdx.y;
+  if (c >= cols) return;
+  const int64_t chunk = (rows + splits - 1) / splits;
+  const int64_t r0 = z * chunk, r1 = (rows < r0 + chunk ? rows : r0 + chunk);
+  float s = 0.0f;
+  for (int64_t r = r0; r < r1; ++r) s += x[r * ld + c];
+  partials[(int64_t)z * cols + c] = s;
+}
+
+// ------------------------------------------------------ segment reduce
+
+__global__ void reduce_segments_kernel(ReduceSegs segs) {
+  const ReduceSeg sg = segs.seg[blockIdx.y];
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < sg.count;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.0f;
+    for (int z = 0; z < sg.splits; ++z) s += sg.src[(int64_t)z * sg.count + i];
+    sg.dst[i] = s;
+  }
+}
+
+// ------------------------------------------------------------ pre-step
+
+__device__ float powi_f(float a, int b) {
+  // square-and-multiply, the f32::powi lowering with a runtime exponent
+  const bool recip = b < 0;
+  float r = 1.0f;
+  for (;;) {
+    if (b & 1) r = __fmul_rn(r, a);
+    b /= 2;
+    if (b == 0) break;
+    a = __fmul_rn(a, a);
+  }
+  return recip ? __fdiv_rn(1.0f, r) : r;
+}
+
+constexpr int kPrestepThreads = 256;
+
+__global__ void __launch_bounds__(kPrestepThreads)
+prestep_kernel(PrestepArgs a, double *partials, unsigned int *ticket) {
+  double sa = 0.0, sc = 0.0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = a.actor_begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+       i < a.actor_end; i += stride) {
+    const double g = a.grads[i];
+    sa += g * g;
+  }
+  for (int64_t i = a.critic_begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+       i < a.critic_end; i += stride) {
+    const double g = a.grads[i];
+    sc += g * g;
+  }
+  __shared__ double sh[32];
+  double ta = block_sum(sa, sh);
+  double tc = block_sum(sc, sh);
+  if (threadIdx.x == 0) {
+    partials[2 * blockIdx.x] = ta;
+    partials[2 * blockIdx.x + 1] = tc;
+  }
+  __threadfence();
+  __shared__ bool last;
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last || threadIdx.x != 0) return;
+  __threadfence();
+  double na = 0.0, nc = 0.0;
+  for (int b = 0; b < (int)gridDim.x; ++b) {
+    na += __ldcg(&partials[2 * b]);
+    nc += __ldcg(&partials[2 * b + 1]);
+  }
+  *ticket = 0u;
+  DevState *st = a.st;
+  st->sumsq[0] = (float)na;
+  st->sumsq[1] = (float)nc;
+  const float kl = a.sums3[2];
+  // entropy of the pre-step log_std (ppo.rs:308-311, 473)
+  const float c = __fadd_rn(0.5f, kLogSqrt2Pi);
+  float ent = 0.0f;
+  for (int k = 0; k < a.A; ++k) ent = __fadd_rn(ent, __fadd_rn(a.log_std[k], c));
+  if (a.count_stats) {
+    st->ep_acc[0] += kl;
+    st->ep_acc[1] += a.sums3[0];
+    st->ep_acc[2] += a.sums3[1];
+    st->ep_acc[3] += ent;
+  }
+  // adaptive LR (ppo.rs:476-482)
+  float lr = st->lr;
+  if (a.adaptive_lr) {
+    if (kl > a.desired_kl * 2.0f)
+      lr = fmaxf(__fdiv_rn(lr, 1.5f), a.lr_min);
+    else if (kl > 0.0f && kl < a.desired_kl / 2.0f)
+      lr = fminf(__fmul_rn(lr, 1.5f), a.lr_max);
+  }
+  st->lr = lr;
+  st->step_lr = lr;
+  // per-net clip (net.rs:197-202)
+  const float norms[2] = {__fsqrt_rn((float)na), __fsqrt_rn((float)nc)};
+  for (int j = 0; j < 2; ++j) {
+    const float n = norms[j];
+    st->clip_scale[j] =
+        (n > a.max_grad_norm && n > 0.0f) ? __fdiv_rn(a.max_grad_norm, n) : 1.0f;
+  }
+  // Adam steps and bias corrections (net.rs:235-238, ppo.rs:497-500)
+  for (int j = 0; j < 3; ++j) {
+    const int t = st->t[j] + 1;
+    st->t[j] = t;
+    st->bc1[j] = __fsub_rn(1.0f, powi_f(0.9f, t));
+    st->bc2[j] = __fsub_rn(1.0f, powi_f(0.999f, t));
+  }
+  if (a.count_stats && a.last_of_epoch) {
+    const float inv = __fdiv_rn(1.0f, (float)a.minibatches);
+    st->stats[0] = st->ep_acc[0] * inv;
+    st->stats[1] = st->ep_acc[1] * inv;
+    st->stats[2] = st->ep_acc[2] * inv;
+    st->stats[3] = st->ep_acc[3] * inv;
+    st->stats[4] = lr;
+    for (int j = 0; j < 4; ++j) st->ep_acc[j] = 0.0f;
+  }
+}
+
+// ------------------------------------------------------------ Adam
+
+__device__ __forceinline__ void adam_one(float &p, float &m, float &v, float g,
+                                         float lr, float bc1, float bc2,
+                                         bool clamp_ls) {
+  const float b1 = 0.9f, b2 = 0.999f, eps = 1e-8f;
+  const float omb1 = 1.0f - b1, omb2 = 1.0f - b2;  // folded in f32
+  m = __fadd_rn(__fmul_rn(b1, m), __fmul_rn(omb1, g));
+  v = __fadd_rn(__fmul_rn(b2, v), __fmul_rn(__fmul_rn(omb2, g), g));
+  const float step = __fdiv_rn(__fmul_rn(lr, __fdiv_rn(m, bc1)),
+                               __fadd_rn(__fsqrt_rn(__fdiv_rn(v, bc2)), eps));
+  float y = __fsub_rn(p, step);
+  if (clamp_ls) y = fminf(fmaxf(y, -1.6f), 1.0f);
+  p = y;
+}
+
+__global__ void adam_kernel(AdamArgs a) {
+  const DevState *st = a.st;
+  const float lr = st->step_lr;
+  const int64_t n4 = a.n / 4;
+  float4 *p4 = reinterpret_cast<float4 *>(a.p);
+  float4 *m4 = reinterpret_cast<float4 *>(a.m);
+  float4 *v4 = reinterpret_cast<float4 *>(a.v);
+  const float4 *g4 = reinterpret_cast<const float4 *>(a.g);
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n4;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = q * 4;  // segment boundaries are multiples of 32
+    const int j = i < a.actor_end ? 0 : (i < a.critic_end ? 1 : 2);
+    const float cs = j < 2 ? st->clip_scale[j] : 1.0f;
+    float4 p = p4[q], m = m4[q], v = v4[q], g = g4[q];
+    if (cs != 1.0f) {
+      g.x = __fmul_rn(g.x, cs);
+      g.y = __fmul_rn(g.y, cs);
+      g.z = __fmul_rn(g.z, cs);
+      g.w = __fmul_rn(g.w, cs);
+    }
+    const float b1c = st->bc1[j], b2c = st->bc2[j];
+    const bool cl = j == 2;
+    adam_one(p.x, m.x, v.x, g.x, lr, b1c, b2c, cl);
+    adam_one(p.y, m.y, v.y, g.y, lr, b1c, b2c, cl);
+    adam_one(p.z, m.z, v.z, g.z, lr, b1c, b2c, cl);
+    adam_one(p.w, m.w, v.w, g.w, lr, b1c, b2c, cl);
+    p4[q] = p;
+    m4[q] = m;
+    v4[q] = v;
+  }
+}
+
+// ------------------------------------------------------------ misc
+
+__global__ void unpad_rows_kernel(const float *src, int64_t rows, int pitch,
+                                  int cols, float *dst) {
+  const int64_t total = rows * cols;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = e / cols;
+    const int c = (int)(e - r * cols);
+    dst[e] = src[r * pitch + c];
+  }
+}
+
+// ------------------------------------------------------ Welford update
+
+// Normalizer::update (ppo.rs:161-168) for n rows in order: one thread per
+// feature runs the sequential recurrence, so the result is bit-identical
+// to folding the rows one by one.
+__global__ void record_obs_kernel(const float *x, int64_t n, int dim,
+                                  float *mean, float *m2, float count0) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= dim) return;
+  float c = count0, mu = mean[i], s = m2[i];
+  for (int64_t r = 0; r < n; ++r) {
+    c = __fadd_rn(c, 1.0f);
+    const float xi = x[r * dim + i];
+    const float d = __fsub_rn(xi, mu);
+    mu = __fadd_rn(mu, __fdiv_rn(d, c));
+    s = __fadd_rn(s, __fmul_rn(d, __fsub_rn(xi, mu)));
+  }
+  mean[i] = mu;
+  m2[i] = s;
+}
+
+// ------------------------------------------------------ rollout sampling
+
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as
+// easy as 1, 2, 3", SC'11): 10 rounds of the 4x32 S-box with the published
+// multipliers and Weyl key increments.
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t lo0 = 0xD2511F53u * c.x, hi0 = __umulhi(0xD2511F53u, c.x);
+    const uint32_t lo1 = 0xCD9E8D57u * c.z, hi1 = __umulhi(0xCD9E8D57u, c.z);
+    c = make_uint4(hi1 ^ c.y ^ k.x, lo1, hi0 ^ c.w ^ k.y, lo0);
+    k.x += 0x9E3779B9u;
+    k.y += 0xBB67AE85u;
+  }
+  return c;
+}
+
+// uniform in (0, 1): the top 24 bits, offset by half a step
+__device__ __forceinline__ float u01(uint32_t x) {
+  return ((float)(x >> 8) + 0.5f) * (1.0f / 16777216.0f);
+}
+
+// One thread per (row, group of 4 action dims): Philox counter
+// (group, row_lo, counter_lo, counter_hi ^ row_hi) under key (seed_lo,
+// seed_hi) gives 4 uniforms -> 2 Box-Muller pairs -> 4 standard normals.
+// action = mean + exp(log_std) * eps; logp (ppo.rs:297-305) is a warp-free
+// second pass per row.
+__global__ void policy_sample_kernel(const float *mean, int pitch,
+                                     const float *log_std, int A, int64_t n,
+                                     uint64_t seed, uint64_t counter,
+                                     float *action, float *mean_out, int64_t row0) {
+  const int groups = (A + 3) / 4;
+  const int64_t total = n * groups;
+  const uint2 key = make_uint2((uint32_t)seed, (uint32_t)(seed >> 32));
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = e / groups;
+    const int gidx = (int)(e - row * groups);
+    const int64_t grow = row + row0;  // global row number: the draw is per row
+    const uint4 ctr = make_uint4((uint32_t)gidx, (uint32_t)grow, (uint32_t)counter,
+                                 (uint32_t)(counter >> 32) ^ (uint32_t)(grow >> 32));
+    const uint4 r = philox4x32_10(ctr, key);
+    const float ra = sqrtf(-2.0f * logf(u01(r.x)));
+    const float rb = sqrtf(-2.0f * logf(u01(r.z)));
+    const float ta = 6.28318548202514648f * u01(r.y);
+    const float tb = 6.28318548202514648f * u01(r.w);
+    const float z[4] = {ra * cosf(ta), ra * sinf(ta), rb * cosf(tb), rb * sinf(tb)};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int k = gidx * 4 + j;
+      if (k < A) {
+        const float mu = mean[row * pitch + k];
+        action[row * A + k] = mu + expf(log_std[k]) * z[j];
+        if (mean_out) mean_out[row * A + k] = mu;
+      }
+    }
+  }
+}
+
+__global__ void logp_rows_kernel(const float *action, const float *mean, int pitch,
+                                 const float *log_std, int A, int64_t n, float *logp) {
+  for (int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; row < n;
+       row += (int64_t)gridDim.x * blockDim.x) {
+    float lp = 0.0f;
+    for (int k = 0; k < A; ++k) {
+      const float d = (action[row * A + k] - mean[row * pitch + k]) / expf(log_std[k]);
+      lp += -0.5f * d * d - log_std[k] - kLogSqrt2Pi;
+    }
+    logp[row] = lp;
+  }
+}
+
+int grid_for(int64_t work, int threads, int cap = 148 * 16) {
+  int64_t g = (work + threads - 1) / threads;
+  if (g < 1) g = 1;
+  if (g > cap) g = cap;
+  return (int)g;
+}
+
+}  // namespace
+
+// ================================================================ wrappers
+
+int gae_blocks(int64_t n_envs) { return (int)((n_envs + kGaeEnvs - 1) / kGaeEnvs); }
+
+void launch_gae(const GaeArgs &a, double *partials, int nblk, cudaStream_t s) {
+  if (a.T <= kGaeMaxStagedT) {
+    const size_t smem = (size_t)kGaeEnvs * a.T * (4 * sizeof(float) + 1);
+    gae_kernel<true><<<nblk, kGaeThreads, smem, s>>>(a, partials);
+  } else {
+    gae_kernel<false><<<nblk, kGaeThreads, 0, s>>>(a, partials);
+  }
+}
+
+int adv_blocks(int64_t n) { return grid_for(n, kAdvThreads, 296); }
+
+void launch_adv_sum(const float *adv, int64_t n, double *partials, int nblk,
+                    cudaStream_t s) {
+  adv_sum_kernel<<<nblk, kAdvThreads, 0, s>>>(adv, n, partials);
+}
+
+void launch_reduce_moment(const double *partials, int nblk, double *moments,
+                          int slot, cudaStream_t s) {
+  reduce_partials_kernel<<<1, 1024, 0, s>>>(partials, nblk, moments, slot);
+}
+
+void launch_adv_sqdev(const float *adv, int64_t n, const double *moments,
+                      int64_t n_global, double *partials, int nblk,
+                      cudaStream_t s) {
+  adv_sqdev_kernel<<<nblk, kAdvThreads, 0, s>>>(adv, n, moments, n_global,
+                                                 partials);
+}
+
+void launch_adv_finalize(const double *moments, int64_t n_global, DevState *st,
+                         cudaStream_t s) {
+  adv_finalize_kernel<<<1, 1, 0, s>>>(moments, n_global, st);
+}
+
+void launch_gather(const GatherArgs &a, cudaStream_t s) {
+  const int threads = 256;
+  gather_kernel<<<grid_for(a.n_used * 32, threads), threads, 0, s>>>(a);
+}
+
+void launch_norm_prepare(const float *m2, float count, int dim, float *sd,
+                         cudaStream_t s) {
+  norm_prepare_kernel<<<(dim + 127) / 128, 128, 0, s>>>(m2, count, dim, sd);
+}
+
+void launch_normalize_rows(const float *x, int64_t n, int dim, int pitch,
+                           const float *mean, const float *sd, float *out,
+                           cudaStream_t s) {
+  normalize_rows_kernel<<<grid_for(n * pitch, 256), 256, 0, s>>>(
+      x, n, dim, pitch, mean, sd, out);
+}
+
+void launch_loss(const LossArgs &a, ReduceScratch &rs, cudaStream_t s) {
+  int blocks = grid_for(a.mb * 32, kLossThreads, rs.max_blocks);
+  if ((a.A + 3) > rs.fwidth) blocks = 0;  // caller sized fwidth >= A + 3
+  if (blocks > 0)
+    loss_kernel<<<blocks, kLossThreads, 0, s>>>(a, rs.fpart, rs.ticket);
+}
+
+void launch_colsum(const float *x, int64_t rows, int cols, int ld,
+                   float *partials, int splits, cudaStream_t s) {
+  dim3 grid((cols + 127) / 128, splits);
+  colsum_kernel<<<grid, 128, 0, s>>>(x, rows, cols, ld, partials, splits);
+}
+
+void launch_reduce_segments(const ReduceSegs &segs, cudaStream_t s) {
+  int64_t mx = 0;
+  for (int i = 0; i < segs.n; ++i) mx = segs.seg[i].count > mx ? segs.seg[i].count : mx;
+  dim3 grid(grid_for(mx, 256, 64), segs.n);
+  reduce_segments_kernel<<<grid, 256, 0, s>>>(segs);
+}
+
+void launch_prestep(const PrestepArgs &a, ReduceScratch &rs, cudaStream_t s) {
+  const int64_t work = (a.actor_end - a.actor_begin);
+  int blocks = grid_for(work, kPrestepThreads, 148);
+  if (blocks > rs.max_blocks) blocks = rs.max_blocks;
+  prestep_kernel<<<blocks, kPrestepThreads, 0, s>>>(a, rs.dpart, rs.ticket + 1);
+}
+
+void launch_adam(const AdamArgs &a, cudaStream_t s) {
+  adam_kernel<<<grid_for(a.n / 4, 256, 148 * 8), 256, 0, s>>>(a);
+}
+
+void launch_unpad_rows(const float *src, int64_t rows, int pitch, int cols,
+                       float *dst, cudaStream_t s) {
+  unpad_rows_kernel<<<grid_for(rows * cols, 256), 256, 0, s>>>(src, rows, pitch,
+                                                               cols, dst);
+}
+
+void launch_record_obs(const float *x, int64_t n, int dim, float *mean, float *m2,
+                       float count0, cudaStream_t s) {
+  record_obs_kernel<<<(dim + 127) / 128, 128, 0, s>>>(x, n, dim, mean, m2, count0);
+}
+
+void launch_policy_sample(const float *mean, int pitch, const float *log_std, int A,
+                          int64_t n, uint64_t seed, uint64_t counter, float *action,
+                          float *logp, float *mean_out, cudaStream_t s, int64_t row0) {
+  const int64_t work = n * ((A + 3) / 4);
+  policy_sample_kernel<<<grid_for(work, 256), 256, 0, s>>>(mean, pitch, log_std, A, n,
+                                                            seed, counter, action,
+                                                            mean_out, row0);
+  if (logp)
+    logp_rows_kernel<<<grid_for(n, 256), 256, 0, s>>>(action, mean, pitch, log_std, A,
+                                                       n, logp);
+}
+
+}  // namespace zrl

@@ -1,0 +1,1570 @@
+// zrl_api.cu -- the C ABI of libzealot_rl.so: context, parameter layout and
+// the PPO update orchestration (zealot-rl/src/ppo.rs:338-510).
+//
+// One update is one stream of kernels with no host synchronisation until
+// the statistics are read back at the end: advantage moments -> per epoch
+// (permutation upload, gather) -> per minibatch (forward x2 nets, loss,
+// backward x2 nets, gradient reduce, [allreduce], pre-step, Adam).  The
+// epoch permutations are computed on the host while the GPU runs the
+// previous epoch.
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "zrl_comm.h"
+#include "zrl_gemm.h"
+#include "zrl_internal.h"
+
+using namespace zrl;
+
+namespace zrl {
+struct StTensor {
+  std::vector<int64_t> shape;
+  std::vector<float> data;
+};
+std::vector<uint8_t> st_serialize(const std::map<std::string, StTensor> &ts);
+bool st_parse(const uint8_t *buf, size_t len, std::map<std::string, StTensor> *out,
+              std::string *err);
+void shuffle_i32(uint64_t seed, int64_t n, int32_t *order);
+void mlp_init_reference(const int32_t *dims, int n_dims, float out_scale,
+                        uint64_t *rng, float *params);
+}
+
+struct zrl_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::string err;
+  zrl_model_config mcfg{};
+  NetLayout net[2];
+  int A = 0, Ap = 0;
+  int64_t ls_off = 0;       // device offset of log_std
+  int64_t dev_params = 0;   // padded parameter count (multiple of 32)
+  int64_t grad_len = 0;     // dev_params + 32 (sums3 slot after the grads)
+  int64_t flat_params = 0;
+  int precision = ZRL_GEMM_TF32;
+
+  float *P = nullptr, *G = nullptr, *M = nullptr, *V = nullptr;
+  float *sums3 = nullptr;   // = G + dev_params
+  DevState *st = nullptr;
+  DevState *st_host = nullptr;  // pinned
+
+  // normalizers (device) and host copies of the counts
+  float *obs_mean = nullptr, *obs_m2 = nullptr, *obs_sd = nullptr;
+  float *crit_mean = nullptr, *crit_m2 = nullptr, *crit_sd = nullptr;
+  float obs_count = 1.0f, crit_count = 1.0f;
+
+  // batch capacity
+  int64_t n_cap = 0;
+  float *b_obs = nullptr, *b_cobs = nullptr, *b_act = nullptr, *b_mo = nullptr;
+  float *b_lpo = nullptr, *b_vo = nullptr, *b_adv = nullptr, *b_ret = nullptr;
+  float *r_rew = nullptr, *r_val = nullptr, *r_lv = nullptr;
+  uint8_t *r_done = nullptr;
+  int64_t env_cap = 0, r_cap = 0;
+  float *e_xa = nullptr, *e_xc = nullptr, *e_act = nullptr, *e_mo = nullptr;
+  float *e_lpo = nullptr, *e_vo = nullptr, *e_adv = nullptr, *e_ret = nullptr;
+  int32_t *order_dev = nullptr;
+  int32_t *order_pinned = nullptr;
+  int64_t order_pinned_cap = 0;
+
+  // minibatch activations / deltas
+  int64_t mb_cap = 0;
+  float *act[2][ZRL_MAX_LAYERS + 1] = {};
+  float *dlt[2][ZRL_MAX_LAYERS] = {};
+
+  // wgrad split-K partials
+  float *wpart = nullptr;
+  int64_t wpart_cap = 0;
+  float *bpart = nullptr;
+  int64_t bpart_cap = 0;
+
+  ReduceScratch rs{};
+  double *adv_part = nullptr;
+  double *moments = nullptr;  // [2]
+  int adv_part_cap = 0;
+
+  int32_t t_logstd_host = 0;
+  float lr_host = 1e-3f;
+  int64_t launches = 0;
+
+  bool profiling = false;
+  std::vector<cudaEvent_t> ev_pool;
+  size_t ev_used = 0;
+  float prof_gemm_ms = 0.0f, prof_update_ms = 0.0f;
+  int64_t prof_gemm_launches = 0;
+
+  Comm comm;
+  GemmEngine gemm;
+};
+
+// ---------------------------------------------------------------- errors
+
+#define CK(call)                                                          \
+  do {                                                                    \
+    cudaError_t e_ = (call);                                              \
+    if (e_ != cudaSuccess) {                                              \
+      ctx->err = std::string(#call) + ": " + cudaGetErrorString(e_);      \
+      return ZRL_CUDA_ERROR;                                              \
+    }                                                                     \
+  } while (0)
+
+#define CHECK_LAUNCH()                                                    \
+  do {                                                                    \
+    cudaError_t e_ = cudaGetLastError();                                  \
+    if (e_ != cudaSuccess) {                                              \
+      ctx->err = std::string("kernel launch: ") + cudaGetErrorString(e_); \
+      return ZRL_CUDA_ERROR;                                              \
+    }                                                                     \
+  } while (0)
+
+#define TRY(expr)                          \
+  do {                                     \
+    zrl_status s_ = (expr);                \
+    if (s_ != ZRL_OK) return s_;           \
+  } while (0)
+
+static zrl_status bad(zrl_ctx *ctx, const char *msg) {
+  if (ctx) ctx->err = msg;
+  return ZRL_INVALID_ARG;
+}
+
+template <typename T>
+static zrl_status dalloc(zrl_ctx *ctx, T **p, int64_t count) {
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  if (count <= 0) return ZRL_OK;
+  cudaError_t e = cudaMalloc((void **)p, sizeof(T) * (size_t)count);
+  if (e != cudaSuccess) {
+    ctx->err = std::string("cudaMalloc: ") + cudaGetErrorString(e);
+    *p = nullptr;
+    return e == cudaErrorMemoryAllocation ? ZRL_OUT_OF_MEMORY : ZRL_CUDA_ERROR;
+  }
+  cudaMemsetAsync(*p, 0, sizeof(T) * (size_t)count, ctx->stream);
+  return ZRL_OK;
+}
+
+// ---------------------------------------------------------------- layout
+
+static void build_layout(zrl_ctx *ctx) {
+  int64_t dev = 0, flat = 0;
+  const int32_t *dims[2] = {ctx->mcfg.actor_dims, ctx->mcfg.critic_dims};
+  const int nd[2] = {ctx->mcfg.n_actor_dims, ctx->mcfg.n_critic_dims};
+  for (int k = 0; k < 2; ++k) {
+    NetLayout &L = ctx->net[k];
+    L.L = nd[k] - 1;
+    for (int l = 0; l < nd[k]; ++l) {
+      L.d[l] = dims[k][l];
+      L.dp[l] = (int)pad_to(dims[k][l], kPad);
+    }
+    L.dev_begin = dev;
+    L.flat_begin = flat;
+    for (int l = 0; l < L.L; ++l) {
+      L.w_off[l] = dev;
+      dev += (int64_t)L.dp[l + 1] * L.dp[l];
+      L.b_off[l] = dev;
+      dev += L.dp[l + 1];
+      L.fw_off[l] = flat;
+      flat += (int64_t)L.d[l + 1] * L.d[l];
+      L.fb_off[l] = flat;
+      flat += L.d[l + 1];
+    }
+    L.dev_end = dev;
+    L.flat_end = flat;
+  }
+  ctx->A = ctx->mcfg.actor_dims[ctx->mcfg.n_actor_dims - 1];
+  ctx->Ap = (int)pad_to(ctx->A, kPad);
+  ctx->ls_off = dev;
+  dev += ctx->Ap;
+  flat += ctx->A;
+  ctx->dev_params = dev;
+  ctx->grad_len = dev + 32;
+  ctx->flat_params = flat;
+}
+
+// flat (save order) -> padded device layout, on the host
+static void flat_to_padded(const zrl_ctx *ctx, const float *flat, float *pad) {
+  memset(pad, 0, sizeof(float) * (size_t)ctx->dev_params);
+  for (int k = 0; k < 2; ++k) {
+    const NetLayout &L = ctx->net[k];
+    for (int l = 0; l < L.L; ++l) {
+      for (int o = 0; o < L.d[l + 1]; ++o) {
+        memcpy(pad + L.w_off[l] + (int64_t)o * L.dp[l],
+               flat + L.fw_off[l] + (int64_t)o * L.d[l], sizeof(float) * L.d[l]);
+        pad[L.b_off[l] + o] = flat[L.fb_off[l] + o];
+      }
+    }
+  }
+  memcpy(pad + ctx->ls_off, flat + ctx->net[1].flat_end, sizeof(float) * ctx->A);
+}
+
+static void padded_to_flat(const zrl_ctx *ctx, const float *pad, float *flat) {
+  for (int k = 0; k < 2; ++k) {
+    const NetLayout &L = ctx->net[k];
+    for (int l = 0; l < L.L; ++l) {
+      for (int o = 0; o < L.d[l + 1]; ++o) {
+        memcpy(flat + L.fw_off[l] + (int64_t)o * L.d[l],
+               pad + L.w_off[l] + (int64_t)o * L.dp[l], sizeof(float) * L.d[l]);
+        flat[L.fb_off[l] + o] = pad[L.b_off[l] + o];
+      }
+    }
+  }
+  memcpy(flat + ctx->net[1].flat_end, pad + ctx->ls_off, sizeof(float) * ctx->A);
+}
+
+// ------------------------------------------------------------- capacity
+
+static zrl_status ensure_batch(zrl_ctx *ctx, int64_t n) {
+  if (n <= ctx->n_cap) return ZRL_OK;
+  const int od = ctx->net[0].d[0], cd = ctx->net[1].d[0];
+  const int odp = ctx->net[0].dp[0], cdp = ctx->net[1].dp[0];
+  const int A = ctx->A;
+  TRY(dalloc(ctx, &ctx->b_obs, n * od));
+  TRY(dalloc(ctx, &ctx->b_cobs, n * cd));
+  TRY(dalloc(ctx, &ctx->b_act, n * A));
+  TRY(dalloc(ctx, &ctx->b_mo, n * A));
+  TRY(dalloc(ctx, &ctx->b_lpo, n));
+  TRY(dalloc(ctx, &ctx->b_vo, n));
+  TRY(dalloc(ctx, &ctx->b_adv, n));
+  TRY(dalloc(ctx, &ctx->b_ret, n));
+  TRY(dalloc(ctx, &ctx->e_xa, n * odp));
+  TRY(dalloc(ctx, &ctx->e_xc, n * cdp));
+  TRY(dalloc(ctx, &ctx->e_act, n * A));
+  TRY(dalloc(ctx, &ctx->e_mo, n * A));
+  TRY(dalloc(ctx, &ctx->e_lpo, n));
+  TRY(dalloc(ctx, &ctx->e_vo, n));
+  TRY(dalloc(ctx, &ctx->e_adv, n));
+  TRY(dalloc(ctx, &ctx->e_ret, n));
+  TRY(dalloc(ctx, &ctx->order_dev, n));
+  const int nb = adv_blocks(n) + gae_blocks(n) + 8;
+  TRY(dalloc(ctx, &ctx->adv_part, nb));
+  ctx->adv_part_cap = nb;
+  ctx->n_cap = n;
+  return ZRL_OK;
+}
+
+static zrl_status ensure_envs(zrl_ctx *ctx, int64_t n_envs, int64_t T) {
+  TRY(ensure_batch(ctx, n_envs * T));
+  // rewards/values/dones are sized by the batch capacity, bootstrap values
+  // by the env count
+  if (!ctx->r_rew || ctx->env_cap < n_envs || ctx->r_cap < ctx->n_cap) {
+    TRY(dalloc(ctx, &ctx->r_rew, ctx->n_cap));
+    TRY(dalloc(ctx, &ctx->r_val, ctx->n_cap));
+    TRY(dalloc(ctx, &ctx->r_done, ctx->n_cap));
+    TRY(dalloc(ctx, &ctx->r_lv, n_envs));
+    ctx->env_cap = n_envs;
+    ctx->r_cap = ctx->n_cap;
+  }
+  const int nb = gae_blocks(n_envs) + 8;
+  if (nb > ctx->adv_part_cap) {
+    TRY(dalloc(ctx, &ctx->adv_part, nb));
+    ctx->adv_part_cap = nb;
+  }
+  return ZRL_OK;
+}
+
+static zrl_status ensure_pinned_orders(zrl_ctx *ctx, int64_t count) {
+  if (count <= ctx->order_pinned_cap) return ZRL_OK;
+  if (ctx->order_pinned) cudaFreeHost(ctx->order_pinned);
+  ctx->order_pinned = nullptr;
+  CK(cudaMallocHost((void **)&ctx->order_pinned, sizeof(int32_t) * (size_t)count));
+  ctx->order_pinned_cap = count;
+  return ZRL_OK;
+}
+
+static int wsplit_for(int64_t mb) {
+  // enough row chunks to fill the machine on the small output tiles, each
+  // chunk at least 512 rows
+  int s = (int)std::min<int64_t>(32, std::max<int64_t>(1, mb / 512));
+  return s;
+}
+
+static zrl_status ensure_mb(zrl_ctx *ctx, int64_t mb) {
+  if (mb <= ctx->mb_cap) return ZRL_OK;
+  for (int k = 0; k < 2; ++k) {
+    const NetLayout &L = ctx->net[k];
+    for (int l = 1; l <= L.L; ++l) TRY(dalloc(ctx, &ctx->act[k][l], mb * L.dp[l]));
+    for (int l = 0; l < L.L; ++l) TRY(dalloc(ctx, &ctx->dlt[k][l], mb * L.dp[l + 1]));
+  }
+  const int S = std::max(wsplit_for(mb), 32);
+  int64_t wp = 0, bp = 0;
+  for (int k = 0; k < 2; ++k) {
+    const NetLayout &L = ctx->net[k];
+    for (int l = 0; l < L.L; ++l) {
+      wp += (int64_t)S * L.dp[l + 1] * L.dp[l];
+      bp += (int64_t)S * L.dp[l + 1];
+    }
+  }
+  TRY(dalloc(ctx, &ctx->wpart, wp));
+  TRY(dalloc(ctx, &ctx->bpart, bp));
+  ctx->wpart_cap = wp;
+  ctx->bpart_cap = bp;
+  // loss-kernel partials: blocks of 8 warps, one sample per warp per pass
+  ctx->mb_cap = mb;
+  return ZRL_OK;
+}
+
+// ---------------------------------------------------------------- events
+
+static cudaEvent_t next_event(zrl_ctx *ctx) {
+  if (ctx->ev_used == ctx->ev_pool.size()) {
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    ctx->ev_pool.push_back(e);
+  }
+  return ctx->ev_pool[ctx->ev_used++];
+}
+
+// ------------------------------------------------------------------ GEMM
+
+static zrl_status run_gemm(zrl_ctx *ctx, const GemmArgs &g) {
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (ctx->profiling) {
+    e0 = next_event(ctx);
+    cudaEventRecord(e0, ctx->stream);
+  }
+  int launched = 0;
+  zrl_status s = ctx->gemm.run(g, ctx->precision, ctx->stream, &launched, &ctx->err);
+  if (s != ZRL_OK) return s;
+  ctx->launches += launched;
+  if (ctx->profiling) {
+    e1 = next_event(ctx);
+    cudaEventRecord(e1, ctx->stream);
+    ctx->prof_gemm_launches += launched;
+  }
+  CHECK_LAUNCH();
+  return ZRL_OK;
+}
+
+// Forward one net over `rows` rows of input x (pitch dp[0]); activations go
+// to ctx->act[k][1..L].
+static zrl_status forward_net(zrl_ctx *ctx, int k, const float *x, int64_t rows) {
+  const NetLayout &L = ctx->net[k];
+  const float *in = x;
+  for (int l = 0; l < L.L; ++l) {
+    GemmArgs g{};
+    g.M = (int)rows;
+    g.N = L.dp[l + 1];
+    g.K = L.dp[l];
+    g.A = in;
+    g.lda = L.dp[l];
+    g.trans_a = false;
+    g.B = ctx->P + L.w_off[l];
+    g.ldb = L.dp[l];
+    g.trans_b = true;
+    g.C = ctx->act[k][l + 1];
+    g.ldc = L.dp[l + 1];
+    g.epi = l < L.L - 1 ? EPI_BIAS_ELU : EPI_BIAS;
+    g.bias = ctx->P + L.b_off[l];
+    g.split_k = 1;
+    TRY(run_gemm(ctx, g));
+    in = ctx->act[k][l + 1];
+  }
+  return ZRL_OK;
+}
+
+// Backward of one net (net.rs:113-140 batched): wgrad split-K partials,
+// bias-gradient column sums, dgrad with the ELU' epilogue.
+static zrl_status backward_net(zrl_ctx *ctx, int k, const float *x, int64_t rows,
+                               float **wp, float **bp, ReduceSegs &segs) {
+  const NetLayout &L = ctx->net[k];
+  for (int l = L.L - 1; l >= 0; --l) {
+    const float *a_in = l == 0 ? x : ctx->act[k][l];
+    const int S = wsplit_for(rows);
+    // dW_l = delta_l^T a_l
+    GemmArgs g{};
+    g.M = L.dp[l + 1];
+    g.N = L.dp[l];
+    g.K = (int)rows;
+    g.A = ctx->dlt[k][l];
+    g.lda = L.dp[l + 1];
+    g.trans_a = true;
+    g.B = a_in;
+    g.ldb = L.dp[l];
+    g.trans_b = false;
+    g.C = *wp;
+    g.ldc = L.dp[l];
+    g.epi = EPI_STORE;
+    g.split_k = S;
+    TRY(run_gemm(ctx, g));
+    ReduceSeg sw{ctx->G + L.w_off[l], *wp, (int64_t)L.dp[l + 1] * L.dp[l], S};
+    segs.seg[segs.n++] = sw;
+    *wp += (int64_t)S * L.dp[l + 1] * L.dp[l];
+    // db_l = column sums of delta_l
+    const int Sb = S;
+    launch_colsum(ctx->dlt[k][l], rows, L.dp[l + 1], L.dp[l + 1], *bp, Sb, ctx->stream);
+    ctx->launches++;
+    CHECK_LAUNCH();
+    ReduceSeg sb{ctx->G + L.b_off[l], *bp, (int64_t)L.dp[l + 1], Sb};
+    segs.seg[segs.n++] = sb;
+    *bp += (int64_t)Sb * L.dp[l + 1];
+    if (l > 0) {
+      // delta_{l-1} = (delta_l W_l) * elu'(a_l)
+      GemmArgs d{};
+      d.M = (int)rows;
+      d.N = L.dp[l];
+      d.K = L.dp[l + 1];
+      d.A = ctx->dlt[k][l];
+      d.lda = L.dp[l + 1];
+      d.trans_a = false;
+      d.B = ctx->P + L.w_off[l];
+      d.ldb = L.dp[l];
+      d.trans_b = false;
+      d.C = ctx->dlt[k][l - 1];
+      d.ldc = L.dp[l];
+      d.epi = EPI_ELU_GRAD;
+      d.aux = ctx->act[k][l];
+      d.ldaux = L.dp[l];
+      d.split_k = 1;
+      TRY(run_gemm(ctx, d));
+    }
+  }
+  return ZRL_OK;
+}
+
+struct MbView {
+  const float *xa, *xc, *act, *mo, *lpo, *vo, *adv, *ret;
+  int64_t rows;
+};
+
+// Gradient accumulation of one minibatch (ppo.rs:388-462): leaves the
+// summed gradient in G (padded layout, log_std included) and the three
+// statistic sums in sums3.
+static zrl_status minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
+                                  const MbView &v, float scale) {
+  TRY(ensure_mb(ctx, std::max<int64_t>(v.rows, 1)));
+  if (v.rows > 0) {
+    TRY(forward_net(ctx, 0, v.xa, v.rows));
+    TRY(forward_net(ctx, 1, v.xc, v.rows));
+  }
+  const NetLayout &La = ctx->net[0], &Lc = ctx->net[1];
+  LossArgs la{};
+  la.mean = ctx->act[0][La.L];
+  la.value = ctx->act[1][Lc.L];
+  la.Ap = La.dp[La.L];
+  la.cp = Lc.dp[Lc.L];
+  la.action = v.act;
+  la.mean_old = v.mo;
+  la.logp_old = v.lpo;
+  la.value_old = v.vo;
+  la.adv = v.adv;
+  la.ret = v.ret;
+  la.log_std = ctx->P + ctx->ls_off;
+  la.A = ctx->A;
+  la.mb = v.rows;
+  la.scale = scale;
+  la.clip = cfg->clip;
+  la.entropy_coef = cfg->entropy_coef;
+  la.value_coef = cfg->value_coef;
+  la.d_actor = ctx->dlt[0][La.L - 1];
+  la.d_critic = ctx->dlt[1][Lc.L - 1];
+  la.g_logstd = ctx->G + ctx->ls_off;
+  la.sums3 = ctx->sums3;
+  if (v.rows > 0) {
+    launch_loss(la, ctx->rs, ctx->stream);
+    ctx->launches++;
+    CHECK_LAUNCH();
+  } else {
+    // a rank with no rows this minibatch contributes zeros (the entropy
+    // term of the log_std gradient is per sample, so zero as well)
+    CK(cudaMemsetAsync(ctx->G, 0, sizeof(float) * ctx->grad_len, ctx->stream));
+    return ZRL_OK;
+  }
+  float *wp = ctx->wpart, *bp = ctx->bpart;
+  ReduceSegs segs{};
+  TRY(backward_net(ctx, 0, v.xa, v.rows, &wp, &bp, segs));
+  TRY(backward_net(ctx, 1, v.xc, v.rows, &wp, &bp, segs));
+  launch_reduce_segments(segs, ctx->stream);
+  ctx->launches++;
+  CHECK_LAUNCH();
+  return ZRL_OK;
+}
+
+static zrl_status allreduce_grads(zrl_ctx *ctx) {
+  if (ctx->comm.world <= 1) return ZRL_OK;
+  return ctx->comm.allreduce_f32(ctx->G, ctx->grad_len, ctx->stream, &ctx->err);
+}
+
+// Stepping half of minibatch_step (ppo.rs:475-489).
+static zrl_status step(zrl_ctx *ctx, const zrl_ppo_config *cfg, int minibatches,
+                       bool last_of_epoch, bool count_stats) {
+  PrestepArgs p{};
+  p.grads = ctx->G;
+  p.actor_begin = ctx->net[0].dev_begin;
+  p.actor_end = ctx->net[0].dev_end;
+  p.critic_begin = ctx->net[1].dev_begin;
+  p.critic_end = ctx->net[1].dev_end;
+  p.log_std = ctx->P + ctx->ls_off;
+  p.A = ctx->A;
+  p.sums3 = ctx->sums3;
+  p.max_grad_norm = cfg->max_grad_norm;
+  p.desired_kl = cfg->desired_kl;
+  p.lr_min = cfg->lr_min;
+  p.lr_max = cfg->lr_max;
+  p.adaptive_lr = cfg->adaptive_lr;
+  p.minibatches = minibatches;
+  p.last_of_epoch = last_of_epoch;
+  p.count_stats = count_stats;
+  p.st = ctx->st;
+  launch_prestep(p, ctx->rs, ctx->stream);
+  ctx->launches++;
+  CHECK_LAUNCH();
+  AdamArgs a{};
+  a.p = ctx->P;
+  a.m = ctx->M;
+  a.v = ctx->V;
+  a.g = ctx->G;
+  a.n = ctx->dev_params;
+  a.actor_end = ctx->net[0].dev_end;
+  a.critic_end = ctx->net[1].dev_end;
+  a.st = ctx->st;
+  launch_adam(a, ctx->stream);
+  ctx->launches++;
+  CHECK_LAUNCH();
+  return ZRL_OK;
+}
+
+// Advantage mean and population sd over the (global) batch, ppo.rs:342-345.
+static zrl_status adv_moments(zrl_ctx *ctx, const float *adv, int64_t n,
+                              int64_t n_global, bool partials_ready,
+                              int partial_blocks) {
+  int nb = partial_blocks;
+  if (!partials_ready) {
+    nb = adv_blocks(n);
+    if (n > 0) {
+      launch_adv_sum(adv, n, ctx->adv_part, nb, ctx->stream);
+      ctx->launches++;
+    } else {
+      CK(cudaMemsetAsync(ctx->adv_part, 0, sizeof(double), ctx->stream));
+      nb = 1;
+    }
+  }
+  launch_reduce_moment(ctx->adv_part, nb, ctx->moments, 0, ctx->stream);
+  ctx->launches++;
+  CHECK_LAUNCH();
+  if (ctx->comm.world > 1)
+    TRY(ctx->comm.allreduce_f64(ctx->moments, 1, ctx->stream, &ctx->err));
+  int nb2 = adv_blocks(std::max<int64_t>(n, 1));
+  if (n > 0) {
+    launch_adv_sqdev(adv, n, ctx->moments, n_global, ctx->adv_part, nb2, ctx->stream);
+    ctx->launches++;
+  } else {
+    CK(cudaMemsetAsync(ctx->adv_part, 0, sizeof(double), ctx->stream));
+    nb2 = 1;
+  }
+  launch_reduce_moment(ctx->adv_part, nb2, ctx->moments, 1, ctx->stream);
+  ctx->launches++;
+  CHECK_LAUNCH();
+  if (ctx->comm.world > 1)
+    TRY(ctx->comm.allreduce_f64(ctx->moments + 1, 1, ctx->stream, &ctx->err));
+  launch_adv_finalize(ctx->moments, n_global, ctx->st, ctx->stream);
+  ctx->launches++;
+  CHECK_LAUNCH();
+  return ZRL_OK;
+}
+
+static GatherArgs gather_args(zrl_ctx *ctx, const float *obs, const float *cobs,
+                              const float *act, const float *mo, const float *lpo,
+                              const float *vo, const float *adv, const float *ret) {
+  GatherArgs g{};
+  g.order = ctx->order_dev;
+  g.obs = obs;
+  g.cobs = cobs;
+  g.action = act;
+  g.mean_old = mo;
+  g.logp_old = lpo;
+  g.value_old = vo;
+  g.adv = adv;
+  g.ret = ret;
+  g.od = ctx->net[0].d[0];
+  g.cd = ctx->net[1].d[0];
+  g.A = ctx->A;
+  g.odp = ctx->net[0].dp[0];
+  g.cdp = ctx->net[1].dp[0];
+  g.obs_mean = ctx->obs_mean;
+  g.obs_sd = ctx->obs_sd;
+  g.crit_mean = ctx->crit_mean;
+  g.crit_sd = ctx->crit_sd;
+  g.st = ctx->st;
+  g.x_a = ctx->e_xa;
+  g.x_c = ctx->e_xc;
+  g.g_action = ctx->e_act;
+  g.g_mean_old = ctx->e_mo;
+  g.g_logp_old = ctx->e_lpo;
+  g.g_value_old = ctx->e_vo;
+  g.g_adv = ctx->e_adv;
+  g.g_ret = ctx->e_ret;
+  return g;
+}
+
+static MbView epoch_view(zrl_ctx *ctx, int64_t off, int64_t rows) {
+  MbView v{};
+  v.xa = ctx->e_xa + off * ctx->net[0].dp[0];
+  v.xc = ctx->e_xc + off * ctx->net[1].dp[0];
+  v.act = ctx->e_act + off * ctx->A;
+  v.mo = ctx->e_mo + off * ctx->A;
+  v.lpo = ctx->e_lpo + off;
+  v.vo = ctx->e_vo + off;
+  v.adv = ctx->e_adv + off;
+  v.ret = ctx->e_ret + off;
+  v.rows = rows;
+  return v;
+}
+
+struct DevBatch {
+  const float *obs, *cobs, *act, *mo, *lpo, *vo, *adv, *ret;
+};
+
+static zrl_status stage_batch(zrl_ctx *ctx, const zrl_batch *b, DevBatch *d,
+                              bool need_adv_ret) {
+  const int od = ctx->net[0].d[0], cd = ctx->net[1].d[0], A = ctx->A;
+  const int64_t n = b->n;
+  if (b->on_device) {
+    *d = DevBatch{b->obs, b->critic_obs, b->action, b->mean_old,
+                  b->logp_old, b->value_old, b->adv, b->ret};
+    return ZRL_OK;
+  }
+  TRY(ensure_batch(ctx, n));
+  auto up = [&](float *dst, const float *src, int64_t cnt) -> zrl_status {
+    if (cnt <= 0) return ZRL_OK;
+    CK(cudaMemcpyAsync(dst, src, sizeof(float) * cnt, cudaMemcpyHostToDevice,
+                       ctx->stream));
+    return ZRL_OK;
+  };
+  TRY(up(ctx->b_obs, b->obs, n * od));
+  TRY(up(ctx->b_cobs, b->critic_obs, n * cd));
+  TRY(up(ctx->b_act, b->action, n * A));
+  TRY(up(ctx->b_mo, b->mean_old, n * A));
+  TRY(up(ctx->b_lpo, b->logp_old, n));
+  TRY(up(ctx->b_vo, b->value_old, n));
+  if (need_adv_ret) {
+    TRY(up(ctx->b_adv, b->adv, n));
+    TRY(up(ctx->b_ret, b->ret, n));
+  }
+  *d = DevBatch{ctx->b_obs, ctx->b_cobs, ctx->b_act, ctx->b_mo,
+                ctx->b_lpo, ctx->b_vo, ctx->b_adv, ctx->b_ret};
+  return ZRL_OK;
+}
+
+static zrl_status check_cfg(zrl_ctx *ctx, const zrl_ppo_config *cfg) {
+  if (!cfg) return bad(ctx, "null config");
+  if (cfg->epochs < 0 || cfg->minibatches < 1)
+    return bad(ctx, "epochs must be >= 0 and minibatches >= 1");
+  return ZRL_OK;
+}
+
+// The epoch/minibatch loop of ActorCritic::update (ppo.rs:350-383) once the
+// batch is on the device and the advantage moments are in ctx->st.
+static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
+                             const DevBatch &d, int64_t n_local,
+                             int64_t n_global, int64_t row_offset) {
+  const int64_t mbs = cfg->minibatches;
+  const int64_t mb = n_global / mbs;
+  const int64_t n_used = mb * mbs;
+  const float scale = 1.0f / (float)mb;
+  // stats start as {0, 0, 0, 0, lr} (ppo.rs:351-354); lr and the Adam
+  // steps stay on the device
+  CK(cudaMemsetAsync(&ctx->st->ep_acc, 0, sizeof(float) * 4, ctx->stream));
+  CK(cudaMemsetAsync(&ctx->st->stats, 0, sizeof(float) * 4, ctx->stream));
+  CK(cudaMemcpyAsync(&ctx->st->stats[4], &ctx->st->lr, sizeof(float),
+                     cudaMemcpyDeviceToDevice, ctx->stream));
+  const bool multi = ctx->comm.world > 1;
+  TRY(ensure_pinned_orders(ctx, (int64_t)std::max(cfg->epochs, 1) * n_global));
+  TRY(ensure_mb(ctx, std::max<int64_t>(multi ? std::min<int64_t>(mb, n_local) : mb, 1)));
+  std::vector<int32_t> perm(multi ? n_global : 0);
+  std::vector<int64_t> counts(mbs), offs(mbs);
+  for (int e = 0; e < cfg->epochs; ++e) {
+    const uint64_t seed = (uint64_t)(ctx->t_logstd_host + e * mbs) + 1ull;
+    int32_t *ord = ctx->order_pinned + (int64_t)e * n_global;
+    int64_t n_rows = 0;
+    if (!multi) {
+      shuffle_i32(seed, n_global, ord);
+      n_rows = n_used;
+      for (int64_t m = 0; m < mbs; ++m) {
+        counts[m] = mb;
+        offs[m] = m * mb;
+      }
+    } else {
+      // every rank computes the global permutation and keeps, per
+      // minibatch, the positions whose rows it owns (in order)
+      shuffle_i32(seed, n_global, perm.data());
+      for (int64_t m = 0; m < mbs; ++m) {
+        offs[m] = n_rows;
+        for (int64_t p = m * mb; p < (m + 1) * mb; ++p) {
+          const int64_t r = perm[p] - row_offset;
+          if (r >= 0 && r < n_local) ord[n_rows++] = (int32_t)r;
+        }
+        counts[m] = n_rows - offs[m];
+      }
+      int64_t mx = 0;
+      for (int64_t m = 0; m < mbs; ++m) mx = std::max(mx, counts[m]);
+      TRY(ensure_mb(ctx, std::max<int64_t>(mx, 1)));
+    }
+    if (n_rows > 0) {
+      CK(cudaMemcpyAsync(ctx->order_dev, ord, sizeof(int32_t) * n_rows,
+                         cudaMemcpyHostToDevice, ctx->stream));
+      GatherArgs g = gather_args(ctx, d.obs, d.cobs, d.act, d.mo, d.lpo, d.vo,
+                                 d.adv, d.ret);
+      g.n_used = n_rows;
+      g.apply_adv_norm = 1;
+      launch_gather(g, ctx->stream);
+      ctx->launches++;
+      CHECK_LAUNCH();
+    }
+    for (int64_t m = 0; m < mbs; ++m) {
+      MbView v = epoch_view(ctx, offs[m], counts[m]);
+      TRY(minibatch_grads(ctx, cfg, v, scale));
+      TRY(allreduce_grads(ctx));
+      TRY(step(ctx, cfg, (int)mbs, m == mbs - 1, true));
+    }
+  }
+  ctx->t_logstd_host += cfg->epochs * (int32_t)mbs;
+  (void)n_local;
+  return ZRL_OK;
+}
+
+static zrl_status finish_update(zrl_ctx *ctx, zrl_stats *out) {
+  CK(cudaMemcpyAsync(ctx->st_host, ctx->st, sizeof(DevState),
+                     cudaMemcpyDeviceToHost, ctx->stream));
+  CK(cudaStreamSynchronize(ctx->stream));
+  ctx->lr_host = ctx->st_host->lr;
+  if (ctx->st_host->t[2] != ctx->t_logstd_host) {
+    ctx->err = "internal: Adam step counter mismatch";
+    return ZRL_CUDA_ERROR;
+  }
+  if (out) {
+    out->kl = ctx->st_host->stats[0];
+    out->surrogate = ctx->st_host->stats[1];
+    out->value_loss = ctx->st_host->stats[2];
+    out->entropy = ctx->st_host->stats[3];
+    out->lr = ctx->st_host->stats[4];
+  }
+  return ZRL_OK;
+}
+
+static zrl_status refresh_norm(zrl_ctx *ctx) {
+  launch_norm_prepare(ctx->obs_m2, ctx->obs_count, ctx->net[0].d[0], ctx->obs_sd,
+                      ctx->stream);
+  launch_norm_prepare(ctx->crit_m2, ctx->crit_count, ctx->net[1].d[0], ctx->crit_sd,
+                      ctx->stream);
+  ctx->launches += 2;
+  CHECK_LAUNCH();
+  return ZRL_OK;
+}
+
+static void prof_begin(zrl_ctx *ctx, cudaEvent_t *u0) {
+  if (!ctx->profiling) return;
+  ctx->ev_used = 0;
+  ctx->prof_gemm_launches = 0;
+  *u0 = next_event(ctx);
+  cudaEventRecord(*u0, ctx->stream);
+}
+
+static void prof_end(zrl_ctx *ctx, cudaEvent_t u0) {
+  if (!ctx->profiling) return;
+  cudaEvent_t u1 = next_event(ctx);
+  cudaEventRecord(u1, ctx->stream);
+  cudaEventSynchronize(u1);
+  float ms = 0.0f;
+  cudaEventElapsedTime(&ms, u0, u1);
+  ctx->prof_update_ms = ms;
+  float g = 0.0f;
+  // events after u0 come in (start, stop) pairs per GEMM, u1 last
+  for (size_t i = 1; i + 1 < ctx->ev_used; i += 2) {
+    float t = 0.0f;
+    cudaEventElapsedTime(&t, ctx->ev_pool[i], ctx->ev_pool[i + 1]);
+    g += t;
+  }
+  ctx->prof_gemm_ms = g;
+}
+
+// =================================================================== ABI
+
+extern "C" {
+
+int32_t zrl_abi_version(void) { return ZRL_ABI_VERSION; }
+
+zrl_status zrl_nccl_unique_id(uint8_t *out) {
+  if (!out) return ZRL_INVALID_ARG;
+  std::string err;
+  zrl_status s = nccl_unique_id(out, &err);
+  if (s != ZRL_OK) fprintf(stderr, "zrl_nccl_unique_id: %s\n", err.c_str());
+  return s;
+}
+
+const char *zrl_last_error(const zrl_ctx *ctx) {
+  return ctx ? ctx->err.c_str() : "null context";
+}
+
+zrl_status zrl_create(const zrl_model_config *cfg, int device,
+                      const zrl_comm *comm, zrl_ctx **out) {
+  if (!cfg || !out) return ZRL_INVALID_ARG;
+  *out = nullptr;
+  if (cfg->n_actor_dims < 2 || cfg->n_critic_dims < 2 ||
+      cfg->n_actor_dims > ZRL_MAX_LAYERS + 1 || cfg->n_critic_dims > ZRL_MAX_LAYERS + 1)
+    return ZRL_INVALID_ARG;
+  if (cfg->critic_dims[cfg->n_critic_dims - 1] != 1) return ZRL_INVALID_ARG;
+  for (int i = 0; i < cfg->n_actor_dims; ++i)
+    if (cfg->actor_dims[i] < 1) return ZRL_INVALID_ARG;
+  for (int i = 0; i < cfg->n_critic_dims; ++i)
+    if (cfg->critic_dims[i] < 1) return ZRL_INVALID_ARG;
+  if (cfg->actor_dims[cfg->n_actor_dims - 1] > 128) return ZRL_NOT_SUPPORTED;
+  if (cfg->precision < 0 || cfg->precision > 2) return ZRL_INVALID_ARG;
+  zrl_ctx *ctx = new zrl_ctx();
+  ctx->mcfg = *cfg;
+  ctx->device = device;
+  ctx->precision = cfg->precision;
+  auto fail = [&](zrl_status s) {
+    zrl_destroy(ctx);
+    return s;
+  };
+  if (cudaSetDevice(device) != cudaSuccess) return fail(ZRL_CUDA_ERROR);
+  if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess)
+    return fail(ZRL_CUDA_ERROR);
+  build_layout(ctx);
+  zrl_status s;
+  if ((s = dalloc(ctx, &ctx->P, ctx->dev_params)) != ZRL_OK) return fail(s);
+  if ((s = dalloc(ctx, &ctx->G, ctx->grad_len)) != ZRL_OK) return fail(s);
+  if ((s = dalloc(ctx, &ctx->M, ctx->dev_params)) != ZRL_OK) return fail(s);
+  if ((s = dalloc(ctx, &ctx->V, ctx->dev_params)) != ZRL_OK) return fail(s);
+  ctx->sums3 = ctx->G + ctx->dev_params;
+  if ((s = dalloc(ctx, &ctx->st, 1)) != ZRL_OK) return fail(s);
+  if (cudaMallocHost((void **)&ctx->st_host, sizeof(DevState)) != cudaSuccess)
+    return fail(ZRL_CUDA_ERROR);
+  memset(ctx->st_host, 0, sizeof(DevState));
+  const int od = ctx->net[0].d[0], cd = ctx->net[1].d[0];
+  if ((s = dalloc(ctx, &ctx->obs_mean, od)) != ZRL_OK) return fail(s);
+  if ((s = dalloc(ctx, &ctx->obs_m2, od)) != ZRL_OK) return fail(s);
+  if ((s = dalloc(ctx, &ctx->obs_sd, od)) != ZRL_OK) return fail(s);
+  if ((s = dalloc(ctx, &ctx->crit_mean, cd)) != ZRL_OK) return fail(s);
+  if ((s = dalloc(ctx, &ctx->crit_m2, cd)) != ZRL_OK) return fail(s);
+  if ((s = dalloc(ctx, &ctx->crit_sd, cd)) != ZRL_OK) return fail(s);
+  if ((s = dalloc(ctx, &ctx->moments, 2)) != ZRL_OK) return fail(s);
+  ctx->rs.max_blocks = 148 * 16;
+  ctx->rs.fwidth = 128 + 3;
+  if ((s = dalloc(ctx, &ctx->rs.fpart, (int64_t)ctx->rs.max_blocks * ctx->rs.fwidth)) != ZRL_OK)
+    return fail(s);
+  if ((s = dalloc(ctx, &ctx->rs.dpart, (int64_t)ctx->rs.max_blocks * 2)) != ZRL_OK)
+    return fail(s);
+  if ((s = dalloc(ctx, &ctx->rs.ticket, 4)) != ZRL_OK) return fail(s);
+  // identity normalizers (Normalizer::new: mean 0, m2 1, count 1)
+  {
+    std::vector<float> ones(std::max(od, cd), 1.0f);
+    cudaMemcpyAsync(ctx->obs_m2, ones.data(), sizeof(float) * od,
+                    cudaMemcpyHostToDevice, ctx->stream);
+    cudaMemcpyAsync(ctx->crit_m2, ones.data(), sizeof(float) * cd,
+                    cudaMemcpyHostToDevice, ctx->stream);
+    if (refresh_norm(ctx) != ZRL_OK) return fail(ZRL_CUDA_ERROR);
+  }
+  ctx->st_host->lr = ctx->lr_host;
+  cudaMemcpyAsync(ctx->st, ctx->st_host, sizeof(DevState), cudaMemcpyHostToDevice,
+                  ctx->stream);
+  if ((s = ctx->gemm.init(ctx->device, &ctx->err)) != ZRL_OK) return fail(s);
+  if (comm && comm->world_size > 1) {
+    if ((s = ctx->comm.init(*comm, &ctx->err)) != ZRL_OK) return fail(s);
+  }
+  if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) return fail(ZRL_CUDA_ERROR);
+  *out = ctx;
+  return ZRL_OK;
+}
+
+zrl_status zrl_destroy(zrl_ctx *ctx) {
+  if (!ctx) return ZRL_OK;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  ctx->comm.destroy();
+  ctx->gemm.destroy();
+  float **bufs[] = {&ctx->P, &ctx->G, &ctx->M, &ctx->V, &ctx->obs_mean, &ctx->obs_m2,
+                    &ctx->obs_sd, &ctx->crit_mean, &ctx->crit_m2, &ctx->crit_sd,
+                    &ctx->b_obs, &ctx->b_cobs, &ctx->b_act, &ctx->b_mo, &ctx->b_lpo,
+                    &ctx->b_vo, &ctx->b_adv, &ctx->b_ret, &ctx->r_rew, &ctx->r_val,
+                    &ctx->r_lv, &ctx->e_xa, &ctx->e_xc, &ctx->e_act, &ctx->e_mo,
+                    &ctx->e_lpo, &ctx->e_vo, &ctx->e_adv, &ctx->e_ret, &ctx->wpart,
+                    &ctx->bpart, &ctx->rs.fpart};
+  for (float **b : bufs)
+    if (*b) cudaFree(*b);
+  for (int k = 0; k < 2; ++k) {
+    for (auto *p : ctx->act[k])
+      if (p) cudaFree(p);
+    for (auto *p : ctx->dlt[k])
+      if (p) cudaFree(p);
+  }
+  if (ctx->r_done) cudaFree(ctx->r_done);
+  if (ctx->order_dev) cudaFree(ctx->order_dev);
+  if (ctx->st) cudaFree(ctx->st);
+  if (ctx->adv_part) cudaFree(ctx->adv_part);
+  if (ctx->moments) cudaFree(ctx->moments);
+  if (ctx->rs.dpart) cudaFree(ctx->rs.dpart);
+  if (ctx->rs.ticket) cudaFree(ctx->rs.ticket);
+  if (ctx->st_host) cudaFreeHost(ctx->st_host);
+  if (ctx->order_pinned) cudaFreeHost(ctx->order_pinned);
+  for (auto e : ctx->ev_pool) cudaEventDestroy(e);
+  if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+  return ZRL_OK;
+}
+
+zrl_status zrl_synchronize(zrl_ctx *ctx) {
+  if (!ctx) return ZRL_INVALID_ARG;
+  CK(cudaStreamSynchronize(ctx->stream));
+  return ZRL_OK;
+}
+
+void *zrl_stream(zrl_ctx *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
+
+int64_t zrl_param_count(const zrl_ctx *ctx) { return ctx ? ctx->flat_params : 0; }
+
+int64_t zrl_kernel_launches(const zrl_ctx *ctx) { return ctx ? ctx->launches : 0; }
+
+static zrl_status reset_adam(zrl_ctx *ctx) {
+  CK(cudaMemsetAsync(ctx->M, 0, sizeof(float) * ctx->dev_params, ctx->stream));
+  CK(cudaMemsetAsync(ctx->V, 0, sizeof(float) * ctx->dev_params, ctx->stream));
+  CK(cudaMemsetAsync(ctx->st->t, 0, sizeof(int32_t) * 3, ctx->stream));
+  ctx->t_logstd_host = 0;
+  return ZRL_OK;
+}
+
+zrl_status zrl_set_params(zrl_ctx *ctx, const float *flat, int64_t count) {
+  if (!ctx || !flat) return ZRL_INVALID_ARG;
+  if (count != ctx->flat_params) return bad(ctx, "parameter count mismatch");
+  CK(cudaSetDevice(ctx->device));
+  std::vector<float> pad(ctx->dev_params);
+  flat_to_padded(ctx, flat, pad.data());
+  CK(cudaMemcpyAsync(ctx->P, pad.data(), sizeof(float) * ctx->dev_params,
+                     cudaMemcpyHostToDevice, ctx->stream));
+  TRY(reset_adam(ctx));
+  CK(cudaStreamSynchronize(ctx->stream));
+  return ZRL_OK;
+}
+
+zrl_status zrl_get_params(zrl_ctx *ctx, float *flat, int64_t count) {
+  if (!ctx || !flat) return ZRL_INVALID_ARG;
+  if (count != ctx->flat_params) return bad(ctx, "parameter count mismatch");
+  CK(cudaSetDevice(ctx->device));
+  std::vector<float> pad(ctx->dev_params);
+  CK(cudaMemcpyAsync(pad.data(), ctx->P, sizeof(float) * ctx->dev_params,
+                     cudaMemcpyDeviceToHost, ctx->stream));
+  CK(cudaStreamSynchronize(ctx->stream));
+  padded_to_flat(ctx, pad.data(), flat);
+  return ZRL_OK;
+}
+
+zrl_status zrl_init_reference(zrl_ctx *ctx, float init_noise_std, float init_lr,
+                              uint64_t *lcg_state) {
+  if (!ctx || !lcg_state || !(init_noise_std > 0.0f)) return ZRL_INVALID_ARG;
+  std::vector<float> flat(ctx->flat_params);
+  const NetLayout &La = ctx->net[0], &Lc = ctx->net[1];
+  mlp_init_reference(ctx->mcfg.actor_dims, ctx->mcfg.n_actor_dims, 0.01f, lcg_state,
+                     flat.data() + La.flat_begin);
+  mlp_init_reference(ctx->mcfg.critic_dims, ctx->mcfg.n_critic_dims, 1.0f, lcg_state,
+                     flat.data() + Lc.flat_begin);
+  const float ls = logf(init_noise_std);
+  for (int k = 0; k < ctx->A; ++k) flat[Lc.flat_end + k] = ls;
+  TRY(zrl_set_params(ctx, flat.data(), ctx->flat_params));
+  return zrl_set_lr(ctx, init_lr);
+}
+
+zrl_status zrl_set_adam_state(zrl_ctx *ctx, const int32_t *t3, const float *m,
+                              const float *v, int64_t count) {
+  if (!ctx || !t3) return ZRL_INVALID_ARG;
+  if ((m || v) && count != ctx->flat_params) return bad(ctx, "parameter count mismatch");
+  CK(cudaSetDevice(ctx->device));
+  std::vector<float> pad(ctx->dev_params);
+  if (m) {
+    flat_to_padded(ctx, m, pad.data());
+    CK(cudaMemcpy(ctx->M, pad.data(), sizeof(float) * ctx->dev_params,
+                  cudaMemcpyHostToDevice));
+  }
+  if (v) {
+    flat_to_padded(ctx, v, pad.data());
+    CK(cudaMemcpy(ctx->V, pad.data(), sizeof(float) * ctx->dev_params,
+                  cudaMemcpyHostToDevice));
+  }
+  CK(cudaStreamSynchronize(ctx->stream));
+  CK(cudaMemcpy(ctx->st->t, t3, sizeof(int32_t) * 3, cudaMemcpyHostToDevice));
+  ctx->t_logstd_host = t3[2];
+  return ZRL_OK;
+}
+
+zrl_status zrl_get_adam_state(zrl_ctx *ctx, int32_t *t3, float *m, float *v,
+                              int64_t count) {
+  if (!ctx || !t3) return ZRL_INVALID_ARG;
+  if ((m || v) && count != ctx->flat_params) return bad(ctx, "parameter count mismatch");
+  CK(cudaSetDevice(ctx->device));
+  CK(cudaStreamSynchronize(ctx->stream));
+  CK(cudaMemcpy(t3, ctx->st->t, sizeof(int32_t) * 3, cudaMemcpyDeviceToHost));
+  std::vector<float> pad(ctx->dev_params);
+  if (m) {
+    CK(cudaMemcpy(pad.data(), ctx->M, sizeof(float) * ctx->dev_params,
+                  cudaMemcpyDeviceToHost));
+    padded_to_flat(ctx, pad.data(), m);
+  }
+  if (v) {
+    CK(cudaMemcpy(pad.data(), ctx->V, sizeof(float) * ctx->dev_params,
+                  cudaMemcpyDeviceToHost));
+    padded_to_flat(ctx, pad.data(), v);
+  }
+  return ZRL_OK;
+}
+
+zrl_status zrl_set_normalizers(zrl_ctx *ctx, const float *obs_mean,
+                               const float *obs_m2, float obs_count,
+                               const float *crit_mean, const float *crit_m2,
+                               float crit_count) {
+  if (!ctx || !obs_mean || !obs_m2 || !crit_mean || !crit_m2) return ZRL_INVALID_ARG;
+  CK(cudaSetDevice(ctx->device));
+  const int od = ctx->net[0].d[0], cd = ctx->net[1].d[0];
+  CK(cudaMemcpyAsync(ctx->obs_mean, obs_mean, sizeof(float) * od, cudaMemcpyHostToDevice, ctx->stream));
+  CK(cudaMemcpyAsync(ctx->obs_m2, obs_m2, sizeof(float) * od, cudaMemcpyHostToDevice, ctx->stream));
+  CK(cudaMemcpyAsync(ctx->crit_mean, crit_mean, sizeof(float) * cd, cudaMemcpyHostToDevice, ctx->stream));
+  CK(cudaMemcpyAsync(ctx->crit_m2, crit_m2, sizeof(float) * cd, cudaMemcpyHostToDevice, ctx->stream));
+  ctx->obs_count = obs_count;
+  ctx->crit_count = crit_count;
+  TRY(refresh_norm(ctx));
+  CK(cudaStreamSynchronize(ctx->stream));
+  return ZRL_OK;
+}
+
+zrl_status zrl_get_normalizers(zrl_ctx *ctx, float *obs_mean, float *obs_m2,
+                               float *obs_count, float *crit_mean, float *crit_m2,
+                               float *crit_count) {
+  if (!ctx) return ZRL_INVALID_ARG;
+  CK(cudaSetDevice(ctx->device));
+  CK(cudaStreamSynchronize(ctx->stream));
+  const int od = ctx->net[0].d[0], cd = ctx->net[1].d[0];
+  if (obs_mean) CK(cudaMemcpy(obs_mean, ctx->obs_mean, sizeof(float) * od, cudaMemcpyDeviceToHost));
+  if (obs_m2) CK(cudaMemcpy(obs_m2, ctx->obs_m2, sizeof(float) * od, cudaMemcpyDeviceToHost));
+  if (crit_mean) CK(cudaMemcpy(crit_mean, ctx->crit_mean, sizeof(float) * cd, cudaMemcpyDeviceToHost));
+  if (crit_m2) CK(cudaMemcpy(crit_m2, ctx->crit_m2, sizeof(float) * cd, cudaMemcpyDeviceToHost));
+  if (obs_count) *obs_count = ctx->obs_count;
+  if (crit_count) *crit_count = ctx->crit_count;
+  return ZRL_OK;
+}
+
+zrl_status zrl_set_lr(zrl_ctx *ctx, float lr) {
+  if (!ctx) return ZRL_INVALID_ARG;
+  CK(cudaSetDevice(ctx->device));
+  ctx->lr_host = lr;
+  CK(cudaMemcpyAsync(&ctx->st->lr, &ctx->lr_host, sizeof(float), cudaMemcpyHostToDevice,
+                     ctx->stream));
+  CK(cudaStreamSynchronize(ctx->stream));
+  return ZRL_OK;
+}
+
+zrl_status zrl_get_lr(zrl_ctx *ctx, float *lr) {
+  if (!ctx || !lr) return ZRL_INVALID_ARG;
+  CK(cudaSetDevice(ctx->device));
+  CK(cudaStreamSynchronize(ctx->stream));
+  CK(cudaMemcpy(lr, &ctx->st->lr, sizeof(float), cudaMemcpyDeviceToHost));
+  ctx->lr_host = *lr;
+  return ZRL_OK;
+}
+
+zrl_status zrl_gae(zrl_ctx *ctx, const float *rewards, const float *values,
+                   const uint8_t *dones, const float *last_values, int64_t n_envs,
+                   int64_t T, float gamma, float lam, float *adv_out, float *ret_out,
+                   int32_t on_device) {
+  if (!ctx || !rewards || !values || !dones || !last_values || !adv_out || !ret_out)
+    return ZRL_INVALID_ARG;
+  if (n_envs < 0 || T < 0) return bad(ctx, "negative size");
+  if (T > 4096) return bad(ctx, "T larger than 4096 is not supported");
+  if (n_envs == 0 || T == 0) return ZRL_OK;
+  CK(cudaSetDevice(ctx->device));
+  TRY(ensure_envs(ctx, n_envs, T));
+  GaeArgs a{};
+  a.n_envs = n_envs;
+  a.T = T;
+  a.gamma = gamma;
+  a.lam = lam;
+  const int64_t n = n_envs * T;
+  if (on_device) {
+    a.rewards = rewards;
+    a.values = values;
+    a.dones = dones;
+    a.last_values = last_values;
+    a.adv = adv_out;
+    a.ret = ret_out;
+  } else {
+    CK(cudaMemcpyAsync(ctx->r_rew, rewards, 4 * n, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(ctx->r_val, values, 4 * n, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(ctx->r_done, dones, n, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(ctx->r_lv, last_values, 4 * n_envs, cudaMemcpyHostToDevice, ctx->stream));
+    a.rewards = ctx->r_rew;
+    a.values = ctx->r_val;
+    a.dones = ctx->r_done;
+    a.last_values = ctx->r_lv;
+    a.adv = ctx->b_adv;
+    a.ret = ctx->b_ret;
+  }
+  launch_gae(a, nullptr, gae_blocks(n_envs), ctx->stream);
+  ctx->launches++;
+  CHECK_LAUNCH();
+  if (!on_device) {
+    CK(cudaMemcpyAsync(adv_out, ctx->b_adv, 4 * n, cudaMemcpyDeviceToHost, ctx->stream));
+    CK(cudaMemcpyAsync(ret_out, ctx->b_ret, 4 * n, cudaMemcpyDeviceToHost, ctx->stream));
+  }
+  CK(cudaStreamSynchronize(ctx->stream));
+  return ZRL_OK;
+}
+
+static zrl_status check_batch(zrl_ctx *ctx, const zrl_batch *b, int64_t *n_global) {
+  if (!b) return bad(ctx, "null batch");
+  if (b->n < 0) return bad(ctx, "negative batch size");
+  *n_global = b->n_global > 0 ? b->n_global : b->n;
+  if (ctx->comm.world <= 1 && *n_global != b->n)
+    return bad(ctx, "n_global != n without a data-parallel group");
+  if (b->row_offset < 0 || b->row_offset + b->n > *n_global)
+    return bad(ctx, "rows outside the global batch");
+  if (*n_global > INT32_MAX) return bad(ctx, "batch larger than 2^31 rows");
+  if (b->n > 0 && (!b->obs || !b->critic_obs || !b->action || !b->mean_old ||
+                   !b->logp_old || !b->value_old))
+    return bad(ctx, "null batch array");
+  return ZRL_OK;
+}
+
+static zrl_status write_back_adv(zrl_ctx *ctx, zrl_batch *b, const float *adv_dev) {
+  if (!b->write_back_adv || b->n == 0) return ZRL_OK;
+  // normalized advantages in the batch's own row order (ppo.rs:346-348):
+  // (adv - mean) / sd with the device moments, applied to a host copy so the
+  // caller's device buffer is only written once
+  std::vector<float> tmp;
+  CK(cudaStreamSynchronize(ctx->stream));
+  DevState st;
+  CK(cudaMemcpy(&st, ctx->st, sizeof(DevState), cudaMemcpyDeviceToHost));
+  tmp.resize(b->n);
+  CK(cudaMemcpy(tmp.data(), adv_dev, 4 * b->n, cudaMemcpyDeviceToHost));
+  for (auto &x : tmp) x = (x - st.adv_mean) / st.adv_sd;
+  if (b->on_device)
+    CK(cudaMemcpy(b->adv, tmp.data(), 4 * b->n, cudaMemcpyHostToDevice));
+  else
+    memcpy(b->adv, tmp.data(), 4 * b->n);
+  return ZRL_OK;
+}
+
+zrl_status zrl_update(zrl_ctx *ctx, const zrl_ppo_config *cfg, zrl_batch *batch,
+                      zrl_stats *out) {
+  if (!ctx) return ZRL_INVALID_ARG;
+  TRY(check_cfg(ctx, cfg));
+  int64_t n_global = 0;
+  TRY(check_batch(ctx, batch, &n_global));
+  if (batch->n > 0 && (!batch->adv || !batch->ret)) return bad(ctx, "null adv/ret");
+  if (n_global < cfg->minibatches) return bad(ctx, "fewer samples than minibatches");
+  CK(cudaSetDevice(ctx->device));
+  cudaEvent_t u0 = nullptr;
+  prof_begin(ctx, &u0);
+  DevBatch d{};
+  TRY(stage_batch(ctx, batch, &d, true));
+  TRY(adv_moments(ctx, d.adv, batch->n, n_global, false, 0));
+  TRY(run_epochs(ctx, cfg, d, batch->n, n_global, batch->row_offset));
+  prof_end(ctx, u0);
+  TRY(write_back_adv(ctx, batch, d.adv));
+  return finish_update(ctx, out);
+}
+
+zrl_status zrl_gae_update(zrl_ctx *ctx, const zrl_ppo_config *cfg,
+                          const zrl_rollout *ro, zrl_batch *batch, zrl_stats *out) {
+  if (!ctx || !ro) return ZRL_INVALID_ARG;
+  TRY(check_cfg(ctx, cfg));
+  int64_t n_global = 0;
+  TRY(check_batch(ctx, batch, &n_global));
+  if (ro->n_envs * ro->T != batch->n) return bad(ctx, "rollout and batch disagree on n");
+  if (ro->T > 4096) return bad(ctx, "T larger than 4096 is not supported");
+  if (n_global < cfg->minibatches) return bad(ctx, "fewer samples than minibatches");
+  CK(cudaSetDevice(ctx->device));
+  cudaEvent_t u0 = nullptr;
+  prof_begin(ctx, &u0);
+  DevBatch d{};
+  TRY(stage_batch(ctx, batch, &d, false));
+  TRY(ensure_envs(ctx, ro->n_envs, ro->T));
+  const int64_t n = batch->n;
+  GaeArgs a{};
+  a.n_envs = ro->n_envs;
+  a.T = ro->T;
+  a.gamma = cfg->gamma;
+  a.lam = cfg->lam;
+  if (batch->on_device) {
+    a.rewards = ro->rewards;
+    a.values = ro->values;
+    a.dones = ro->dones;
+    a.last_values = ro->last_values;
+  } else {
+    CK(cudaMemcpyAsync(ctx->r_rew, ro->rewards, 4 * n, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(ctx->r_val, ro->values, 4 * n, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(ctx->r_done, ro->dones, n, cudaMemcpyHostToDevice, ctx->stream));
+    CK(cudaMemcpyAsync(ctx->r_lv, ro->last_values, 4 * ro->n_envs, cudaMemcpyHostToDevice,
+                       ctx->stream));
+    a.rewards = ctx->r_rew;
+    a.values = ctx->r_val;
+    a.dones = ctx->r_done;
+    a.last_values = ctx->r_lv;
+  }
+  a.adv = ctx->b_adv;
+  a.ret = ctx->b_ret;
+  const int gb = gae_blocks(ro->n_envs);
+  if (n > 0) {
+    launch_gae(a, ctx->adv_part, gb, ctx->stream);
+    ctx->launches++;
+    CHECK_LAUNCH();
+  }
+  d.adv = ctx->b_adv;
+  d.ret = ctx->b_ret;
+  TRY(adv_moments(ctx, d.adv, n, n_global, n > 0, n > 0 ? gb : 0));
+  TRY(run_epochs(ctx, cfg, d, n, n_global, batch->row_offset));
+  prof_end(ctx, u0);
+  return finish_update(ctx, out);
+}
+
+zrl_status zrl_forward(zrl_ctx *ctx, const float *obs, const float *critic_obs,
+                       int64_t n, float *mean_out, float *value_out, int32_t on_device) {
+  if (!ctx) return ZRL_INVALID_ARG;
+  if (n < 0) return bad(ctx, "negative n");
+  if ((mean_out && !obs) || (value_out && !critic_obs)) return bad(ctx, "null input");
+  if (n == 0) return ZRL_OK;
+  CK(cudaSetDevice(ctx->device));
+  const int od = ctx->net[0].d[0], cd = ctx->net[1].d[0];
+  const int odp = ctx->net[0].dp[0], cdp = ctx->net[1].dp[0];
+  const int64_t chunk = std::min<int64_t>(n, 65536);
+  TRY(ensure_batch(ctx, chunk));
+  TRY(ensure_mb(ctx, chunk));
+  for (int64_t r0 = 0; r0 < n; r0 += chunk) {
+    const int64_t rows = std::min(chunk, n - r0);
+    for (int k = 0; k < 2; ++k) {
+      float *outp = k == 0 ? mean_out : value_out;
+      if (!outp) continue;
+      const float *src = k == 0 ? obs : critic_obs;
+      const int dim = k == 0 ? od : cd;
+      const int pitch = k == 0 ? odp : cdp;
+      const float *x = src + r0 * dim;
+      float *raw = k == 0 ? ctx->b_obs : ctx->b_cobs;
+      if (!on_device) {
+        CK(cudaMemcpyAsync(raw, x, sizeof(float) * rows * dim, cudaMemcpyHostToDevice,
+                           ctx->stream));
+        x = raw;
+      }
+      float *xn = k == 0 ? ctx->e_xa : ctx->e_xc;
+      launch_normalize_rows(x, rows, dim, pitch, k == 0 ? ctx->obs_mean : ctx->crit_mean,
+                            k == 0 ? ctx->obs_sd : ctx->crit_sd, xn, ctx->stream);
+      ctx->launches++;
+      CHECK_LAUNCH();
+      TRY(forward_net(ctx, k, xn, rows));
+      const NetLayout &L = ctx->net[k];
+      const int cols = k == 0 ? ctx->A : 1;
+      float *dst = outp + r0 * cols;
+      float *tmp = k == 0 ? ctx->e_act : ctx->e_vo;
+      launch_unpad_rows(ctx->act[k][L.L], rows, L.dp[L.L], cols,
+                        on_device ? dst : tmp, ctx->stream);
+      ctx->launches++;
+      CHECK_LAUNCH();
+      if (!on_device)
+        CK(cudaMemcpyAsync(dst, tmp, sizeof(float) * rows * cols, cudaMemcpyDeviceToHost,
+                           ctx->stream));
+    }
+  }
+  CK(cudaStreamSynchronize(ctx->stream));
+  return ZRL_OK;
+}
+
+zrl_status zrl_minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
+                               const zrl_batch *batch, const int64_t *idx,
+                               int64_t n_idx, float *grads_out, float *sums3_out) {
+  if (!ctx || !idx || !grads_out) return ZRL_INVALID_ARG;
+  TRY(check_cfg(ctx, cfg));
+  int64_t n_global = 0;
+  TRY(check_batch(ctx, batch, &n_global));
+  if (ctx->comm.world > 1) return bad(ctx, "minibatch_grads is a single-rank hook");
+  if (n_idx < 1) return bad(ctx, "empty index set");
+  for (int64_t i = 0; i < n_idx; ++i)
+    if (idx[i] < 0 || idx[i] >= batch->n) return bad(ctx, "index out of range");
+  CK(cudaSetDevice(ctx->device));
+  DevBatch d{};
+  TRY(stage_batch(ctx, batch, &d, true));
+  TRY(ensure_batch(ctx, std::max(n_idx, batch->n)));
+  TRY(ensure_pinned_orders(ctx, n_idx));
+  for (int64_t i = 0; i < n_idx; ++i) ctx->order_pinned[i] = (int32_t)idx[i];
+  CK(cudaMemcpyAsync(ctx->order_dev, ctx->order_pinned, sizeof(int32_t) * n_idx,
+                     cudaMemcpyHostToDevice, ctx->stream));
+  GatherArgs g = gather_args(ctx, d.obs, d.cobs, d.act, d.mo, d.lpo, d.vo, d.adv, d.ret);
+  g.n_used = n_idx;
+  g.apply_adv_norm = 0;  // the hook takes advantages as given
+  launch_gather(g, ctx->stream);
+  ctx->launches++;
+  CHECK_LAUNCH();
+  TRY(minibatch_grads(ctx, cfg, epoch_view(ctx, 0, n_idx), 1.0f / (float)n_idx));
+  std::vector<float> pad(ctx->grad_len);
+  CK(cudaMemcpyAsync(pad.data(), ctx->G, sizeof(float) * ctx->grad_len,
+                     cudaMemcpyDeviceToHost, ctx->stream));
+  CK(cudaStreamSynchronize(ctx->stream));
+  padded_to_flat(ctx, pad.data(), grads_out);
+  if (sums3_out) memcpy(sums3_out, pad.data() + ctx->dev_params, sizeof(float) * 3);
+  return ZRL_OK;
+}
+
+zrl_status zrl_apply_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg, const float *grads,
+                           float kl) {
+  if (!ctx || !grads) return ZRL_INVALID_ARG;
+  TRY(check_cfg(ctx, cfg));
+  CK(cudaSetDevice(ctx->device));
+  std::vector<float> pad(ctx->grad_len, 0.0f);
+  flat_to_padded(ctx, grads, pad.data());
+  pad[ctx->dev_params + 2] = kl;
+  CK(cudaMemcpyAsync(ctx->G, pad.data(), sizeof(float) * ctx->grad_len,
+                     cudaMemcpyHostToDevice, ctx->stream));
+  TRY(step(ctx, cfg, cfg->minibatches, false, false));
+  CK(cudaStreamSynchronize(ctx->stream));
+  ctx->t_logstd_host += 1;
+  float lr = 0.0f;
+  return zrl_get_lr(ctx, &lr);
+}
+
+zrl_status zrl_set_profiling(zrl_ctx *ctx, int32_t enabled) {
+  if (!ctx) return ZRL_INVALID_ARG;
+  ctx->profiling = enabled != 0;
+  return ZRL_OK;
+}
+
+zrl_status zrl_get_profile(zrl_ctx *ctx, float *gemm_ms, float *update_ms,
+                           int64_t *gemm_launches) {
+  if (!ctx) return ZRL_INVALID_ARG;
+  if (gemm_ms) *gemm_ms = ctx->prof_gemm_ms;
+  if (update_ms) *update_ms = ctx->prof_update_ms;
+  if (gemm_launches) *gemm_launches = ctx->prof_gemm_launches;
+  return ZRL_OK;
+}
+
+zrl_status zrl_record_obs(zrl_ctx *ctx, const float *obs, const float *critic_obs,
+                          int64_t n) {
+  if (!ctx || (n > 0 && (!obs || !critic_obs))) return ZRL_INVALID_ARG;
+  if (n < 0) return bad(ctx, "negative n");
+  if (n == 0) return ZRL_OK;
+  CK(cudaSetDevice(ctx->device));
+  const int od = ctx->net[0].d[0], cd = ctx->net[1].d[0];
+  TRY(ensure_batch(ctx, n));
+  CK(cudaMemcpyAsync(ctx->b_obs, obs, sizeof(float) * n * od, cudaMemcpyHostToDevice,
+                     ctx->stream));
+  CK(cudaMemcpyAsync(ctx->b_cobs, critic_obs, sizeof(float) * n * cd,
+                     cudaMemcpyHostToDevice, ctx->stream));
+  launch_record_obs(ctx->b_obs, n, od, ctx->obs_mean, ctx->obs_m2, ctx->obs_count,
+                    ctx->stream);
+  launch_record_obs(ctx->b_cobs, n, cd, ctx->crit_mean, ctx->crit_m2, ctx->crit_count,
+                    ctx->stream);
+  ctx->launches += 2;
+  CHECK_LAUNCH();
+  for (int64_t r = 0; r < n; ++r) {  // the same f32 count recurrence
+    ctx->obs_count += 1.0f;
+    ctx->crit_count += 1.0f;
+  }
+  TRY(refresh_norm(ctx));
+  CK(cudaStreamSynchronize(ctx->stream));
+  return ZRL_OK;
+}
+
+zrl_status zrl_policy_step(zrl_ctx *ctx, const float *obs, const float *critic_obs,
+                           int64_t n, uint64_t seed, uint64_t counter, float *action,
+                           float *logp, float *mean, float *value, int32_t on_device) {
+  if (!ctx || !obs || !action) return ZRL_INVALID_ARG;
+  if (value && !critic_obs) return bad(ctx, "value requested without critic_obs");
+  if (n < 0) return bad(ctx, "negative n");
+  if (n == 0) return ZRL_OK;
+  CK(cudaSetDevice(ctx->device));
+  const int od = ctx->net[0].d[0], cd = ctx->net[1].d[0];
+  const int odp = ctx->net[0].dp[0], cdp = ctx->net[1].dp[0];
+  const int A = ctx->A;
+  const int64_t chunk = std::min<int64_t>(n, 65536);
+  TRY(ensure_batch(ctx, chunk));
+  TRY(ensure_mb(ctx, chunk));
+  const NetLayout &La = ctx->net[0], &Lc = ctx->net[1];
+  for (int64_t r0 = 0; r0 < n; r0 += chunk) {
+    const int64_t rows = std::min(chunk, n - r0);
+    const float *x = obs + r0 * od;
+    if (!on_device) {
+      CK(cudaMemcpyAsync(ctx->b_obs, x, sizeof(float) * rows * od, cudaMemcpyHostToDevice,
+                         ctx->stream));
+      x = ctx->b_obs;
+    }
+    launch_normalize_rows(x, rows, od, odp, ctx->obs_mean, ctx->obs_sd, ctx->e_xa,
+                          ctx->stream);
+    ctx->launches++;
+    TRY(forward_net(ctx, 0, ctx->e_xa, rows));
+    float *act_d = on_device ? action + r0 * A : ctx->e_act;
+    float *lp_d = logp ? (on_device ? logp + r0 : ctx->e_lpo) : nullptr;
+    float *mean_d = mean ? (on_device ? mean + r0 * A : ctx->e_mo) : nullptr;
+    // rows are numbered globally so a chunked call draws the same numbers
+    launch_policy_sample(ctx->act[0][La.L], La.dp[La.L], ctx->P + ctx->ls_off, A, rows,
+                         seed, counter, act_d, lp_d, mean_d, ctx->stream, r0);
+    ctx->launches += logp ? 2 : 1;
+    CHECK_LAUNCH();
+    if (value) {
+      const float *c = critic_obs + r0 * cd;
+      if (!on_device) {
+        CK(cudaMemcpyAsync(ctx->b_cobs, c, sizeof(float) * rows * cd,
+                           cudaMemcpyHostToDevice, ctx->stream));
+        c = ctx->b_cobs;
+      }
+      launch_normalize_rows(c, rows, cd, cdp, ctx->crit_mean, ctx->crit_sd, ctx->e_xc,
+                            ctx->stream);
+      ctx->launches++;
+      TRY(forward_net(ctx, 1, ctx->e_xc, rows));
+      float *v_d = on_device ? value + r0 : ctx->e_vo;
+      launch_unpad_rows(ctx->act[1][Lc.L], rows, Lc.dp[Lc.L], 1, v_d, ctx->stream);
+      ctx->launches++;
+      CHECK_LAUNCH();
+      if (!on_device)
+        CK(cudaMemcpyAsync(value + r0, v_d, sizeof(float) * rows, cudaMemcpyDeviceToHost,
+                           ctx->stream));
+    }
+    if (!on_device) {
+      CK(cudaMemcpyAsync(action + r0 * A, act_d, sizeof(float) * rows * A,
+                         cudaMemcpyDeviceToHost, ctx->stream));
+      if (logp)
+        CK(cudaMemcpyAsync(logp + r0, lp_d, sizeof(float) * rows, cudaMemcpyDeviceToHost,
+                           ctx->stream));
+      if (mean)
+        CK(cudaMemcpyAsync(mean + r0 * A, mean_d, sizeof(float) * rows * A,
+                           cudaMemcpyDeviceToHost, ctx->stream));
+    }
+    // keep the staging buffers alive until the copies drain
+    CK(cudaStreamSynchronize(ctx->stream));
+  }
+  return ZRL_OK;
+}
+
+// ---------------------------------------------------------------- I/O
+
+static zrl_status build_checkpoint(zrl_ctx *ctx, std::vector<uint8_t> *out) {
+  std::vector<float> flat(ctx->flat_params);
+  TRY(zrl_get_params(ctx, flat.data(), ctx->flat_params));
+  const int od = ctx->net[0].d[0], cd = ctx->net[1].d[0];
+  std::vector<float> om(od), om2(od), cm(cd), cm2(cd);
+  float oc = 0, cc = 0, lr = 0;
+  TRY(zrl_get_normalizers(ctx, om.data(), om2.data(), &oc, cm.data(), cm2.data(), &cc));
+  TRY(zrl_get_lr(ctx, &lr));
+  std::map<std::string, StTensor> ts;
+  const char *prefix[2] = {"actor", "critic"};
+  for (int k = 0; k < 2; ++k) {
+    const NetLayout &L = ctx->net[k];
+    for (int l = 0; l < L.L; ++l) {
+      StTensor w, b;
+      w.shape = {L.d[l + 1], L.d[l]};
+      w.data.assign(flat.begin() + L.fw_off[l],
+                    flat.begin() + L.fw_off[l] + (int64_t)L.d[l + 1] * L.d[l]);
+      b.shape = {L.d[l + 1]};
+      b.data.assign(flat.begin() + L.fb_off[l], flat.begin() + L.fb_off[l] + L.d[l + 1]);
+      ts[std::string(prefix[k]) + ".w_" + std::to_string(l)] = w;
+      ts[std::string(prefix[k]) + ".b_" + std::to_string(l)] = b;
+    }
+  }
+  auto vec = [](std::vector<float> v) {
+    StTensor t;
+    t.shape = {(int64_t)v.size()};
+    t.data = std::move(v);
+    return t;
+  };
+  ts["log_std"] = vec(std::vector<float>(flat.begin() + ctx->net[1].flat_end, flat.end()));
+  ts["obs_norm.mean"] = vec(om);
+  ts["obs_norm.m2"] = vec(om2);
+  ts["obs_norm.count"] = vec({oc});
+  ts["critic_norm.mean"] = vec(cm);
+  ts["critic_norm.m2"] = vec(cm2);
+  ts["critic_norm.count"] = vec({cc});
+  ts["lr"] = vec({lr});
+  *out = st_serialize(ts);
+  return ZRL_OK;
+}
+
+zrl_status zrl_save(zrl_ctx *ctx, const char *path) {
+  if (!ctx || !path) return ZRL_INVALID_ARG;
+  std::vector<uint8_t> bytes;
+  TRY(build_checkpoint(ctx, &bytes));
+  FILE *f = fopen(path, "wb");
+  if (!f) {
+    ctx->err = std::string("cannot open ") + path + " for writing";
+    return ZRL_IO_ERROR;
+  }
+  const size_t w = fwrite(bytes.data(), 1, bytes.size(), f);
+  const int c = fclose(f);
+  if (w != bytes.size() || c != 0) {
+    ctx->err = std::string("short write to ") + path;
+    return ZRL_IO_ERROR;
+  }
+  return ZRL_OK;
+}
+
+zrl_status zrl_load_from_bytes(zrl_ctx *ctx, const uint8_t *bytes, size_t len) {
+  if (!ctx || !bytes) return ZRL_INVALID_ARG;
+  std::map<std::string, StTensor> ts;
+  if (!st_parse(bytes, len, &ts, &ctx->err)) return ZRL_IO_ERROR;
+  std::vector<float> flat(ctx->flat_params);
+  const char *prefix[2] = {"actor", "critic"};
+  for (int k = 0; k < 2; ++k) {
+    const NetLayout &L = ctx->net[k];
+    // layers are the contiguous w_{l} from 0 (ppo.rs:594-609)
+    int layers = 0;
+    while (ts.count(std::string(prefix[k]) + ".w_" + std::to_string(layers))) ++layers;
+    if (layers != L.L) {
+      ctx->err = std::string("checkpoint ") + prefix[k] + " has " + std::to_string(layers) +
+                 " layers, context has " + std::to_string(L.L);
+      return ZRL_INVALID_ARG;
+    }
+    for (int l = 0; l < L.L; ++l) {
+      const std::string wn = std::string(prefix[k]) + ".w_" + std::to_string(l);
+      const std::string bn = std::string(prefix[k]) + ".b_" + std::to_string(l);
+      if (!ts.count(bn)) {
+        ctx->err = "checkpoint lacks " + bn;
+        return ZRL_IO_ERROR;
+      }
+      const StTensor &w = ts[wn], &b = ts[bn];
+      if (w.shape.size() != 2) {
+        ctx->err = wn + ": expected 2D";
+        return ZRL_IO_ERROR;
+      }
+      if (w.shape[0] != L.d[l + 1] || w.shape[1] != L.d[l] ||
+          (int64_t)b.data.size() != L.d[l + 1]) {
+        ctx->err = wn + ": shape does not match the context";
+        return ZRL_INVALID_ARG;
+      }
+      std::copy(w.data.begin(), w.data.end(), flat.begin() + L.fw_off[l]);
+      std::copy(b.data.begin(), b.data.end(), flat.begin() + L.fb_off[l]);
+    }
+  }
+  const char *need[] = {"log_std", "obs_norm.mean", "obs_norm.m2", "obs_norm.count",
+                        "critic_norm.mean", "critic_norm.m2", "critic_norm.count", "lr"};
+  for (const char *nm : need)
+    if (!ts.count(nm) || ts[nm].data.empty()) {
+      ctx->err = std::string("checkpoint lacks ") + nm;
+      return ZRL_IO_ERROR;
+    }
+  const int od = ctx->net[0].d[0], cd = ctx->net[1].d[0];
+  if ((int)ts["log_std"].data.size() != ctx->A || (int)ts["obs_norm.mean"].data.size() != od ||
+      (int)ts["obs_norm.m2"].data.size() != od || (int)ts["critic_norm.mean"].data.size() != cd ||
+      (int)ts["critic_norm.m2"].data.size() != cd) {
+    ctx->err = "checkpoint vector sizes do not match the context";
+    return ZRL_INVALID_ARG;
+  }
+  std::copy(ts["log_std"].data.begin(), ts["log_std"].data.end(),
+            flat.begin() + ctx->net[1].flat_end);
+  TRY(zrl_set_params(ctx, flat.data(), ctx->flat_params));  // resets Adam
+  TRY(zrl_set_normalizers(ctx, ts["obs_norm.mean"].data.data(), ts["obs_norm.m2"].data.data(),
+                          ts["obs_norm.count"].data[0], ts["critic_norm.mean"].data.data(),
+                          ts["critic_norm.m2"].data.data(), ts["critic_norm.count"].data[0]));
+  return zrl_set_lr(ctx, ts["lr"].data[0]);
+}
+
+zrl_status zrl_load(zrl_ctx *ctx, const char *path) {
+  if (!ctx || !path) return ZRL_INVALID_ARG;
+  FILE *f = fopen(path, "rb");
+  if (!f) {
+    ctx->err = std::string("cannot open ") + path;
+    return ZRL_IO_ERROR;
+  }
+  std::vector<uint8_t> bytes;
+  uint8_t buf[1 << 16];
+  size_t r;
+  while ((r = fread(buf, 1, sizeof(buf), f)) > 0) bytes.insert(bytes.end(), buf, buf + r);
+  fclose(f);
+  return zrl_load_from_bytes(ctx, bytes.data(), bytes.size());
+}
+
+}  // extern "C"

@@ -1,0 +1,48 @@
+// zrl_gemm.h -- GEMM dispatch for the MLP forward/backward.
+//
+// ZRL_GEMM_FP32 runs the CUDA-core kernel (gemm_simt.cu); ZRL_GEMM_TF32 and
+// ZRL_GEMM_BF16 run the tcgen05 tensor-core kernels (gemm_tc.cu).  There is
+// no silent substitution: a shape the tensor-core kernels do not take is an
+// error, not a fallback.
+#pragma once
+
+#include <string>
+
+#include "zrl_internal.h"
+
+namespace zrl {
+
+// Tensor-core GEMM (gemm_tc.cu).  Returns the number of kernels launched.
+zrl_status gemm_tc(const GemmArgs &g, int precision, cudaStream_t s,
+                   int *launched, std::string *err);
+zrl_status gemm_tc_init(int device, std::string *err);
+
+struct GemmEngine {
+  bool tc_ready = false;
+  zrl_status init(int device, std::string *err) {
+    (void)device;
+    (void)err;
+    return ZRL_OK;
+  }
+  zrl_status run(const GemmArgs &g, int precision, cudaStream_t s, int *launched,
+                 std::string *err) {
+    if (g.M <= 0 || g.N <= 0) {
+      *launched = 0;
+      return ZRL_OK;
+    }
+    if (precision == ZRL_GEMM_FP32) {
+      gemm_simt(g, s);
+      *launched = 1;
+      return ZRL_OK;
+    }
+    if (!tc_ready) {
+      zrl_status st = gemm_tc_init(0, err);
+      if (st != ZRL_OK) return st;
+      tc_ready = true;
+    }
+    return gemm_tc(g, precision, s, launched, err);
+  }
+  void destroy() {}
+};
+
+}  // namespace zrl

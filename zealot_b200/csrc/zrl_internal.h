@@ -1,0 +1,227 @@
+// zrl_internal.h -- shared definitions of libzealot_rl.so (not part of the
+// ABI).  Device layouts:
+//
+//  * Parameters live in one padded device buffer: for each net (actor, then
+//    critic) and each layer l, W_l [dp_{l+1} x dp_l] row-major followed by
+//    b_l [dp_{l+1}], then log_std padded to 32.  dp = dim rounded up to 32,
+//    so every tensor starts on a 128-byte boundary (TMA-legal) and every
+//    GEMM dimension is a multiple of 32.  Padding entries are zero and stay
+//    zero (their gradients are zero).  Gradients, Adam m and v share the
+//    layout, so the optimizer is one pass over one flat buffer.
+//  * Samples are stored sample-major: row = sample, columns = features, so a
+//    minibatch gather is a row gather and every activation is [rows x dp].
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/zealot_rl.h"
+
+namespace zrl {
+
+constexpr int kPad = 32;
+inline int64_t pad_to(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+struct NetLayout {
+  int L = 0;                  // layers
+  int d[ZRL_MAX_LAYERS + 1];  // true dims
+  int dp[ZRL_MAX_LAYERS + 1]; // padded dims
+  int64_t w_off[ZRL_MAX_LAYERS], b_off[ZRL_MAX_LAYERS];   // device (padded)
+  int64_t fw_off[ZRL_MAX_LAYERS], fb_off[ZRL_MAX_LAYERS]; // flat save order
+  int64_t dev_begin = 0, dev_end = 0;
+  int64_t flat_begin = 0, flat_end = 0;
+};
+
+// Per-minibatch scalar state that lives on the device (so a whole update
+// can run without host round trips).
+struct DevState {
+  float lr;
+  int32_t t[3];          // Adam steps: actor, critic, log_std
+  float ep_acc[4];       // epoch accumulators: kl, surrogate, value_loss, entropy
+  float stats[5];        // last finished epoch: kl, surr, vloss, entropy, lr
+  // written by the pre-step for the Adam pass of the same minibatch
+  float step_lr;
+  float clip_scale[2];   // actor, critic
+  float bc1[3], bc2[3];
+  float sumsq[2];        // squared grad norms (actor, critic), diagnostics
+  float adv_mean, adv_sd;
+  int32_t err;           // device-side error flags
+};
+
+// Reduction scratch used by the "last block finishes" kernels: block
+// partials, and one arrival counter per kernel kind (reset to 0 by the last
+// block, so the scratch is reusable by the next launch on the stream).
+struct ReduceScratch {
+  float *fpart;          // [max_blocks * fwidth]
+  double *dpart;         // [max_blocks * 2]
+  unsigned int *ticket;  // [4]
+  int max_blocks;
+  int fwidth;
+};
+
+// ---- kernel launch wrappers (kernels.cu) ------------------------------
+
+struct GaeArgs {
+  const float *rewards, *values, *last_values;
+  const uint8_t *dones;
+  float *adv, *ret;
+  int64_t n_envs, T;
+  float gamma, lam;
+};
+void launch_gae(const GaeArgs &a, double *adv_sum_partials, int nblk,
+                cudaStream_t s);
+int gae_blocks(int64_t n_envs);
+
+// Advantage moments (ppo.rs:342-345) in two passes over the batch: the sum
+// (GAE produces its block partials directly), then the squared deviations
+// from the global mean.  moments[0] = sum, moments[1] = sum of squares of
+// deviations, both in double; a data-parallel group allreduces each slot
+// before the next pass reads it.  finalize writes adv_mean / adv_sd.
+int adv_blocks(int64_t n);
+void launch_adv_sum(const float *adv, int64_t n, double *partials, int nblk,
+                    cudaStream_t s);
+void launch_reduce_moment(const double *partials, int nblk, double *moments,
+                          int slot, cudaStream_t s);
+void launch_adv_sqdev(const float *adv, int64_t n, const double *moments,
+                      int64_t n_global, double *partials, int nblk,
+                      cudaStream_t s);
+void launch_adv_finalize(const double *moments, int64_t n_global, DevState *st,
+                         cudaStream_t s);
+
+// Epoch gather: rows order[p] of the raw batch -> position p, with the
+// observation normalizers and the advantage normalization applied.
+struct GatherArgs {
+  const int32_t *order;  // [n_used] local row indices
+  int64_t n_used;
+  const float *obs, *cobs, *action, *mean_old, *logp_old, *value_old, *adv,
+      *ret;
+  int od, cd, A;          // true dims
+  int odp, cdp;           // padded row pitch of the outputs
+  const float *obs_mean, *obs_sd;       // [od]
+  const float *crit_mean, *crit_sd;     // [cd]
+  const DevState *st;   // adv_mean / adv_sd
+  float *x_a, *x_c;     // [n_used, odp], [n_used, cdp]
+  float *g_action, *g_mean_old;         // [n_used, A]
+  float *g_logp_old, *g_value_old, *g_adv, *g_ret;
+  int apply_adv_norm;
+};
+void launch_gather(const GatherArgs &a, cudaStream_t s);
+// Normalizer divisors: sd = sqrt(max(m2/count, 1e-8)) (ppo.rs:201-202).
+void launch_norm_prepare(const float *m2, float count, int dim, float *sd,
+                         cudaStream_t s);
+void launch_normalize_rows(const float *x, int64_t n, int dim, int pitch,
+                           const float *mean, const float *sd, float *out,
+                           cudaStream_t s);
+
+// PPO losses (ppo.rs:410-452) over one minibatch.
+struct LossArgs {
+  const float *mean;      // actor output [mb, Ap]
+  const float *value;     // critic output [mb, cp] (column 0)
+  int Ap, cp;
+  const float *action, *mean_old;       // [mb, A]
+  const float *logp_old, *value_old, *adv, *ret;  // [mb]
+  const float *log_std;   // [A]
+  int A;
+  int64_t mb;
+  float scale;            // 1 / global minibatch size
+  float clip, entropy_coef, value_coef;
+  float *d_actor;         // [mb, Ap] delta of the actor output layer
+  float *d_critic;        // [mb, cp] delta of the critic output layer
+  float *g_logstd;        // [A] written (sum over the minibatch)
+  float *sums3;           // surr, vloss, kl (sums of scaled terms)
+};
+void launch_loss(const LossArgs &a, ReduceScratch &rs, cudaStream_t s);
+
+// Column sums of a [rows, cols] matrix, split over row chunks into
+// partials [splits, cols].
+void launch_colsum(const float *x, int64_t rows, int cols, int ld,
+                   float *partials, int splits, cudaStream_t s);
+
+// Sum `splits` partial buffers into dst for a list of segments.
+struct ReduceSeg {
+  float *dst;
+  const float *src;      // [splits][count]
+  int64_t count;
+  int splits;
+};
+constexpr int kMaxSegs = 2 * ZRL_MAX_LAYERS * 2;
+struct ReduceSegs {
+  ReduceSeg seg[kMaxSegs];
+  int n;
+};
+void launch_reduce_segments(const ReduceSegs &segs, cudaStream_t s);
+
+// Squared norms of the actor/critic gradient segments, then the pre-step
+// scalars (ppo.rs:473-482, net.rs:197-202, net.rs:235-238, ppo.rs:497-500)
+// computed by the last block.
+struct PrestepArgs {
+  const float *grads;
+  int64_t actor_begin, actor_end, critic_begin, critic_end;
+  const float *log_std;
+  int A;
+  const float *sums3;
+  float max_grad_norm, desired_kl, lr_min, lr_max;
+  int adaptive_lr;
+  int minibatches;
+  int last_of_epoch;
+  int count_stats;
+  DevState *st;
+};
+void launch_prestep(const PrestepArgs &a, ReduceScratch &rs, cudaStream_t s);
+
+// Adam over the whole padded parameter buffer (net.rs:233-251,
+// ppo.rs:496-510), with the per-net clip scale folded in.
+struct AdamArgs {
+  float *p, *m, *v;
+  const float *g;
+  int64_t n;
+  int64_t actor_end, critic_end;  // [0,actor_end) actor, [.., critic_end) critic, rest log_std
+  const DevState *st;
+};
+void launch_adam(const AdamArgs &a, cudaStream_t s);
+
+// Copy an n-element slice of a padded [rows, pitch] buffer into a dense
+// [rows, cols] one (and back).
+void launch_unpad_rows(const float *src, int64_t rows, int pitch, int cols,
+                       float *dst, cudaStream_t s);
+// Rollout sampling: action = mean + exp(log_std) * eps, eps from
+// Philox4x32-10 keyed by (seed, counter); logp per row (may be null).
+void launch_policy_sample(const float *mean, int pitch, const float *log_std,
+                          int A, int64_t n, uint64_t seed, uint64_t counter,
+                          float *action, float *logp, float *mean_out,
+                          cudaStream_t s, int64_t row0 = 0);
+// Normalizer::update over n rows in order (bit-exact Welford).
+void launch_record_obs(const float *x, int64_t n, int dim, float *mean,
+                       float *m2, float count0, cudaStream_t s);
+
+// ---- GEMMs (gemm_simt.cu / gemm_tc.cu) ---------------------------------
+
+enum Epilogue {
+  EPI_STORE = 0,      // C = acc
+  EPI_BIAS = 1,       // C = acc + bias[n]
+  EPI_BIAS_ELU = 2,   // C = elu(acc + bias[n])
+  EPI_ELU_GRAD = 3    // C = acc * elu'(aux[m][n]) from the post-activation
+};
+
+// C[M,N] = op(A)[M,K] * op(B)[K,N] with fp32 FMA on CUDA cores.
+//   trans_a: A is stored [K, M] (lda = its row pitch)
+//   trans_b: B is stored [N, K]
+// split_k > 1 writes partial sums to C + z*ldc*M for z < split_k.
+struct GemmArgs {
+  int M, N, K;
+  const float *A; int lda; bool trans_a;
+  const float *B; int ldb; bool trans_b;
+  float *C; int ldc;
+  int epi;
+  const float *bias;
+  const float *aux; int ldaux;
+  int split_k;
+};
+void gemm_simt(const GemmArgs &g, cudaStream_t s);
+
+}  // namespace zrl
+
+#define ZRL_CUDA_CHECK_LAUNCH() (cudaGetLastError())
