@@ -107,3 +107,65 @@ def tensor_rel(a, b, adims, cdims):
     for (name, x), (_, y) in zip(split_tensors(a, adims, cdims), split_tensors(b, adims, cdims)):
         out[name] = rel(x, y)
     return out
+
+
+def oracle_update_with_drift(case: Case, ocfg, threads=(3, 7)):
+    """Run the oracle update single-threaded (the reference order) and with
+    other thread counts.  The reference reduces per-thread gradients in a
+    rayon-dependent order (ppo.rs:406-462), so its own result moves with the
+    thread count; Adam amplifies such summation-order differences wherever
+    first moments nearly cancel.  Returns (delta params, stats, per-tensor
+    drift = the largest relative change of the delta across thread counts)."""
+    orc = case.oracle_ac()
+    st = orc.update(case.oracle_batch(), ocfg, n_threads=1)
+    dp = orc.params - case.params
+    drift = {}
+    for nt in threads:
+        o2 = case.oracle_ac()
+        o2.update(case.oracle_batch(), ocfg, n_threads=nt)
+        for k, v in tensor_l2(o2.params - case.params, dp, case.adims, case.cdims).items():
+            drift[k] = max(drift.get(k, 0.0), v)
+    return dp, st, orc, drift
+
+
+def tensor_l2(a, b, adims, cdims):
+    out = {}
+    for (name, x), (_, y) in zip(split_tensors(a, adims, cdims), split_tensors(b, adims, cdims)):
+        x = np.asarray(x, np.float64)
+        y = np.asarray(y, np.float64)
+        out[name] = float(np.linalg.norm(x - y) / max(np.linalg.norm(y), 1e-30))
+    return out
+
+
+def assert_update_close(gpu_dp, ref_dp, drift, adims, cdims, l2_floor=1e-2):
+    """Parameter change of a whole update, per tensor.
+
+    Adam's step is lr * m_hat / (sqrt(v_hat) + eps), at t=1 about
+    lr * sign(g): an element whose gradient sits at the rounding-noise floor
+    may step either way in any two implementations (the oracle against
+    itself with another thread count included), so a max-norm is
+    ill-conditioned.  The check is: relative L2 error <= max(l2_floor,
+    3 x the oracle's own thread-count drift), and at most 0.1% of the
+    elements (at least one) differing by more than 5% of the largest step."""
+    l2 = tensor_l2(gpu_dp, ref_dp, adims, cdims)
+    bad = {}
+    for (name, x), (_, y) in zip(split_tensors(gpu_dp, adims, cdims),
+                                 split_tensors(ref_dp, adims, cdims)):
+        lim = max(l2_floor, 3.0 * drift.get(name, 0.0))
+        big = int(np.sum(np.abs(np.asarray(x, np.float64) - y) > 0.05 * np.abs(y).max()))
+        if l2[name] > lim or big > max(1, int(0.001 * y.size)):
+            bad[name] = (l2[name], lim, big, y.size)
+    assert not bad, bad
+
+
+def with_own_rollout_policy(case: Case, gpu_ac, batch):
+    """mean_old/logp_old recomputed by the GPU's own forward, as a GPU
+    rollout would record them (ppo.rs:313-323): the first minibatch's KL is
+    then exactly 0 in both implementations, so the adaptive-LR branch
+    (kl > 0, ppo.rs:479) is taken alike."""
+    from zealot_b200 import synth
+    mean, _ = gpu_ac.forward(case.ro.obs)
+    batch.mean_old = np.ascontiguousarray(mean, np.float32)
+    ls = gpu_ac.log_std
+    batch.logp_old = synth.logp_rows(case.ro.action, mean, ls)
+    return batch

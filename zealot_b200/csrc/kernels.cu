@@ -15,6 +15,14 @@ namespace {
 
 constexpr float kLogSqrt2Pi = 0.9189385f;  // ppo.rs:18
 
+// tf32 with round-to-nearest (ties away): the tensor-core GEMMs then read
+// these operands exactly instead of truncating them.
+__device__ __forceinline__ float rna_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -202,7 +210,7 @@ __global__ void gather_kernel(GatherArgs a) {
         y = __fdiv_rn(__fsub_rn(o[i], a.obs_mean[i]), a.obs_sd[i]);
         y = fminf(fmaxf(y, -5.0f), 5.0f);
       }
-      xo[i] = y;
+      xo[i] = a.round_tf32 ? rna_tf32(y) : y;
     }
     const float *c = a.cobs + r * a.cd;
     float *xc = a.x_c + p * a.cdp;
@@ -212,7 +220,7 @@ __global__ void gather_kernel(GatherArgs a) {
         y = __fdiv_rn(__fsub_rn(c[i], a.crit_mean[i]), a.crit_sd[i]);
         y = fminf(fmaxf(y, -5.0f), 5.0f);
       }
-      xc[i] = y;
+      xc[i] = a.round_tf32 ? rna_tf32(y) : y;
     }
     for (int k = lane; k < a.A; k += 32) {
       a.g_action[p * a.A + k] = a.action[r * a.A + k];
@@ -243,7 +251,7 @@ __global__ void norm_prepare_kernel(const float *m2, float count, int dim,
 
 __global__ void normalize_rows_kernel(const float *x, int64_t n, int dim,
                                       int pitch, const float *mean,
-                                      const float *sd, float *out) {
+                                      const float *sd, float *out, int round) {
   const int64_t total = n * pitch;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
        e += (int64_t)gridDim.x * blockDim.x) {
@@ -254,8 +262,14 @@ __global__ void normalize_rows_kernel(const float *x, int64_t n, int dim,
       y = __fdiv_rn(__fsub_rn(x[r * dim + i], mean[i]), sd[i]);
       y = fminf(fmaxf(y, -5.0f), 5.0f);
     }
-    out[e] = y;
+    out[e] = round ? rna_tf32(y) : y;
   }
+}
+
+__global__ void round_copy_kernel(const float *src, float *dst, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = rna_tf32(src[i]);
 }
 
 // ------------------------------------------------------------ PPO loss
@@ -328,7 +342,7 @@ loss_kernel(LossArgs a, float *partials, unsigned int *ticket) {
         }
         gls[j] += ent_term;
       }
-      if (k < a.Ap) a.d_actor[s * a.Ap + k] = g;
+      if (k < a.Ap) a.d_actor[s * a.Ap + k] = a.round_tf32 ? rna_tf32(g) : g;
     }
     if (lane == 0) {
       acc_surr += surr * a.scale;
@@ -349,7 +363,8 @@ loss_kernel(LossArgs a, float *partials, unsigned int *ticket) {
         dv = 2.0f * eu;
       }
       acc_vloss += vloss * a.scale;
-      a.d_critic[s * a.cp] = a.value_coef * dv * a.scale;
+      const float gv = a.value_coef * dv * a.scale;
+      a.d_critic[s * a.cp] = a.round_tf32 ? rna_tf32(gv) : gv;
     }
   }
   // ---- block partials: warp values into shared memory, summed in order
@@ -559,6 +574,9 @@ __global__ void adam_kernel(AdamArgs a) {
     adam_one(p.z, m.z, v.z, g.z, lr, b1c, b2c, cl);
     adam_one(p.w, m.w, v.w, g.w, lr, b1c, b2c, cl);
     p4[q] = p;
+    if (a.p_round)
+      reinterpret_cast<float4 *>(a.p_round)[q] =
+          make_float4(rna_tf32(p.x), rna_tf32(p.y), rna_tf32(p.z), rna_tf32(p.w));
     m4[q] = m;
     v4[q] = v;
   }
@@ -728,9 +746,13 @@ void launch_norm_prepare(const float *m2, float count, int dim, float *sd,
 
 void launch_normalize_rows(const float *x, int64_t n, int dim, int pitch,
                            const float *mean, const float *sd, float *out,
-                           cudaStream_t s) {
+                           int round_tf32, cudaStream_t s) {
   normalize_rows_kernel<<<grid_for(n * pitch, 256), 256, 0, s>>>(
-      x, n, dim, pitch, mean, sd, out);
+      x, n, dim, pitch, mean, sd, out, round_tf32);
+}
+
+void launch_round_copy(const float *src, float *dst, int64_t n, cudaStream_t s) {
+  round_copy_kernel<<<grid_for(n, 256), 256, 0, s>>>(src, dst, n);
 }
 
 void launch_loss(const LossArgs &a, ReduceScratch &rs, cudaStream_t s) {

@@ -49,6 +49,11 @@ struct zrl_ctx {
   int precision = ZRL_GEMM_TF32;
 
   float *P = nullptr, *G = nullptr, *M = nullptr, *V = nullptr;
+  // tf32 mode: the weights rounded to tf32 (RN), the tensor-core GEMMs'
+  // operand copy; P stays the fp32 master copy (bias reads, Adam)
+  float *Ptc = nullptr;
+  bool tc() const { return precision == ZRL_GEMM_TF32; }
+  const float *Wgemm() const { return tc() ? Ptc : P; }
   float *sums3 = nullptr;   // = G + dev_params
   DevState *st = nullptr;
   DevState *st_host = nullptr;  // pinned
@@ -352,12 +357,15 @@ static zrl_status forward_net(zrl_ctx *ctx, int k, const float *x, int64_t rows)
     g.A = in;
     g.lda = L.dp[l];
     g.trans_a = false;
-    g.B = ctx->P + L.w_off[l];
+    g.B = ctx->Wgemm() + L.w_off[l];
     g.ldb = L.dp[l];
     g.trans_b = true;
     g.C = ctx->act[k][l + 1];
     g.ldc = L.dp[l + 1];
     g.epi = l < L.L - 1 ? EPI_BIAS_ELU : EPI_BIAS;
+    // hidden activations feed later GEMMs: store them tf32-rounded; the
+    // output layer (action mean / value) feeds the loss and stays fp32
+    g.round_out = ctx->tc() && l < L.L - 1;
     g.bias = ctx->P + L.b_off[l];
     g.split_k = 1;
     TRY(run_gemm(ctx, g));
@@ -410,7 +418,8 @@ static zrl_status backward_net(zrl_ctx *ctx, int k, const float *x, int64_t rows
       d.A = ctx->dlt[k][l];
       d.lda = L.dp[l + 1];
       d.trans_a = false;
-      d.B = ctx->P + L.w_off[l];
+      d.B = ctx->Wgemm() + L.w_off[l];
+      d.round_out = ctx->tc();
       d.ldb = L.dp[l];
       d.trans_b = false;
       d.C = ctx->dlt[k][l - 1];
@@ -459,6 +468,7 @@ static zrl_status minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
   la.clip = cfg->clip;
   la.entropy_coef = cfg->entropy_coef;
   la.value_coef = cfg->value_coef;
+  la.round_tf32 = ctx->tc();
   la.d_actor = ctx->dlt[0][La.L - 1];
   la.d_critic = ctx->dlt[1][Lc.L - 1];
   la.g_logstd = ctx->G + ctx->ls_off;
@@ -521,6 +531,7 @@ static zrl_status step(zrl_ctx *ctx, const zrl_ppo_config *cfg, int minibatches,
   a.actor_end = ctx->net[0].dev_end;
   a.critic_end = ctx->net[1].dev_end;
   a.st = ctx->st;
+  a.p_round = ctx->tc() ? ctx->Ptc : nullptr;
   launch_adam(a, ctx->stream);
   ctx->launches++;
   CHECK_LAUNCH();
@@ -597,6 +608,7 @@ static GatherArgs gather_args(zrl_ctx *ctx, const float *obs, const float *cobs,
   g.g_value_old = ctx->e_vo;
   g.g_adv = ctx->e_adv;
   g.g_ret = ctx->e_ret;
+  g.round_tf32 = ctx->tc();
   return g;
 }
 
@@ -726,10 +738,27 @@ static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
   return ZRL_OK;
 }
 
+// A tensor-core pipeline wait that ran out of polls leaves a code in the
+// engine's device flag (1: producer, 2: MMA issuer, 3: epilogue).
+static zrl_status check_device_error(zrl_ctx *ctx) {
+  if (!ctx->gemm.err_dev) return ZRL_OK;
+  int code = 0;
+  CK(cudaMemcpy(&code, ctx->gemm.err_dev, sizeof(int), cudaMemcpyDeviceToHost));
+  if (code != 0) {
+    cudaMemset(ctx->gemm.err_dev, 0, sizeof(int));
+    ctx->err = "tensor-core GEMM pipeline wait timed out (code " + std::to_string(code) + ")";
+    return ZRL_TIMEOUT;
+  }
+  return ZRL_OK;
+}
+
 static zrl_status finish_update(zrl_ctx *ctx, zrl_stats *out) {
   CK(cudaMemcpyAsync(ctx->st_host, ctx->st, sizeof(DevState),
                      cudaMemcpyDeviceToHost, ctx->stream));
+  if (ctx->comm.world > 1)
+    TRY(ctx->comm.wait(ctx->stream, &ctx->err));  // bounded: peers may be gone
   CK(cudaStreamSynchronize(ctx->stream));
+  TRY(check_device_error(ctx));
   ctx->lr_host = ctx->st_host->lr;
   if (ctx->st_host->t[2] != ctx->t_logstd_host) {
     ctx->err = "internal: Adam step counter mismatch";
@@ -830,6 +859,7 @@ zrl_status zrl_create(const zrl_model_config *cfg, int device,
   if ((s = dalloc(ctx, &ctx->G, ctx->grad_len)) != ZRL_OK) return fail(s);
   if ((s = dalloc(ctx, &ctx->M, ctx->dev_params)) != ZRL_OK) return fail(s);
   if ((s = dalloc(ctx, &ctx->V, ctx->dev_params)) != ZRL_OK) return fail(s);
+  if (ctx->tc() && (s = dalloc(ctx, &ctx->Ptc, ctx->dev_params)) != ZRL_OK) return fail(s);
   ctx->sums3 = ctx->G + ctx->dev_params;
   if ((s = dalloc(ctx, &ctx->st, 1)) != ZRL_OK) return fail(s);
   if (cudaMallocHost((void **)&ctx->st_host, sizeof(DevState)) != cudaSuccess)
@@ -883,7 +913,7 @@ zrl_status zrl_destroy(zrl_ctx *ctx) {
                     &ctx->b_vo, &ctx->b_adv, &ctx->b_ret, &ctx->r_rew, &ctx->r_val,
                     &ctx->r_lv, &ctx->e_xa, &ctx->e_xc, &ctx->e_act, &ctx->e_mo,
                     &ctx->e_lpo, &ctx->e_vo, &ctx->e_adv, &ctx->e_ret, &ctx->wpart,
-                    &ctx->bpart, &ctx->rs.fpart};
+                    &ctx->bpart, &ctx->rs.fpart, &ctx->Ptc};
   for (float **b : bufs)
     if (*b) cudaFree(*b);
   for (int k = 0; k < 2; ++k) {
@@ -935,6 +965,11 @@ zrl_status zrl_set_params(zrl_ctx *ctx, const float *flat, int64_t count) {
   flat_to_padded(ctx, flat, pad.data());
   CK(cudaMemcpyAsync(ctx->P, pad.data(), sizeof(float) * ctx->dev_params,
                      cudaMemcpyHostToDevice, ctx->stream));
+  if (ctx->tc()) {
+    launch_round_copy(ctx->P, ctx->Ptc, ctx->dev_params, ctx->stream);
+    ctx->launches++;
+    CHECK_LAUNCH();
+  }
   TRY(reset_adam(ctx));
   CK(cudaStreamSynchronize(ctx->stream));
   return ZRL_OK;
@@ -1246,7 +1281,8 @@ zrl_status zrl_forward(zrl_ctx *ctx, const float *obs, const float *critic_obs,
       }
       float *xn = k == 0 ? ctx->e_xa : ctx->e_xc;
       launch_normalize_rows(x, rows, dim, pitch, k == 0 ? ctx->obs_mean : ctx->crit_mean,
-                            k == 0 ? ctx->obs_sd : ctx->crit_sd, xn, ctx->stream);
+                            k == 0 ? ctx->obs_sd : ctx->crit_sd, xn, ctx->tc(),
+                            ctx->stream);
       ctx->launches++;
       CHECK_LAUNCH();
       TRY(forward_net(ctx, k, xn, rows));
@@ -1385,7 +1421,7 @@ zrl_status zrl_policy_step(zrl_ctx *ctx, const float *obs, const float *critic_o
       x = ctx->b_obs;
     }
     launch_normalize_rows(x, rows, od, odp, ctx->obs_mean, ctx->obs_sd, ctx->e_xa,
-                          ctx->stream);
+                          ctx->tc(), ctx->stream);
     ctx->launches++;
     TRY(forward_net(ctx, 0, ctx->e_xa, rows));
     float *act_d = on_device ? action + r0 * A : ctx->e_act;
@@ -1404,7 +1440,7 @@ zrl_status zrl_policy_step(zrl_ctx *ctx, const float *obs, const float *critic_o
         c = ctx->b_cobs;
       }
       launch_normalize_rows(c, rows, cd, cdp, ctx->crit_mean, ctx->crit_sd, ctx->e_xc,
-                            ctx->stream);
+                            ctx->tc(), ctx->stream);
       ctx->launches++;
       TRY(forward_net(ctx, 1, ctx->e_xc, rows));
       float *v_d = on_device ? value + r0 : ctx->e_vo;

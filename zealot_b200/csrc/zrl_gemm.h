@@ -1,9 +1,9 @@
 // zrl_gemm.h -- GEMM dispatch for the MLP forward/backward.
 //
-// ZRL_GEMM_FP32 runs the CUDA-core kernel (gemm_simt.cu); ZRL_GEMM_TF32 and
-// ZRL_GEMM_BF16 run the tcgen05 tensor-core kernels (gemm_tc.cu).  There is
-// no silent substitution: a shape the tensor-core kernels do not take is an
-// error, not a fallback.
+// ZRL_GEMM_FP32 runs the CUDA-core kernel (gemm_simt.cu); ZRL_GEMM_TF32
+// runs the tcgen05 tensor-core kernels (gemm_tc.cu).  There is no silent
+// substitution: a shape the tensor-core kernel does not take is an error,
+// not a fallback.
 #pragma once
 
 #include <string>
@@ -12,24 +12,25 @@
 
 namespace zrl {
 
-// Tensor-core GEMM (gemm_tc.cu).  Returns the number of kernels launched.
-zrl_status gemm_tc(const GemmArgs &g, int precision, cudaStream_t s,
+struct GemmEngine;
+
+// Tensor-core GEMM (gemm_tc.cu).  *launched receives the kernel count.
+zrl_status gemm_tc(GemmEngine *eng, const GemmArgs &g, int precision, cudaStream_t s,
                    int *launched, std::string *err);
 zrl_status gemm_tc_init(int device, std::string *err);
 
 struct GemmEngine {
   bool tc_ready = false;
-  zrl_status init(int device, std::string *err) {
-    (void)device;
-    (void)err;
-    return ZRL_OK;
-  }
+  void *cache = nullptr;  // tensor-map cache (gemm_tc.cu)
+  int *err_dev = nullptr; // device flag set by a timed-out pipeline wait
+
+  zrl_status init(int device, std::string *err);
+  void destroy();
+
   zrl_status run(const GemmArgs &g, int precision, cudaStream_t s, int *launched,
                  std::string *err) {
-    if (g.M <= 0 || g.N <= 0) {
-      *launched = 0;
-      return ZRL_OK;
-    }
+    *launched = 0;
+    if (g.M <= 0 || g.N <= 0) return ZRL_OK;
     if (precision == ZRL_GEMM_FP32) {
       gemm_simt(g, s);
       *launched = 1;
@@ -40,9 +41,8 @@ struct GemmEngine {
       if (st != ZRL_OK) return st;
       tc_ready = true;
     }
-    return gemm_tc(g, precision, s, launched, err);
+    return gemm_tc(this, g, precision, s, launched, err);
   }
-  void destroy() {}
 };
 
 }  // namespace zrl

@@ -107,6 +107,7 @@ struct GatherArgs {
   float *g_action, *g_mean_old;         // [n_used, A]
   float *g_logp_old, *g_value_old, *g_adv, *g_ret;
   int apply_adv_norm;
+  int round_tf32;       // round the normalized observations to tf32 (RN)
 };
 void launch_gather(const GatherArgs &a, cudaStream_t s);
 // Normalizer divisors: sd = sqrt(max(m2/count, 1e-8)) (ppo.rs:201-202).
@@ -114,7 +115,9 @@ void launch_norm_prepare(const float *m2, float count, int dim, float *sd,
                          cudaStream_t s);
 void launch_normalize_rows(const float *x, int64_t n, int dim, int pitch,
                            const float *mean, const float *sd, float *out,
-                           cudaStream_t s);
+                           int round_tf32, cudaStream_t s);
+// dst = tf32(src) (round to nearest) over n floats.
+void launch_round_copy(const float *src, float *dst, int64_t n, cudaStream_t s);
 
 // PPO losses (ppo.rs:410-452) over one minibatch.
 struct LossArgs {
@@ -132,6 +135,7 @@ struct LossArgs {
   float *d_critic;        // [mb, cp] delta of the critic output layer
   float *g_logstd;        // [A] written (sum over the minibatch)
   float *sums3;           // surr, vloss, kl (sums of scaled terms)
+  int round_tf32;         // round the two output deltas to tf32 (RN)
 };
 void launch_loss(const LossArgs &a, ReduceScratch &rs, cudaStream_t s);
 
@@ -180,6 +184,7 @@ struct AdamArgs {
   int64_t n;
   int64_t actor_end, critic_end;  // [0,actor_end) actor, [.., critic_end) critic, rest log_std
   const DevState *st;
+  float *p_round;  // optional: tf32-rounded copy of p for the tensor-core GEMMs
 };
 void launch_adam(const AdamArgs &a, cudaStream_t s);
 
@@ -219,6 +224,7 @@ struct GemmArgs {
   const float *bias;
   const float *aux; int ldaux;
   int split_k;
+  int round_out;  // tensor-core path: round the outputs to tf32 (RN)
 };
 void gemm_simt(const GemmArgs &g, cudaStream_t s);
 
