@@ -216,6 +216,17 @@ zrl_status zrl_minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
                                const zrl_batch *batch, const int64_t *idx,
                                int64_t n_idx, float *grads_out,
                                float *sums3_out);
+/* One MLP GEMM through the context's GEMM engine (the precision it was
+ * created with), on device pointers, fp32 row-major:
+ *   layout 0: C[M,N] = A[M,K] * B[N,K]^T   (forward:  X W^T)
+ *   layout 1: C[M,N] = A[M,K] * B[K,N]     (dgrad:    Delta W)
+ *   layout 2: C[M,N] = A[K,M]^T * B[K,N]   (wgrad:    Delta^T X)
+ * split_k > 1 writes split_k partial products at C + z*M*ldc.  The
+ * counterpart of the cuTile GEMM self-test (src/biped/cutile_gemm.rs:
+ * 695-828), which checks the same three layouts. */
+zrl_status zrl_gemm(zrl_ctx *ctx, int32_t layout, int32_t M, int32_t N,
+                    int32_t K, const float *A, int32_t lda, const float *B,
+                    int32_t ldb, float *C, int32_t ldc, int32_t split_k);
 /* The stepping half of minibatch_step (ppo.rs:475-489): adaptive LR from
  * kl, per-net gradient clip, Adam for actor and critic, step_log_std. */
 zrl_status zrl_apply_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,

@@ -96,21 +96,31 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// 128B-swizzled shared-memory matrix descriptors (sm_100 format: start
-// address, leading / stride byte offsets in 16-byte units, version 1 at
-// bit 46, layout SWIZZLE_128B = 2 at bits 61-63).
-//  K-major: 8-row x 128-byte atoms stacked along M/N every 1024 bytes.
-//  MN-major: 128 bytes (32 elements) of M/N per row, 8 K-rows per atom;
-//            successive 32-element M/N chunks every `lbo` bytes.
-__device__ __forceinline__ uint64_t desc_sw128(uint32_t addr, uint32_t lbo,
-                                               uint32_t sbo) {
+// Shared-memory matrix descriptors (sm_100 format: start address, leading /
+// stride byte offsets in 16-byte units, version 1 at bit 46, layout type at
+// bits 61-63).
+//  K-major (layout 2, 128-byte swizzle of 16-byte chunks): 8-row x 128-byte
+//    atoms stacked along M/N every 1024 bytes (sbo); lbo unused.
+//  MN-major (layout 1, 128-byte swizzle of 32-byte chunks -- the only
+//    MN-major layout tf32 operands support): 128 bytes (32 elements) of
+//    M/N per K-row, 4 K-rows per atom; K-row groups every 512 bytes (sbo),
+//    32-element M/N chunks every `lbo` bytes.
+__device__ __forceinline__ uint64_t make_desc(uint32_t addr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
   uint64_t d = 0;
   d |= (uint64_t)((addr & 0x3FFFF) >> 4);
   d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
   d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
   d |= 1ull << 46;
-  d |= 2ull << 61;
+  d |= (uint64_t)layout << 61;
   return d;
+}
+constexpr uint32_t kLayoutSw128 = 2, kLayoutSw128Base32 = 1;
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t addr) {
+  return make_desc(addr, 16, 1024, kLayoutSw128);
+}
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t addr) {
+  return make_desc(addr, 4096, 512, kLayoutSw128Base32);
 }
 
 // Instruction descriptor for kind::tf32 with an f32 accumulator.
@@ -172,6 +182,7 @@ struct TcArgs {
   const float *aux;
   int ldaux;
   int round_out;
+  float *colsum;  // optional per-tile column sums [grid.y][N] (no split-K)
   int *err;
 };
 
@@ -263,10 +274,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
       for (int j = 0; j < 4; ++j) {
         // K-major: advance 32 bytes inside the swizzle row; MN-major:
         // advance 8 K-rows = 1024 bytes
-        const uint64_t da = A_MN ? desc_sw128(a_s + 1024 * j, 4096, 1024)
-                                 : desc_sw128(a_s + 32 * j, 16, 1024);
-        const uint64_t db = B_MN ? desc_sw128(b_s + 1024 * j, 4096, 1024)
-                                 : desc_sw128(b_s + 32 * j, 16, 1024);
+        const uint64_t da = A_MN ? desc_mnmajor(a_s + 1024 * j) : desc_kmajor(a_s + 32 * j);
+        const uint64_t db = B_MN ? desc_mnmajor(b_s + 1024 * j) : desc_kmajor(b_s + 32 * j);
         mma_tf32(tmem, da, db, idesc, (kb > 0 || j > 0) ? 1u : 0u);
       }
       mma_commit(&empty[s]);
@@ -290,47 +299,100 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
   tc_fence_after();
   const bool go = __all_sync(0xffffffffu, acc_ok) &&
                   __shfl_sync(0xffffffffu, lane == 0 ? *(volatile int *)g.err : 0, 0) == 0;
+  // column-sum scratch [4 warps][BN] in stage 0 (free: every TMA write has
+  // been consumed by the MMAs that the accumulator barrier waited for)
+  float *red = reinterpret_cast<float *>(smem);
+  const bool row_ok = row < g.M;
   if (go) {
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       uint32_t r[32];
       tmem_ld32(t_row + c * 32, r);  // warp-collective: every lane runs it
       const int n = n0 + c * 32;
-      if (row >= g.M || n >= g.N) continue;
+      if (n >= g.N) continue;        // uniform across the warp
+      const bool full_chunk = n + 32 <= g.N;
       float v[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-      if (EPI == EPI_BIAS || EPI == EPI_BIAS_ELU) {
+      if (row_ok) {
+        if (EPI == EPI_BIAS || EPI == EPI_BIAS_ELU) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] += __ldg(&g.bias[n + i]);
-      }
-      if (EPI == EPI_BIAS_ELU) {
+          for (int i = 0; i < 32; ++i)
+            if (full_chunk || n + i < g.N) v[i] += __ldg(&g.bias[n + i]);
+        }
+        if (EPI == EPI_BIAS_ELU) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = v[i] > 0.0f ? v[i] : expf(v[i]) - 1.0f;
-      }
-      if (EPI == EPI_ELU_GRAD) {
-        const float4 *ap = reinterpret_cast<const float4 *>(g.aux + (int64_t)row * g.ldaux + n);
+          for (int i = 0; i < 32; ++i) v[i] = v[i] > 0.0f ? v[i] : expf(v[i]) - 1.0f;
+        }
+        if (EPI == EPI_ELU_GRAD) {
+          const float *ap = g.aux + (int64_t)row * g.ldaux + n;
+          if (full_chunk) {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float4 y = __ldg(ap + q);
-          v[4 * q + 0] *= y.x > 0.0f ? 1.0f : y.x + 1.0f;
-          v[4 * q + 1] *= y.y > 0.0f ? 1.0f : y.y + 1.0f;
-          v[4 * q + 2] *= y.z > 0.0f ? 1.0f : y.z + 1.0f;
-          v[4 * q + 3] *= y.w > 0.0f ? 1.0f : y.w + 1.0f;
+            for (int q = 0; q < 8; ++q) {
+              const float4 y = __ldg(reinterpret_cast<const float4 *>(ap) + q);
+              v[4 * q + 0] *= y.x > 0.0f ? 1.0f : y.x + 1.0f;
+              v[4 * q + 1] *= y.y > 0.0f ? 1.0f : y.y + 1.0f;
+              v[4 * q + 2] *= y.z > 0.0f ? 1.0f : y.z + 1.0f;
+              v[4 * q + 3] *= y.w > 0.0f ? 1.0f : y.w + 1.0f;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (n + i < g.N) {
+                const float y = __ldg(ap + i);
+                v[i] *= y > 0.0f ? 1.0f : y + 1.0f;
+              }
+          }
         }
       }
+      if (g.colsum) {
+        // per-column sums over this warp's 32 rows, taken before rounding:
+        // a butterfly reduce-scatter (31 shuffles) leaves column c*32+lane
+        // in s[0] of lane `lane`
+        float s[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[i] = (row_ok && (full_chunk || n + i < g.N)) ? v[i] : 0.0f;
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+          const bool upper = (lane & o) != 0;
+#pragma unroll
+          for (int i = 0; i < o; ++i) {
+            const float send = upper ? s[i] : s[i + o];
+            const float keep = upper ? s[i + o] : s[i];
+            s[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+          }
+        }
+        red[warp * BN + c * 32 + lane] = s[0];
+      }
+      if (!row_ok) continue;
       if (g.round_out) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = round_tf32(v[i]);
       }
-      float4 *cp = reinterpret_cast<float4 *>(Cz + (int64_t)row * g.ldc + n);
+      float *cp = Cz + (int64_t)row * g.ldc + n;
+      if (full_chunk) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        cp[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        for (int q = 0; q < 8; ++q)
+          reinterpret_cast<float4 *>(cp)[q] =
+              make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (n + i < g.N) cp[i] = v[i];
+      }
     }
+  } else if (g.colsum) {
+    for (int c = 0; c < BN / 32; ++c) red[warp * BN + c * 32 + lane] = 0.0f;
   }
   tc_fence_before();
   __syncthreads();
+  if (g.colsum && threadIdx.x < BN) {
+    const int n = n0 + threadIdx.x;
+    if (n < g.N)
+      g.colsum[(int64_t)blockIdx.y * g.N + n] =
+          red[threadIdx.x] + red[BN + threadIdx.x] + red[2 * BN + threadIdx.x] +
+          red[3 * BN + threadIdx.x];
+  }
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
@@ -350,15 +412,19 @@ EncodeTiledFn g_encode = nullptr;
 std::mutex g_mu;
 
 // Row-major fp32 matrix [rows, cols] with row pitch ld (elements), read in
-// boxes of [box_rows, 32] with the 128-byte swizzle.
+// boxes of [box_rows, 32].  K-major operands use the 128-byte swizzle of
+// 16-byte chunks; MN-major ones the 128-byte swizzle of 32-byte chunks
+// (the layout the MN-major tf32 descriptor expects).
 bool make_map(CUtensorMap *m, const float *base, int64_t rows, int64_t cols, int64_t ld,
-              int box_rows, std::string *err) {
+              int box_rows, bool mn_major, std::string *err) {
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
   cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw =
+      mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box,
-                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     *err = "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")";
@@ -404,18 +470,18 @@ cudaError_t dispatch_bn(int kind, int epi, const CUtensorMap &ta, const CUtensor
 }  // namespace
 
 struct TcCache {
-  std::map<std::tuple<const void *, int64_t, int64_t, int64_t, int>, CUtensorMap> maps;
+  std::map<std::tuple<const void *, int64_t, int64_t, int64_t, int, bool>, CUtensorMap> maps;
 };
 
 static const CUtensorMap *cached_map(GemmEngine *eng, const float *base, int64_t rows,
-                                     int64_t cols, int64_t ld, int box_rows,
+                                     int64_t cols, int64_t ld, int box_rows, bool mn_major,
                                      std::string *err) {
   TcCache *c = static_cast<TcCache *>(eng->cache);
-  auto key = std::make_tuple((const void *)base, rows, cols, ld, box_rows);
+  auto key = std::make_tuple((const void *)base, rows, cols, ld, box_rows, mn_major);
   auto it = c->maps.find(key);
   if (it != c->maps.end()) return &it->second;
   CUtensorMap m;
-  if (!make_map(&m, base, rows, cols, ld, box_rows, err)) return nullptr;
+  if (!make_map(&m, base, rows, cols, ld, box_rows, mn_major, err)) return nullptr;
   if (c->maps.size() > 4096) c->maps.clear();
   return &(c->maps[key] = m);
 }
@@ -469,9 +535,13 @@ zrl_status gemm_tc(GemmEngine *eng, const GemmArgs &g, int precision, cudaStream
     *err = "unsupported operand layout for the tensor-core GEMM";
     return ZRL_NOT_SUPPORTED;
   }
-  if (g.N % 32 || (kind != 2 && g.K % 32) || g.lda % 4 || g.ldb % 4 || g.ldc % 4 ||
-      (g.aux && g.ldaux % 4)) {
-    *err = "tensor-core GEMM needs N (and K outside wgrad) multiples of 32";
+  // TMA needs 16-byte aligned bases and row pitches; the vector epilogue
+  // needs 16-byte aligned output/aux rows.  Ragged M, N and K are handled
+  // (out-of-range TMA reads are zero-filled, ragged columns are masked).
+  auto a16 = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
+  if (g.lda % 4 || g.ldb % 4 || g.ldc % 4 || (g.aux && g.ldaux % 4) || !a16(g.A) ||
+      !a16(g.B) || !a16(g.C) || (g.aux && !a16(g.aux))) {
+    *err = "tensor-core GEMM needs 16-byte aligned operands and row pitches (multiples of 4)";
     return ZRL_INVALID_ARG;
   }
   if (g.K <= 0) {
@@ -480,11 +550,11 @@ zrl_status gemm_tc(GemmEngine *eng, const GemmArgs &g, int precision, cudaStream
   }
   const int BN = g.N <= 32 ? 32 : (g.N <= 64 ? 64 : 128);
   // A: [M rows, K cols] K-major, or [K rows, M cols] MN-major (wgrad)
-  const CUtensorMap *ta = kind == 2 ? cached_map(eng, g.A, g.K, g.M, g.lda, 32, err)
-                                    : cached_map(eng, g.A, g.M, g.K, g.lda, BM, err);
+  const CUtensorMap *ta = kind == 2 ? cached_map(eng, g.A, g.K, g.M, g.lda, 32, true, err)
+                                    : cached_map(eng, g.A, g.M, g.K, g.lda, BM, false, err);
   // B: [N rows, K cols] K-major (forward) or [K rows, N cols] MN-major
-  const CUtensorMap *tb = kind == 0 ? cached_map(eng, g.B, g.N, g.K, g.ldb, BN, err)
-                                    : cached_map(eng, g.B, g.K, g.N, g.ldb, 32, err);
+  const CUtensorMap *tb = kind == 0 ? cached_map(eng, g.B, g.N, g.K, g.ldb, BN, false, err)
+                                    : cached_map(eng, g.B, g.K, g.N, g.ldb, 32, true, err);
   if (!ta || !tb) return ZRL_CUDA_ERROR;
   int split = g.split_k < 1 ? 1 : g.split_k;
   int kc = (g.K + split - 1) / split;
@@ -501,6 +571,11 @@ zrl_status gemm_tc(GemmEngine *eng, const GemmArgs &g, int precision, cudaStream
   a.aux = g.aux;
   a.ldaux = g.ldaux;
   a.round_out = g.round_out;
+  a.colsum = g.colsum;
+  if (g.colsum && split != 1) {
+    *err = "column sums are taken on unsplit GEMMs only";
+    return ZRL_INVALID_ARG;
+  }
   a.err = eng->err_dev;
   dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, split);
   cudaError_t e;

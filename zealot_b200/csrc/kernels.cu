@@ -288,8 +288,9 @@ loss_kernel(LossArgs a, float *partials, unsigned int *ticket) {
   const int64_t gw = (int64_t)blockIdx.x * nwb + wid;
   const int64_t nw = (int64_t)gridDim.x * nwb;
   const int A = a.A;
-  const int width = A + 3;
-  float ls[4], sd[4], inv_var[4], inv_sd[4], gls[4];
+  // per-block partial row: [g_logstd (A) | db_actor (A) | surr vloss kl | db_critic]
+  const int width = 2 * A + 4;
+  float ls[4], sd[4], inv_var[4], inv_sd[4], gls[4], gmu[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int k = lane + 32 * j;
@@ -298,8 +299,9 @@ loss_kernel(LossArgs a, float *partials, unsigned int *ticket) {
     inv_var[j] = expf(-2.0f * ls[j]);
     inv_sd[j] = expf(-ls[j]);
     gls[j] = 0.0f;
+    gmu[j] = 0.0f;
   }
-  float acc_surr = 0.0f, acc_vloss = 0.0f, acc_kl = 0.0f;
+  float acc_surr = 0.0f, acc_vloss = 0.0f, acc_kl = 0.0f, acc_gv = 0.0f;
   const float lo = 1.0f - a.clip, hi = 1.0f + a.clip;
   const float ent_term = -a.entropy_coef * a.scale;
   for (int64_t s = gw; s < a.mb; s += nw) {
@@ -341,6 +343,7 @@ loss_kernel(LossArgs a, float *partials, unsigned int *ticket) {
           gls[j] += -dls * a.scale;
         }
         gls[j] += ent_term;
+        gmu[j] += g;
       }
       if (k < a.Ap) a.d_actor[s * a.Ap + k] = a.round_tf32 ? rna_tf32(g) : g;
     }
@@ -364,20 +367,25 @@ loss_kernel(LossArgs a, float *partials, unsigned int *ticket) {
       }
       acc_vloss += vloss * a.scale;
       const float gv = a.value_coef * dv * a.scale;
+      acc_gv += gv;
       a.d_critic[s * a.cp] = a.round_tf32 ? rna_tf32(gv) : gv;
     }
   }
   // ---- block partials: warp values into shared memory, summed in order
-  __shared__ float sh[kLossThreads / 32][kLossMaxA + 3];
+  __shared__ float sh[kLossThreads / 32][2 * kLossMaxA + 4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int k = lane + 32 * j;
-    if (k < A) sh[wid][k] = gls[j];
+    if (k < A) {
+      sh[wid][k] = gls[j];
+      sh[wid][A + k] = gmu[j];
+    }
   }
   if (lane == 0) {
-    sh[wid][A] = acc_surr;
-    sh[wid][A + 1] = acc_vloss;
-    sh[wid][A + 2] = acc_kl;
+    sh[wid][2 * A] = acc_surr;
+    sh[wid][2 * A + 1] = acc_vloss;
+    sh[wid][2 * A + 2] = acc_kl;
+    sh[wid][2 * A + 3] = acc_gv;
   }
   __syncthreads();
   for (int c = threadIdx.x; c < width; c += blockDim.x) {
@@ -399,8 +407,12 @@ loss_kernel(LossArgs a, float *partials, unsigned int *ticket) {
       t += __ldcg(&partials[(int64_t)b * width + c]);
     if (c < A)
       a.g_logstd[c] = t;
+    else if (c < 2 * A)
+      a.db_actor[c - A] = t;
+    else if (c < 2 * A + 3)
+      a.sums3[c - 2 * A] = t;
     else
-      a.sums3[c - A] = t;
+      a.db_critic[0] = t;
   }
   if (threadIdx.x == 0) *ticket = 0u;
 }
@@ -757,7 +769,7 @@ void launch_round_copy(const float *src, float *dst, int64_t n, cudaStream_t s) 
 
 void launch_loss(const LossArgs &a, ReduceScratch &rs, cudaStream_t s) {
   int blocks = grid_for(a.mb * 32, kLossThreads, rs.max_blocks);
-  if ((a.A + 3) > rs.fwidth) blocks = 0;  // caller sized fwidth >= A + 3
+  if ((2 * a.A + 4) > rs.fwidth) blocks = 0;  // caller sized fwidth >= 2A + 4
   if (blocks > 0)
     loss_kernel<<<blocks, kLossThreads, 0, s>>>(a, rs.fpart, rs.ticket);
 }

@@ -300,7 +300,9 @@ static zrl_status ensure_mb(zrl_ctx *ctx, int64_t mb) {
     const NetLayout &L = ctx->net[k];
     for (int l = 0; l < L.L; ++l) {
       wp += (int64_t)S * L.dp[l + 1] * L.dp[l];
-      bp += (int64_t)S * L.dp[l + 1];
+      // bias-gradient partials: S row chunks (CUDA-core colsum) or one row
+      // per 128-row tile (tensor-core dgrad epilogue)
+      bp += (int64_t)std::max<int64_t>(S, (mb + 127) / 128) * L.dp[l + 1];
     }
   }
   TRY(dalloc(ctx, &ctx->wpart, wp));
@@ -375,10 +377,15 @@ static zrl_status forward_net(zrl_ctx *ctx, int k, const float *x, int64_t rows)
 }
 
 // Backward of one net (net.rs:113-140 batched): wgrad split-K partials,
-// bias-gradient column sums, dgrad with the ELU' epilogue.
+// bias gradients, dgrad with the ELU' epilogue.  Bias gradients are column
+// sums of the deltas taken in fp32 where each delta is produced: the
+// output layer's in the loss kernel, a hidden layer's in the epilogue of
+// the tensor-core dgrad that produces it (a separate column-sum pass in the
+// CUDA-core mode).
 static zrl_status backward_net(zrl_ctx *ctx, int k, const float *x, int64_t rows,
                                float **wp, float **bp, ReduceSegs &segs) {
   const NetLayout &L = ctx->net[k];
+  const int m_tiles = (int)((rows + 127) / 128);
   for (int l = L.L - 1; l >= 0; --l) {
     const float *a_in = l == 0 ? x : ctx->act[k][l];
     const int S = wsplit_for(rows);
@@ -401,14 +408,16 @@ static zrl_status backward_net(zrl_ctx *ctx, int k, const float *x, int64_t rows
     ReduceSeg sw{ctx->G + L.w_off[l], *wp, (int64_t)L.dp[l + 1] * L.dp[l], S};
     segs.seg[segs.n++] = sw;
     *wp += (int64_t)S * L.dp[l + 1] * L.dp[l];
-    // db_l = column sums of delta_l
-    const int Sb = S;
-    launch_colsum(ctx->dlt[k][l], rows, L.dp[l + 1], L.dp[l + 1], *bp, Sb, ctx->stream);
-    ctx->launches++;
-    CHECK_LAUNCH();
-    ReduceSeg sb{ctx->G + L.b_off[l], *bp, (int64_t)L.dp[l + 1], Sb};
-    segs.seg[segs.n++] = sb;
-    *bp += (int64_t)Sb * L.dp[l + 1];
+    if (l < L.L - 1 && !ctx->tc()) {
+      // db_l = column sums of delta_l (CUDA-core mode)
+      const int Sb = S;
+      launch_colsum(ctx->dlt[k][l], rows, L.dp[l + 1], L.dp[l + 1], *bp, Sb, ctx->stream);
+      ctx->launches++;
+      CHECK_LAUNCH();
+      ReduceSeg sb{ctx->G + L.b_off[l], *bp, (int64_t)L.dp[l + 1], Sb};
+      segs.seg[segs.n++] = sb;
+      *bp += (int64_t)Sb * L.dp[l + 1];
+    }
     if (l > 0) {
       // delta_{l-1} = (delta_l W_l) * elu'(a_l)
       GemmArgs d{};
@@ -428,6 +437,13 @@ static zrl_status backward_net(zrl_ctx *ctx, int k, const float *x, int64_t rows
       d.aux = ctx->act[k][l];
       d.ldaux = L.dp[l];
       d.split_k = 1;
+      if (ctx->tc()) {
+        // db_{l-1}: per-tile column sums of delta_{l-1} from the epilogue
+        d.colsum = *bp;
+        ReduceSeg sb{ctx->G + L.b_off[l - 1], *bp, (int64_t)L.dp[l], m_tiles};
+        segs.seg[segs.n++] = sb;
+        *bp += (int64_t)m_tiles * L.dp[l];
+      }
       TRY(run_gemm(ctx, d));
     }
   }
@@ -473,6 +489,8 @@ static zrl_status minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
   la.d_critic = ctx->dlt[1][Lc.L - 1];
   la.g_logstd = ctx->G + ctx->ls_off;
   la.sums3 = ctx->sums3;
+  la.db_actor = ctx->G + La.b_off[La.L - 1];
+  la.db_critic = ctx->G + Lc.b_off[Lc.L - 1];
   if (v.rows > 0) {
     launch_loss(la, ctx->rs, ctx->stream);
     ctx->launches++;
@@ -874,7 +892,7 @@ zrl_status zrl_create(const zrl_model_config *cfg, int device,
   if ((s = dalloc(ctx, &ctx->crit_sd, cd)) != ZRL_OK) return fail(s);
   if ((s = dalloc(ctx, &ctx->moments, 2)) != ZRL_OK) return fail(s);
   ctx->rs.max_blocks = 148 * 16;
-  ctx->rs.fwidth = 128 + 3;
+  ctx->rs.fwidth = 2 * 128 + 4;  // loss-kernel partial row for A <= 128
   if ((s = dalloc(ctx, &ctx->rs.fpart, (int64_t)ctx->rs.max_blocks * ctx->rs.fwidth)) != ZRL_OK)
     return fail(s);
   if ((s = dalloc(ctx, &ctx->rs.dpart, (int64_t)ctx->rs.max_blocks * 2)) != ZRL_OK)
@@ -1300,7 +1318,33 @@ zrl_status zrl_forward(zrl_ctx *ctx, const float *obs, const float *critic_obs,
     }
   }
   CK(cudaStreamSynchronize(ctx->stream));
-  return ZRL_OK;
+  return check_device_error(ctx);
+}
+
+zrl_status zrl_gemm(zrl_ctx *ctx, int32_t layout, int32_t M, int32_t N, int32_t K,
+                    const float *A, int32_t lda, const float *B, int32_t ldb, float *C,
+                    int32_t ldc, int32_t split_k) {
+  if (!ctx || !A || !B || !C) return ZRL_INVALID_ARG;
+  if (layout < 0 || layout > 2 || M < 0 || N < 0 || K < 0 || split_k < 1 || split_k > 64)
+    return bad(ctx, "invalid GEMM arguments");
+  CK(cudaSetDevice(ctx->device));
+  GemmArgs g{};
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.A = A;
+  g.lda = lda;
+  g.trans_a = layout == 2;
+  g.B = B;
+  g.ldb = ldb;
+  g.trans_b = layout == 0;
+  g.C = C;
+  g.ldc = ldc;
+  g.epi = EPI_STORE;
+  g.split_k = split_k;
+  TRY(run_gemm(ctx, g));
+  CK(cudaStreamSynchronize(ctx->stream));
+  return check_device_error(ctx);
 }
 
 zrl_status zrl_minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
@@ -1333,6 +1377,7 @@ zrl_status zrl_minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
   CK(cudaMemcpyAsync(pad.data(), ctx->G, sizeof(float) * ctx->grad_len,
                      cudaMemcpyDeviceToHost, ctx->stream));
   CK(cudaStreamSynchronize(ctx->stream));
+  TRY(check_device_error(ctx));
   padded_to_flat(ctx, pad.data(), grads_out);
   if (sums3_out) memcpy(sums3_out, pad.data() + ctx->dev_params, sizeof(float) * 3);
   return ZRL_OK;
@@ -1464,7 +1509,7 @@ zrl_status zrl_policy_step(zrl_ctx *ctx, const float *obs, const float *critic_o
     // keep the staging buffers alive until the copies drain
     CK(cudaStreamSynchronize(ctx->stream));
   }
-  return ZRL_OK;
+  return check_device_error(ctx);
 }
 
 // ---------------------------------------------------------------- I/O

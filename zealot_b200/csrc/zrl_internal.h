@@ -135,6 +135,9 @@ struct LossArgs {
   float *d_critic;        // [mb, cp] delta of the critic output layer
   float *g_logstd;        // [A] written (sum over the minibatch)
   float *sums3;           // surr, vloss, kl (sums of scaled terms)
+  // output-layer bias gradients = column sums of the two deltas, taken in
+  // fp32 before any rounding: db_actor [A], db_critic [1]
+  float *db_actor, *db_critic;
   int round_tf32;         // round the two output deltas to tf32 (RN)
 };
 void launch_loss(const LossArgs &a, ReduceScratch &rs, cudaStream_t s);
@@ -225,6 +228,9 @@ struct GemmArgs {
   const float *aux; int ldaux;
   int split_k;
   int round_out;  // tensor-core path: round the outputs to tf32 (RN)
+  // tensor-core dgrad: column sums of the (unrounded) outputs, one row of N
+  // partials per 128-row tile: colsum[tile_m * N + n]
+  float *colsum;
 };
 void gemm_simt(const GemmArgs &g, cudaStream_t s);
 

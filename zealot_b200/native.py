@@ -103,6 +103,8 @@ _SIGS = {
     "zrl_minibatch_grads": (C.c_int, [_P, C.POINTER(PpoConfigC), C.POINTER(BatchC), _P,
                                       C.c_int64, _P, _P]),
     "zrl_apply_grads": (C.c_int, [_P, C.POINTER(PpoConfigC), _P, C.c_float]),
+    "zrl_gemm": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, C.c_int32,
+                           _P, C.c_int32, _P, C.c_int32, C.c_int32]),
     "zrl_save": (C.c_int, [_P, C.c_char_p]),
     "zrl_load": (C.c_int, [_P, C.c_char_p]),
     "zrl_load_from_bytes": (C.c_int, [_P, _P, C.c_size_t]),
