@@ -347,15 +347,18 @@ class ActorCritic:
         return act, lp, mean, val
 
     # -- training --------------------------------------------------------
-    def update(self, batch, cfg: PpoConfig, n_global=0, row_offset=0) -> PpoStats:
+    def update(self, batch, cfg: PpoConfig, n_global=0, row_offset=0,
+               write_back_adv=False) -> PpoStats:
         """ActorCritic::update (ppo.rs:338-384).  A list of Samples has its
-        advantages normalized in place, as in the reference."""
+        advantages normalized in place, as in the reference; a SoaBatch
+        does when write_back_adv is set."""
         samples = None
         if isinstance(batch, (list, tuple)):
             samples = batch
             batch = SoaBatch.from_samples(batch)
         st = N.StatsC()
-        bc = batch.c(n_global, row_offset, write_back_adv=samples is not None)
+        bc = batch.c(n_global, row_offset,
+                     write_back_adv=samples is not None or write_back_adv)
         cc = cfg.c()
         self.ctx.call("zrl_update", C.byref(cc), C.byref(bc), C.byref(st))
         if samples is not None:
