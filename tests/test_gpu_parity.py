@@ -187,10 +187,14 @@ def test_update_c1_matches_oracle_tf32(adaptive):
     g_ref, _ = case.oracle_ac().minibatch_grads(ob, idx, ocfg, n_threads=8)
     errs = tensor_rel(g, g_ref, case.adims, case.cdims)
     assert max(errs.values()) < 2e-3, errs
-    # 3. the oracle's step on that gradient
+    # 3. the oracle's step on that gradient: Adam's outputs (the parameters)
+    # within 1e-5; the step itself within 1e-4 (the clip norm is summed in
+    # another order, so the new parameters may differ by an ulp or two,
+    # ~1e-5 of a 1e-3 step)
     o3 = case.oracle_ac()
     o3.apply(ocfg, g, 0.0)
-    assert rel(gpu.params - case.params, o3.params - case.params) < 1e-5
+    assert rel(gpu.params, o3.params) < 1e-5
+    assert rel(gpu.params - case.params, o3.params - case.params) < 1e-4
 
 
 def test_update_tf32_multi_epoch_stats():

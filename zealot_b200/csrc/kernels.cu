@@ -768,7 +768,9 @@ void launch_round_copy(const float *src, float *dst, int64_t n, cudaStream_t s) 
 }
 
 void launch_loss(const LossArgs &a, ReduceScratch &rs, cudaStream_t s) {
-  int blocks = grid_for(a.mb * 32, kLossThreads, rs.max_blocks);
+  // two blocks per SM, each warp looping over samples: the last block's
+  // ordered sum of the block partials then stays short
+  int blocks = grid_for(a.mb * 32, kLossThreads, 2 * 148);
   if ((2 * a.A + 4) > rs.fwidth) blocks = 0;  // caller sized fwidth >= 2A + 4
   if (blocks > 0)
     loss_kernel<<<blocks, kLossThreads, 0, s>>>(a, rs.fpart, rs.ticket);
@@ -783,7 +785,8 @@ void launch_colsum(const float *x, int64_t rows, int cols, int ld,
 void launch_reduce_segments(const ReduceSegs &segs, cudaStream_t s) {
   int64_t mx = 0;
   for (int i = 0; i < segs.n; ++i) mx = segs.seg[i].count > mx ? segs.seg[i].count : mx;
-  dim3 grid(grid_for(mx, 256, 64), segs.n);
+  // enough blocks that the largest segment gets one element per thread
+  dim3 grid(grid_for(mx, 256, 4096), segs.n);
   reduce_segments_kernel<<<grid, 256, 0, s>>>(segs);
 }
 
