@@ -105,6 +105,8 @@ _SIGS = {
     "zrl_apply_grads": (C.c_int, [_P, C.POINTER(PpoConfigC), _P, C.c_float]),
     "zrl_gemm": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, C.c_int32,
                            _P, C.c_int32, _P, C.c_int32, C.c_int32]),
+    "zrl_gae_normalize_noalloc": (C.c_int, [_P, _P, _P, _P, C.c_int64, C.c_int64,
+                                            C.c_float, C.c_float, _P, _P, _P, _P]),
     "zrl_save": (C.c_int, [_P, C.c_char_p]),
     "zrl_load": (C.c_int, [_P, C.c_char_p]),
     "zrl_load_from_bytes": (C.c_int, [_P, _P, C.c_size_t]),
