@@ -43,7 +43,10 @@ constexpr int BM = 128;          // UMMA M (cta_group::1)
 constexpr int BKB = 128;         // bytes of K per k-block (one swizzle row)
 constexpr int kEpiWarps = 8;  // two per TMEM lane quarter
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr uint32_t kWaitLimit = 1u << 26;  // try_wait polls before giving up
+// a second bound on a wait, on the number of polls, should the global timer
+// not advance; the wall-time bound (kWaitNs) is the one that normally ends
+// a wait that never completes
+constexpr uint32_t kWaitLimit = 1u << 24;
 
 // ------------------------------------------------------------ PTX helpers
 
@@ -65,11 +68,29 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *b) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
 
+// try_wait with a suspend-time hint: a waiting thread sleeps until the
+// phase completes (or ~1 ms passes) instead of spinning and taking issue
+// slots from the producer / MMA threads.
+constexpr uint32_t kSuspendNs = 1000000;
 __device__ __forceinline__ bool mbar_try(uint64_t *b, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+
+// Non-blocking probe: the single-thread producer and MMA roles spin on it
+// (a suspended try_wait wakes up too late for a per-k-block handshake).
+__device__ __forceinline__ bool mbar_test(uint64_t *b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(smem_u32(b)), "r"(parity)
@@ -77,12 +98,35 @@ __device__ __forceinline__ bool mbar_try(uint64_t *b, uint32_t parity) {
   return ok != 0;
 }
 
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 // Bounded wait: true when the phase completed, false (and *err set) when
-// the poll budget ran out.
+// kWaitNs of wall time passed without it (however long each poll slept).
+constexpr uint64_t kWaitNs = 20ull * 1000 * 1000 * 1000;
 __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, int *err,
                                           int code) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i)
+  if (mbar_try(b, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
     if (mbar_try(b, parity)) return true;
+    if (global_ns() - t0 > kWaitNs) break;
+  }
+  atomicExch(err, code);
+  return false;
+}
+
+// Bounded spin for the latency-critical single-thread roles.
+__device__ __forceinline__ bool mbar_spin(uint64_t *b, uint32_t parity, int *err, int code) {
+  if (mbar_test(b, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_test(b, parity)) return true;
+    if ((i & 255) == 255 && global_ns() - t0 > kWaitNs) break;
+  }
   atomicExch(err, code);
   return false;
 }
@@ -215,6 +259,14 @@ __device__ __forceinline__ float round_tf32(float x) {
   return __uint_as_float(r);
 }
 
+// e^x = 2^(x log2 e) with one ex2.approx: relative error about 2^-22 plus
+// |x| 2^-24 from rounding the product; 0 below x = -87 (flush to zero)
+__device__ __forceinline__ float exp_sfu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.44269504088896341f));
+  return y;
+}
+
 struct TcArgs {
   int M, N, K;
   int kc;          // K per split (multiple of 32); split z covers [z*kc, ...)
@@ -233,7 +285,7 @@ struct Smem {
   static constexpr int kB = BN * BKB;                 // BN * 128 B
   static constexpr int kStage = kA + kB;
   static constexpr int kStageBytes = STAGES * kStage;
-  static constexpr int kStaging = kEpiWarps * 2 * 4096;  // 2 x [32 x 32] fp32 per warp
+  static constexpr int kStaging = kEpiWarps * 4096;  // one [32 x 32] fp32 chunk per warp
   static constexpr int kRed = 4 * BN * 4;             // column sums per lane quarter
   static constexpr int kBarOff = kStageBytes + kStaging + kRed;
   static constexpr int kBars = 2 * STAGES + 4;        // full, empty, acc_full x2, acc_empty x2
@@ -319,7 +371,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
         for (int kb = 0; kb < tl.nk; ++kb, ++kbg) {
           const int s = kbg % STAGES;
           const uint32_t ph = (uint32_t)(kbg / STAGES) & 1u;
-          if (kbg >= STAGES && !(ok = mbar_wait(&empty[s], ph ^ 1u, g.err, 1))) break;
+          if (kbg >= STAGES && !(ok = mbar_spin(&empty[s], ph ^ 1u, g.err, 1))) break;
           uint8_t *a_s = smem + s * S::kStage;
           uint8_t *b_s = a_s + S::kA;
           const int k0 = tl.kbeg + kb * 32;
@@ -352,13 +404,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
         const int ab = it & 1;
         const uint32_t aph = (uint32_t)(it >> 1) & 1u;
         // the epilogue must have drained this accumulator (tile it-2)
-        if (it >= 2 && !(ok = mbar_wait(&acce[ab], aph ^ 1u, g.err, 4))) break;
+        if (it >= 2 && !(ok = mbar_spin(&acce[ab], aph ^ 1u, g.err, 4))) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(ab * BN);
         for (int kb = 0; kb < tl.nk; ++kb, ++kbg) {
           const int s = kbg % STAGES;
           const uint32_t ph = (uint32_t)(kbg / STAGES) & 1u;
-          if (!(ok = mbar_wait(&full[s], ph, g.err, 2))) break;
+          if (!(ok = mbar_spin(&full[s], ph, g.err, 2))) break;
           tc_fence_after();
           const uint32_t a_s = smem_u32(smem + s * S::kStage);
           const uint32_t b_s = a_s + S::kA;
@@ -384,8 +436,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
     const int ew = warp - 2;       // 0..kEpiWarps-1
     const int quarter = warp & 3;  // TMEM lane quarter = rows of this warp
     const int half = ew >> 2;      // chunks c with c % 2 == half
-    float *stg = (float *)(smem + S::kStageBytes + ew * 8192);  // 2 x 4 KB
-    int sbuf = 0, it = 0;
+    float *buf = (float *)(smem + S::kStageBytes + ew * 4096);  // this warp's staging chunk
+    int it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
       const Tile tl = decode_tile<BN>(t, tiles_m, tiles_n, g);
@@ -429,10 +481,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
             }
           }
           if (EPI == EPI_BIAS_ELU) {
-            // ELU (net.rs:13-16) with the fast exponential: its error
-            // (a few ulp) is far below the tf32 rounding applied next
+            // ELU (net.rs:13-16); exp on the special-function unit, whose
+            // error is far below the tf32 rounding applied next
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = v[i] > 0.0f ? v[i] : __expf(v[i]) - 1.0f;
+            for (int i = 0; i < 32; ++i) v[i] = v[i] > 0.0f ? v[i] : exp_sfu(v[i]) - 1.0f;
           }
           if (EPI == EPI_ELU_GRAD && row_ok) {
             const float4 *ap =
@@ -459,7 +511,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
               x = 0.0f;
             } else {
               if (EPI == EPI_BIAS || EPI == EPI_BIAS_ELU) x += __ldg(&g.bias[n + i]);
-              if (EPI == EPI_BIAS_ELU) x = x > 0.0f ? x : __expf(x) - 1.0f;
+              if (EPI == EPI_BIAS_ELU) x = x > 0.0f ? x : exp_sfu(x) - 1.0f;
               if (EPI == EPI_ELU_GRAD) {
                 const float y = __ldg(&g.aux[(int64_t)row * g.ldaux + n + i]);
                 x *= y > 0.0f ? 1.0f : y + 1.0f;
@@ -468,46 +520,45 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
             v[i] = x;
           }
         }
-        if (g.colsum) {
-          // per-column sums over this warp's 32 rows before rounding: a
-          // butterfly reduce-scatter (31 shuffles) leaves column c*32+lane
-          // in s[0] of lane `lane` (invalid rows/columns hold 0 here)
-          float s[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) s[i] = v[i];
-#pragma unroll
-          for (int o = 16; o >= 1; o >>= 1) {
-            const bool upper = (lane & o) != 0;
-#pragma unroll
-            for (int i = 0; i < o; ++i) {
-              const float send = upper ? s[i] : s[i + o];
-              const float keep = upper ? s[i + o] : s[i];
-              s[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-            }
-          }
-          red[quarter * BN + c * 32 + lane] = s[0];
-        }
-        if (g.round_out) {
+        // stage the 32 x 32 chunk in the 128B-swizzled layout (16-byte
+        // chunk q of row r at position q ^ (r & 7): conflict-free) for one
+        // TMA store; the store clips rows >= M and columns >= N
+        if (lane == 0) bulk_wait_read<0>();  // the previous store has read buf
+        __syncwarp();
+        float4 *rowp = reinterpret_cast<float4 *>(buf + lane * 32);
+        const bool cs = g.colsum != nullptr;
+        if (g.round_out && !cs) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = round_tf32(v[i]);
         }
-        // stage the 32 x 32 chunk in the 128B-swizzled layout (16-byte
-        // chunk q of row r at position q ^ (r & 7): conflict-free) and let
-        // one TMA store write it; the store clips rows >= M and columns >= N
-        float *buf = stg + sbuf * 1024;
-        if (lane == 0) bulk_wait_read<1>();  // the store that last used buf has read it
-        __syncwarp();
-        float4 *rowp = reinterpret_cast<float4 *>(buf + lane * 32);
 #pragma unroll
         for (int q = 0; q < 8; ++q)
           rowp[q ^ (lane & 7)] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        if (cs) {
+          // bias gradient: column sums of the unrounded chunk (invalid rows
+          // and columns hold 0), lane j summing column j over the 32 rows in
+          // row order (conflict-free reads of the swizzled rows)
+          __syncwarp();
+          float sum = 0.0f;
+#pragma unroll 8
+          for (int r = 0; r < 32; ++r)
+            sum += buf[r * 32 + ((((lane >> 2) ^ (r & 7)) << 2) | (lane & 3))];
+          red[quarter * BN + c * 32 + lane] = sum;
+          if (g.round_out) {
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              rowp[q ^ (lane & 7)] =
+                  make_float4(round_tf32(v[4 * q]), round_tf32(v[4 * q + 1]),
+                              round_tf32(v[4 * q + 2]), round_tf32(v[4 * q + 3]));
+          }
+        }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0 && row0 < g.M) {
           tma_store_3d(&tmC, buf, n, row0, tl.z);
           bulk_commit();
         }
-        sbuf ^= 1;
       }
       // accumulator drained: let the MMA warp reuse it
       tc_fence_before();
@@ -610,7 +661,8 @@ template <int BN>
 cudaError_t dispatch_bn(int kind, int epi, const CUtensorMap &ta, const CUtensorMap &tb,
                         const CUtensorMap &tc, const TcArgs &a, int tiles, cudaStream_t s) {
   // the deepest stage ring that fits next to the epilogue staging buffers
-  constexpr int ST = BN >= 256 ? 3 : 4;
+  // (more k-blocks in flight hide the TMA -> MMA -> release round trip)
+  constexpr int ST = BN >= 256 ? 3 : (BN >= 128 ? 5 : 6);
   if (kind == 0) {  // forward
     if (epi == EPI_BIAS_ELU)
       return launch_one<BN, false, false, EPI_BIAS_ELU, ST>(ta, tb, tc, a, tiles, s);

@@ -200,39 +200,51 @@ __global__ void gather_kernel(GatherArgs a) {
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const float am = a.st->adv_mean, asd = a.st->adv_sd;
+  const int qa = a.odp / 4, qc = a.cdp / 4;  // float4 per padded row
   for (int64_t p = warp; p < a.n_used; p += nwarps) {
     const int64_t r = a.order[p];
-    const float *o = a.obs + r * a.od;
-    float *xo = a.x_a + p * a.odp;
-    for (int i = lane; i < a.odp; i += 32) {
-      float y = 0.0f;
-      if (i < a.od) {
-        y = __fdiv_rn(__fsub_rn(o[i], a.obs_mean[i]), a.obs_sd[i]);
-        y = fminf(fmaxf(y, -5.0f), 5.0f);
+    const float4 *xa = reinterpret_cast<const float4 *>(a.xn_a) + r * qa;
+    const float4 *xc = reinterpret_cast<const float4 *>(a.xn_c) + r * qc;
+    float4 *ya = reinterpret_cast<float4 *>(a.x_a) + p * qa;
+    float4 *yc = reinterpret_cast<float4 *>(a.x_c) + p * qc;
+    if (qa <= 32 && qc <= 32 && a.A <= 32) {
+      // every load of the row first, then every store
+      float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vc = va;
+      float act = 0.0f, mo = 0.0f, scal = 0.0f;
+      if (lane < qa) va = xa[lane];
+      if (lane < qc) vc = xc[lane];
+      if (lane < a.A) {
+        act = a.action[r * a.A + lane];
+        mo = a.mean_old[r * a.A + lane];
       }
-      xo[i] = a.round_tf32 ? rna_tf32(y) : y;
-    }
-    const float *c = a.cobs + r * a.cd;
-    float *xc = a.x_c + p * a.cdp;
-    for (int i = lane; i < a.cdp; i += 32) {
-      float y = 0.0f;
-      if (i < a.cd) {
-        y = __fdiv_rn(__fsub_rn(c[i], a.crit_mean[i]), a.crit_sd[i]);
-        y = fminf(fmaxf(y, -5.0f), 5.0f);
+      if (lane == 0) scal = a.logp_old[r];
+      else if (lane == 1) scal = a.value_old[r];
+      else if (lane == 2) scal = a.adv[r];
+      else if (lane == 3) scal = a.ret[r];
+      if (lane < qa) ya[lane] = va;
+      if (lane < qc) yc[lane] = vc;
+      if (lane < a.A) {
+        a.g_action[p * a.A + lane] = act;
+        a.g_mean_old[p * a.A + lane] = mo;
       }
-      xc[i] = a.round_tf32 ? rna_tf32(y) : y;
-    }
-    for (int k = lane; k < a.A; k += 32) {
-      a.g_action[p * a.A + k] = a.action[r * a.A + k];
-      a.g_mean_old[p * a.A + k] = a.mean_old[r * a.A + k];
-    }
-    if (lane == 0) {
-      a.g_logp_old[p] = a.logp_old[r];
-      a.g_value_old[p] = a.value_old[r];
-      float ad = a.adv[r];
-      if (a.apply_adv_norm) ad = __fdiv_rn(__fsub_rn(ad, am), asd);
-      a.g_adv[p] = ad;
-      a.g_ret[p] = a.ret[r];
+      if (lane == 0) a.g_logp_old[p] = scal;
+      else if (lane == 1) a.g_value_old[p] = scal;
+      else if (lane == 2) a.g_adv[p] = a.apply_adv_norm ? __fdiv_rn(__fsub_rn(scal, am), asd) : scal;
+      else if (lane == 3) a.g_ret[p] = scal;
+    } else {
+      for (int i = lane; i < qa; i += 32) ya[i] = xa[i];
+      for (int i = lane; i < qc; i += 32) yc[i] = xc[i];
+      for (int k = lane; k < a.A; k += 32) {
+        a.g_action[p * a.A + k] = a.action[r * a.A + k];
+        a.g_mean_old[p * a.A + k] = a.mean_old[r * a.A + k];
+      }
+      if (lane == 0) {
+        a.g_logp_old[p] = a.logp_old[r];
+        a.g_value_old[p] = a.value_old[r];
+        const float ad = a.adv[r];
+        a.g_adv[p] = a.apply_adv_norm ? __fdiv_rn(__fsub_rn(ad, am), asd) : ad;
+        a.g_ret[p] = a.ret[r];
+      }
     }
   }
 }
@@ -308,6 +320,14 @@ loss_kernel(LossArgs a, float *partials, unsigned int *ticket) {
     const float *mu = a.mean + s * a.Ap;
     const float *ac = a.action + s * A;
     const float *mo = a.mean_old + s * A;
+    // the five per-sample scalars, one per lane, loaded together with the
+    // action rows below (one memory round trip per sample)
+    float scal = 0.0f;
+    if (lane == 0) scal = a.logp_old[s];
+    else if (lane == 1) scal = a.adv[s];
+    else if (lane == 2) scal = a.value[s * a.cp];
+    else if (lane == 3) scal = a.value_old[s];
+    else if (lane == 4) scal = a.ret[s];
     float mu_r[4], d_r[4];
     float lp = 0.0f, kl = 0.0f;
 #pragma unroll
@@ -326,8 +346,11 @@ loss_kernel(LossArgs a, float *partials, unsigned int *ticket) {
     }
     lp = warp_sum(lp);
     kl = warp_sum(kl);
-    const float ratio = expf(lp - a.logp_old[s]);
-    const float adv = a.adv[s];
+    const float ratio = expf(lp - __shfl_sync(0xffffffffu, scal, 0));
+    const float adv = __shfl_sync(0xffffffffu, scal, 1);
+    const float v = __shfl_sync(0xffffffffu, scal, 2);
+    const float vo = __shfl_sync(0xffffffffu, scal, 3);
+    const float R = __shfl_sync(0xffffffffu, scal, 4);
     const float rc = fminf(fmaxf(ratio, lo), hi);
     const float surr = fminf(ratio * adv, rc * adv);
     const bool clipped = (adv >= 0.0f && ratio > hi) || (adv < 0.0f && ratio < lo);
@@ -351,9 +374,6 @@ loss_kernel(LossArgs a, float *partials, unsigned int *ticket) {
       acc_surr += surr * a.scale;
       acc_kl += kl * a.scale;
       // clipped value loss, ppo.rs:439-449
-      const float v = a.value[s * a.cp];
-      const float vo = a.value_old[s];
-      const float R = a.ret[s];
       const float vc = vo + fminf(fmaxf(v - vo, -a.clip), a.clip);
       const float eu = v - R, ec = vc - R;
       const float lu = eu * eu, lc = ec * ec;
@@ -401,10 +421,14 @@ loss_kernel(LossArgs a, float *partials, unsigned int *ticket) {
   __syncthreads();
   if (!last) return;
   __threadfence();
-  for (int c = threadIdx.x; c < width; c += blockDim.x) {
+  // one warp per column: lanes take strided block partials (independent
+  // loads), then a fixed-order warp sum -- deterministic and short
+  for (int c = wid; c < width; c += nwb) {
     float t = 0.0f;
-    for (int b = 0; b < (int)gridDim.x; ++b)
+    for (int b = lane; b < (int)gridDim.x; b += 32)
       t += __ldcg(&partials[(int64_t)b * width + c]);
+    t = warp_sum(t);
+    if (lane != 0) continue;
     if (c < A)
       a.g_logstd[c] = t;
     else if (c < 2 * A)
@@ -433,13 +457,58 @@ __global__ void colsum_kernel(const float *x, int64_t rows, int cols, int ld,
 
 // ------------------------------------------------------ segment reduce
 
-__global__ void reduce_segments_kernel(ReduceSegs segs) {
-  const ReduceSeg sg = segs.seg[blockIdx.y];
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < sg.count;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    float s = 0.0f;
-    for (int z = 0; z < sg.splits; ++z) s += sg.src[(int64_t)z * sg.count + i];
-    sg.dst[i] = s;
+// One block per (segment, 128-float column block).  The block's eight
+// warps are eight split groups: warp j sums splits j, j+8, j+16, ... of its
+// 32 float4 columns in split order (each load a coalesced 512-byte row
+// piece, several in flight), and warp 0 then adds the eight group sums in
+// group order -- a fixed order, so every run gives the same bits.  Every
+// segment count is a multiple of 4 floats and every pointer 16-byte
+// aligned (the padded layout guarantees both).
+constexpr int kRsCols4 = 32, kRsGroups = 8;
+
+__device__ __forceinline__ int64_t rs_blocks(int64_t count) {
+  return (count / 4 + kRsCols4 - 1) / kRsCols4;
+}
+
+__global__ void __launch_bounds__(kRsCols4 * kRsGroups)
+reduce_segments_kernel(ReduceSegs segs) {
+  int si = 0;
+  int64_t b = blockIdx.x;
+  while (si + 1 < segs.n && b >= rs_blocks(segs.seg[si].count)) {
+    b -= rs_blocks(segs.seg[si].count);
+    ++si;
+  }
+  const ReduceSeg &sg = segs.seg[si];
+  const int c = threadIdx.x & 31, grp = threadIdx.x >> 5;
+  const int64_t stride4 = sg.count / 4;
+  const int64_t i4 = b * kRsCols4 + c;
+  const bool live = i4 < stride4;
+  const float4 *src = reinterpret_cast<const float4 *>(sg.src) + i4;
+  float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  if (live) {
+#pragma unroll 4
+    for (int z = grp; z < sg.splits; z += kRsGroups) {
+      const float4 x = __ldcs(src + (int64_t)z * stride4);  // read once: streaming
+      t.x += x.x;
+      t.y += x.y;
+      t.z += x.z;
+      t.w += x.w;
+    }
+  }
+  __shared__ float4 part[kRsGroups][kRsCols4];
+  part[grp][c] = t;
+  __syncthreads();
+  if (grp == 0 && live) {
+    float4 s = part[0][c];
+#pragma unroll
+    for (int j = 1; j < kRsGroups; ++j) {
+      const float4 x = part[j][c];
+      s.x += x.x;
+      s.y += x.y;
+      s.z += x.z;
+      s.w += x.w;
+    }
+    reinterpret_cast<float4 *>(sg.dst)[i4] = s;
   }
 }
 
@@ -464,11 +533,13 @@ __global__ void __launch_bounds__(kPrestepThreads)
 prestep_kernel(PrestepArgs a, double *partials, unsigned int *ticket) {
   double sa = 0.0, sc = 0.0;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+#pragma unroll 4
   for (int64_t i = a.actor_begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
        i < a.actor_end; i += stride) {
     const double g = a.grads[i];
     sa += g * g;
   }
+#pragma unroll 4
   for (int64_t i = a.critic_begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
        i < a.critic_end; i += stride) {
     const double g = a.grads[i];
@@ -486,13 +557,17 @@ prestep_kernel(PrestepArgs a, double *partials, unsigned int *ticket) {
   __syncthreads();
   if (threadIdx.x == 0) last = atomicAdd(ticket, 1u) == gridDim.x - 1;
   __syncthreads();
-  if (!last || threadIdx.x != 0) return;
+  if (!last || threadIdx.x >= 32) return;
   __threadfence();
+  // warp 0: lanes take strided block partials, fixed-order warp sum
   double na = 0.0, nc = 0.0;
-  for (int b = 0; b < (int)gridDim.x; ++b) {
+  for (int b = threadIdx.x; b < (int)gridDim.x; b += 32) {
     na += __ldcg(&partials[2 * b]);
     nc += __ldcg(&partials[2 * b + 1]);
   }
+  na = warp_sum_d(na);
+  nc = warp_sum_d(nc);
+  if (threadIdx.x != 0) return;
   *ticket = 0u;
   DevState *st = a.st;
   st->sumsq[0] = (float)na;
@@ -768,9 +843,11 @@ void launch_round_copy(const float *src, float *dst, int64_t n, cudaStream_t s) 
 }
 
 void launch_loss(const LossArgs &a, ReduceScratch &rs, cudaStream_t s) {
-  // two blocks per SM, each warp looping over samples: the last block's
-  // ordered sum of the block partials then stays short
-  int blocks = grid_for(a.mb * 32, kLossThreads, 2 * 148);
+  // four blocks per SM, a few samples per warp (latency-bound per
+  // sample); the last block's ordered sum over the block partials is one
+  // warp per column with strided loads
+  int blocks = grid_for(a.mb * 32, kLossThreads, 4 * 148);
+  if (blocks > rs.max_blocks) blocks = rs.max_blocks;
   if ((2 * a.A + 4) > rs.fwidth) blocks = 0;  // caller sized fwidth >= 2A + 4
   if (blocks > 0)
     loss_kernel<<<blocks, kLossThreads, 0, s>>>(a, rs.fpart, rs.ticket);
@@ -783,16 +860,15 @@ void launch_colsum(const float *x, int64_t rows, int cols, int ld,
 }
 
 void launch_reduce_segments(const ReduceSegs &segs, cudaStream_t s) {
-  int64_t mx = 0;
-  for (int i = 0; i < segs.n; ++i) mx = segs.seg[i].count > mx ? segs.seg[i].count : mx;
-  // enough blocks that the largest segment gets one element per thread
-  dim3 grid(grid_for(mx, 256, 4096), segs.n);
-  reduce_segments_kernel<<<grid, 256, 0, s>>>(segs);
+  int64_t blocks = 0;
+  for (int i = 0; i < segs.n; ++i) blocks += (segs.seg[i].count / 4 + kRsCols4 - 1) / kRsCols4;
+  if (blocks == 0) return;
+  reduce_segments_kernel<<<(unsigned)blocks, kRsCols4 * kRsGroups, 0, s>>>(segs);
 }
 
 void launch_prestep(const PrestepArgs &a, ReduceScratch &rs, cudaStream_t s) {
   const int64_t work = (a.actor_end - a.actor_begin);
-  int blocks = grid_for(work, kPrestepThreads, 148);
+  int blocks = grid_for(work, kPrestepThreads, 4 * 148);
   if (blocks > rs.max_blocks) blocks = rs.max_blocks;
   prestep_kernel<<<blocks, kPrestepThreads, 0, s>>>(a, rs.dpart, rs.ticket + 1);
 }

@@ -70,6 +70,9 @@ struct zrl_ctx {
   float *r_rew = nullptr, *r_val = nullptr, *r_lv = nullptr;
   uint8_t *r_done = nullptr;
   int64_t env_cap = 0, r_cap = 0;
+  // normalized observations of the whole batch, padded rows (computed once
+  // per update; the epochs permute rows of these)
+  float *n_xa = nullptr, *n_xc = nullptr;
   float *e_xa = nullptr, *e_xc = nullptr, *e_act = nullptr, *e_mo = nullptr;
   float *e_lpo = nullptr, *e_vo = nullptr, *e_adv = nullptr, *e_ret = nullptr;
   int32_t *order_dev = nullptr;
@@ -235,6 +238,8 @@ static zrl_status ensure_batch(zrl_ctx *ctx, int64_t n) {
   TRY(dalloc(ctx, &ctx->b_vo, n));
   TRY(dalloc(ctx, &ctx->b_adv, n));
   TRY(dalloc(ctx, &ctx->b_ret, n));
+  TRY(dalloc(ctx, &ctx->n_xa, n * odp));
+  TRY(dalloc(ctx, &ctx->n_xc, n * cdp));
   TRY(dalloc(ctx, &ctx->e_xa, n * odp));
   TRY(dalloc(ctx, &ctx->e_xc, n * cdp));
   TRY(dalloc(ctx, &ctx->e_act, n * A));
@@ -595,28 +600,38 @@ static zrl_status adv_moments(zrl_ctx *ctx, const float *adv, int64_t n,
   return ZRL_OK;
 }
 
-static GatherArgs gather_args(zrl_ctx *ctx, const float *obs, const float *cobs,
-                              const float *act, const float *mo, const float *lpo,
-                              const float *vo, const float *adv, const float *ret) {
+// Normalized, clamped (tf32-rounded in the tensor-core modes) observation
+// rows of the whole batch, padded to the GEMM pitch: Normalizer::normalize
+// (ppo.rs:196-205) applied once per update, since the normalizers do not
+// change during it.
+static zrl_status normalize_batch(zrl_ctx *ctx, const float *obs, const float *cobs,
+                                  int64_t n) {
+  if (n <= 0) return ZRL_OK;
+  launch_normalize_rows(obs, n, ctx->net[0].d[0], ctx->net[0].dp[0], ctx->obs_mean,
+                        ctx->obs_sd, ctx->n_xa, ctx->tc(), ctx->stream);
+  launch_normalize_rows(cobs, n, ctx->net[1].d[0], ctx->net[1].dp[0], ctx->crit_mean,
+                        ctx->crit_sd, ctx->n_xc, ctx->tc(), ctx->stream);
+  ctx->launches += 2;
+  CHECK_LAUNCH();
+  return ZRL_OK;
+}
+
+static GatherArgs gather_args(zrl_ctx *ctx, const float *act, const float *mo,
+                              const float *lpo, const float *vo, const float *adv,
+                              const float *ret) {
   GatherArgs g{};
   g.order = ctx->order_dev;
-  g.obs = obs;
-  g.cobs = cobs;
+  g.xn_a = ctx->n_xa;
+  g.xn_c = ctx->n_xc;
   g.action = act;
   g.mean_old = mo;
   g.logp_old = lpo;
   g.value_old = vo;
   g.adv = adv;
   g.ret = ret;
-  g.od = ctx->net[0].d[0];
-  g.cd = ctx->net[1].d[0];
   g.A = ctx->A;
   g.odp = ctx->net[0].dp[0];
   g.cdp = ctx->net[1].dp[0];
-  g.obs_mean = ctx->obs_mean;
-  g.obs_sd = ctx->obs_sd;
-  g.crit_mean = ctx->crit_mean;
-  g.crit_sd = ctx->crit_sd;
   g.st = ctx->st;
   g.x_a = ctx->e_xa;
   g.x_c = ctx->e_xc;
@@ -626,7 +641,6 @@ static GatherArgs gather_args(zrl_ctx *ctx, const float *obs, const float *cobs,
   g.g_value_old = ctx->e_vo;
   g.g_adv = ctx->e_adv;
   g.g_ret = ctx->e_ret;
-  g.round_tf32 = ctx->tc();
   return g;
 }
 
@@ -652,12 +666,12 @@ static zrl_status stage_batch(zrl_ctx *ctx, const zrl_batch *b, DevBatch *d,
                               bool need_adv_ret) {
   const int od = ctx->net[0].d[0], cd = ctx->net[1].d[0], A = ctx->A;
   const int64_t n = b->n;
+  TRY(ensure_batch(ctx, n));  // the epoch buffers, for device batches too
   if (b->on_device) {
     *d = DevBatch{b->obs, b->critic_obs, b->action, b->mean_old,
                   b->logp_old, b->value_old, b->adv, b->ret};
     return ZRL_OK;
   }
-  TRY(ensure_batch(ctx, n));
   auto up = [&](float *dst, const float *src, int64_t cnt) -> zrl_status {
     if (cnt <= 0) return ZRL_OK;
     CK(cudaMemcpyAsync(dst, src, sizeof(float) * cnt, cudaMemcpyHostToDevice,
@@ -706,6 +720,7 @@ static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
   TRY(ensure_mb(ctx, std::max<int64_t>(multi ? std::min<int64_t>(mb, n_local) : mb, 1)));
   std::vector<int32_t> perm(multi ? n_global : 0);
   std::vector<int64_t> counts(mbs), offs(mbs);
+  if (cfg->epochs > 0) TRY(normalize_batch(ctx, d.obs, d.cobs, n_local));
   for (int e = 0; e < cfg->epochs; ++e) {
     const uint64_t seed = (uint64_t)(ctx->t_logstd_host + e * mbs) + 1ull;
     int32_t *ord = ctx->order_pinned + (int64_t)e * n_global;
@@ -736,8 +751,7 @@ static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
     if (n_rows > 0) {
       CK(cudaMemcpyAsync(ctx->order_dev, ord, sizeof(int32_t) * n_rows,
                          cudaMemcpyHostToDevice, ctx->stream));
-      GatherArgs g = gather_args(ctx, d.obs, d.cobs, d.act, d.mo, d.lpo, d.vo,
-                                 d.adv, d.ret);
+      GatherArgs g = gather_args(ctx, d.act, d.mo, d.lpo, d.vo, d.adv, d.ret);
       g.n_used = n_rows;
       g.apply_adv_norm = 1;
       launch_gather(g, ctx->stream);
@@ -929,7 +943,7 @@ zrl_status zrl_destroy(zrl_ctx *ctx) {
                     &ctx->obs_sd, &ctx->crit_mean, &ctx->crit_m2, &ctx->crit_sd,
                     &ctx->b_obs, &ctx->b_cobs, &ctx->b_act, &ctx->b_mo, &ctx->b_lpo,
                     &ctx->b_vo, &ctx->b_adv, &ctx->b_ret, &ctx->r_rew, &ctx->r_val,
-                    &ctx->r_lv, &ctx->e_xa, &ctx->e_xc, &ctx->e_act, &ctx->e_mo,
+                    &ctx->r_lv, &ctx->n_xa, &ctx->n_xc, &ctx->e_xa, &ctx->e_xc, &ctx->e_act, &ctx->e_mo,
                     &ctx->e_lpo, &ctx->e_vo, &ctx->e_adv, &ctx->e_ret, &ctx->wpart,
                     &ctx->bpart, &ctx->rs.fpart, &ctx->Ptc};
   for (float **b : bufs)
@@ -1366,7 +1380,8 @@ zrl_status zrl_minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
   for (int64_t i = 0; i < n_idx; ++i) ctx->order_pinned[i] = (int32_t)idx[i];
   CK(cudaMemcpyAsync(ctx->order_dev, ctx->order_pinned, sizeof(int32_t) * n_idx,
                      cudaMemcpyHostToDevice, ctx->stream));
-  GatherArgs g = gather_args(ctx, d.obs, d.cobs, d.act, d.mo, d.lpo, d.vo, d.adv, d.ret);
+  TRY(normalize_batch(ctx, d.obs, d.cobs, batch->n));
+  GatherArgs g = gather_args(ctx, d.act, d.mo, d.lpo, d.vo, d.adv, d.ret);
   g.n_used = n_idx;
   g.apply_adv_norm = 0;  // the hook takes advantages as given
   launch_gather(g, ctx->stream);

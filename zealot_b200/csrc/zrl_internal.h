@@ -96,18 +96,15 @@ void launch_adv_finalize(const double *moments, int64_t n_global, DevState *st,
 struct GatherArgs {
   const int32_t *order;  // [n_used] local row indices
   int64_t n_used;
-  const float *obs, *cobs, *action, *mean_old, *logp_old, *value_old, *adv,
-      *ret;
-  int od, cd, A;          // true dims
-  int odp, cdp;           // padded row pitch of the outputs
-  const float *obs_mean, *obs_sd;       // [od]
-  const float *crit_mean, *crit_sd;     // [cd]
+  const float *xn_a, *xn_c;  // normalized observation rows, pitch odp / cdp
+  const float *action, *mean_old, *logp_old, *value_old, *adv, *ret;
+  int A;
+  int odp, cdp;           // padded row pitch (multiples of 32 floats)
   const DevState *st;   // adv_mean / adv_sd
   float *x_a, *x_c;     // [n_used, odp], [n_used, cdp]
   float *g_action, *g_mean_old;         // [n_used, A]
   float *g_logp_old, *g_value_old, *g_adv, *g_ret;
   int apply_adv_norm;
-  int round_tf32;       // round the normalized observations to tf32 (RN)
 };
 void launch_gather(const GatherArgs &a, cudaStream_t s);
 // Normalizer divisors: sd = sqrt(max(m2/count, 1e-8)) (ppo.rs:201-202).
