@@ -8,21 +8,25 @@
 //   wgrad    dW[out,in]  = Delta^T X  (split-K)  A MN-major, B MN-major
 //
 // One CTA per SM walks the 128 x BN output tiles (m fastest, so CTAs that
-// run together share the B tile in L2).  Six warps:
+// run together share the B tile in L2).  Ten warps:
 //   warp 0, one lane: TMA producer -- streams A/B k-blocks of 128 bytes
 //     (32 tf32) into a ring of shared-memory stages;
 //   warp 1, one lane: MMA issuer -- tcgen05.mma kind::tf32 (M=128, N=BN,
 //     K=8, four per k-block) into one of two TMEM accumulators, committing
 //     each stage back to the producer and each finished tile to the
 //     epilogue;
-//   warps 2-5: epilogue -- tcgen05.ld of the accumulator (warp w reads TMEM
-//     lanes 32*(w%4).. = tile rows), bias + ELU (forward) or ELU' from the
-//     stored post-activation (dgrad) or nothing (wgrad), optional per-tile
-//     column sums (the bias gradient, taken before rounding), rounding to
-//     tf32 for outputs that feed later GEMMs, then a 128B-swizzled staging
-//     buffer and one TMA tensor store per 32 x 32 chunk.
+//   warps 2-9: epilogue -- two warps per TMEM lane quarter (warp w reads
+//     lanes 32*(w%4).. = tile rows), taking alternate 32-column chunks:
+//     tcgen05.ld of the chunk (the accumulator goes back to the MMA warp
+//     after the tile's last load), bias + ELU (forward) or ELU' from the
+//     stored post-activation (dgrad; that box arrives by TMA into the
+//     warp's staging slot one chunk ahead) or nothing (wgrad), optional
+//     per-tile column sums (the bias gradient, taken before rounding, by a
+//     shuffle butterfly), rounding to tf32 for outputs that feed later
+//     GEMMs, then the 128B-swizzled staging slot and one TMA tensor store
+//     per 32 x 32 chunk.
 // With two accumulators the epilogue of tile i overlaps the MMAs of tile
-// i+1, and the TMA engine does all global reads and writes.
+// i+1, and the TMA engine does all bulk global reads and writes.
 //
 // Every mbarrier wait is bounded; a timeout sets *err and the waiting role
 // leaves its loop.  No TMA multicast is used.
@@ -42,6 +46,7 @@ namespace {
 constexpr int BM = 128;          // UMMA M (cta_group::1)
 constexpr int BKB = 128;         // bytes of K per k-block (one swizzle row)
 constexpr int kEpiWarps = 8;  // two per TMEM lane quarter
+constexpr int kEpiPerQuarter = kEpiWarps / 4;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 // a second bound on a wait, on the number of polls, should the global timer
 // not advance; the wall-time bound (kWaitNs) is the one that normally ends
@@ -267,6 +272,34 @@ __device__ __forceinline__ float exp_sfu(float x) {
   return y;
 }
 
+// Column sums of a [32 x 32] chunk held one row per lane: five butterfly
+// steps, each exchanging half of the remaining columns with the partner
+// lane, leave the sum of column `lane` in lane `lane` (a fixed summation
+// tree, so the same bits every run).
+__device__ __forceinline__ float colsum32(const float (&v)[32], int lane) {
+  float w[16];
+  {
+    const bool up = lane & 16;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float send = up ? v[i] : v[i + 16];
+      const float keep = up ? v[i + 16] : v[i];
+      w[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+  }
+#pragma unroll
+  for (int h = 8; h >= 1; h >>= 1) {
+    const bool up = lane & h;
+#pragma unroll
+    for (int i = 0; i < h; ++i) {
+      const float send = up ? w[i] : w[i + h];
+      const float keep = up ? w[i + h] : w[i];
+      w[i] = keep + __shfl_xor_sync(0xffffffffu, send, h);
+    }
+  }
+  return w[0];
+}
+
 struct TcArgs {
   int M, N, K;
   int kc;          // K per split (multiple of 32); split z covers [z*kc, ...)
@@ -279,16 +312,23 @@ struct TcArgs {
   int *err;
 };
 
-template <int BN, int STAGES>
+// Staging slots per epilogue warp, each one [32 x 32] fp32 box: one for the
+// output; two for the dgrad epilogue, whose slots also receive the
+// TMA-loaded post-activation one chunk ahead.
+constexpr int slots_for(int epi) { return epi == EPI_ELU_GRAD ? 2 : 1; }
+
+template <int BN, int STAGES, int EPI>
 struct Smem {
   static constexpr int kA = BM * BKB;                 // 16 KB
   static constexpr int kB = BN * BKB;                 // BN * 128 B
   static constexpr int kStage = kA + kB;
   static constexpr int kStageBytes = STAGES * kStage;
-  static constexpr int kStaging = kEpiWarps * 4096;  // one [32 x 32] fp32 chunk per warp
+  static constexpr int kSlots = slots_for(EPI);
+  static constexpr int kStaging = kEpiWarps * kSlots * 4096;
   static constexpr int kRed = 4 * BN * 4;             // column sums per lane quarter
   static constexpr int kBarOff = kStageBytes + kStaging + kRed;
-  static constexpr int kBars = 2 * STAGES + 4;        // full, empty, acc_full x2, acc_empty x2
+  // full, empty, acc_full x2, acc_empty x2, one aux barrier per staging slot
+  static constexpr int kBars = 2 * STAGES + 4 + kEpiWarps * kSlots;
   static constexpr int kBytes = 1024 /*align*/ + kBarOff + kBars * 8 + 16;
 };
 
@@ -314,16 +354,18 @@ template <int BN, bool A_MN, bool B_MN, int EPI, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                const __grid_constant__ CUtensorMap tmB,
-               const __grid_constant__ CUtensorMap tmC, TcArgs g) {
+               const __grid_constant__ CUtensorMap tmC,
+               const __grid_constant__ CUtensorMap tmX, TcArgs g) {
   static_assert(BN == 32 || BN == 64 || BN == 128 || BN == 256, "BN");
-  using S = Smem<BN, STAGES>;
+  using S = Smem<BN, STAGES, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t *full = (uint64_t *)(smem + S::kBarOff);
   uint64_t *empty = full + STAGES;
   uint64_t *accf = empty + STAGES;  // [2]
   uint64_t *acce = accf + 2;        // [2]
-  uint32_t *tmem_slot = (uint32_t *)(acce + 2);
+  uint64_t *xbar = acce + 2;        // [kEpiWarps][kSlots]
+  uint32_t *tmem_slot = (uint32_t *)(xbar + kEpiWarps * S::kSlots);
   float *red = (float *)(smem + S::kStageBytes + S::kStaging);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -340,6 +382,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
       mbar_init(&accf[b], 1);
       mbar_init(&acce[b], kEpiWarps);
     }
+    for (int b = 0; b < kEpiWarps * S::kSlots; ++b) mbar_init(&xbar[b], 1);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -347,6 +390,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
       prefetch_tmap(&tmA);
       prefetch_tmap(&tmB);
       prefetch_tmap(&tmC);
+      if (EPI == EPI_ELU_GRAD) prefetch_tmap(&tmX);
     }
     __syncwarp();
     // TMEM: two BN-column fp32 accumulators of 128 lanes
@@ -432,13 +476,34 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
   } else {
     // ---------------------------------------------------- epilogue
     // two warps per TMEM lane quarter (warp w may only read lanes
-    // 32*(w%4)..+31), taking alternate 32-column chunks
+    // 32*(w%4)..+31), taking alternate 32-column chunks.  A warp's chunks,
+    // numbered j = 0, 1, ... over its tiles, cycle through its kSlots
+    // staging slots.
+    constexpr int NS = S::kSlots;
     const int ew = warp - 2;       // 0..kEpiWarps-1
     const int quarter = warp & 3;  // TMEM lane quarter = rows of this warp
     const int half = ew >> 2;      // chunks c with c % 2 == half
-    float *buf = (float *)(smem + S::kStageBytes + ew * 4096);  // this warp's staging chunk
-    int it = 0;
-    bool ok = true;
+    const int cpt = (BN / 32 - half + 1) / 2;  // chunks per tile of this warp
+    uint8_t *slots = smem + S::kStageBytes + ew * (NS * 4096);
+    uint64_t *wbar = xbar + ew * NS;
+    uint32_t xph = 0;  // phase bit per slot of the aux barriers
+    // dgrad: TMA load of the stored post-activation box of chunk j into its
+    // slot (the slot's previous store must be done reading it)
+    auto issue_aux = [&](int j) {
+      if (cpt == 0) return;
+      const int t = blockIdx.x + (j / cpt) * gridDim.x;
+      if (t >= tiles) return;
+      const Tile tl = decode_tile<BN>(t, tiles_m, tiles_n, g);
+      const int n = tl.n0 + (half + 2 * (j % cpt)) * 32, r0 = tl.m0 + quarter * 32;
+      if (n >= g.N || r0 >= g.M) return;
+      const int sl = j % NS;
+      mbar_expect_tx(&wbar[sl], 4096);
+      tma_load_2d(slots + sl * 4096, &tmX, &wbar[sl], n, r0);
+    };
+    if (EPI == EPI_ELU_GRAD && lane == 0)
+      for (int p = 0; p < NS - 1; ++p) issue_aux(p);
+    int it = 0, j = 0;
+    bool ok = true, prev_store = false;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
       const Tile tl = decode_tile<BN>(t, tiles_m, tiles_n, g);
       const int ab = it & 1;
@@ -451,12 +516,16 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
       const bool row_ok = row < g.M;
       const uint32_t taddr = tmem + (uint32_t)(ab * BN) + ((uint32_t)(quarter * 32) << 16);
       const bool have = ok && tl.nk > 0;
+      bool released = false;
 #pragma unroll 1
-      for (int c = half; c < BN / 32; c += 2) {
+      for (int k = 0; k < cpt; ++k, ++j) {
+        const int c = half + 2 * k;
         const int n = tl.n0 + c * 32;
-        if (n >= g.N) break;  // uniform
+        const int sl = j % NS;
+        float *buf = (float *)(slots + sl * 4096);
+        const bool live = n < g.N && row0 < g.M;  // uniform over the warp
         float v[32];
-        if (have) {
+        if (live && have) {
           uint32_t r[32];
           tmem_ld32(taddr + c * 32, r);
 #pragma unroll
@@ -465,19 +534,32 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = 0.0f;
         }
-        const bool full_chunk = n + 32 <= g.N;
-        if (full_chunk) {
-          // the common case: 32 valid columns, vector loads, no per-element
-          // predicates
+        if (k == cpt - 1) {
+          // last read of this accumulator: hand it back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acce[ab]);
+          released = true;
+        }
+        bool stored = false;
+        if (live) {
+          const bool full_chunk = n + 32 <= g.N;
+          float4 *rowp = reinterpret_cast<float4 *>(buf + lane * 32);
           if (EPI == EPI_BIAS || EPI == EPI_BIAS_ELU) {
-            const float4 *bp = reinterpret_cast<const float4 *>(g.bias + n);
+            if (full_chunk) {
+              const float4 *bp = reinterpret_cast<const float4 *>(g.bias + n);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const float4 b = __ldg(bp + q);
-              v[4 * q + 0] += b.x;
-              v[4 * q + 1] += b.y;
-              v[4 * q + 2] += b.z;
-              v[4 * q + 3] += b.w;
+              for (int q = 0; q < 8; ++q) {
+                const float4 b = __ldg(bp + q);
+                v[4 * q + 0] += b.x;
+                v[4 * q + 1] += b.y;
+                v[4 * q + 2] += b.z;
+                v[4 * q + 3] += b.w;
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (n + i < g.N) v[i] += __ldg(&g.bias[n + i]);
             }
           }
           if (EPI == EPI_BIAS_ELU) {
@@ -486,84 +568,77 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = v[i] > 0.0f ? v[i] : exp_sfu(v[i]) - 1.0f;
           }
-          if (EPI == EPI_ELU_GRAD && row_ok) {
-            const float4 *ap =
-                reinterpret_cast<const float4 *>(g.aux + (int64_t)row * g.ldaux + n);
+          if (EPI == EPI_ELU_GRAD) {
+            // ELU' from the stored post-activation y (net.rs:19-22), whose
+            // box the TMA has put in this slot (zero-filled out of range)
+            if (!mbar_wait(&wbar[sl], (xph >> sl) & 1u, g.err, 5)) ok = false;
+            xph ^= 1u << sl;
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
-              const float4 y = __ldg(ap + q);
+              const float4 y = rowp[q ^ (lane & 7)];
               v[4 * q + 0] *= y.x > 0.0f ? 1.0f : y.x + 1.0f;
               v[4 * q + 1] *= y.y > 0.0f ? 1.0f : y.y + 1.0f;
               v[4 * q + 2] *= y.z > 0.0f ? 1.0f : y.z + 1.0f;
               v[4 * q + 3] *= y.w > 0.0f ? 1.0f : y.w + 1.0f;
             }
           }
+          // invalid rows and columns hold 0 (column sums, clipped stores)
           if (!row_ok) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = 0.0f;
           }
-        } else {
-          // ragged last chunk (only the general zrl_gemm entry point)
+          if (!full_chunk) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float x = v[i];
-            if (!row_ok || n + i >= g.N) {
-              x = 0.0f;
-            } else {
-              if (EPI == EPI_BIAS || EPI == EPI_BIAS_ELU) x += __ldg(&g.bias[n + i]);
-              if (EPI == EPI_BIAS_ELU) x = x > 0.0f ? x : exp_sfu(x) - 1.0f;
-              if (EPI == EPI_ELU_GRAD) {
-                const float y = __ldg(&g.aux[(int64_t)row * g.ldaux + n + i]);
-                x *= y > 0.0f ? 1.0f : y + 1.0f;
-              }
-            }
-            v[i] = x;
+            for (int i = 0; i < 32; ++i)
+              if (n + i >= g.N) v[i] = 0.0f;
           }
-        }
-        // stage the 32 x 32 chunk in the 128B-swizzled layout (16-byte
-        // chunk q of row r at position q ^ (r & 7): conflict-free) for one
-        // TMA store; the store clips rows >= M and columns >= N
-        if (lane == 0) bulk_wait_read<0>();  // the previous store has read buf
-        __syncwarp();
-        float4 *rowp = reinterpret_cast<float4 *>(buf + lane * 32);
-        const bool cs = g.colsum != nullptr;
-        if (g.round_out && !cs) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = round_tf32(v[i]);
-        }
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          rowp[q ^ (lane & 7)] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-        if (cs) {
-          // bias gradient: column sums of the unrounded chunk (invalid rows
-          // and columns hold 0), lane j summing column j over the 32 rows in
-          // row order (conflict-free reads of the swizzled rows)
-          __syncwarp();
-          float sum = 0.0f;
-#pragma unroll 8
-          for (int r = 0; r < 32; ++r)
-            sum += buf[r * 32 + ((((lane >> 2) ^ (r & 7)) << 2) | (lane & 3))];
-          red[quarter * BN + c * 32 + lane] = sum;
+          if (g.colsum) {
+            // bias gradient: column sums of the unrounded chunk over its 32
+            // rows (lane = row), a butterfly that leaves column `lane` in
+            // lane `lane`
+            red[quarter * BN + c * 32 + lane] = colsum32(v, lane);
+          }
           if (g.round_out) {
-            __syncwarp();
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-              rowp[q ^ (lane & 7)] =
-                  make_float4(round_tf32(v[4 * q]), round_tf32(v[4 * q + 1]),
-                              round_tf32(v[4 * q + 2]), round_tf32(v[4 * q + 3]));
+            for (int i = 0; i < 32; ++i) v[i] = round_tf32(v[i]);
           }
+          if (EPI != EPI_ELU_GRAD) {
+            // the store that last used this slot (NS chunks back) must be
+            // done reading it
+            if (lane == 0) {
+              if (prev_store) bulk_wait_read<NS - 1>();
+              else bulk_wait_read<0>();
+            }
+            __syncwarp();
+          }
+          // stage in the 128B-swizzled layout (16-byte chunk q of row r at
+          // position q ^ (r & 7): conflict-free) for one TMA store; the
+          // store clips rows >= M and columns >= N
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            rowp[q ^ (lane & 7)] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tmC, buf, n, row0, tl.z);
+            bulk_commit();
+          }
+          stored = true;
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0 && row0 < g.M) {
-          tma_store_3d(&tmC, buf, n, row0, tl.z);
-          bulk_commit();
+        if (!live && g.colsum && n < g.N) red[quarter * BN + c * 32 + lane] = 0.0f;  // no rows
+        if (EPI == EPI_ELU_GRAD && lane == 0) {
+          // refill the slot of chunk j-1 with the aux box of chunk j+NS-1
+          if (stored) bulk_wait_read<1>();
+          else bulk_wait_read<0>();
+          issue_aux(j + NS - 1);
         }
+        prev_store = stored;
       }
-      // accumulator drained: let the MMA warp reuse it
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acce[ab]);
+      if (!released) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce[ab]);
+      }
       if (g.colsum) {
         named_bar_sync(1, 32 * kEpiWarps);
         for (int i = ew * 32 + lane; i < BN; i += 32 * kEpiWarps) {
@@ -639,12 +714,25 @@ bool make_out_map(CUtensorMap *m, float *base, int64_t rows, int64_t cols, int64
   return true;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, int STAGES>
+// The deepest stage ring (at most 6) that fits next to the epilogue
+// staging slots: more k-blocks in flight hide the TMA -> MMA -> release
+// round trip.
+template <int BN, int EPI>
+constexpr int stages_for() {
+  constexpr int avail = 227 * 1024 - 1024 - kEpiWarps * slots_for(EPI) * 4096 - 4 * BN * 4 -
+                        (8 + kEpiWarps * slots_for(EPI)) * 8 - 64;
+  constexpr int st = avail / (BM * BKB + BN * BKB);
+  return st > 6 ? 6 : st;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
 cudaError_t launch_one(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
-                       const TcArgs &a, int tiles, cudaStream_t s) {
-  using S = Smem<BN, STAGES>;
+                       const CUtensorMap &tx, const TcArgs &a, int tiles, cudaStream_t s) {
+  constexpr int ST = stages_for<BN, EPI>();
+  static_assert(ST >= 2, "stage ring");
+  using S = Smem<BN, ST, EPI>;
   static_assert(S::kBytes <= 227 * 1024, "shared memory");
-  auto kfn = tc_gemm_kernel<BN, A_MN, B_MN, EPI, STAGES>;
+  auto kfn = tc_gemm_kernel<BN, A_MN, B_MN, EPI, ST>;
   static bool attr = false;  // set once per instantiation (same value on every device)
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -653,28 +741,26 @@ cudaError_t launch_one(const CUtensorMap &ta, const CUtensorMap &tb, const CUten
     attr = true;
   }
   const int grid = tiles < g_sms ? tiles : g_sms;
-  kfn<<<grid, kThreads, S::kBytes, s>>>(ta, tb, tc, a);
+  kfn<<<grid, kThreads, S::kBytes, s>>>(ta, tb, tc, tx, a);
   return cudaGetLastError();
 }
 
 template <int BN>
 cudaError_t dispatch_bn(int kind, int epi, const CUtensorMap &ta, const CUtensorMap &tb,
-                        const CUtensorMap &tc, const TcArgs &a, int tiles, cudaStream_t s) {
-  // the deepest stage ring that fits next to the epilogue staging buffers
-  // (more k-blocks in flight hide the TMA -> MMA -> release round trip)
-  constexpr int ST = BN >= 256 ? 3 : (BN >= 128 ? 5 : 6);
+                        const CUtensorMap &tc, const CUtensorMap &tx, const TcArgs &a,
+                        int tiles, cudaStream_t s) {
   if (kind == 0) {  // forward
     if (epi == EPI_BIAS_ELU)
-      return launch_one<BN, false, false, EPI_BIAS_ELU, ST>(ta, tb, tc, a, tiles, s);
-    if (epi == EPI_BIAS) return launch_one<BN, false, false, EPI_BIAS, ST>(ta, tb, tc, a, tiles, s);
-    return launch_one<BN, false, false, EPI_STORE, ST>(ta, tb, tc, a, tiles, s);
+      return launch_one<BN, false, false, EPI_BIAS_ELU>(ta, tb, tc, tx, a, tiles, s);
+    if (epi == EPI_BIAS) return launch_one<BN, false, false, EPI_BIAS>(ta, tb, tc, tx, a, tiles, s);
+    return launch_one<BN, false, false, EPI_STORE>(ta, tb, tc, tx, a, tiles, s);
   }
   if (kind == 1) {  // dgrad
     if (epi == EPI_ELU_GRAD)
-      return launch_one<BN, false, true, EPI_ELU_GRAD, ST>(ta, tb, tc, a, tiles, s);
-    return launch_one<BN, false, true, EPI_STORE, ST>(ta, tb, tc, a, tiles, s);
+      return launch_one<BN, false, true, EPI_ELU_GRAD>(ta, tb, tc, tx, a, tiles, s);
+    return launch_one<BN, false, true, EPI_STORE>(ta, tb, tc, tx, a, tiles, s);
   }
-  return launch_one<BN, true, true, EPI_STORE, ST>(ta, tb, tc, a, tiles, s);  // wgrad
+  return launch_one<BN, true, true, EPI_STORE>(ta, tb, tc, tx, a, tiles, s);  // wgrad
 }
 
 }  // namespace
@@ -780,6 +866,10 @@ zrl_status gemm_tc(GemmEngine *eng, const GemmArgs &g, int precision, cudaStream
                                     : cached_map(eng, g.B, g.K, g.N, g.ldb, 32, 1, err);
   const CUtensorMap *tc = cached_map(eng, g.C, g.M, g.N, g.ldc, split, 2, err);
   if (!ta || !tb || !tc) return ZRL_CUDA_ERROR;
+  // dgrad: the post-activation read by the epilogue in [32 x 32] boxes
+  const bool aux_tma = kind == 1 && g.epi == EPI_ELU_GRAD;
+  const CUtensorMap *tx = aux_tma ? cached_map(eng, g.aux, g.M, g.N, g.ldaux, 32, 0, err) : tc;
+  if (!tx) return ZRL_CUDA_ERROR;
   int kc = (g.K + split - 1) / split;
   kc = (kc + 31) / 32 * 32;
   TcArgs a{};
@@ -796,10 +886,10 @@ zrl_status gemm_tc(GemmEngine *eng, const GemmArgs &g, int precision, cudaStream
   a.err = eng->err_dev;
   const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN) * split;
   cudaError_t e;
-  if (BN == 32) e = dispatch_bn<32>(kind, g.epi, *ta, *tb, *tc, a, tiles, s);
-  else if (BN == 64) e = dispatch_bn<64>(kind, g.epi, *ta, *tb, *tc, a, tiles, s);
-  else if (BN == 128) e = dispatch_bn<128>(kind, g.epi, *ta, *tb, *tc, a, tiles, s);
-  else e = dispatch_bn<256>(kind, g.epi, *ta, *tb, *tc, a, tiles, s);
+  if (BN == 32) e = dispatch_bn<32>(kind, g.epi, *ta, *tb, *tc, *tx, a, tiles, s);
+  else if (BN == 64) e = dispatch_bn<64>(kind, g.epi, *ta, *tb, *tc, *tx, a, tiles, s);
+  else if (BN == 128) e = dispatch_bn<128>(kind, g.epi, *ta, *tb, *tc, *tx, a, tiles, s);
+  else e = dispatch_bn<256>(kind, g.epi, *ta, *tb, *tc, *tx, a, tiles, s);
   if (e != cudaSuccess) {
     *err = std::string("tensor-core GEMM launch: ") + cudaGetErrorString(e);
     return ZRL_CUDA_ERROR;
