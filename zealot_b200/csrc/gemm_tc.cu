@@ -34,6 +34,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -46,7 +48,6 @@ namespace {
 constexpr int BM = 128;          // UMMA M (cta_group::1)
 constexpr int BKB = 128;         // bytes of K per k-block (one swizzle row)
 constexpr int kEpiWarps = 8;  // two per TMEM lane quarter
-constexpr int kEpiPerQuarter = kEpiWarps / 4;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 // a second bound on a wait, on the number of polls, should the global timer
 // not advance; the wall-time bound (kWaitNs) is the one that normally ends
@@ -177,6 +178,13 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)m) : "memory");
 }
 
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
@@ -300,16 +308,31 @@ __device__ __forceinline__ float colsum32(const float (&v)[32], int lane) {
   return w[0];
 }
 
-struct TcArgs {
+// One GEMM of a grouped launch.  A launch runs up to kMaxProbs GEMMs of
+// one kind and epilogue (e.g. the same layer of the actor and the critic,
+// or every weight gradient of both nets) as one flat tile space, problem
+// after problem.
+constexpr int kMaxProbs = 8;
+struct TcProb {
   int M, N, K;
   int kc;          // K per split (multiple of 32); split z covers [z*kc, ...)
   int splits;
+  int tiles_m, tiles_n;
+  int tile0;       // first flat tile index of this problem
   const float *bias;
-  const float *aux;
-  int ldaux;
   int round_out;
   float *colsum;   // optional per-m-tile column sums [tiles_m][N] (no split-K)
+};
+struct TcGroup {
+  TcProb p[kMaxProbs];
+  int n;       // problems
+  int tiles;   // total tiles
   int *err;
+};
+// Tensor maps per problem: A and B operands, the output C (3-D, split
+// index outermost) and the dgrad epilogue's post-activation X.
+struct TcMaps {
+  CUtensorMap a[kMaxProbs], b[kMaxProbs], c[kMaxProbs], x[kMaxProbs];
 };
 
 // Staging slots per epilogue warp, each one [32 x 32] fp32 box: one for the
@@ -333,29 +356,32 @@ struct Smem {
 };
 
 struct Tile {
-  int m0, n0, z, kbeg, nk;
+  int p, m0, n0, z, kbeg, nk;
 };
 
+// Flat tile t -> problem, then m fastest, n, split.
 template <int BN>
-__device__ __forceinline__ Tile decode_tile(int t, int tiles_m, int tiles_n, const TcArgs &g) {
+__device__ __forceinline__ Tile decode_tile(int t, const TcGroup &g) {
   Tile tl;
-  const int mt = t % tiles_m;
-  const int rest = t / tiles_m;
+  int p = 0;
+  while (p + 1 < g.n && t >= g.p[p + 1].tile0) ++p;
+  const TcProb &pr = g.p[p];
+  const int lt = t - pr.tile0;
+  tl.p = p;
+  const int mt = lt % pr.tiles_m;
+  const int rest = lt / pr.tiles_m;
   tl.m0 = mt * BM;
-  tl.n0 = (rest % tiles_n) * BN;
-  tl.z = rest / tiles_n;
-  tl.kbeg = tl.z * g.kc;
-  const int kend = min(g.K, tl.kbeg + g.kc);
+  tl.n0 = (rest % pr.tiles_n) * BN;
+  tl.z = rest / pr.tiles_n;
+  tl.kbeg = tl.z * pr.kc;
+  const int kend = min(pr.K, tl.kbeg + pr.kc);
   tl.nk = kend > tl.kbeg ? (kend - tl.kbeg + 31) / 32 : 0;
   return tl;
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
-tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-               const __grid_constant__ CUtensorMap tmB,
-               const __grid_constant__ CUtensorMap tmC,
-               const __grid_constant__ CUtensorMap tmX, TcArgs g) {
+tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGroup g) {
   static_assert(BN == 32 || BN == 64 || BN == 128 || BN == 256, "BN");
   using S = Smem<BN, STAGES, EPI>;
   extern __shared__ uint8_t smem_raw[];
@@ -369,9 +395,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
   float *red = (float *)(smem + S::kStageBytes + S::kStaging);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tiles_m = (g.M + BM - 1) / BM;
-  const int tiles_n = (g.N + BN - 1) / BN;
-  const int tiles = tiles_m * tiles_n * g.splits;
+  const int tiles = g.tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -386,11 +410,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
     fence_barrier_init();
   }
   if (warp == 0) {
-    if (lane == 0) {
-      prefetch_tmap(&tmA);
-      prefetch_tmap(&tmB);
-      prefetch_tmap(&tmC);
-      if (EPI == EPI_ELU_GRAD) prefetch_tmap(&tmX);
+    if (lane < g.n) {
+      prefetch_tmap(&maps.a[lane]);
+      prefetch_tmap(&maps.b[lane]);
+      prefetch_tmap(&maps.c[lane]);
+      if (EPI == EPI_ELU_GRAD) prefetch_tmap(&maps.x[lane]);
     }
     __syncwarp();
     // TMEM: two BN-column fp32 accumulators of 128 lanes
@@ -404,6 +428,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // programmatic dependent launch: the set-up above overlapped the previous
+  // kernel's tail; every global access below waits for that kernel to have
+  // completed, and the next kernel may start its own set-up from here
+  grid_dependency_wait();
+  if (threadIdx.x == 0) grid_launch_dependents();
 
   if (warp == 0) {
     // ---------------------------------------------------- TMA producer
@@ -411,7 +440,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
       int kbg = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        const Tile tl = decode_tile<BN>(t, tiles_m, tiles_n, g);
+        const Tile tl = decode_tile<BN>(t, g);
         for (int kb = 0; kb < tl.nk; ++kb, ++kbg) {
           const int s = kbg % STAGES;
           const uint32_t ph = (uint32_t)(kbg / STAGES) & 1u;
@@ -423,16 +452,16 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
           if (A_MN) {  // Delta [K rows, M cols]: four 32-column boxes of 32 rows
 #pragma unroll
             for (int c = 0; c < BM / 32; ++c)
-              tma_load_2d(a_s + c * 4096, &tmA, &full[s], tl.m0 + 32 * c, k0);
+              tma_load_2d(a_s + c * 4096, &maps.a[tl.p], &full[s], tl.m0 + 32 * c, k0);
           } else {     // [M rows, K cols]: one box of 128 rows x 32
-            tma_load_2d(a_s, &tmA, &full[s], k0, tl.m0);
+            tma_load_2d(a_s, &maps.a[tl.p], &full[s], k0, tl.m0);
           }
           if (B_MN) {
 #pragma unroll
             for (int c = 0; c < BN / 32; ++c)
-              tma_load_2d(b_s + c * 4096, &tmB, &full[s], tl.n0 + 32 * c, k0);
+              tma_load_2d(b_s + c * 4096, &maps.b[tl.p], &full[s], tl.n0 + 32 * c, k0);
           } else {
-            tma_load_2d(b_s, &tmB, &full[s], k0, tl.n0);
+            tma_load_2d(b_s, &maps.b[tl.p], &full[s], k0, tl.n0);
           }
         }
       }
@@ -444,7 +473,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
       int kbg = 0, it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
-        const Tile tl = decode_tile<BN>(t, tiles_m, tiles_n, g);
+        const Tile tl = decode_tile<BN>(t, g);
         const int ab = it & 1;
         const uint32_t aph = (uint32_t)(it >> 1) & 1u;
         // the epilogue must have drained this accumulator (tile it-2)
@@ -493,19 +522,21 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
       if (cpt == 0) return;
       const int t = blockIdx.x + (j / cpt) * gridDim.x;
       if (t >= tiles) return;
-      const Tile tl = decode_tile<BN>(t, tiles_m, tiles_n, g);
+      const Tile tl = decode_tile<BN>(t, g);
+      const TcProb &pr = g.p[tl.p];
       const int n = tl.n0 + (half + 2 * (j % cpt)) * 32, r0 = tl.m0 + quarter * 32;
-      if (n >= g.N || r0 >= g.M) return;
+      if (n >= pr.N || r0 >= pr.M) return;
       const int sl = j % NS;
       mbar_expect_tx(&wbar[sl], 4096);
-      tma_load_2d(slots + sl * 4096, &tmX, &wbar[sl], n, r0);
+      tma_load_2d(slots + sl * 4096, &maps.x[tl.p], &wbar[sl], n, r0);
     };
     if (EPI == EPI_ELU_GRAD && lane == 0)
       for (int p = 0; p < NS - 1; ++p) issue_aux(p);
     int it = 0, j = 0;
     bool ok = true, prev_store = false;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
-      const Tile tl = decode_tile<BN>(t, tiles_m, tiles_n, g);
+      const Tile tl = decode_tile<BN>(t, g);
+      const TcProb &pr = g.p[tl.p];
       const int ab = it & 1;
       const uint32_t aph = (uint32_t)(it >> 1) & 1u;
       if (ok) ok = mbar_wait(&accf[ab], aph, g.err, 3);
@@ -513,7 +544,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
       tc_fence_after();
       const int row0 = tl.m0 + quarter * 32;
       const int row = row0 + lane;
-      const bool row_ok = row < g.M;
+      const bool row_ok = row < pr.M;
       const uint32_t taddr = tmem + (uint32_t)(ab * BN) + ((uint32_t)(quarter * 32) << 16);
       const bool have = ok && tl.nk > 0;
       bool released = false;
@@ -523,7 +554,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
         const int n = tl.n0 + c * 32;
         const int sl = j % NS;
         float *buf = (float *)(slots + sl * 4096);
-        const bool live = n < g.N && row0 < g.M;  // uniform over the warp
+        const bool live = n < pr.N && row0 < pr.M;  // uniform over the warp
         float v[32];
         if (live && have) {
           uint32_t r[32];
@@ -543,11 +574,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
         }
         bool stored = false;
         if (live) {
-          const bool full_chunk = n + 32 <= g.N;
+          const bool full_chunk = n + 32 <= pr.N;
           float4 *rowp = reinterpret_cast<float4 *>(buf + lane * 32);
           if (EPI == EPI_BIAS || EPI == EPI_BIAS_ELU) {
             if (full_chunk) {
-              const float4 *bp = reinterpret_cast<const float4 *>(g.bias + n);
+              const float4 *bp = reinterpret_cast<const float4 *>(pr.bias + n);
 #pragma unroll
               for (int q = 0; q < 8; ++q) {
                 const float4 b = __ldg(bp + q);
@@ -559,7 +590,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
             } else {
 #pragma unroll
               for (int i = 0; i < 32; ++i)
-                if (n + i < g.N) v[i] += __ldg(&g.bias[n + i]);
+                if (n + i < pr.N) v[i] += __ldg(&pr.bias[n + i]);
             }
           }
           if (EPI == EPI_BIAS_ELU) {
@@ -590,15 +621,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
           if (!full_chunk) {
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-              if (n + i >= g.N) v[i] = 0.0f;
+              if (n + i >= pr.N) v[i] = 0.0f;
           }
-          if (g.colsum) {
+          if (pr.colsum) {
             // bias gradient: column sums of the unrounded chunk over its 32
             // rows (lane = row), a butterfly that leaves column `lane` in
             // lane `lane`
             red[quarter * BN + c * 32 + lane] = colsum32(v, lane);
           }
-          if (g.round_out) {
+          if (pr.round_out) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = round_tf32(v[i]);
           }
@@ -620,12 +651,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_3d(&tmC, buf, n, row0, tl.z);
+            tma_store_3d(&maps.c[tl.p], buf, n, row0, tl.z);
             bulk_commit();
           }
           stored = true;
         }
-        if (!live && g.colsum && n < g.N) red[quarter * BN + c * 32 + lane] = 0.0f;  // no rows
+        if (!live && pr.colsum && n < pr.N) red[quarter * BN + c * 32 + lane] = 0.0f;  // no rows
         if (EPI == EPI_ELU_GRAD && lane == 0) {
           // refill the slot of chunk j-1 with the aux box of chunk j+NS-1
           if (stored) bulk_wait_read<1>();
@@ -639,12 +670,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
         __syncwarp();
         if (lane == 0) mbar_arrive(&acce[ab]);
       }
-      if (g.colsum) {
+      if (pr.colsum) {
         named_bar_sync(1, 32 * kEpiWarps);
         for (int i = ew * 32 + lane; i < BN; i += 32 * kEpiWarps) {
           const int n = tl.n0 + i;
-          if (n < g.N)
-            g.colsum[(int64_t)(tl.m0 / BM) * g.N + n] =
+          if (n < pr.N)
+            pr.colsum[(int64_t)(tl.m0 / BM) * pr.N + n] =
                 red[i] + red[BN + i] + red[2 * BN + i] + red[3 * BN + i];
         }
         named_bar_sync(1, 32 * kEpiWarps);
@@ -726,8 +757,7 @@ constexpr int stages_for() {
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
-cudaError_t launch_one(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tc,
-                       const CUtensorMap &tx, const TcArgs &a, int tiles, cudaStream_t s) {
+cudaError_t launch_one(const TcMaps &maps, const TcGroup &grp, cudaStream_t s) {
   constexpr int ST = stages_for<BN, EPI>();
   static_assert(ST >= 2, "stage ring");
   using S = Smem<BN, ST, EPI>;
@@ -740,27 +770,33 @@ cudaError_t launch_one(const CUtensorMap &ta, const CUtensorMap &tb, const CUten
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  const int grid = tiles < g_sms ? tiles : g_sms;
-  kfn<<<grid, kThreads, S::kBytes, s>>>(ta, tb, tc, tx, a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grp.tiles < g_sms ? grp.tiles : g_sms);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = S::kBytes;
+  cfg.stream = s;
+  // may start (set-up only) while the previous kernel in the stream ends
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kfn, maps, grp);
 }
 
 template <int BN>
-cudaError_t dispatch_bn(int kind, int epi, const CUtensorMap &ta, const CUtensorMap &tb,
-                        const CUtensorMap &tc, const CUtensorMap &tx, const TcArgs &a,
-                        int tiles, cudaStream_t s) {
+cudaError_t dispatch_bn(int kind, int epi, const TcMaps &maps, const TcGroup &grp,
+                        cudaStream_t s) {
   if (kind == 0) {  // forward
-    if (epi == EPI_BIAS_ELU)
-      return launch_one<BN, false, false, EPI_BIAS_ELU>(ta, tb, tc, tx, a, tiles, s);
-    if (epi == EPI_BIAS) return launch_one<BN, false, false, EPI_BIAS>(ta, tb, tc, tx, a, tiles, s);
-    return launch_one<BN, false, false, EPI_STORE>(ta, tb, tc, tx, a, tiles, s);
+    if (epi == EPI_BIAS_ELU) return launch_one<BN, false, false, EPI_BIAS_ELU>(maps, grp, s);
+    if (epi == EPI_BIAS) return launch_one<BN, false, false, EPI_BIAS>(maps, grp, s);
+    return launch_one<BN, false, false, EPI_STORE>(maps, grp, s);
   }
   if (kind == 1) {  // dgrad
-    if (epi == EPI_ELU_GRAD)
-      return launch_one<BN, false, true, EPI_ELU_GRAD>(ta, tb, tc, tx, a, tiles, s);
-    return launch_one<BN, false, true, EPI_STORE>(ta, tb, tc, tx, a, tiles, s);
+    if (epi == EPI_ELU_GRAD) return launch_one<BN, false, true, EPI_ELU_GRAD>(maps, grp, s);
+    return launch_one<BN, false, true, EPI_STORE>(maps, grp, s);
   }
-  return launch_one<BN, true, true, EPI_STORE>(ta, tb, tc, tx, a, tiles, s);  // wgrad
+  return launch_one<BN, true, true, EPI_STORE>(maps, grp, s);  // wgrad
 }
 
 }  // namespace
@@ -822,80 +858,118 @@ void GemmEngine::destroy() {
   err_dev = nullptr;
 }
 
-zrl_status gemm_tc(GemmEngine *eng, const GemmArgs &g, int precision, cudaStream_t s,
-                   int *launched, std::string *err) {
+static int layout_kind(const GemmArgs &g) {
+  if (!g.trans_a && g.trans_b) return 0;   // forward
+  if (!g.trans_a && !g.trans_b) return 1;  // dgrad
+  if (g.trans_a && !g.trans_b) return 2;   // wgrad
+  return -1;
+}
+
+zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precision,
+                         cudaStream_t s, int *launched, std::string *err) {
   *launched = 0;
   if (precision != ZRL_GEMM_TF32) {
     *err = "bf16 tensor-core GEMMs are not built in this library";
     return ZRL_NOT_SUPPORTED;
   }
-  int kind;
-  if (!g.trans_a && g.trans_b) kind = 0;
-  else if (!g.trans_a && !g.trans_b) kind = 1;
-  else if (g.trans_a && !g.trans_b) kind = 2;
-  else {
+  if (n < 1 || n > kMaxProbs) {
+    *err = "a grouped tensor-core GEMM takes 1 to 8 problems";
+    return ZRL_INVALID_ARG;
+  }
+  const int kind = layout_kind(gs[0]);
+  if (kind < 0) {
     *err = "unsupported operand layout for the tensor-core GEMM";
     return ZRL_NOT_SUPPORTED;
   }
-  // TMA needs 16-byte aligned bases and row pitches; the aux reads of the
-  // dgrad epilogue are vectorised.  Ragged M, N and K are handled
-  // (out-of-range TMA reads are zero-filled, stores are clipped).
-  auto a16 = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
-  if (g.lda % 4 || g.ldb % 4 || g.ldc % 4 || (g.aux && g.ldaux % 4) || !a16(g.A) ||
-      !a16(g.B) || !a16(g.C) || (g.aux && !a16(g.aux))) {
-    *err = "tensor-core GEMM needs 16-byte aligned operands and row pitches (multiples of 4)";
-    return ZRL_INVALID_ARG;
-  }
-  if (g.K <= 0) {
-    *err = "tensor-core GEMM with K = 0";
-    return ZRL_INVALID_ARG;
-  }
-  int split = g.split_k < 1 ? 1 : g.split_k;
-  if (g.colsum && split != 1) {
-    *err = "column sums are taken on unsplit GEMMs only";
-    return ZRL_INVALID_ARG;
+  int maxN = 0;
+  for (int i = 0; i < n; ++i) {
+    const GemmArgs &g = gs[i];
+    if (layout_kind(g) != kind || g.epi != gs[0].epi) {
+      *err = "the GEMMs of one group share operand layout and epilogue";
+      return ZRL_INVALID_ARG;
+    }
+    // TMA needs 16-byte aligned bases and row pitches.  Ragged M, N and K
+    // are handled (out-of-range TMA reads are zero-filled, stores clipped).
+    auto a16 = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
+    if (g.lda % 4 || g.ldb % 4 || g.ldc % 4 || (g.aux && g.ldaux % 4) || !a16(g.A) ||
+        !a16(g.B) || !a16(g.C) || (g.aux && !a16(g.aux))) {
+      *err = "tensor-core GEMM needs 16-byte aligned operands and row pitches (multiples of 4)";
+      return ZRL_INVALID_ARG;
+    }
+    if (g.M <= 0 || g.N <= 0 || g.K <= 0) {
+      *err = "tensor-core GEMM with an empty dimension";
+      return ZRL_INVALID_ARG;
+    }
+    if (g.colsum && g.split_k > 1) {
+      *err = "column sums are taken on unsplit GEMMs only";
+      return ZRL_INVALID_ARG;
+    }
+    if (kind == 1 && g.epi == EPI_ELU_GRAD && !g.aux) {
+      *err = "the ELU' epilogue needs the post-activation";
+      return ZRL_INVALID_ARG;
+    }
+    maxN = std::max(maxN, g.N);
   }
   // 128-column tiles from N = 128 up: at M = 24,576 rows that gives 2.6 to
-  // 5.2 tiles per SM, a better balance than 256-column tiles (1.3 to 2.6)
-  const int BN = g.N <= 32 ? 32 : (g.N <= 64 ? 64 : 128);
-  // A: [M rows, K cols] K-major, or [K rows, M cols] MN-major (wgrad)
-  const CUtensorMap *ta = kind == 2 ? cached_map(eng, g.A, g.K, g.M, g.lda, 32, 1, err)
-                                    : cached_map(eng, g.A, g.M, g.K, g.lda, BM, 0, err);
-  // B: [N rows, K cols] K-major (forward) or [K rows, N cols] MN-major
-  const CUtensorMap *tb = kind == 0 ? cached_map(eng, g.B, g.N, g.K, g.ldb, BN, 0, err)
-                                    : cached_map(eng, g.B, g.K, g.N, g.ldb, 32, 1, err);
-  const CUtensorMap *tc = cached_map(eng, g.C, g.M, g.N, g.ldc, split, 2, err);
-  if (!ta || !tb || !tc) return ZRL_CUDA_ERROR;
-  // dgrad: the post-activation read by the epilogue in [32 x 32] boxes
-  const bool aux_tma = kind == 1 && g.epi == EPI_ELU_GRAD;
-  const CUtensorMap *tx = aux_tma ? cached_map(eng, g.aux, g.M, g.N, g.ldaux, 32, 0, err) : tc;
-  if (!tx) return ZRL_CUDA_ERROR;
-  int kc = (g.K + split - 1) / split;
-  kc = (kc + 31) / 32 * 32;
-  TcArgs a{};
-  a.M = g.M;
-  a.N = g.N;
-  a.K = g.K;
-  a.kc = kc;
-  a.splits = split;
-  a.bias = g.bias;
-  a.aux = g.aux;
-  a.ldaux = g.ldaux;
-  a.round_out = g.round_out;
-  a.colsum = g.colsum;
-  a.err = eng->err_dev;
-  const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN) * split;
+  // 5.2 tiles per SM per GEMM, a better balance than 256-column tiles
+  const int BN = maxN <= 32 ? 32 : (maxN <= 64 ? 64 : 128);
+  TcMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  TcGroup grp;
+  memset(&grp, 0, sizeof(grp));
+  int tiles = 0;
+  for (int i = 0; i < n; ++i) {
+    const GemmArgs &g = gs[i];
+    const int split = g.split_k < 1 ? 1 : g.split_k;
+    // A: [M rows, K cols] K-major, or [K rows, M cols] MN-major (wgrad)
+    const CUtensorMap *ta = kind == 2 ? cached_map(eng, g.A, g.K, g.M, g.lda, 32, 1, err)
+                                      : cached_map(eng, g.A, g.M, g.K, g.lda, BM, 0, err);
+    // B: [N rows, K cols] K-major (forward) or [K rows, N cols] MN-major
+    const CUtensorMap *tb = kind == 0 ? cached_map(eng, g.B, g.N, g.K, g.ldb, BN, 0, err)
+                                      : cached_map(eng, g.B, g.K, g.N, g.ldb, 32, 1, err);
+    const CUtensorMap *tc = cached_map(eng, g.C, g.M, g.N, g.ldc, split, 2, err);
+    if (!ta || !tb || !tc) return ZRL_CUDA_ERROR;
+    maps.a[i] = *ta;
+    maps.b[i] = *tb;
+    maps.c[i] = *tc;
+    if (kind == 1 && g.epi == EPI_ELU_GRAD) {
+      // the post-activation read by the dgrad epilogue in [32 x 32] boxes
+      const CUtensorMap *tx = cached_map(eng, g.aux, g.M, g.N, g.ldaux, 32, 0, err);
+      if (!tx) return ZRL_CUDA_ERROR;
+      maps.x[i] = *tx;
+    }
+    TcProb &pr = grp.p[i];
+    pr.M = g.M;
+    pr.N = g.N;
+    pr.K = g.K;
+    pr.kc = ((g.K + split - 1) / split + 31) / 32 * 32;
+    pr.splits = split;
+    pr.tiles_m = (g.M + BM - 1) / BM;
+    pr.tiles_n = (g.N + BN - 1) / BN;
+    pr.tile0 = tiles;
+    pr.bias = g.bias;
+    pr.round_out = g.round_out;
+    pr.colsum = g.colsum;
+    tiles += pr.tiles_m * pr.tiles_n * split;
+  }
+  grp.n = n;
+  grp.tiles = tiles;
+  grp.err = eng->err_dev;
   cudaError_t e;
-  if (BN == 32) e = dispatch_bn<32>(kind, g.epi, *ta, *tb, *tc, *tx, a, tiles, s);
-  else if (BN == 64) e = dispatch_bn<64>(kind, g.epi, *ta, *tb, *tc, *tx, a, tiles, s);
-  else if (BN == 128) e = dispatch_bn<128>(kind, g.epi, *ta, *tb, *tc, *tx, a, tiles, s);
-  else e = dispatch_bn<256>(kind, g.epi, *ta, *tb, *tc, *tx, a, tiles, s);
+  if (BN == 32) e = dispatch_bn<32>(kind, gs[0].epi, maps, grp, s);
+  else if (BN == 64) e = dispatch_bn<64>(kind, gs[0].epi, maps, grp, s);
+  else e = dispatch_bn<128>(kind, gs[0].epi, maps, grp, s);
   if (e != cudaSuccess) {
     *err = std::string("tensor-core GEMM launch: ") + cudaGetErrorString(e);
     return ZRL_CUDA_ERROR;
   }
   *launched = 1;
   return ZRL_OK;
+}
+
+zrl_status gemm_tc(GemmEngine *eng, const GemmArgs &g, int precision, cudaStream_t s,
+                   int *launched, std::string *err) {
+  return gemm_tc_group(eng, &g, 1, precision, s, launched, err);
 }
 
 }  // namespace zrl

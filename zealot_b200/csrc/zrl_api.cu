@@ -351,107 +351,172 @@ static zrl_status run_gemm(zrl_ctx *ctx, const GemmArgs &g) {
   return ZRL_OK;
 }
 
-// Forward one net over `rows` rows of input x (pitch dp[0]); activations go
-// to ctx->act[k][1..L].
-static zrl_status forward_net(zrl_ctx *ctx, int k, const float *x, int64_t rows) {
+static GemmArgs fwd_args(zrl_ctx *ctx, int k, int l, const float *in, int64_t rows) {
   const NetLayout &L = ctx->net[k];
-  const float *in = x;
-  for (int l = 0; l < L.L; ++l) {
-    GemmArgs g{};
-    g.M = (int)rows;
-    g.N = L.dp[l + 1];
-    g.K = L.dp[l];
-    g.A = in;
-    g.lda = L.dp[l];
-    g.trans_a = false;
-    g.B = ctx->Wgemm() + L.w_off[l];
-    g.ldb = L.dp[l];
-    g.trans_b = true;
-    g.C = ctx->act[k][l + 1];
-    g.ldc = L.dp[l + 1];
-    g.epi = l < L.L - 1 ? EPI_BIAS_ELU : EPI_BIAS;
-    // hidden activations feed later GEMMs: store them tf32-rounded; the
-    // output layer (action mean / value) feeds the loss and stays fp32
-    g.round_out = ctx->tc() && l < L.L - 1;
-    g.bias = ctx->P + L.b_off[l];
-    g.split_k = 1;
-    TRY(run_gemm(ctx, g));
-    in = ctx->act[k][l + 1];
+  GemmArgs g{};
+  g.M = (int)rows;
+  g.N = L.dp[l + 1];
+  g.K = L.dp[l];
+  g.A = in;
+  g.lda = L.dp[l];
+  g.trans_a = false;
+  g.B = ctx->Wgemm() + L.w_off[l];
+  g.ldb = L.dp[l];
+  g.trans_b = true;
+  g.C = ctx->act[k][l + 1];
+  g.ldc = L.dp[l + 1];
+  g.epi = l < L.L - 1 ? EPI_BIAS_ELU : EPI_BIAS;
+  // hidden activations feed later GEMMs: store them tf32-rounded; the
+  // output layer (action mean / value) feeds the loss and stays fp32
+  g.round_out = ctx->tc() && l < L.L - 1;
+  g.bias = ctx->P + L.b_off[l];
+  g.split_k = 1;
+  return g;
+}
+
+static zrl_status run_group(zrl_ctx *ctx, const GemmArgs *gs, int n) {
+  if (n <= 0) return ZRL_OK;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (ctx->profiling) {
+    e0 = next_event(ctx);
+    cudaEventRecord(e0, ctx->stream);
+  }
+  int launched = 0;
+  zrl_status s = ctx->gemm.run_group(gs, n, ctx->precision, ctx->stream, &launched, &ctx->err);
+  if (s != ZRL_OK) return s;
+  ctx->launches += launched;
+  if (ctx->profiling) {
+    e1 = next_event(ctx);
+    cudaEventRecord(e1, ctx->stream);
+    ctx->prof_gemm_launches += launched;
+  }
+  CHECK_LAUNCH();
+  return ZRL_OK;
+}
+
+// Forward of both nets over `rows` rows (inputs xa, xc with pitch dp[0]):
+// layer l of the actor and of the critic run as one grouped launch when
+// they share the epilogue.
+static zrl_status forward_both(zrl_ctx *ctx, const float *xa, const float *xc, int64_t rows) {
+  const int maxL = std::max(ctx->net[0].L, ctx->net[1].L);
+  for (int l = 0; l < maxL; ++l) {
+    GemmArgs g[2];
+    int n = 0;
+    for (int k = 0; k < 2; ++k) {
+      if (l >= ctx->net[k].L) continue;
+      const float *in = l == 0 ? (k == 0 ? xa : xc) : ctx->act[k][l];
+      g[n++] = fwd_args(ctx, k, l, in, rows);
+    }
+    if (n == 2 && g[0].epi != g[1].epi) {
+      TRY(run_group(ctx, &g[0], 1));
+      TRY(run_group(ctx, &g[1], 1));
+    } else {
+      TRY(run_group(ctx, g, n));
+    }
   }
   return ZRL_OK;
 }
 
-// Backward of one net (net.rs:113-140 batched): wgrad split-K partials,
-// bias gradients, dgrad with the ELU' epilogue.  Bias gradients are column
-// sums of the deltas taken in fp32 where each delta is produced: the
-// output layer's in the loss kernel, a hidden layer's in the epilogue of
-// the tensor-core dgrad that produces it (a separate column-sum pass in the
-// CUDA-core mode).
-static zrl_status backward_net(zrl_ctx *ctx, int k, const float *x, int64_t rows,
-                               float **wp, float **bp, ReduceSegs &segs) {
+// Forward one net over `rows` rows of input x (pitch dp[0]); activations go
+// to ctx->act[k][1..L].
+static zrl_status forward_net(zrl_ctx *ctx, int k, const float *x, int64_t rows) {
   const NetLayout &L = ctx->net[k];
+  for (int l = 0; l < L.L; ++l) {
+    const GemmArgs g = fwd_args(ctx, k, l, l == 0 ? x : ctx->act[k][l], rows);
+    TRY(run_group(ctx, &g, 1));
+  }
+  return ZRL_OK;
+}
+
+// Backward of both nets (net.rs:113-140 batched).  The dgrad chain runs
+// level by level, actor and critic layer l in one launch, each with the
+// ELU' epilogue; then every weight gradient (split-K partials) of both
+// nets runs as grouped launches.  Bias gradients are column sums of the
+// deltas taken in fp32 where each delta is produced: the output layer's in
+// the loss kernel, a hidden layer's in the epilogue of the tensor-core
+// dgrad that produces it (a separate column-sum pass in the CUDA-core
+// mode).
+static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, int64_t rows,
+                                float **wp, float **bp, ReduceSegs &segs) {
   const int m_tiles = (int)((rows + 127) / 128);
-  for (int l = L.L - 1; l >= 0; --l) {
-    const float *a_in = l == 0 ? x : ctx->act[k][l];
-    const int S = wsplit_for(rows);
-    // dW_l = delta_l^T a_l
-    GemmArgs g{};
-    g.M = L.dp[l + 1];
-    g.N = L.dp[l];
-    g.K = (int)rows;
-    g.A = ctx->dlt[k][l];
-    g.lda = L.dp[l + 1];
-    g.trans_a = true;
-    g.B = a_in;
-    g.ldb = L.dp[l];
-    g.trans_b = false;
-    g.C = *wp;
-    g.ldc = L.dp[l];
-    g.epi = EPI_STORE;
-    g.split_k = S;
-    TRY(run_gemm(ctx, g));
-    ReduceSeg sw{ctx->G + L.w_off[l], *wp, (int64_t)L.dp[l + 1] * L.dp[l], S};
-    segs.seg[segs.n++] = sw;
-    *wp += (int64_t)S * L.dp[l + 1] * L.dp[l];
-    if (l < L.L - 1 && !ctx->tc()) {
-      // db_l = column sums of delta_l (CUDA-core mode)
-      const int Sb = S;
-      launch_colsum(ctx->dlt[k][l], rows, L.dp[l + 1], L.dp[l + 1], *bp, Sb, ctx->stream);
-      ctx->launches++;
-      CHECK_LAUNCH();
-      ReduceSeg sb{ctx->G + L.b_off[l], *bp, (int64_t)L.dp[l + 1], Sb};
-      segs.seg[segs.n++] = sb;
-      *bp += (int64_t)Sb * L.dp[l + 1];
-    }
-    if (l > 0) {
+  const int maxL = std::max(ctx->net[0].L, ctx->net[1].L);
+  for (int l = maxL - 1; l >= 1; --l) {
+    GemmArgs d[2];
+    int n = 0;
+    for (int k = 0; k < 2; ++k) {
+      const NetLayout &L = ctx->net[k];
+      if (l >= L.L) continue;
       // delta_{l-1} = (delta_l W_l) * elu'(a_l)
-      GemmArgs d{};
-      d.M = (int)rows;
-      d.N = L.dp[l];
-      d.K = L.dp[l + 1];
-      d.A = ctx->dlt[k][l];
-      d.lda = L.dp[l + 1];
-      d.trans_a = false;
-      d.B = ctx->Wgemm() + L.w_off[l];
-      d.round_out = ctx->tc();
-      d.ldb = L.dp[l];
-      d.trans_b = false;
-      d.C = ctx->dlt[k][l - 1];
-      d.ldc = L.dp[l];
-      d.epi = EPI_ELU_GRAD;
-      d.aux = ctx->act[k][l];
-      d.ldaux = L.dp[l];
-      d.split_k = 1;
+      GemmArgs &g = d[n++];
+      g = GemmArgs{};
+      g.M = (int)rows;
+      g.N = L.dp[l];
+      g.K = L.dp[l + 1];
+      g.A = ctx->dlt[k][l];
+      g.lda = L.dp[l + 1];
+      g.trans_a = false;
+      g.B = ctx->Wgemm() + L.w_off[l];
+      g.round_out = ctx->tc();
+      g.ldb = L.dp[l];
+      g.trans_b = false;
+      g.C = ctx->dlt[k][l - 1];
+      g.ldc = L.dp[l];
+      g.epi = EPI_ELU_GRAD;
+      g.aux = ctx->act[k][l];
+      g.ldaux = L.dp[l];
+      g.split_k = 1;
       if (ctx->tc()) {
         // db_{l-1}: per-tile column sums of delta_{l-1} from the epilogue
-        d.colsum = *bp;
+        g.colsum = *bp;
         ReduceSeg sb{ctx->G + L.b_off[l - 1], *bp, (int64_t)L.dp[l], m_tiles};
         segs.seg[segs.n++] = sb;
         *bp += (int64_t)m_tiles * L.dp[l];
       }
-      TRY(run_gemm(ctx, d));
+    }
+    TRY(run_group(ctx, d, n));
+  }
+  const int S = wsplit_for(rows);
+  if (!ctx->tc()) {
+    // db_l = column sums of delta_l for the hidden layers (CUDA-core mode)
+    for (int k = 0; k < 2; ++k) {
+      const NetLayout &L = ctx->net[k];
+      for (int l = 0; l < L.L - 1; ++l) {
+        launch_colsum(ctx->dlt[k][l], rows, L.dp[l + 1], L.dp[l + 1], *bp, S, ctx->stream);
+        ctx->launches++;
+        CHECK_LAUNCH();
+        ReduceSeg sb{ctx->G + L.b_off[l], *bp, (int64_t)L.dp[l + 1], S};
+        segs.seg[segs.n++] = sb;
+        *bp += (int64_t)S * L.dp[l + 1];
+      }
     }
   }
+  // dW_l = delta_l^T a_l for every layer of both nets
+  GemmArgs w[2 * ZRL_MAX_LAYERS];
+  int nw = 0;
+  for (int k = 0; k < 2; ++k) {
+    const NetLayout &L = ctx->net[k];
+    for (int l = L.L - 1; l >= 0; --l) {
+      GemmArgs &g = w[nw++];
+      g = GemmArgs{};
+      g.M = L.dp[l + 1];
+      g.N = L.dp[l];
+      g.K = (int)rows;
+      g.A = ctx->dlt[k][l];
+      g.lda = L.dp[l + 1];
+      g.trans_a = true;
+      g.B = l == 0 ? (k == 0 ? xa : xc) : ctx->act[k][l];
+      g.ldb = L.dp[l];
+      g.trans_b = false;
+      g.C = *wp;
+      g.ldc = L.dp[l];
+      g.epi = EPI_STORE;
+      g.split_k = S;
+      ReduceSeg sw{ctx->G + L.w_off[l], *wp, (int64_t)L.dp[l + 1] * L.dp[l], S};
+      segs.seg[segs.n++] = sw;
+      *wp += (int64_t)S * L.dp[l + 1] * L.dp[l];
+    }
+  }
+  for (int i = 0; i < nw; i += 8) TRY(run_group(ctx, w + i, std::min(8, nw - i)));
   return ZRL_OK;
 }
 
@@ -466,10 +531,7 @@ struct MbView {
 static zrl_status minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
                                   const MbView &v, float scale) {
   TRY(ensure_mb(ctx, std::max<int64_t>(v.rows, 1)));
-  if (v.rows > 0) {
-    TRY(forward_net(ctx, 0, v.xa, v.rows));
-    TRY(forward_net(ctx, 1, v.xc, v.rows));
-  }
+  if (v.rows > 0) TRY(forward_both(ctx, v.xa, v.xc, v.rows));
   const NetLayout &La = ctx->net[0], &Lc = ctx->net[1];
   LossArgs la{};
   la.mean = ctx->act[0][La.L];
@@ -508,8 +570,7 @@ static zrl_status minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
   }
   float *wp = ctx->wpart, *bp = ctx->bpart;
   ReduceSegs segs{};
-  TRY(backward_net(ctx, 0, v.xa, v.rows, &wp, &bp, segs));
-  TRY(backward_net(ctx, 1, v.xc, v.rows, &wp, &bp, segs));
+  TRY(backward_both(ctx, v.xa, v.xc, v.rows, &wp, &bp, segs));
   launch_reduce_segments(segs, ctx->stream);
   ctx->launches++;
   CHECK_LAUNCH();

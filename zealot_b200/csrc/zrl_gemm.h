@@ -17,6 +17,9 @@ struct GemmEngine;
 // Tensor-core GEMM (gemm_tc.cu).  *launched receives the kernel count.
 zrl_status gemm_tc(GemmEngine *eng, const GemmArgs &g, int precision, cudaStream_t s,
                    int *launched, std::string *err);
+// n GEMMs (1..8) of one operand layout and epilogue in one launch.
+zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precision,
+                         cudaStream_t s, int *launched, std::string *err);
 zrl_status gemm_tc_init(int device, std::string *err);
 
 struct GemmEngine {
@@ -42,6 +45,27 @@ struct GemmEngine {
       tc_ready = true;
     }
     return gemm_tc(this, g, precision, s, launched, err);
+  }
+
+  // Several GEMMs of one layout and epilogue: one grouped launch on the
+  // tensor cores, one launch each on the CUDA cores.
+  zrl_status run_group(const GemmArgs *gs, int n, int precision, cudaStream_t s,
+                       int *launched, std::string *err) {
+    *launched = 0;
+    if (precision == ZRL_GEMM_FP32) {
+      for (int i = 0; i < n; ++i) {
+        if (gs[i].M <= 0 || gs[i].N <= 0) continue;
+        gemm_simt(gs[i], s);
+        ++*launched;
+      }
+      return ZRL_OK;
+    }
+    if (!tc_ready) {
+      zrl_status st = gemm_tc_init(0, err);
+      if (st != ZRL_OK) return st;
+      tc_ready = true;
+    }
+    return gemm_tc_group(this, gs, n, precision, s, launched, err);
   }
 };
 
