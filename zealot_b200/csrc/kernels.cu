@@ -316,41 +316,57 @@ loss_kernel(LossArgs a, float *partials, unsigned int *ticket) {
   float acc_surr = 0.0f, acc_vloss = 0.0f, acc_kl = 0.0f, acc_gv = 0.0f;
   const float lo = 1.0f - a.clip, hi = 1.0f + a.clip;
   const float ent_term = -a.entropy_coef * a.scale;
+  // The loads of one sample: its action-dimension rows by lane (4 per lane
+  // for A <= 128) and the five per-sample scalars by lanes 0-4.  The warp
+  // walks its samples with the next sample's loads in flight while the
+  // current one is computed.
+  struct Row {
+    float mu[4], ac[4], mo[4], scal;
+  };
+  auto fetch = [&](int64_t s, Row &r) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int k = lane + 32 * j;
+      r.mu[j] = r.ac[j] = r.mo[j] = 0.0f;
+      if (k < A) {
+        r.mu[j] = a.mean[s * a.Ap + k];
+        r.ac[j] = a.action[s * A + k];
+        r.mo[j] = a.mean_old[s * A + k];
+      }
+    }
+    r.scal = 0.0f;
+    if (lane == 0) r.scal = a.logp_old[s];
+    else if (lane == 1) r.scal = a.adv[s];
+    else if (lane == 2) r.scal = a.value[s * a.cp];
+    else if (lane == 3) r.scal = a.value_old[s];
+    else if (lane == 4) r.scal = a.ret[s];
+  };
+  Row nxt;
+  if (gw < a.mb) fetch(gw, nxt);
   for (int64_t s = gw; s < a.mb; s += nw) {
-    const float *mu = a.mean + s * a.Ap;
-    const float *ac = a.action + s * A;
-    const float *mo = a.mean_old + s * A;
-    // the five per-sample scalars, one per lane, loaded together with the
-    // action rows below (one memory round trip per sample)
-    float scal = 0.0f;
-    if (lane == 0) scal = a.logp_old[s];
-    else if (lane == 1) scal = a.adv[s];
-    else if (lane == 2) scal = a.value[s * a.cp];
-    else if (lane == 3) scal = a.value_old[s];
-    else if (lane == 4) scal = a.ret[s];
-    float mu_r[4], d_r[4];
+    const Row cur = nxt;
+    if (s + nw < a.mb) fetch(s + nw, nxt);
+    float d_r[4];
     float lp = 0.0f, kl = 0.0f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int k = lane + 32 * j;
-      mu_r[j] = 0.0f;
       d_r[j] = 0.0f;
       if (k < A) {
-        mu_r[j] = mu[k];
-        d_r[j] = ac[k] - mu_r[j];
+        d_r[j] = cur.ac[j] - cur.mu[j];
         const float z = d_r[j] / sd[j];
         lp += -0.5f * z * z - ls[j] - kLogSqrt2Pi;
-        const float dk = (mu_r[j] - mo[k]) * inv_sd[j];
+        const float dk = (cur.mu[j] - cur.mo[j]) * inv_sd[j];
         kl += 0.5f * (dk * dk);
       }
     }
     lp = warp_sum(lp);
     kl = warp_sum(kl);
-    const float ratio = expf(lp - __shfl_sync(0xffffffffu, scal, 0));
-    const float adv = __shfl_sync(0xffffffffu, scal, 1);
-    const float v = __shfl_sync(0xffffffffu, scal, 2);
-    const float vo = __shfl_sync(0xffffffffu, scal, 3);
-    const float R = __shfl_sync(0xffffffffu, scal, 4);
+    const float ratio = expf(lp - __shfl_sync(0xffffffffu, cur.scal, 0));
+    const float adv = __shfl_sync(0xffffffffu, cur.scal, 1);
+    const float v = __shfl_sync(0xffffffffu, cur.scal, 2);
+    const float vo = __shfl_sync(0xffffffffu, cur.scal, 3);
+    const float R = __shfl_sync(0xffffffffu, cur.scal, 4);
     const float rc = fminf(fmaxf(ratio, lo), hi);
     const float surr = fminf(ratio * adv, rc * adv);
     const bool clipped = (adv >= 0.0f && ratio > hi) || (adv < 0.0f && ratio < lo);
@@ -421,22 +437,32 @@ loss_kernel(LossArgs a, float *partials, unsigned int *ticket) {
   __syncthreads();
   if (!last) return;
   __threadfence();
-  // one warp per column: lanes take strided block partials (independent
-  // loads), then a fixed-order warp sum -- deterministic and short
-  for (int c = wid; c < width; c += nwb) {
+  // thread (c, grp) sums the partial rows grp, grp+4, ... of column c
+  // (independent loads, eight in flight), then the four group sums are
+  // added in group order -- a fixed order, deterministic
+  __shared__ float red[4][64];
+  const int cc = threadIdx.x & 63, grp = threadIdx.x >> 6;
+  for (int c0 = 0; c0 < width; c0 += 64) {
+    const int c = c0 + cc;
     float t = 0.0f;
-    for (int b = lane; b < (int)gridDim.x; b += 32)
-      t += __ldcg(&partials[(int64_t)b * width + c]);
-    t = warp_sum(t);
-    if (lane != 0) continue;
-    if (c < A)
-      a.g_logstd[c] = t;
-    else if (c < 2 * A)
-      a.db_actor[c - A] = t;
-    else if (c < 2 * A + 3)
-      a.sums3[c - 2 * A] = t;
-    else
-      a.db_critic[0] = t;
+    if (c < width) {
+#pragma unroll 8
+      for (int b = grp; b < (int)gridDim.x; b += 4) t += __ldcg(&partials[(int64_t)b * width + c]);
+    }
+    red[grp][cc] = t;
+    __syncthreads();
+    if (grp == 0 && c < width) {
+      t = ((red[0][cc] + red[1][cc]) + red[2][cc]) + red[3][cc];
+      if (c < A)
+        a.g_logstd[c] = t;
+      else if (c < 2 * A)
+        a.db_actor[c - A] = t;
+      else if (c < 2 * A + 3)
+        a.sums3[c - 2 * A] = t;
+      else
+        a.db_critic[0] = t;
+    }
+    __syncthreads();
   }
   if (threadIdx.x == 0) *ticket = 0u;
 }
@@ -557,16 +583,17 @@ prestep_kernel(PrestepArgs a, double *partials, unsigned int *ticket) {
   __syncthreads();
   if (threadIdx.x == 0) last = atomicAdd(ticket, 1u) == gridDim.x - 1;
   __syncthreads();
-  if (!last || threadIdx.x >= 32) return;
+  if (!last) return;
   __threadfence();
-  // warp 0: lanes take strided block partials, fixed-order warp sum
+  // the whole last block: thread b takes block partials b, b + blockDim,
+  // ..., then the fixed-order block sum
   double na = 0.0, nc = 0.0;
-  for (int b = threadIdx.x; b < (int)gridDim.x; b += 32) {
+  for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) {
     na += __ldcg(&partials[2 * b]);
     nc += __ldcg(&partials[2 * b + 1]);
   }
-  na = warp_sum_d(na);
-  nc = warp_sum_d(nc);
+  na = block_sum(na, sh);
+  nc = block_sum(nc, sh);
   if (threadIdx.x != 0) return;
   *ticket = 0u;
   DevState *st = a.st;
@@ -843,10 +870,10 @@ void launch_round_copy(const float *src, float *dst, int64_t n, cudaStream_t s) 
 }
 
 void launch_loss(const LossArgs &a, ReduceScratch &rs, cudaStream_t s) {
-  // four blocks per SM, a few samples per warp (latency-bound per
-  // sample); the last block's ordered sum over the block partials is one
-  // warp per column with strided loads
-  int blocks = grid_for(a.mb * 32, kLossThreads, 4 * 148);
+  // one block per SM: each warp walks its samples with the next sample's
+  // loads in flight, and the last block's sum over the block partials
+  // stays short
+  int blocks = grid_for(a.mb * 32, kLossThreads, 148);
   if (blocks > rs.max_blocks) blocks = rs.max_blocks;
   if ((2 * a.A + 4) > rs.fwidth) blocks = 0;  // caller sized fwidth >= 2A + 4
   if (blocks > 0)
@@ -868,7 +895,7 @@ void launch_reduce_segments(const ReduceSegs &segs, cudaStream_t s) {
 
 void launch_prestep(const PrestepArgs &a, ReduceScratch &rs, cudaStream_t s) {
   const int64_t work = (a.actor_end - a.actor_begin);
-  int blocks = grid_for(work, kPrestepThreads, 4 * 148);
+  int blocks = grid_for(work, kPrestepThreads, 148);
   if (blocks > rs.max_blocks) blocks = rs.max_blocks;
   prestep_kernel<<<blocks, kPrestepThreads, 0, s>>>(a, rs.dpart, rs.ticket + 1);
 }
