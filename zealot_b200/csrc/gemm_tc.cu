@@ -35,6 +35,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <climits>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -146,6 +147,12 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map,
       : "memory");
 }
 
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"((uint64_t)map),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *src,
                                              int x, int y, int z) {
   asm volatile(
@@ -166,13 +173,24 @@ __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+__device__ __forceinline__ void st_shared4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+__device__ __forceinline__ float4 ld_shared4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-__device__ __forceinline__ void named_bar_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)m) : "memory");
@@ -244,6 +262,59 @@ __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b
       : "memory");
 }
 
+// The CTA pair (cta_group::2): a cluster of two CTAs on two SMs whose
+// tensor cores act as one, with M = 256 rows -- 128 in each CTA's TMEM --
+// and the B tile split by columns between the two CTAs' shared memory.
+// The even CTA issues the MMAs.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// The shared::cluster address of this CTA's shared-memory offset `addr` in
+// the CTA of rank `rank`.
+__device__ __forceinline__ uint32_t peer_addr(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+// TMA load into this CTA's shared memory whose completion is counted on the
+// mbarrier at cluster address `bar` (the even CTA's, for the pair).
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, uint32_t bar,
+                                                 int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void mma_tf32_pair(uint32_t tmem_d, uint64_t a, uint64_t b,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Completion of the pair's MMAs arrives on the mbarrier at this offset in
+// both CTAs.
+__device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar)
+               : "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -266,10 +337,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// min(a, b) that returns NaN when either input is NaN
+__device__ __forceinline__ float fmin_nan(float a, float b) {
+  float r;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// Round to the tf32 grid (10 mantissa bits), to nearest with ties away
+// from zero, as cvt.rna.tf32.f32 does for every non-NaN input: add half a
+// tf32 ulp to the magnitude bits, then clear the 13 low bits (a carry into
+// the exponent is the correct round-up, to infinity past the largest value).
 __device__ __forceinline__ float round_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
 // e^x = 2^(x log2 e) with one ex2.approx: relative error about 2^-22 plus
@@ -280,48 +360,31 @@ __device__ __forceinline__ float exp_sfu(float x) {
   return y;
 }
 
-// Column sums of a [32 x 32] chunk held one row per lane: five butterfly
-// steps, each exchanging half of the remaining columns with the partner
-// lane, leave the sum of column `lane` in lane `lane` (a fixed summation
-// tree, so the same bits every run).
-__device__ __forceinline__ float colsum32(const float (&v)[32], int lane) {
-  float w[16];
-  {
-    const bool up = lane & 16;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float send = up ? v[i] : v[i + 16];
-      const float keep = up ? v[i + 16] : v[i];
-      w[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-    }
-  }
-#pragma unroll
-  for (int h = 8; h >= 1; h >>= 1) {
-    const bool up = lane & h;
-#pragma unroll
-    for (int i = 0; i < h; ++i) {
-      const float send = up ? w[i] : w[i + h];
-      const float keep = up ? w[i + h] : w[i];
-      w[i] = keep + __shfl_xor_sync(0xffffffffu, send, h);
-    }
-  }
-  return w[0];
-}
-
 // One GEMM of a grouped launch.  A launch runs up to kMaxProbs GEMMs of
 // one kind and epilogue (e.g. the same layer of the actor and the critic,
 // or every weight gradient of both nets) as one flat tile space, problem
 // after problem.
 constexpr int kMaxProbs = 8;
+// n / d for 0 <= n < 2^31 as (umulhi(n, mul) + n) >> shift (Granlund and
+// Montgomery's division by invariant integers; the host picks mul, shift).
+struct FastDiv {
+  uint32_t d, mul, shift;
+};
+__device__ __forceinline__ int fdiv(int n, const FastDiv &f) {
+  return (int)((__umulhi((uint32_t)n, f.mul) + (uint32_t)n) >> f.shift);
+}
+
 struct TcProb {
   int M, N, K;
   int kc;          // K per split (multiple of 32); split z covers [z*kc, ...)
   int splits;
   int tiles_m, tiles_n;
+  FastDiv div_m, div_n;  // by tiles_m, by tiles_n
   int tile0;       // first flat tile index of this problem
   const float *bias;
   int round_out;
-  float *colsum;   // optional per-m-tile column sums [tiles_m][N] (no split-K)
+  float *colsum;   // optional column sums per 32-row quarter of each 128-row
+                   // block: [ceil(M / 128) * 4][N] (no split-K)
 };
 struct TcGroup {
   TcProb p[kMaxProbs];
@@ -335,21 +398,24 @@ struct TcMaps {
   CUtensorMap a[kMaxProbs], b[kMaxProbs], c[kMaxProbs], x[kMaxProbs];
 };
 
-// Staging slots per epilogue warp, each one [32 x 32] fp32 box: one for the
-// output; two for the dgrad epilogue, whose slots also receive the
-// TMA-loaded post-activation one chunk ahead.
-constexpr int slots_for(int epi) { return epi == EPI_ELU_GRAD ? 2 : 1; }
+// Staging slots per epilogue warp, each one [32 x 32] fp32 box: two, so a
+// chunk is staged while the previous chunk's store still reads its slot;
+// in the dgrad epilogue a slot first receives the chunk's TMA-loaded
+// post-activation (one chunk ahead).
+constexpr int slots_for(int) { return 2; }
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, int EPI, int CG>
 struct Smem {
   static constexpr int kA = BM * BKB;                 // 16 KB
-  static constexpr int kB = BN * BKB;                 // BN * 128 B
+  static constexpr int kB = BN / CG * BKB;            // this CTA's B columns * 128 B
   static constexpr int kStage = kA + kB;
   static constexpr int kStageBytes = STAGES * kStage;
   static constexpr int kSlots = slots_for(EPI);
   static constexpr int kStaging = kEpiWarps * kSlots * 4096;
-  static constexpr int kRed = 4 * BN * 4;             // column sums per lane quarter
-  static constexpr int kBarOff = kStageBytes + kStaging + kRed;
+  // the bias of a warp's chunks in the current tile
+  static constexpr int kCptMax = BN >= 64 ? BN / 64 : 1;
+  static constexpr int kBias = kEpiWarps * kCptMax * 32 * 4;
+  static constexpr int kBarOff = kStageBytes + kStaging + kBias;
   // full, empty, acc_full x2, acc_empty x2, one aux barrier per staging slot
   static constexpr int kBars = 2 * STAGES + 4 + kEpiWarps * kSlots;
   static constexpr int kBytes = 1024 /*align*/ + kBarOff + kBars * 8 + 16;
@@ -359,8 +425,9 @@ struct Tile {
   int p, m0, n0, z, kbeg, nk;
 };
 
-// Flat tile t -> problem, then m fastest, n, split.
-template <int BN>
+// Flat tile t -> problem, then m fastest, n, split.  Tiles are BM * CG
+// rows (the CTA pair's tile: 256 rows).
+template <int BN, int CG>
 __device__ __forceinline__ Tile decode_tile(int t, const TcGroup &g) {
   Tile tl;
   int p = 0;
@@ -368,22 +435,118 @@ __device__ __forceinline__ Tile decode_tile(int t, const TcGroup &g) {
   const TcProb &pr = g.p[p];
   const int lt = t - pr.tile0;
   tl.p = p;
-  const int mt = lt % pr.tiles_m;
-  const int rest = lt / pr.tiles_m;
-  tl.m0 = mt * BM;
-  tl.n0 = (rest % pr.tiles_n) * BN;
-  tl.z = rest / pr.tiles_n;
+  const int rest = fdiv(lt, pr.div_m);
+  const int mt = lt - rest * pr.tiles_m;
+  const int z = fdiv(rest, pr.div_n);
+  tl.m0 = mt * BM * CG;
+  tl.n0 = (rest - z * pr.tiles_n) * BN;
+  tl.z = z;
   tl.kbeg = tl.z * pr.kc;
   const int kend = min(pr.K, tl.kbeg + pr.kc);
   tl.nk = kend > tl.kbeg ? (kend - tl.kbeg + 31) / 32 : 0;
   return tl;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, int STAGES>
+// One 32 x 32 chunk of the epilogue for one warp (lane = row): TMEM ->
+// registers, the epilogue function, the optional column sums, rounding,
+// and the 128B-swizzled staging for the TMA store.
+struct EpiChunk {
+  uint32_t taddr;    // TMEM address of the chunk (0xFFFFFFFF: accumulator not written)
+  uint32_t slot;     // shared address of this lane's row in the staging slot
+  uint32_t sw;       // swizzle phase of the row (lane & 7)
+  uint32_t bias;     // shared address of the chunk's 32 bias values
+  int round;         // round the stored values to tf32
+  float *colsum;     // this quarter's partial row at the chunk's first column
+};
+
+template <int EPI, bool FULL, typename Release>
+__device__ __forceinline__ void epi_chunk(const EpiChunk &e, int lane, bool last,
+                                          Release release, bool row_ok, int valid_cols) {
+  float v[32];
+  if (!FULL && e.taddr == 0xFFFFFFFFu) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+  } else {
+    uint32_t r[32];
+    tmem_ld32(e.taddr, r);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+    // last read of this accumulator: hand it back to the MMA warp
+    if (last) release();
+  }
+  if (EPI == EPI_BIAS || EPI == EPI_BIAS_ELU) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 b = ld_shared4(e.bias + 16u * q);  // broadcast
+      v[4 * q + 0] += b.x;
+      v[4 * q + 1] += b.y;
+      v[4 * q + 2] += b.z;
+      v[4 * q + 3] += b.w;
+    }
+  }
+  if (EPI == EPI_BIAS_ELU) {
+    // ELU (net.rs:13-16); exp on the special-function unit, whose error is
+    // far below the tf32 rounding applied next
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = v[i] > 0.0f ? v[i] : exp_sfu(v[i]) - 1.0f;
+  }
+  if (EPI == EPI_ELU_GRAD) {
+    // ELU' from the stored post-activation y in the slot (net.rs:19-22):
+    // 1 for y > 0, else y + 1 = min(y + 1, 1) (NaN kept)
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 y = ld_shared4(e.slot + ((q ^ e.sw) << 4));
+      v[4 * q + 0] *= fmin_nan(y.x + 1.0f, 1.0f);
+      v[4 * q + 1] *= fmin_nan(y.y + 1.0f, 1.0f);
+      v[4 * q + 2] *= fmin_nan(y.z + 1.0f, 1.0f);
+      v[4 * q + 3] *= fmin_nan(y.w + 1.0f, 1.0f);
+    }
+  }
+  if (!FULL) {
+    // invalid rows and columns hold 0 (column sums; the store clips them)
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (!row_ok || i >= valid_cols) v[i] = 0.0f;
+  }
+  if (e.colsum) {
+    // bias gradient: column sums of the unrounded chunk, staged first;
+    // lane j then adds column j over the 32 rows in row order
+    // (conflict-free: row r's 16-byte piece q sits at q ^ (r & 7))
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      st_shared4(e.slot + ((q ^ e.sw) << 4), v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    __syncwarp();
+    const uint32_t base = e.slot - (uint32_t)lane * 128u;
+    const uint32_t q = (uint32_t)lane >> 2, w = ((uint32_t)lane & 3u) * 4u;
+    float cs = 0.0f;
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      float x;
+      asm volatile("ld.shared.f32 %0, [%1];"
+                   : "=f"(x)
+                   : "r"(base + r * 128u + (((q ^ (uint32_t)(r & 7))) << 4) + w)
+                   : "memory");
+      cs += x;
+    }
+    if (lane < valid_cols) e.colsum[lane] = cs;
+    __syncwarp();
+  }
+  if (e.round) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = round_tf32(v[i]);
+  }
+  // stage for the TMA store
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    st_shared4(e.slot + ((q ^ e.sw) << 4), v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI, int STAGES, int CG>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGroup g) {
   static_assert(BN == 32 || BN == 64 || BN == 128 || BN == 256, "BN");
-  using S = Smem<BN, STAGES, EPI>;
+  static_assert(CG == 1 || (CG == 2 && BN >= 64), "a CTA pair splits B in 32-column boxes");
+  using S = Smem<BN, STAGES, EPI, CG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t *full = (uint64_t *)(smem + S::kBarOff);
@@ -392,10 +555,14 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
   uint64_t *acce = accf + 2;        // [2]
   uint64_t *xbar = acce + 2;        // [kEpiWarps][kSlots]
   uint32_t *tmem_slot = (uint32_t *)(xbar + kEpiWarps * S::kSlots);
-  float *red = (float *)(smem + S::kStageBytes + S::kStaging);
+  float *bias_sh = (float *)(smem + S::kStageBytes + S::kStaging);  // [kEpiWarps][kCptMax][32]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles = g.tiles;
+  // CTA pairs walk the tiles together: pair index, pair count, rank
+  const uint32_t rank = CG == 2 ? cluster_rank() : 0u;
+  const int unit = CG == 2 ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int units = CG == 2 ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -404,7 +571,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], kEpiWarps);
+      mbar_init(&acce[b], CG * kEpiWarps);  // the pair's epilogue warps
     }
     for (int b = 0; b < kEpiWarps * S::kSlots; ++b) mbar_init(&xbar[b], 1);
     fence_barrier_init();
@@ -417,15 +584,27 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
       if (EPI == EPI_ELU_GRAD) prefetch_tmap(&maps.x[lane]);
     }
     __syncwarp();
-    // TMEM: two BN-column fp32 accumulators of 128 lanes
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
-                 "r"((uint32_t)(2 * BN))
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    // TMEM: two BN-column fp32 accumulators of 128 lanes (per CTA; for the
+    // pair one warp of each CTA allocates jointly)
+    if (CG == 2) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(tmem_slot)),
+                   "r"((uint32_t)(2 * BN))
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(tmem_slot)),
+                   "r"((uint32_t)(2 * BN))
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if (CG == 2)
+    cluster_sync();  // both CTAs' barriers initialised before any remote arrive
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   // programmatic dependent launch: the set-up above overlapped the previous
@@ -439,8 +618,11 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
     if (lane == 0) {
       int kbg = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        const Tile tl = decode_tile<BN>(t, g);
+      for (int t = unit; t < tiles && ok; t += units) {
+        const Tile tl = decode_tile<BN, CG>(t, g);
+        // this CTA's rows of A and columns of B
+        const int am = tl.m0 + BM * (int)rank;
+        const int bn = tl.n0 + BN / CG * (int)rank;
         for (int kb = 0; kb < tl.nk; ++kb, ++kbg) {
           const int s = kbg % STAGES;
           const uint32_t ph = (uint32_t)(kbg / STAGES) & 1u;
@@ -448,32 +630,52 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
           uint8_t *a_s = smem + s * S::kStage;
           uint8_t *b_s = a_s + S::kA;
           const int k0 = tl.kbeg + kb * 32;
-          mbar_expect_tx(&full[s], S::kStage);
-          if (A_MN) {  // Delta [K rows, M cols]: four 32-column boxes of 32 rows
+          if (CG == 2) {
+            // both CTAs' boxes count on the even CTA's full barrier
+            const uint32_t fb = peer_addr(smem_u32(&full[s]), 0);
+            if (rank == 0) mbar_expect_tx(&full[s], 2 * S::kStage);
+            if (A_MN) {
 #pragma unroll
-            for (int c = 0; c < BM / 32; ++c)
-              tma_load_2d(a_s + c * 4096, &maps.a[tl.p], &full[s], tl.m0 + 32 * c, k0);
-          } else {     // [M rows, K cols]: one box of 128 rows x 32
-            tma_load_2d(a_s, &maps.a[tl.p], &full[s], k0, tl.m0);
-          }
-          if (B_MN) {
+              for (int c = 0; c < BM / 32; ++c)
+                tma_load_2d_pair(a_s + c * 4096, &maps.a[tl.p], fb, am + 32 * c, k0);
+            } else {
+              tma_load_2d_pair(a_s, &maps.a[tl.p], fb, k0, am);
+            }
+            if (B_MN) {
 #pragma unroll
-            for (int c = 0; c < BN / 32; ++c)
-              tma_load_2d(b_s + c * 4096, &maps.b[tl.p], &full[s], tl.n0 + 32 * c, k0);
+              for (int c = 0; c < BN / CG / 32; ++c)
+                tma_load_2d_pair(b_s + c * 4096, &maps.b[tl.p], fb, bn + 32 * c, k0);
+            } else {
+              tma_load_2d_pair(b_s, &maps.b[tl.p], fb, k0, bn);
+            }
           } else {
-            tma_load_2d(b_s, &maps.b[tl.p], &full[s], k0, tl.n0);
+            mbar_expect_tx(&full[s], S::kStage);
+            if (A_MN) {  // Delta [K rows, M cols]: four 32-column boxes of 32 rows
+#pragma unroll
+              for (int c = 0; c < BM / 32; ++c)
+                tma_load_2d(a_s + c * 4096, &maps.a[tl.p], &full[s], am + 32 * c, k0);
+            } else {     // [M rows, K cols]: one box of 128 rows x 32
+              tma_load_2d(a_s, &maps.a[tl.p], &full[s], k0, am);
+            }
+            if (B_MN) {
+#pragma unroll
+              for (int c = 0; c < BN / 32; ++c)
+                tma_load_2d(b_s + c * 4096, &maps.b[tl.p], &full[s], bn + 32 * c, k0);
+            } else {
+              tma_load_2d(b_s, &maps.b[tl.p], &full[s], k0, bn);
+            }
           }
         }
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_tf32(BM * CG, BN, A_MN, B_MN);
       int kbg = 0, it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
-        const Tile tl = decode_tile<BN>(t, g);
+      for (int t = unit; t < tiles && ok; t += units, ++it) {
+        const Tile tl = decode_tile<BN, CG>(t, g);
         const int ab = it & 1;
         const uint32_t aph = (uint32_t)(it >> 1) & 1u;
         // the epilogue must have drained this accumulator (tile it-2)
@@ -493,203 +695,208 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
             // K-rows (1024 bytes) further
             const uint64_t da = A_MN ? desc_mnmajor(a_s + 1024 * j) : desc_kmajor(a_s + 32 * j);
             const uint64_t db = B_MN ? desc_mnmajor(b_s + 1024 * j) : desc_kmajor(b_s + 32 * j);
-            mma_tf32(d, da, db, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+            if (CG == 2)
+              mma_tf32_pair(d, da, db, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+            else
+              mma_tf32(d, da, db, idesc, (kb > 0 || j > 0) ? 1u : 0u);
           }
-          mma_commit(&empty[s]);
+          if (CG == 2)
+            mma_commit_pair(&empty[s]);
+          else
+            mma_commit(&empty[s]);
         }
         // completes when every MMA above has finished (at once for an empty
         // K range, whose accumulator the epilogue does not read)
-        mma_commit(&accf[ab]);
+        if (CG == 2)
+          mma_commit_pair(&accf[ab]);
+        else
+          mma_commit(&accf[ab]);
       }
     }
   } else {
     // ---------------------------------------------------- epilogue
     // two warps per TMEM lane quarter (warp w may only read lanes
-    // 32*(w%4)..+31), taking alternate 32-column chunks.  A warp's chunks,
-    // numbered j = 0, 1, ... over its tiles, cycle through its kSlots
+    // 32*(w%4)..+31), taking alternate 32-column chunks (CPT per tile; for
+    // BN = 32 the second warp of a quarter has none).  A warp's chunks,
+    // numbered j = 0, 1, ... over its tiles, alternate between its two
     // staging slots.
-    constexpr int NS = S::kSlots;
+    static_assert(S::kSlots == 2, "two staging slots per warp");
+    constexpr int CPT = BN >= 64 ? BN / 64 : 1;
     const int ew = warp - 2;       // 0..kEpiWarps-1
     const int quarter = warp & 3;  // TMEM lane quarter = rows of this warp
     const int half = ew >> 2;      // chunks c with c % 2 == half
-    const int cpt = (BN / 32 - half + 1) / 2;  // chunks per tile of this warp
-    uint8_t *slots = smem + S::kStageBytes + ew * (NS * 4096);
-    uint64_t *wbar = xbar + ew * NS;
+    const bool idle = BN < 64 && half == 1;
+    const uint32_t slots = smem_u32(smem + S::kStageBytes + ew * (2 * 4096));
+    uint64_t *wbar = xbar + ew * 2;
+    const uint32_t row_addr = (uint32_t)lane * 128u;  // this lane's row in a slot
+    const uint32_t sw = (uint32_t)(lane & 7);         // its 128B-swizzle phase
     uint32_t xph = 0;  // phase bit per slot of the aux barriers
     // dgrad: TMA load of the stored post-activation box of chunk j into its
     // slot (the slot's previous store must be done reading it)
     auto issue_aux = [&](int j) {
-      if (cpt == 0) return;
-      const int t = blockIdx.x + (j / cpt) * gridDim.x;
-      if (t >= tiles) return;
-      const Tile tl = decode_tile<BN>(t, g);
+      const int t = unit + (j / CPT) * units;
+      if (idle || t >= tiles) return;
+      const Tile tl = decode_tile<BN, CG>(t, g);
       const TcProb &pr = g.p[tl.p];
-      const int n = tl.n0 + (half + 2 * (j % cpt)) * 32, r0 = tl.m0 + quarter * 32;
+      const int n = tl.n0 + (half + 2 * (j % CPT)) * 32;
+      const int r0 = tl.m0 + BM * (int)rank + quarter * 32;
       if (n >= pr.N || r0 >= pr.M) return;
-      const int sl = j % NS;
+      const int sl = j & 1;
       mbar_expect_tx(&wbar[sl], 4096);
-      tma_load_2d(slots + sl * 4096, &maps.x[tl.p], &wbar[sl], n, r0);
+      tma_load_2d(smem + S::kStageBytes + ew * (2 * 4096) + sl * 4096, &maps.x[tl.p], &wbar[sl],
+                  n, r0);
     };
-    if (EPI == EPI_ELU_GRAD && lane == 0)
-      for (int p = 0; p < NS - 1; ++p) issue_aux(p);
+    if (EPI == EPI_ELU_GRAD && lane == 0) issue_aux(0);
     int it = 0, j = 0;
     bool ok = true, prev_store = false;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
-      const Tile tl = decode_tile<BN>(t, g);
+    // the pair's MMA warp waits on the even CTA's acc_empty barriers
+    const uint32_t acce_pair = peer_addr(smem_u32(acce), 0);
+    const uint32_t wbias = smem_u32(bias_sh + ew * (S::kCptMax * 32));
+    for (int t = unit; t < tiles; t += units, ++it) {
+      const Tile tl = decode_tile<BN, CG>(t, g);
       const TcProb &pr = g.p[tl.p];
       const int ab = it & 1;
       const uint32_t aph = (uint32_t)(it >> 1) & 1u;
+      const int row0 = tl.m0 + BM * (int)rank + quarter * 32;
+      if ((EPI == EPI_BIAS || EPI == EPI_BIAS_ELU) && !idle) {
+        // this tile's bias for the warp's chunks, one coalesced load per
+        // chunk before the accumulator wait (0 past N)
+#pragma unroll
+        for (int k = 0; k < CPT; ++k) {
+          const int n = tl.n0 + (half + 2 * k) * 32 + lane;
+          const float b = n < pr.N ? __ldg(pr.bias + n) : 0.0f;
+          asm volatile("st.shared.f32 [%0], %1;" ::"r"(wbias + (uint32_t)(k * 32 + lane) * 4u),
+                       "f"(b)
+                       : "memory");
+        }
+        __syncwarp();
+      }
+      if (EPI == EPI_ELU_GRAD && lane == 0 && !idle && t + units < tiles) {
+        // the next tile's post-activation boxes of this warp into L2
+        const Tile nt = decode_tile<BN, CG>(t + units, g);
+        const TcProb &np = g.p[nt.p];
+        const int r0 = nt.m0 + BM * (int)rank + quarter * 32;
+#pragma unroll
+        for (int k = 0; k < CPT; ++k) {
+          const int n = nt.n0 + (half + 2 * k) * 32;
+          if (n < np.N && r0 < np.M) tma_prefetch_2d(&maps.x[nt.p], n, r0);
+        }
+      }
       if (ok) ok = mbar_wait(&accf[ab], aph, g.err, 3);
       ok = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld is collective
       tc_fence_after();
-      const int row0 = tl.m0 + quarter * 32;
-      const int row = row0 + lane;
-      const bool row_ok = row < pr.M;
+      const bool rows_full = row0 + 32 <= pr.M;  // uniform
+      const bool row_ok = row0 + lane < pr.M;
       const uint32_t taddr = tmem + (uint32_t)(ab * BN) + ((uint32_t)(quarter * 32) << 16);
       const bool have = ok && tl.nk > 0;
-      bool released = false;
 #pragma unroll 1
-      for (int k = 0; k < cpt; ++k, ++j) {
+      for (int k = 0; k < CPT; ++k, ++j) {
         const int c = half + 2 * k;
         const int n = tl.n0 + c * 32;
-        const int sl = j % NS;
-        float *buf = (float *)(slots + sl * 4096);
-        const bool live = n < pr.N && row0 < pr.M;  // uniform over the warp
-        float v[32];
-        if (live && have) {
-          uint32_t r[32];
-          tmem_ld32(taddr + c * 32, r);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.0f;
-        }
-        if (k == cpt - 1) {
-          // last read of this accumulator: hand it back to the MMA warp
+        const uint32_t slot = slots + (uint32_t)(j & 1) * 4096u;
+        const bool live = !idle && n < pr.N && row0 < pr.M;  // uniform over the warp
+        if (k == CPT - 1 && !(live && have)) {
+          // (no TMEM read in this chunk) hand the accumulator back now
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&acce[ab]);
-          released = true;
+          if (lane == 0) {
+            if (CG == 2)
+              mbar_arrive_cluster(acce_pair + 8u * ab);
+            else
+              mbar_arrive(&acce[ab]);
+          }
         }
         bool stored = false;
         if (live) {
-          const bool full_chunk = n + 32 <= pr.N;
-          float4 *rowp = reinterpret_cast<float4 *>(buf + lane * 32);
-          if (EPI == EPI_BIAS || EPI == EPI_BIAS_ELU) {
-            if (full_chunk) {
-              const float4 *bp = reinterpret_cast<const float4 *>(pr.bias + n);
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                const float4 b = __ldg(bp + q);
-                v[4 * q + 0] += b.x;
-                v[4 * q + 1] += b.y;
-                v[4 * q + 2] += b.z;
-                v[4 * q + 3] += b.w;
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (n + i < pr.N) v[i] += __ldg(&pr.bias[n + i]);
-            }
-          }
-          if (EPI == EPI_BIAS_ELU) {
-            // ELU (net.rs:13-16); exp on the special-function unit, whose
-            // error is far below the tf32 rounding applied next
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = v[i] > 0.0f ? v[i] : exp_sfu(v[i]) - 1.0f;
-          }
           if (EPI == EPI_ELU_GRAD) {
-            // ELU' from the stored post-activation y (net.rs:19-22), whose
-            // box the TMA has put in this slot (zero-filled out of range)
-            if (!mbar_wait(&wbar[sl], (xph >> sl) & 1u, g.err, 5)) ok = false;
-            xph ^= 1u << sl;
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const float4 y = rowp[q ^ (lane & 7)];
-              v[4 * q + 0] *= y.x > 0.0f ? 1.0f : y.x + 1.0f;
-              v[4 * q + 1] *= y.y > 0.0f ? 1.0f : y.y + 1.0f;
-              v[4 * q + 2] *= y.z > 0.0f ? 1.0f : y.z + 1.0f;
-              v[4 * q + 3] *= y.w > 0.0f ? 1.0f : y.w + 1.0f;
-            }
-          }
-          // invalid rows and columns hold 0 (column sums, clipped stores)
-          if (!row_ok) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = 0.0f;
-          }
-          if (!full_chunk) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (n + i >= pr.N) v[i] = 0.0f;
-          }
-          if (pr.colsum) {
-            // bias gradient: column sums of the unrounded chunk over its 32
-            // rows (lane = row), a butterfly that leaves column `lane` in
-            // lane `lane`
-            red[quarter * BN + c * 32 + lane] = colsum32(v, lane);
-          }
-          if (pr.round_out) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = round_tf32(v[i]);
+            // the post-activation box of this chunk (TMA, one chunk ahead)
+            if (!mbar_wait(&wbar[j & 1], (xph >> (j & 1)) & 1u, g.err, 5)) ok = false;
+            xph ^= 1u << (j & 1);
           }
           if (EPI != EPI_ELU_GRAD) {
-            // the store that last used this slot (NS chunks back) must be
+            // the store that last used this slot (two chunks back) must be
             // done reading it
             if (lane == 0) {
-              if (prev_store) bulk_wait_read<NS - 1>();
+              if (prev_store) bulk_wait_read<1>();
               else bulk_wait_read<0>();
             }
             __syncwarp();
           }
-          // stage in the 128B-swizzled layout (16-byte chunk q of row r at
-          // position q ^ (r & 7): conflict-free) for one TMA store; the
-          // store clips rows >= M and columns >= N
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            rowp[q ^ (lane & 7)] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          EpiChunk ec;
+          ec.taddr = have ? taddr + c * 32 : 0xFFFFFFFFu;
+          ec.slot = slot + row_addr;
+          ec.sw = sw;
+          ec.bias = wbias + (uint32_t)(k * 32) * 4u;
+          ec.round = pr.round_out;
+          ec.colsum = pr.colsum
+                          ? pr.colsum + ((int64_t)(tl.m0 / BM + rank) * 4 + quarter) * pr.N + n
+                          : nullptr;
+          // the common case (every row and column valid, accumulator
+          // written) has its own code path, free of per-element predicates
+          const int valid_cols = pr.N - n < 32 ? pr.N - n : 32;
+          if (have && rows_full && valid_cols == 32) {
+            epi_chunk<EPI, true>(ec, lane, k == CPT - 1, [&] {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) {
+                if (CG == 2)
+                  mbar_arrive_cluster(acce_pair + 8u * ab);
+                else
+                  mbar_arrive(&acce[ab]);
+              }
+            }, true, 32);
+          } else {
+            epi_chunk<EPI, false>(ec, lane, k == CPT - 1 && have, [&] {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) {
+                if (CG == 2)
+                  mbar_arrive_cluster(acce_pair + 8u * ab);
+                else
+                  mbar_arrive(&acce[ab]);
+              }
+            }, row_ok, valid_cols);
+          }
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_3d(&maps.c[tl.p], buf, n, row0, tl.z);
+            tma_store_3d(&maps.c[tl.p], smem + (slot - smem_u32(smem)), n, row0, tl.z);
             bulk_commit();
           }
           stored = true;
+        } else if (!idle && pr.colsum && n < pr.N && n + lane < pr.N &&
+                   tl.m0 + BM * (int)rank < pr.M) {
+          // a quarter past the last row: its partial row is 0
+          pr.colsum[((int64_t)(tl.m0 / BM + rank) * 4 + quarter) * pr.N + n + lane] = 0.0f;
         }
-        if (!live && pr.colsum && n < pr.N) red[quarter * BN + c * 32 + lane] = 0.0f;  // no rows
         if (EPI == EPI_ELU_GRAD && lane == 0) {
-          // refill the slot of chunk j-1 with the aux box of chunk j+NS-1
+          // refill the slot of chunk j-1 with the aux box of chunk j+1
           if (stored) bulk_wait_read<1>();
           else bulk_wait_read<0>();
-          issue_aux(j + NS - 1);
+          issue_aux(j + 1);
         }
         prev_store = stored;
-      }
-      if (!released) {
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acce[ab]);
-      }
-      if (pr.colsum) {
-        named_bar_sync(1, 32 * kEpiWarps);
-        for (int i = ew * 32 + lane; i < BN; i += 32 * kEpiWarps) {
-          const int n = tl.n0 + i;
-          if (n < pr.N)
-            pr.colsum[(int64_t)(tl.m0 / BM) * pr.N + n] =
-                red[i] + red[BN + i] + red[2 * BN + i] + red[3 * BN + i];
-        }
-        named_bar_sync(1, 32 * kEpiWarps);
       }
     }
     if (lane == 0) bulk_wait_all();  // stores done before shared memory goes away
   }
   tc_fence_before();
-  __syncthreads();
+  // neither CTA of a pair leaves while the other may still signal its
+  // barriers
+  if (CG == 2)
+    cluster_sync();
+  else
+    __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"((uint32_t)(2 * BN))
-                 : "memory");
+    if (CG == 2)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                   "r"((uint32_t)(2 * BN))
+                   : "memory");
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                   "r"((uint32_t)(2 * BN))
+                   : "memory");
   }
 }
 
@@ -748,21 +955,48 @@ bool make_out_map(CUtensorMap *m, float *base, int64_t rows, int64_t cols, int64
 // The deepest stage ring (at most 6) that fits next to the epilogue
 // staging slots: more k-blocks in flight hide the TMA -> MMA -> release
 // round trip.
-template <int BN, int EPI>
+template <int BN, int EPI, int CG>
 constexpr int stages_for() {
-  constexpr int avail = 227 * 1024 - 1024 - kEpiWarps * slots_for(EPI) * 4096 - 4 * BN * 4 -
+  constexpr int avail = 227 * 1024 - 1024 - kEpiWarps * slots_for(EPI) * 4096 -
+                        kEpiWarps * (BN >= 64 ? BN / 64 : 1) * 32 * 4 -
                         (8 + kEpiWarps * slots_for(EPI)) * 8 - 64;
-  constexpr int st = avail / (BM * BKB + BN * BKB);
+  constexpr int st = avail / (BM * BKB + BN / CG * BKB);
   return st > 6 ? 6 : st;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+// Co-resident CTA pairs of one instantiation (its shared memory and the
+// GPCs decide), cached.
+template <typename K>
+int max_pairs(K kfn, int smem) {
+  static int cached = 0;
+  if (cached > 0) return cached;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * 64);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    n = g_sms / 2;
+  }
+  cached = n;
+  return n;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI, int CG>
 cudaError_t launch_one(const TcMaps &maps, const TcGroup &grp, cudaStream_t s) {
-  constexpr int ST = stages_for<BN, EPI>();
+  constexpr int ST = stages_for<BN, EPI, CG>();
   static_assert(ST >= 2, "stage ring");
-  using S = Smem<BN, ST, EPI>;
+  using S = Smem<BN, ST, EPI, CG>;
   static_assert(S::kBytes <= 227 * 1024, "shared memory");
-  auto kfn = tc_gemm_kernel<BN, A_MN, B_MN, EPI, ST>;
+  auto kfn = tc_gemm_kernel<BN, A_MN, B_MN, EPI, ST, CG>;
   static bool attr = false;  // set once per instantiation (same value on every device)
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -771,32 +1005,38 @@ cudaError_t launch_one(const TcMaps &maps, const TcGroup &grp, cudaStream_t s) {
     attr = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grp.tiles < g_sms ? grp.tiles : g_sms);
+  int units = CG == 2 ? max_pairs(kfn, S::kBytes) : g_sms;
+  if (grp.tiles < units) units = grp.tiles;
+  cfg.gridDim = dim3(CG * units);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = S::kBytes;
   cfg.stream = s;
+  cudaLaunchAttribute at[2];
   // may start (set-up only) while the previous kernel in the stream ends
-  cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
+  at[1].id = cudaLaunchAttributeClusterDimension;
+  at[1].val.clusterDim.x = CG;
+  at[1].val.clusterDim.y = 1;
+  at[1].val.clusterDim.z = 1;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = CG == 2 ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kfn, maps, grp);
 }
 
-template <int BN>
+template <int BN, int CG>
 cudaError_t dispatch_bn(int kind, int epi, const TcMaps &maps, const TcGroup &grp,
                         cudaStream_t s) {
   if (kind == 0) {  // forward
-    if (epi == EPI_BIAS_ELU) return launch_one<BN, false, false, EPI_BIAS_ELU>(maps, grp, s);
-    if (epi == EPI_BIAS) return launch_one<BN, false, false, EPI_BIAS>(maps, grp, s);
-    return launch_one<BN, false, false, EPI_STORE>(maps, grp, s);
+    if (epi == EPI_BIAS_ELU) return launch_one<BN, false, false, EPI_BIAS_ELU, CG>(maps, grp, s);
+    if (epi == EPI_BIAS) return launch_one<BN, false, false, EPI_BIAS, CG>(maps, grp, s);
+    return launch_one<BN, false, false, EPI_STORE, CG>(maps, grp, s);
   }
   if (kind == 1) {  // dgrad
-    if (epi == EPI_ELU_GRAD) return launch_one<BN, false, true, EPI_ELU_GRAD>(maps, grp, s);
-    return launch_one<BN, false, true, EPI_STORE>(maps, grp, s);
+    if (epi == EPI_ELU_GRAD) return launch_one<BN, false, true, EPI_ELU_GRAD, CG>(maps, grp, s);
+    return launch_one<BN, false, true, EPI_STORE, CG>(maps, grp, s);
   }
-  return launch_one<BN, true, true, EPI_STORE>(maps, grp, s);  // wgrad
+  return launch_one<BN, true, true, EPI_STORE, CG>(maps, grp, s);  // wgrad
 }
 
 }  // namespace
@@ -858,6 +1098,18 @@ void GemmEngine::destroy() {
   err_dev = nullptr;
 }
 
+// Multiplier and shift for fdiv by d >= 1 (n < 2^31): shift = ceil(log2 d),
+// mul = floor(2^32 (2^shift - d) / d) + 1.
+static FastDiv fast_div(uint32_t d) {
+  uint32_t l = 0;
+  while ((1ull << l) < d) ++l;
+  FastDiv f;
+  f.d = d;
+  f.shift = l;
+  f.mul = (uint32_t)((((1ull << l) - d) << 32) / d + 1);
+  return f;
+}
+
 static int layout_kind(const GemmArgs &g) {
   if (!g.trans_a && g.trans_b) return 0;   // forward
   if (!g.trans_a && !g.trans_b) return 1;  // dgrad
@@ -881,7 +1133,7 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
     *err = "unsupported operand layout for the tensor-core GEMM";
     return ZRL_NOT_SUPPORTED;
   }
-  int maxN = 0;
+  int maxN = 0, minM = INT32_MAX;
   for (int i = 0; i < n; ++i) {
     const GemmArgs &g = gs[i];
     if (layout_kind(g) != kind || g.epi != gs[0].epi) {
@@ -909,10 +1161,14 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
       return ZRL_INVALID_ARG;
     }
     maxN = std::max(maxN, g.N);
+    minM = std::min(minM, g.M);
   }
-  // 128-column tiles from N = 128 up: at M = 24,576 rows that gives 2.6 to
-  // 5.2 tiles per SM per GEMM, a better balance than 256-column tiles
-  const int BN = maxN <= 32 ? 32 : (maxN <= 64 ? 64 : 128);
+  // Tall GEMMs (every M >= 256) run on CTA pairs with 256 x BN tiles,
+  // BN up to 256: each SM then stages half of the B tile, which halves
+  // the shared-memory and L2 bytes per flop.  Others run on single CTAs
+  // with 128 x BN tiles, BN up to 128.
+  const int CG = (minM >= 256 && maxN > 32) ? 2 : 1;
+  const int BN = maxN <= 32 ? 32 : (maxN <= 64 ? 64 : (maxN <= 128 || CG == 1 ? 128 : 256));
   TcMaps maps;
   memset(&maps, 0, sizeof(maps));
   TcGroup grp;
@@ -925,7 +1181,7 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
     const CUtensorMap *ta = kind == 2 ? cached_map(eng, g.A, g.K, g.M, g.lda, 32, 1, err)
                                       : cached_map(eng, g.A, g.M, g.K, g.lda, BM, 0, err);
     // B: [N rows, K cols] K-major (forward) or [K rows, N cols] MN-major
-    const CUtensorMap *tb = kind == 0 ? cached_map(eng, g.B, g.N, g.K, g.ldb, BN, 0, err)
+    const CUtensorMap *tb = kind == 0 ? cached_map(eng, g.B, g.N, g.K, g.ldb, BN / CG, 0, err)
                                       : cached_map(eng, g.B, g.K, g.N, g.ldb, 32, 1, err);
     const CUtensorMap *tc = cached_map(eng, g.C, g.M, g.N, g.ldc, split, 2, err);
     if (!ta || !tb || !tc) return ZRL_CUDA_ERROR;
@@ -944,8 +1200,10 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
     pr.K = g.K;
     pr.kc = ((g.K + split - 1) / split + 31) / 32 * 32;
     pr.splits = split;
-    pr.tiles_m = (g.M + BM - 1) / BM;
+    pr.tiles_m = (g.M + BM * CG - 1) / (BM * CG);
+    pr.div_m = fast_div((uint32_t)pr.tiles_m);
     pr.tiles_n = (g.N + BN - 1) / BN;
+    pr.div_n = fast_div((uint32_t)pr.tiles_n);
     pr.tile0 = tiles;
     pr.bias = g.bias;
     pr.round_out = g.round_out;
@@ -956,9 +1214,15 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
   grp.tiles = tiles;
   grp.err = eng->err_dev;
   cudaError_t e;
-  if (BN == 32) e = dispatch_bn<32>(kind, gs[0].epi, maps, grp, s);
-  else if (BN == 64) e = dispatch_bn<64>(kind, gs[0].epi, maps, grp, s);
-  else e = dispatch_bn<128>(kind, gs[0].epi, maps, grp, s);
+  if (CG == 1) {
+    if (BN == 32) e = dispatch_bn<32, 1>(kind, gs[0].epi, maps, grp, s);
+    else if (BN == 64) e = dispatch_bn<64, 1>(kind, gs[0].epi, maps, grp, s);
+    else e = dispatch_bn<128, 1>(kind, gs[0].epi, maps, grp, s);
+  } else {
+    if (BN == 64) e = dispatch_bn<64, 2>(kind, gs[0].epi, maps, grp, s);
+    else if (BN == 128) e = dispatch_bn<128, 2>(kind, gs[0].epi, maps, grp, s);
+    else e = dispatch_bn<256, 2>(kind, gs[0].epi, maps, grp, s);
+  }
   if (e != cudaSuccess) {
     *err = std::string("tensor-core GEMM launch: ") + cudaGetErrorString(e);
     return ZRL_CUDA_ERROR;

@@ -306,8 +306,8 @@ static zrl_status ensure_mb(zrl_ctx *ctx, int64_t mb) {
     for (int l = 0; l < L.L; ++l) {
       wp += (int64_t)S * L.dp[l + 1] * L.dp[l];
       // bias-gradient partials: S row chunks (CUDA-core colsum) or one row
-      // per 128-row tile (tensor-core dgrad epilogue)
-      bp += (int64_t)std::max<int64_t>(S, (mb + 127) / 128) * L.dp[l + 1];
+      // per 32-row quarter of each 128-row block (tensor-core dgrad epilogue)
+      bp += (int64_t)std::max<int64_t>(S, 4 * ((mb + 127) / 128)) * L.dp[l + 1];
     }
   }
   TRY(dalloc(ctx, &ctx->wpart, wp));
@@ -466,11 +466,12 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
       g.ldaux = L.dp[l];
       g.split_k = 1;
       if (ctx->tc()) {
-        // db_{l-1}: per-tile column sums of delta_{l-1} from the epilogue
+        // db_{l-1}: column sums of delta_{l-1} from the epilogue, one
+        // partial row per 32-row quarter of each 128-row block
         g.colsum = *bp;
-        ReduceSeg sb{ctx->G + L.b_off[l - 1], *bp, (int64_t)L.dp[l], m_tiles};
+        ReduceSeg sb{ctx->G + L.b_off[l - 1], *bp, (int64_t)L.dp[l], 4 * m_tiles};
         segs.seg[segs.n++] = sb;
-        *bp += (int64_t)m_tiles * L.dp[l];
+        *bp += (int64_t)4 * m_tiles * L.dp[l];
       }
     }
     TRY(run_group(ctx, d, n));
