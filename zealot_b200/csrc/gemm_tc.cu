@@ -400,9 +400,9 @@ struct TcMaps {
 
 // Staging slots per epilogue warp, each one [32 x 32] fp32 box: two, so a
 // chunk is staged while the previous chunk's store still reads its slot;
-// in the dgrad epilogue a slot first receives the chunk's TMA-loaded
-// post-activation (one chunk ahead).
-constexpr int slots_for(int) { return 2; }
+// three in the dgrad epilogue, where a slot first receives the chunk's
+// TMA-loaded post-activation, two chunks ahead.
+constexpr int slots_for(int epi) { return epi == EPI_ELU_GRAD ? 3 : 2; }
 
 template <int BN, int STAGES, int EPI, int CG>
 struct Smem {
@@ -718,16 +718,16 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
     // two warps per TMEM lane quarter (warp w may only read lanes
     // 32*(w%4)..+31), taking alternate 32-column chunks (CPT per tile; for
     // BN = 32 the second warp of a quarter has none).  A warp's chunks,
-    // numbered j = 0, 1, ... over its tiles, alternate between its two
-    // staging slots.
-    static_assert(S::kSlots == 2, "two staging slots per warp");
+    // numbered j = 0, 1, ... over its tiles, cycle through its NS staging
+    // slots.
+    constexpr int NS = S::kSlots;
     constexpr int CPT = BN >= 64 ? BN / 64 : 1;
     const int ew = warp - 2;       // 0..kEpiWarps-1
     const int quarter = warp & 3;  // TMEM lane quarter = rows of this warp
     const int half = ew >> 2;      // chunks c with c % 2 == half
     const bool idle = BN < 64 && half == 1;
-    const uint32_t slots = smem_u32(smem + S::kStageBytes + ew * (2 * 4096));
-    uint64_t *wbar = xbar + ew * 2;
+    const uint32_t slots = smem_u32(smem + S::kStageBytes + ew * (NS * 4096));
+    uint64_t *wbar = xbar + ew * NS;
     const uint32_t row_addr = (uint32_t)lane * 128u;  // this lane's row in a slot
     const uint32_t sw = (uint32_t)(lane & 7);         // its 128B-swizzle phase
     uint32_t xph = 0;  // phase bit per slot of the aux barriers
@@ -741,12 +741,13 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
       const int n = tl.n0 + (half + 2 * (j % CPT)) * 32;
       const int r0 = tl.m0 + BM * (int)rank + quarter * 32;
       if (n >= pr.N || r0 >= pr.M) return;
-      const int sl = j & 1;
+      const int sl = j % NS;
       mbar_expect_tx(&wbar[sl], 4096);
-      tma_load_2d(smem + S::kStageBytes + ew * (2 * 4096) + sl * 4096, &maps.x[tl.p], &wbar[sl],
+      tma_load_2d(smem + S::kStageBytes + ew * (NS * 4096) + sl * 4096, &maps.x[tl.p], &wbar[sl],
                   n, r0);
     };
-    if (EPI == EPI_ELU_GRAD && lane == 0) issue_aux(0);
+    if (EPI == EPI_ELU_GRAD && lane == 0)
+      for (int p = 0; p < NS - 1; ++p) issue_aux(p);
     int it = 0, j = 0;
     bool ok = true, prev_store = false;
     // the pair's MMA warp waits on the even CTA's acc_empty barriers
@@ -793,7 +794,8 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
       for (int k = 0; k < CPT; ++k, ++j) {
         const int c = half + 2 * k;
         const int n = tl.n0 + c * 32;
-        const uint32_t slot = slots + (uint32_t)(j & 1) * 4096u;
+        const int sl = j % NS;
+        const uint32_t slot = slots + (uint32_t)sl * 4096u;
         const bool live = !idle && n < pr.N && row0 < pr.M;  // uniform over the warp
         if (k == CPT - 1 && !(live && have)) {
           // (no TMEM read in this chunk) hand the accumulator back now
@@ -810,8 +812,8 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
         if (live) {
           if (EPI == EPI_ELU_GRAD) {
             // the post-activation box of this chunk (TMA, one chunk ahead)
-            if (!mbar_wait(&wbar[j & 1], (xph >> (j & 1)) & 1u, g.err, 5)) ok = false;
-            xph ^= 1u << (j & 1);
+            if (!mbar_wait(&wbar[sl], (xph >> sl) & 1u, g.err, 5)) ok = false;
+            xph ^= 1u << sl;
           }
           if (EPI != EPI_ELU_GRAD) {
             // the store that last used this slot (two chunks back) must be
@@ -870,10 +872,10 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
           pr.colsum[((int64_t)(tl.m0 / BM + rank) * 4 + quarter) * pr.N + n + lane] = 0.0f;
         }
         if (EPI == EPI_ELU_GRAD && lane == 0) {
-          // refill the slot of chunk j-1 with the aux box of chunk j+1
+          // refill the slot of chunk j-1 with the aux box of chunk j+NS-1
           if (stored) bulk_wait_read<1>();
           else bulk_wait_read<0>();
-          issue_aux(j + 1);
+          issue_aux(j + NS - 1);
         }
         prev_store = stored;
       }

@@ -294,7 +294,7 @@ constexpr int kLossMaxA = 128;  // 4 action dims per lane
 // log_std gradient and of the three statistics are written to scratch; the
 // last block to finish adds the partials in block order (deterministic).
 __global__ void __launch_bounds__(kLossThreads)
-loss_kernel(LossArgs a, float *partials, unsigned int *ticket) {
+loss_kernel(LossArgs a) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int nwb = blockDim.x >> 5;
   const int64_t gw = (int64_t)blockIdx.x * nwb + wid;
@@ -407,7 +407,9 @@ loss_kernel(LossArgs a, float *partials, unsigned int *ticket) {
       a.d_critic[s * a.cp] = a.round_tf32 ? rna_tf32(gv) : gv;
     }
   }
-  // ---- block partials: warp values into shared memory, summed in order
+  // ---- the block's partial row, its warps summed in warp order:
+  // [g_logstd (Ap) | db_actor (Ap) | surr vloss kl 0 | db_critic (cp)],
+  // zero in the padding; the segment reduce adds the rows of all blocks
   __shared__ float sh[kLossThreads / 32][2 * kLossMaxA + 4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -424,47 +426,19 @@ loss_kernel(LossArgs a, float *partials, unsigned int *ticket) {
     sh[wid][2 * A + 3] = acc_gv;
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < width; c += blockDim.x) {
+  float *row = a.part + (int64_t)blockIdx.x * a.width;
+  for (int c = threadIdx.x; c < a.width; c += blockDim.x) {
+    // column c of the row -> column of the warp sums (or padding)
+    int src = -1;
+    if (c < a.Ap) src = c < A ? c : -1;
+    else if (c < 2 * a.Ap) src = c - a.Ap < A ? A + (c - a.Ap) : -1;
+    else if (c < 2 * a.Ap + 4) src = c - 2 * a.Ap < 3 ? 2 * A + (c - 2 * a.Ap) : -1;
+    else src = c == 2 * a.Ap + 4 ? 2 * A + 3 : -1;
     float t = 0.0f;
-    for (int w = 0; w < nwb; ++w) t += sh[w][c];
-    partials[(int64_t)blockIdx.x * width + c] = t;
+    if (src >= 0)
+      for (int w = 0; w < nwb; ++w) t += sh[w][src];
+    row[c] = t;
   }
-  // ---- last block adds the block partials in block order
-  __threadfence();
-  __shared__ bool last;
-  __syncthreads();
-  if (threadIdx.x == 0) last = atomicAdd(ticket, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  // thread (c, grp) sums the partial rows grp, grp+4, ... of column c
-  // (independent loads, eight in flight), then the four group sums are
-  // added in group order -- a fixed order, deterministic
-  __shared__ float red[4][64];
-  const int cc = threadIdx.x & 63, grp = threadIdx.x >> 6;
-  for (int c0 = 0; c0 < width; c0 += 64) {
-    const int c = c0 + cc;
-    float t = 0.0f;
-    if (c < width) {
-#pragma unroll 8
-      for (int b = grp; b < (int)gridDim.x; b += 4) t += __ldcg(&partials[(int64_t)b * width + c]);
-    }
-    red[grp][cc] = t;
-    __syncthreads();
-    if (grp == 0 && c < width) {
-      t = ((red[0][cc] + red[1][cc]) + red[2][cc]) + red[3][cc];
-      if (c < A)
-        a.g_logstd[c] = t;
-      else if (c < 2 * A)
-        a.db_actor[c - A] = t;
-      else if (c < 2 * A + 3)
-        a.sums3[c - 2 * A] = t;
-      else
-        a.db_critic[0] = t;
-    }
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) *ticket = 0u;
 }
 
 // ------------------------------------------------------------ colsum
@@ -483,37 +457,45 @@ __global__ void colsum_kernel(const float *x, int64_t rows, int cols, int ld,
 
 // ------------------------------------------------------ segment reduce
 
-// One block per (segment, 128-float column block).  The block's eight
-// warps are eight split groups: warp j sums splits j, j+8, j+16, ... of its
-// 32 float4 columns in split order (each load a coalesced 512-byte row
-// piece, several in flight), and warp 0 then adds the eight group sums in
-// group order -- a fixed order, so every run gives the same bits.  Every
-// segment count is a multiple of 4 floats and every pointer 16-byte
-// aligned (the padded layout guarantees both).
-constexpr int kRsCols4 = 32, kRsGroups = 8;
+// Sum of split partials.  A segment with `splits` partial rows is cut into
+// G = clamp(splits / 8, 1, 32) split groups (a power of two); a block of
+// 1024 threads covers 1024 / G float4 columns x G groups, consecutive
+// threads on consecutive columns (coalesced).  Group j sums splits j, j+G,
+// j+2G, ... in split order, several loads in flight, and the G group sums
+// are then added in group order -- a fixed order, so every run gives the
+// same bits.  Every segment count and stride is a multiple of 4 floats and
+// every pointer 16-byte aligned (the padded layout guarantees both).
+constexpr int kRsThreads = 1024;
 
-__device__ __forceinline__ int64_t rs_blocks(int64_t count) {
-  return (count / 4 + kRsCols4 - 1) / kRsCols4;
+__host__ __device__ __forceinline__ int rs_groups(int splits) {
+  int g = 1;
+  while (g < 32 && g * 8 < splits) g *= 2;
+  return g;
+}
+__host__ __device__ __forceinline__ int64_t rs_blocks(const ReduceSeg &sg) {
+  const int64_t cols4 = kRsThreads / rs_groups(sg.splits);
+  return (sg.count / 4 + cols4 - 1) / cols4;
 }
 
-__global__ void __launch_bounds__(kRsCols4 * kRsGroups)
-reduce_segments_kernel(ReduceSegs segs) {
+__global__ void __launch_bounds__(kRsThreads) reduce_segments_kernel(ReduceSegs segs) {
   int si = 0;
   int64_t b = blockIdx.x;
-  while (si + 1 < segs.n && b >= rs_blocks(segs.seg[si].count)) {
-    b -= rs_blocks(segs.seg[si].count);
+  while (si + 1 < segs.n && b >= rs_blocks(segs.seg[si])) {
+    b -= rs_blocks(segs.seg[si]);
     ++si;
   }
   const ReduceSeg &sg = segs.seg[si];
-  const int c = threadIdx.x & 31, grp = threadIdx.x >> 5;
-  const int64_t stride4 = sg.count / 4;
-  const int64_t i4 = b * kRsCols4 + c;
-  const bool live = i4 < stride4;
+  const int G = rs_groups(sg.splits);
+  const int cols4 = kRsThreads / G;
+  const int c = threadIdx.x % cols4, grp = threadIdx.x / cols4;
+  const int64_t i4 = b * cols4 + c;
+  const bool live = i4 < sg.count / 4;
+  const int64_t stride4 = sg.stride / 4;
   const float4 *src = reinterpret_cast<const float4 *>(sg.src) + i4;
   float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   if (live) {
-#pragma unroll 4
-    for (int z = grp; z < sg.splits; z += kRsGroups) {
+#pragma unroll 8
+    for (int z = grp; z < sg.splits; z += G) {
       const float4 x = __ldcs(src + (int64_t)z * stride4);  // read once: streaming
       t.x += x.x;
       t.y += x.y;
@@ -521,20 +503,19 @@ reduce_segments_kernel(ReduceSegs segs) {
       t.w += x.w;
     }
   }
-  __shared__ float4 part[kRsGroups][kRsCols4];
-  part[grp][c] = t;
+  __shared__ float4 part[kRsThreads];
+  part[threadIdx.x] = t;
   __syncthreads();
   if (grp == 0 && live) {
-    float4 s = part[0][c];
-#pragma unroll
-    for (int j = 1; j < kRsGroups; ++j) {
-      const float4 x = part[j][c];
-      s.x += x.x;
-      s.y += x.y;
-      s.z += x.z;
-      s.w += x.w;
+    float4 s4 = part[c];
+    for (int j = 1; j < G; ++j) {
+      const float4 x = part[j * cols4 + c];
+      s4.x += x.x;
+      s4.y += x.y;
+      s4.z += x.z;
+      s4.w += x.w;
     }
-    reinterpret_cast<float4 *>(sg.dst)[i4] = s;
+    reinterpret_cast<float4 *>(sg.dst)[i4] = s4;
   }
 }
 
@@ -869,15 +850,14 @@ void launch_round_copy(const float *src, float *dst, int64_t n, cudaStream_t s) 
   round_copy_kernel<<<grid_for(n, 256), 256, 0, s>>>(src, dst, n);
 }
 
-void launch_loss(const LossArgs &a, ReduceScratch &rs, cudaStream_t s) {
-  // one block per SM: each warp walks its samples with the next sample's
-  // loads in flight, and the last block's sum over the block partials
-  // stays short
-  int blocks = grid_for(a.mb * 32, kLossThreads, 148);
-  if (blocks > rs.max_blocks) blocks = rs.max_blocks;
-  if ((2 * a.A + 4) > rs.fwidth) blocks = 0;  // caller sized fwidth >= 2A + 4
-  if (blocks > 0)
-    loss_kernel<<<blocks, kLossThreads, 0, s>>>(a, rs.fpart, rs.ticket);
+int loss_blocks(int64_t mb) { return grid_for(mb * 32, kLossThreads, 4 * 148); }
+
+void launch_loss(const LossArgs &a, cudaStream_t s) {
+  // four blocks per SM, each warp walking its samples with the next
+  // sample's loads in flight; the block rows are summed by the segment
+  // reduce that follows the backward pass
+  const int blocks = loss_blocks(a.mb);
+  loss_kernel<<<blocks, kLossThreads, 0, s>>>(a);
 }
 
 void launch_colsum(const float *x, int64_t rows, int cols, int ld,
@@ -888,9 +868,9 @@ void launch_colsum(const float *x, int64_t rows, int cols, int ld,
 
 void launch_reduce_segments(const ReduceSegs &segs, cudaStream_t s) {
   int64_t blocks = 0;
-  for (int i = 0; i < segs.n; ++i) blocks += (segs.seg[i].count / 4 + kRsCols4 - 1) / kRsCols4;
+  for (int i = 0; i < segs.n; ++i) blocks += rs_blocks(segs.seg[i]);
   if (blocks == 0) return;
-  reduce_segments_kernel<<<(unsigned)blocks, kRsCols4 * kRsGroups, 0, s>>>(segs);
+  reduce_segments_kernel<<<(unsigned)blocks, kRsThreads, 0, s>>>(segs);
 }
 
 void launch_prestep(const PrestepArgs &a, ReduceScratch &rs, cudaStream_t s) {

@@ -469,7 +469,8 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
         // db_{l-1}: column sums of delta_{l-1} from the epilogue, one
         // partial row per 32-row quarter of each 128-row block
         g.colsum = *bp;
-        ReduceSeg sb{ctx->G + L.b_off[l - 1], *bp, (int64_t)L.dp[l], 4 * m_tiles};
+        ReduceSeg sb{ctx->G + L.b_off[l - 1], *bp, (int64_t)L.dp[l], 4 * m_tiles,
+                     (int64_t)L.dp[l]};
         segs.seg[segs.n++] = sb;
         *bp += (int64_t)4 * m_tiles * L.dp[l];
       }
@@ -485,7 +486,7 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
         launch_colsum(ctx->dlt[k][l], rows, L.dp[l + 1], L.dp[l + 1], *bp, S, ctx->stream);
         ctx->launches++;
         CHECK_LAUNCH();
-        ReduceSeg sb{ctx->G + L.b_off[l], *bp, (int64_t)L.dp[l + 1], S};
+        ReduceSeg sb{ctx->G + L.b_off[l], *bp, (int64_t)L.dp[l + 1], S, (int64_t)L.dp[l + 1]};
         segs.seg[segs.n++] = sb;
         *bp += (int64_t)S * L.dp[l + 1];
       }
@@ -512,12 +513,24 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
       g.ldc = L.dp[l];
       g.epi = EPI_STORE;
       g.split_k = S;
-      ReduceSeg sw{ctx->G + L.w_off[l], *wp, (int64_t)L.dp[l + 1] * L.dp[l], S};
+      ReduceSeg sw{ctx->G + L.w_off[l], *wp, (int64_t)L.dp[l + 1] * L.dp[l], S,
+                   (int64_t)L.dp[l + 1] * L.dp[l]};
       segs.seg[segs.n++] = sw;
       *wp += (int64_t)S * L.dp[l + 1] * L.dp[l];
     }
   }
-  for (int i = 0; i < nw; i += 8) TRY(run_group(ctx, w + i, std::min(8, nw - i)));
+  // tall weight gradients (dp[l+1] >= 256 rows) go to CTA-pair tiles, the
+  // rest to single-CTA tiles: one grouped launch (of at most 8) each
+  GemmArgs tall[2 * ZRL_MAX_LAYERS], flat[2 * ZRL_MAX_LAYERS];
+  int nt = 0, nf = 0;
+  for (int i = 0; i < nw; ++i) {
+    if (w[i].M >= 256)
+      tall[nt++] = w[i];
+    else
+      flat[nf++] = w[i];
+  }
+  for (int i = 0; i < nt; i += 8) TRY(run_group(ctx, tall + i, std::min(8, nt - i)));
+  for (int i = 0; i < nf; i += 8) TRY(run_group(ctx, flat + i, std::min(8, nf - i)));
   return ZRL_OK;
 }
 
@@ -555,22 +568,31 @@ static zrl_status minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
   la.round_tf32 = ctx->tc();
   la.d_actor = ctx->dlt[0][La.L - 1];
   la.d_critic = ctx->dlt[1][Lc.L - 1];
-  la.g_logstd = ctx->G + ctx->ls_off;
-  la.sums3 = ctx->sums3;
-  la.db_actor = ctx->G + La.b_off[La.L - 1];
-  la.db_critic = ctx->G + Lc.b_off[Lc.L - 1];
-  if (v.rows > 0) {
-    launch_loss(la, ctx->rs, ctx->stream);
-    ctx->launches++;
-    CHECK_LAUNCH();
-  } else {
+  la.part = ctx->rs.fpart;
+  la.width = 2 * la.Ap + 4 + la.cp;
+  if (v.rows <= 0) {
     // a rank with no rows this minibatch contributes zeros (the entropy
     // term of the log_std gradient is per sample, so zero as well)
     CK(cudaMemsetAsync(ctx->G, 0, sizeof(float) * ctx->grad_len, ctx->stream));
     return ZRL_OK;
   }
+  const int lb = loss_blocks(v.rows);
+  if (la.width > ctx->rs.fwidth || lb > ctx->rs.max_blocks) return bad(ctx, "loss scratch too small");
+  launch_loss(la, ctx->stream);
+  ctx->launches++;
+  CHECK_LAUNCH();
   float *wp = ctx->wpart, *bp = ctx->bpart;
   ReduceSegs segs{};
+  {
+    // the loss kernel's block rows: log_std gradient, output-layer bias
+    // gradients of both nets, statistic sums
+    const int64_t w = la.width;
+    float *fp = ctx->rs.fpart;
+    segs.seg[segs.n++] = ReduceSeg{ctx->G + ctx->ls_off, fp, (int64_t)la.Ap, lb, w};
+    segs.seg[segs.n++] = ReduceSeg{ctx->G + La.b_off[La.L - 1], fp + la.Ap, (int64_t)la.Ap, lb, w};
+    segs.seg[segs.n++] = ReduceSeg{ctx->sums3, fp + 2 * la.Ap, 4, lb, w};
+    segs.seg[segs.n++] = ReduceSeg{ctx->G + Lc.b_off[Lc.L - 1], fp + 2 * la.Ap + 4, (int64_t)la.cp, lb, w};
+  }
   TRY(backward_both(ctx, v.xa, v.xc, v.rows, &wp, &bp, segs));
   launch_reduce_segments(segs, ctx->stream);
   ctx->launches++;
@@ -968,7 +990,7 @@ zrl_status zrl_create(const zrl_model_config *cfg, int device,
   if ((s = dalloc(ctx, &ctx->crit_sd, cd)) != ZRL_OK) return fail(s);
   if ((s = dalloc(ctx, &ctx->moments, 2)) != ZRL_OK) return fail(s);
   ctx->rs.max_blocks = 148 * 16;
-  ctx->rs.fwidth = 2 * 128 + 4;  // loss-kernel partial row for A <= 128
+  ctx->rs.fwidth = 2 * 128 + 4 + 128;  // loss-kernel partial row for Ap, cp <= 128
   if ((s = dalloc(ctx, &ctx->rs.fpart, (int64_t)ctx->rs.max_blocks * ctx->rs.fwidth)) != ZRL_OK)
     return fail(s);
   if ((s = dalloc(ctx, &ctx->rs.dpart, (int64_t)ctx->rs.max_blocks * 2)) != ZRL_OK)

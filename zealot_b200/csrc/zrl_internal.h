@@ -130,14 +130,16 @@ struct LossArgs {
   float clip, entropy_coef, value_coef;
   float *d_actor;         // [mb, Ap] delta of the actor output layer
   float *d_critic;        // [mb, cp] delta of the critic output layer
-  float *g_logstd;        // [A] written (sum over the minibatch)
-  float *sums3;           // surr, vloss, kl (sums of scaled terms)
-  // output-layer bias gradients = column sums of the two deltas, taken in
-  // fp32 before any rounding: db_actor [A], db_critic [1]
-  float *db_actor, *db_critic;
+  // one partial row per block, width = 2 Ap + 4 + cp floats:
+  // [g_logstd | db_actor | surr vloss kl 0 | db_critic], the log_std
+  // gradient, the output-layer bias gradients (column sums of the two
+  // deltas, taken in fp32 before any rounding) and the statistic sums
+  float *part;
+  int width;
   int round_tf32;         // round the two output deltas to tf32 (RN)
 };
-void launch_loss(const LossArgs &a, ReduceScratch &rs, cudaStream_t s);
+void launch_loss(const LossArgs &a, cudaStream_t s);
+int loss_blocks(int64_t mb);  // the partial rows launch_loss writes
 
 // Column sums of a [rows, cols] matrix, split over row chunks into
 // partials [splits, cols].
@@ -147,11 +149,12 @@ void launch_colsum(const float *x, int64_t rows, int cols, int ld,
 // Sum `splits` partial buffers into dst for a list of segments.
 struct ReduceSeg {
   float *dst;
-  const float *src;      // [splits][count]
+  const float *src;      // splits partial rows of count floats, stride apart
   int64_t count;
   int splits;
+  int64_t stride;        // floats between partial rows (>= count)
 };
-constexpr int kMaxSegs = 2 * ZRL_MAX_LAYERS * 2;
+constexpr int kMaxSegs = 2 * ZRL_MAX_LAYERS * 2 + 4;
 struct ReduceSegs {
   ReduceSeg seg[kMaxSegs];
   int n;
