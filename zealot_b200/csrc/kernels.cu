@@ -300,8 +300,6 @@ loss_kernel(LossArgs a) {
   const int64_t gw = (int64_t)blockIdx.x * nwb + wid;
   const int64_t nw = (int64_t)gridDim.x * nwb;
   const int A = a.A;
-  // per-block partial row: [g_logstd (A) | db_actor (A) | surr vloss kl | db_critic]
-  const int width = 2 * A + 4;
   float ls[4], sd[4], inv_var[4], inv_sd[4], gls[4], gmu[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -458,49 +456,58 @@ __global__ void colsum_kernel(const float *x, int64_t rows, int cols, int ld,
 // ------------------------------------------------------ segment reduce
 
 // Sum of split partials.  A segment with `splits` partial rows is cut into
-// G = clamp(splits / 8, 1, 32) split groups (a power of two); a block of
-// 1024 threads covers 1024 / G float4 columns x G groups, consecutive
-// threads on consecutive columns (coalesced).  Group j sums splits j, j+G,
-// j+2G, ... in split order, several loads in flight, and the G group sums
-// are then added in group order -- a fixed order, so every run gives the
-// same bits.  Every segment count and stride is a multiple of 4 floats and
-// every pointer 16-byte aligned (the padded layout guarantees both).
-constexpr int kRsThreads = 1024;
+// G = clamp(splits / 8, 1, 16) split groups (a power of two); a block of
+// 512 threads covers 512 / G float4 columns x G groups, consecutive threads
+// on consecutive columns (coalesced).  Group j sums splits j, j+G, j+2G,
+// ... in split order, loading eight rows at a time before adding them, and
+// the G group sums are then added in group order -- a fixed order, so every
+// run gives the same bits.  Every segment count and stride is a multiple of
+// 4 floats and every pointer 16-byte aligned (the padded layout guarantees
+// both).
+constexpr int kRsThreads = 512;
 
 __host__ __device__ __forceinline__ int rs_groups(int splits) {
   int g = 1;
-  while (g < 32 && g * 8 < splits) g *= 2;
+  while (g < 16 && g * 8 < splits) g *= 2;
   return g;
 }
-__host__ __device__ __forceinline__ int64_t rs_blocks(const ReduceSeg &sg) {
-  const int64_t cols4 = kRsThreads / rs_groups(sg.splits);
-  return (sg.count / 4 + cols4 - 1) / cols4;
+__host__ __device__ __forceinline__ int64_t rs_blocks(int64_t count, int splits) {
+  const int64_t cols4 = kRsThreads / rs_groups(splits);
+  return (count / 4 + cols4 - 1) / cols4;
 }
 
-__global__ void __launch_bounds__(kRsThreads) reduce_segments_kernel(ReduceSegs segs) {
+__global__ void __launch_bounds__(kRsThreads, 2) reduce_segments_kernel(ReduceSegs segs) {
   int si = 0;
-  int64_t b = blockIdx.x;
-  while (si + 1 < segs.n && b >= rs_blocks(segs.seg[si])) {
-    b -= rs_blocks(segs.seg[si]);
-    ++si;
-  }
-  const ReduceSeg &sg = segs.seg[si];
-  const int G = rs_groups(sg.splits);
+  while (si + 1 < segs.n && (int)blockIdx.x >= segs.first_block[si + 1]) ++si;
+  const int b = (int)blockIdx.x - segs.first_block[si];
+  const float *src0 = segs.seg[si].src;
+  float *dst = segs.seg[si].dst;
+  const int64_t count4 = segs.seg[si].count / 4;
+  const int splits = segs.seg[si].splits;
+  const int64_t stride4 = segs.seg[si].stride / 4;
+  const int G = segs.groups[si];
   const int cols4 = kRsThreads / G;
-  const int c = threadIdx.x % cols4, grp = threadIdx.x / cols4;
-  const int64_t i4 = b * cols4 + c;
-  const bool live = i4 < sg.count / 4;
-  const int64_t stride4 = sg.stride / 4;
-  const float4 *src = reinterpret_cast<const float4 *>(sg.src) + i4;
+  const int c = threadIdx.x & (cols4 - 1), grp = threadIdx.x / cols4;
+  const int64_t i4 = (int64_t)b * cols4 + c;
+  const bool live = i4 < count4;
+  const float4 *src = reinterpret_cast<const float4 *>(src0) + i4;
   float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   if (live) {
-#pragma unroll 8
-    for (int z = grp; z < sg.splits; z += G) {
-      const float4 x = __ldcs(src + (int64_t)z * stride4);  // read once: streaming
-      t.x += x.x;
-      t.y += x.y;
-      t.z += x.z;
-      t.w += x.w;
+    for (int z0 = grp; z0 < splits; z0 += 8 * G) {
+      float4 x[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int z = z0 + u * G;
+        x[u] = z < splits ? __ldcs(src + (int64_t)z * stride4)  // read once: streaming
+                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        t.x += x[u].x;
+        t.y += x[u].y;
+        t.z += x[u].z;
+        t.w += x[u].w;
+      }
     }
   }
   __shared__ float4 part[kRsThreads];
@@ -515,7 +522,7 @@ __global__ void __launch_bounds__(kRsThreads) reduce_segments_kernel(ReduceSegs 
       s4.z += x.z;
       s4.w += x.w;
     }
-    reinterpret_cast<float4 *>(sg.dst)[i4] = s4;
+    reinterpret_cast<float4 *>(dst)[i4] = s4;
   }
 }
 
@@ -866,9 +873,23 @@ void launch_colsum(const float *x, int64_t rows, int cols, int ld,
   colsum_kernel<<<grid, 128, 0, s>>>(x, rows, cols, ld, partials, splits);
 }
 
-void launch_reduce_segments(const ReduceSegs &segs, cudaStream_t s) {
+void launch_reduce_segments(const ReduceSegs &segs_in, cudaStream_t s) {
+  // segments with the most splits first: their blocks run longest, so they
+  // start in the first wave
+  ReduceSegs segs = segs_in;
+  for (int i = 1; i < segs.n; ++i)
+    for (int j = i; j > 0 && segs.seg[j].splits > segs.seg[j - 1].splits; --j) {
+      const ReduceSeg t = segs.seg[j];
+      segs.seg[j] = segs.seg[j - 1];
+      segs.seg[j - 1] = t;
+    }
   int64_t blocks = 0;
-  for (int i = 0; i < segs.n; ++i) blocks += rs_blocks(segs.seg[i]);
+  for (int i = 0; i < segs.n; ++i) {
+    segs.first_block[i] = (int)blocks;
+    segs.groups[i] = rs_groups(segs.seg[i].splits);
+    blocks += rs_blocks(segs.seg[i].count, segs.seg[i].splits);
+  }
+  segs.first_block[segs.n] = (int)blocks;
   if (blocks == 0) return;
   reduce_segments_kernel<<<(unsigned)blocks, kRsThreads, 0, s>>>(segs);
 }

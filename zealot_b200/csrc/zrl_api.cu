@@ -12,6 +12,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <future>
 #include <map>
 #include <string>
 #include <vector>
@@ -34,6 +35,60 @@ void shuffle_i32(uint64_t seed, int64_t n, int32_t *order);
 void mlp_init_reference(const int32_t *dims, int n_dims, float out_scale,
                         uint64_t *rng, float *params);
 }
+
+// The sample orders of one update (ppo.rs:360-366): per epoch the
+// permutation of the global sample indices (Lcg seed = step + e * mbs + 1),
+// cut into minibatches; with several ranks each rank keeps, per minibatch,
+// the positions of the rows it holds, in order.  Each epoch's order is
+// computed on its own worker thread into pinned memory, so the sequential
+// shuffles run in parallel with each other and with the enqueueing of GPU
+// work -- and, speculatively, during the previous update.
+struct OrderPlan {
+  int32_t *buf = nullptr;  // pinned [epochs][n_global]
+  int64_t cap = 0;
+  bool valid = false;
+  uint64_t seed0 = 0;
+  int64_t n_global = 0, n_local = 0, row_offset = 0;
+  int epochs = 0, mbs = 0, world = 1;
+  std::vector<int64_t> counts, offs, rows;  // [epochs * mbs], [epochs * mbs], [epochs]
+  std::vector<std::future<void>> jobs;
+
+  bool matches(uint64_t s0, int64_t ng, int64_t nl, int64_t ro, int ep, int mb, int w) const {
+    return valid && seed0 == s0 && n_global == ng && n_local == nl && row_offset == ro &&
+           epochs == ep && mbs == mb && world == w;
+  }
+  void wait_all() {
+    for (auto &j : jobs)
+      if (j.valid()) j.wait();
+    jobs.clear();
+  }
+  void compute(int e) {
+    const uint64_t seed = seed0 + (uint64_t)e * (uint64_t)mbs + 1ull;
+    int32_t *ord = buf + (int64_t)e * n_global;
+    const int64_t mb = n_global / mbs;
+    if (world == 1) {
+      zrl::shuffle_i32(seed, n_global, ord);
+      rows[e] = mb * mbs;
+      for (int m = 0; m < mbs; ++m) {
+        counts[e * mbs + m] = mb;
+        offs[e * mbs + m] = (int64_t)m * mb;
+      }
+      return;
+    }
+    std::vector<int32_t> perm(n_global);
+    zrl::shuffle_i32(seed, n_global, perm.data());
+    int64_t n = 0;
+    for (int m = 0; m < mbs; ++m) {
+      offs[e * mbs + m] = n;
+      for (int64_t p = (int64_t)m * mb; p < (int64_t)(m + 1) * mb; ++p) {
+        const int64_t r = perm[p] - row_offset;
+        if (r >= 0 && r < n_local) ord[n++] = (int32_t)r;
+      }
+      counts[e * mbs + m] = n - offs[e * mbs + m];
+    }
+    rows[e] = n;
+  }
+};
 
 struct zrl_ctx {
   int device = 0;
@@ -78,6 +133,7 @@ struct zrl_ctx {
   int32_t *order_dev = nullptr;
   int32_t *order_pinned = nullptr;
   int64_t order_pinned_cap = 0;
+  OrderPlan plan[2];  // this update's and (speculatively) the next one's
 
   // minibatch activations / deltas
   int64_t mb_cap = 0;
@@ -282,6 +338,34 @@ static zrl_status ensure_pinned_orders(zrl_ctx *ctx, int64_t count) {
   ctx->order_pinned = nullptr;
   CK(cudaMallocHost((void **)&ctx->order_pinned, sizeof(int32_t) * (size_t)count));
   ctx->order_pinned_cap = count;
+  return ZRL_OK;
+}
+
+static zrl_status start_plan(zrl_ctx *ctx, OrderPlan &P, uint64_t seed0, int64_t n_global,
+                             int64_t n_local, int64_t row_offset, int epochs, int mbs) {
+  P.wait_all();
+  P.valid = false;
+  const int64_t need = (int64_t)std::max(epochs, 1) * n_global;
+  if (need > P.cap) {
+    if (P.buf) cudaFreeHost(P.buf);
+    P.buf = nullptr;
+    P.cap = 0;
+    CK(cudaMallocHost((void **)&P.buf, sizeof(int32_t) * (size_t)need));
+    P.cap = need;
+  }
+  P.seed0 = seed0;
+  P.n_global = n_global;
+  P.n_local = n_local;
+  P.row_offset = row_offset;
+  P.epochs = epochs;
+  P.mbs = mbs;
+  P.world = ctx->comm.world;
+  P.counts.assign((size_t)epochs * mbs, 0);
+  P.offs.assign((size_t)epochs * mbs, 0);
+  P.rows.assign((size_t)epochs, 0);
+  for (int e = 0; e < epochs; ++e)
+    P.jobs.push_back(std::async(std::launch::async, [&P, e] { P.compute(e); }));
+  P.valid = true;
   return ZRL_OK;
 }
 
@@ -791,7 +875,6 @@ static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
                              int64_t n_global, int64_t row_offset) {
   const int64_t mbs = cfg->minibatches;
   const int64_t mb = n_global / mbs;
-  const int64_t n_used = mb * mbs;
   const float scale = 1.0f / (float)mb;
   // stats start as {0, 0, 0, 0, lr} (ppo.rs:351-354); lr and the Adam
   // steps stay on the device
@@ -800,41 +883,24 @@ static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
   CK(cudaMemcpyAsync(&ctx->st->stats[4], &ctx->st->lr, sizeof(float),
                      cudaMemcpyDeviceToDevice, ctx->stream));
   const bool multi = ctx->comm.world > 1;
-  TRY(ensure_pinned_orders(ctx, (int64_t)std::max(cfg->epochs, 1) * n_global));
   TRY(ensure_mb(ctx, std::max<int64_t>(multi ? std::min<int64_t>(mb, n_local) : mb, 1)));
-  std::vector<int32_t> perm(multi ? n_global : 0);
-  std::vector<int64_t> counts(mbs), offs(mbs);
-  if (cfg->epochs > 0) TRY(normalize_batch(ctx, d.obs, d.cobs, n_local));
-  for (int e = 0; e < cfg->epochs; ++e) {
-    const uint64_t seed = (uint64_t)(ctx->t_logstd_host + e * mbs) + 1ull;
-    int32_t *ord = ctx->order_pinned + (int64_t)e * n_global;
-    int64_t n_rows = 0;
-    if (!multi) {
-      shuffle_i32(seed, n_global, ord);
-      n_rows = n_used;
-      for (int64_t m = 0; m < mbs; ++m) {
-        counts[m] = mb;
-        offs[m] = m * mb;
-      }
-    } else {
-      // every rank computes the global permutation and keeps, per
-      // minibatch, the positions whose rows it owns (in order)
-      shuffle_i32(seed, n_global, perm.data());
-      for (int64_t m = 0; m < mbs; ++m) {
-        offs[m] = n_rows;
-        for (int64_t p = m * mb; p < (m + 1) * mb; ++p) {
-          const int64_t r = perm[p] - row_offset;
-          if (r >= 0 && r < n_local) ord[n_rows++] = (int32_t)r;
-        }
-        counts[m] = n_rows - offs[m];
-      }
-      int64_t mx = 0;
-      for (int64_t m = 0; m < mbs; ++m) mx = std::max(mx, counts[m]);
-      TRY(ensure_mb(ctx, std::max<int64_t>(mx, 1)));
-    }
+  const uint64_t seed0 = (uint64_t)ctx->t_logstd_host;
+  const int epochs = std::max(cfg->epochs, 0);
+  // this update's orders: a speculative plan that matches, or start now
+  OrderPlan *P = nullptr;
+  for (auto &q : ctx->plan)
+    if (q.matches(seed0, n_global, n_local, row_offset, epochs, (int)mbs, ctx->comm.world)) P = &q;
+  if (!P) {
+    P = &ctx->plan[0];
+    TRY(start_plan(ctx, *P, seed0, n_global, n_local, row_offset, epochs, (int)mbs));
+  }
+  if (epochs > 0) TRY(normalize_batch(ctx, d.obs, d.cobs, n_local));
+  for (int e = 0; e < epochs; ++e) {
+    P->jobs[e].wait();
+    const int64_t n_rows = P->rows[e];
     if (n_rows > 0) {
-      CK(cudaMemcpyAsync(ctx->order_dev, ord, sizeof(int32_t) * n_rows,
-                         cudaMemcpyHostToDevice, ctx->stream));
+      CK(cudaMemcpyAsync(ctx->order_dev, P->buf + (int64_t)e * n_global,
+                         sizeof(int32_t) * n_rows, cudaMemcpyHostToDevice, ctx->stream));
       GatherArgs g = gather_args(ctx, d.act, d.mo, d.lpo, d.vo, d.adv, d.ret);
       g.n_used = n_rows;
       g.apply_adv_norm = 1;
@@ -843,14 +909,19 @@ static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
       CHECK_LAUNCH();
     }
     for (int64_t m = 0; m < mbs; ++m) {
-      MbView v = epoch_view(ctx, offs[m], counts[m]);
+      MbView v = epoch_view(ctx, P->offs[e * mbs + m], P->counts[e * mbs + m]);
       TRY(minibatch_grads(ctx, cfg, v, scale));
       TRY(allreduce_grads(ctx));
       TRY(step(ctx, cfg, (int)mbs, m == mbs - 1, true));
     }
   }
+  // the next update's orders, computed while this one runs (in the other
+  // plan: this plan's pinned orders may still be in flight to the device)
+  OrderPlan &Q = P == &ctx->plan[0] ? ctx->plan[1] : ctx->plan[0];
+  if (epochs > 0)
+    TRY(start_plan(ctx, Q, seed0 + (uint64_t)epochs * (uint64_t)mbs, n_global, n_local,
+                   row_offset, epochs, (int)mbs));
   ctx->t_logstd_host += cfg->epochs * (int32_t)mbs;
-  (void)n_local;
   return ZRL_OK;
 }
 
@@ -1046,6 +1117,11 @@ zrl_status zrl_destroy(zrl_ctx *ctx) {
   if (ctx->rs.dpart) cudaFree(ctx->rs.dpart);
   if (ctx->rs.ticket) cudaFree(ctx->rs.ticket);
   if (ctx->st_host) cudaFreeHost(ctx->st_host);
+  for (auto &q : ctx->plan) {
+    q.wait_all();
+    if (q.buf) cudaFreeHost(q.buf);
+    q.buf = nullptr;
+  }
   if (ctx->order_pinned) cudaFreeHost(ctx->order_pinned);
   for (auto e : ctx->ev_pool) cudaEventDestroy(e);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);

@@ -158,6 +158,10 @@ constexpr int kMaxSegs = 2 * ZRL_MAX_LAYERS * 2 + 4;
 struct ReduceSegs {
   ReduceSeg seg[kMaxSegs];
   int n;
+  // filled by launch_reduce_segments: first block and split groups of
+  // each segment
+  int first_block[kMaxSegs + 1];
+  int groups[kMaxSegs];
 };
 void launch_reduce_segments(const ReduceSegs &segs, cudaStream_t s);
 
