@@ -261,20 +261,25 @@ __global__ void norm_prepare_kernel(const float *m2, float count, int dim,
   }
 }
 
+// One warp per row (rows strided over the grid): lane i takes columns
+// i, i+32, ... of the padded row, so the index math has no division.
 __global__ void normalize_rows_kernel(const float *x, int64_t n, int dim,
                                       int pitch, const float *mean,
                                       const float *sd, float *out, int round) {
-  const int64_t total = n * pitch;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = e / pitch;
-    const int i = (int)(e - r * pitch);
-    float y = 0.0f;
-    if (i < dim) {
-      y = __fdiv_rn(__fsub_rn(x[r * dim + i], mean[i]), sd[i]);
-      y = fminf(fmaxf(y, -5.0f), 5.0f);
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp; r < n; r += nwarps) {
+    const float *xr = x + r * dim;
+    float *o = out + r * pitch;
+    for (int i = lane; i < pitch; i += 32) {
+      float y = 0.0f;
+      if (i < dim) {
+        y = __fdiv_rn(__fsub_rn(xr[i], mean[i]), sd[i]);
+        y = fminf(fmaxf(y, -5.0f), 5.0f);
+      }
+      o[i] = round ? rna_tf32(y) : y;
     }
-    out[e] = round ? rna_tf32(y) : y;
   }
 }
 
@@ -849,8 +854,8 @@ void launch_norm_prepare(const float *m2, float count, int dim, float *sd,
 void launch_normalize_rows(const float *x, int64_t n, int dim, int pitch,
                            const float *mean, const float *sd, float *out,
                            int round_tf32, cudaStream_t s) {
-  normalize_rows_kernel<<<grid_for(n * pitch, 256), 256, 0, s>>>(
-      x, n, dim, pitch, mean, sd, out, round_tf32);
+  normalize_rows_kernel<<<grid_for(n * 32, 256), 256, 0, s>>>(x, n, dim, pitch, mean, sd, out,
+                                                               round_tf32);
 }
 
 void launch_round_copy(const float *src, float *dst, int64_t n, cudaStream_t s) {

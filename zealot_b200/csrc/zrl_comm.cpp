@@ -16,7 +16,7 @@ typedef struct {
   char internal[128];
 } nccl_unique_id_t;
 enum { kNcclSum = 0 };
-enum { kNcclFloat32 = 7, kNcclFloat64 = 9 };
+enum { kNcclFloat32 = 7, kNcclFloat64 = 8 };  // ncclFloat, ncclDouble (nccl.h)
 enum { kNcclInProgress = 7 };
 
 struct NcclApi {
