@@ -40,7 +40,7 @@ METRIC = "PPO-update samples/s (fwd+bwd+GAE+Adam)"
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--config", default=None, choices=["c1", "c2", "c4", "c5"])
@@ -92,7 +92,7 @@ class Clocks:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -102,6 +102,16 @@ class Clocks:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+
+    def wait_first(self, timeout=5.0):
+        """Block until nvidia-smi has printed its first sample (it takes a
+        few hundred ms to start), so the timed region is sampled."""
+        t0 = time.time()
+        while self.proc and not self.lines and time.time() - t0 < timeout:
+            time.sleep(0.02)
+
+    def mark(self):
+        self.i0 = len(self.lines)
 
     def stop(self):
         if not self.proc:
@@ -113,7 +123,13 @@ class Clocks:
             self.proc.kill()
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        # the samples taken during the timed region (from the mark on); if
+        # the region was shorter than the sampling period, the sample just
+        # before it and the one after it (both under load)
+        lines = self.lines[getattr(self, "i0", 0):]
+        if len(lines) < 2:
+            lines = self.lines[max(getattr(self, "i0", 0) - 1, 0):]
+        for ln in lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -377,9 +393,12 @@ def main():
 
     clocks = Clocks(local)
     clocks.start()
+    clocks.wait_first()
+    step_device()  # keep the GPU under load while the sampler settles
     l0 = ac.kernel_launches()
     barrier()
     torch.cuda.synchronize()
+    clocks.mark()
     times, st = timed(step_device, args.steps)
     torch.cuda.synchronize()
     barrier()
