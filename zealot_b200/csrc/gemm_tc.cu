@@ -380,6 +380,7 @@ struct TcProb {
   int splits;
   int tiles_m, tiles_n;
   FastDiv div_m, div_n;  // by tiles_m, by tiles_n
+  int bn;          // this problem's tile width: the launch's BN or BN / 2
   int tile0;       // first flat tile index of this problem
   const float *bias;
   int round_out;
@@ -422,7 +423,7 @@ struct Smem {
 };
 
 struct Tile {
-  int p, m0, n0, z, kbeg, nk;
+  int p, m0, n0, z, kbeg, nk, bn;
 };
 
 // Flat tile t -> problem, then m fastest, n, split.  Tiles are BM * CG
@@ -439,7 +440,8 @@ __device__ __forceinline__ Tile decode_tile(int t, const TcGroup &g) {
   const int mt = lt - rest * pr.tiles_m;
   const int z = fdiv(rest, pr.div_n);
   tl.m0 = mt * BM * CG;
-  tl.n0 = (rest - z * pr.tiles_n) * BN;
+  tl.bn = pr.bn;
+  tl.n0 = (rest - z * pr.tiles_n) * pr.bn;
   tl.z = z;
   tl.kbeg = tl.z * pr.kc;
   const int kend = min(pr.K, tl.kbeg + pr.kc);
@@ -622,7 +624,10 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
         const Tile tl = decode_tile<BN, CG>(t, g);
         // this CTA's rows of A and columns of B
         const int am = tl.m0 + BM * (int)rank;
-        const int bn = tl.n0 + BN / CG * (int)rank;
+        const int bn = tl.n0 + tl.bn / CG * (int)rank;
+        // bytes of one stage in each CTA: A, and this CTA's tl.bn / CG
+        // columns of B
+        const uint32_t stage_bytes = (uint32_t)(S::kA + tl.bn / CG * BKB);
         for (int kb = 0; kb < tl.nk; ++kb, ++kbg) {
           const int s = kbg % STAGES;
           const uint32_t ph = (uint32_t)(kbg / STAGES) & 1u;
@@ -633,7 +638,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
           if (CG == 2) {
             // both CTAs' boxes count on the even CTA's full barrier
             const uint32_t fb = peer_addr(smem_u32(&full[s]), 0);
-            if (rank == 0) mbar_expect_tx(&full[s], 2 * S::kStage);
+            if (rank == 0) mbar_expect_tx(&full[s], 2 * stage_bytes);
             if (A_MN) {
 #pragma unroll
               for (int c = 0; c < BM / 32; ++c)
@@ -644,12 +649,13 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
             if (B_MN) {
 #pragma unroll
               for (int c = 0; c < BN / CG / 32; ++c)
-                tma_load_2d_pair(b_s + c * 4096, &maps.b[tl.p], fb, bn + 32 * c, k0);
+                if (c < tl.bn / CG / 32)
+                  tma_load_2d_pair(b_s + c * 4096, &maps.b[tl.p], fb, bn + 32 * c, k0);
             } else {
               tma_load_2d_pair(b_s, &maps.b[tl.p], fb, k0, bn);
             }
           } else {
-            mbar_expect_tx(&full[s], S::kStage);
+            mbar_expect_tx(&full[s], stage_bytes);
             if (A_MN) {  // Delta [K rows, M cols]: four 32-column boxes of 32 rows
 #pragma unroll
               for (int c = 0; c < BM / 32; ++c)
@@ -660,7 +666,8 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
             if (B_MN) {
 #pragma unroll
               for (int c = 0; c < BN / 32; ++c)
-                tma_load_2d(b_s + c * 4096, &maps.b[tl.p], &full[s], bn + 32 * c, k0);
+                if (c < tl.bn / 32)
+                  tma_load_2d(b_s + c * 4096, &maps.b[tl.p], &full[s], bn + 32 * c, k0);
             } else {
               tma_load_2d(b_s, &maps.b[tl.p], &full[s], k0, bn);
             }
@@ -671,7 +678,8 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
   } else if (warp == 1) {
     // ---------------------------------------------------- MMA issuer
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = idesc_tf32(BM * CG, BN, A_MN, B_MN);
+      constexpr uint32_t idesc_full = idesc_tf32(BM * CG, BN, A_MN, B_MN);
+      constexpr uint32_t idesc_half = idesc_tf32(BM * CG, BN / 2, A_MN, B_MN);
       int kbg = 0, it = 0;
       bool ok = true;
       for (int t = unit; t < tiles && ok; t += units, ++it) {
@@ -682,6 +690,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
         if (it >= 2 && !(ok = mbar_spin(&acce[ab], aph ^ 1u, g.err, 4))) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(ab * BN);
+        const uint32_t idesc = tl.bn == BN ? idesc_full : idesc_half;
         for (int kb = 0; kb < tl.nk; ++kb, ++kbg) {
           const int s = kbg % STAGES;
           const uint32_t ph = (uint32_t)(kbg / STAGES) & 1u;
@@ -738,9 +747,10 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
       if (idle || t >= tiles) return;
       const Tile tl = decode_tile<BN, CG>(t, g);
       const TcProb &pr = g.p[tl.p];
-      const int n = tl.n0 + (half + 2 * (j % CPT)) * 32;
+      const int c = half + 2 * (j % CPT);
+      const int n = tl.n0 + c * 32;
       const int r0 = tl.m0 + BM * (int)rank + quarter * 32;
-      if (n >= pr.N || r0 >= pr.M) return;
+      if (c * 32 >= tl.bn || n >= pr.N || r0 >= pr.M) return;
       const int sl = j % NS;
       mbar_expect_tx(&wbar[sl], 4096);
       tma_load_2d(smem + S::kStageBytes + ew * (NS * 4096) + sl * 4096, &maps.x[tl.p], &wbar[sl],
@@ -780,7 +790,8 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
 #pragma unroll
         for (int k = 0; k < CPT; ++k) {
           const int n = nt.n0 + (half + 2 * k) * 32;
-          if (n < np.N && r0 < np.M) tma_prefetch_2d(&maps.x[nt.p], n, r0);
+          if ((half + 2 * k) * 32 < nt.bn && n < np.N && r0 < np.M)
+            tma_prefetch_2d(&maps.x[nt.p], n, r0);
         }
       }
       if (ok) ok = mbar_wait(&accf[ab], aph, g.err, 3);
@@ -796,7 +807,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
         const int n = tl.n0 + c * 32;
         const int sl = j % NS;
         const uint32_t slot = slots + (uint32_t)sl * 4096u;
-        const bool live = !idle && n < pr.N && row0 < pr.M;  // uniform over the warp
+        const bool live = !idle && c * 32 < tl.bn && n < pr.N && row0 < pr.M;  // warp-uniform
         if (k == CPT - 1 && !(live && have)) {
           // (no TMEM read in this chunk) hand the accumulator back now
           tc_fence_before();
@@ -866,7 +877,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
             bulk_commit();
           }
           stored = true;
-        } else if (!idle && pr.colsum && n < pr.N && n + lane < pr.N &&
+        } else if (!idle && pr.colsum && c * 32 < tl.bn && n < pr.N && n + lane < pr.N &&
                    tl.m0 + BM * (int)rank < pr.M) {
           // a quarter past the last row: its partial row is 0
           pr.colsum[((int64_t)(tl.m0 / BM + rank) * 4 + quarter) * pr.N + n + lane] = 0.0f;
@@ -1183,7 +1194,10 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
     const CUtensorMap *ta = kind == 2 ? cached_map(eng, g.A, g.K, g.M, g.lda, 32, 1, err)
                                       : cached_map(eng, g.A, g.M, g.K, g.lda, BM, 0, err);
     // B: [N rows, K cols] K-major (forward) or [K rows, N cols] MN-major
-    const CUtensorMap *tb = kind == 0 ? cached_map(eng, g.B, g.N, g.K, g.ldb, BN / CG, 0, err)
+    // a problem at most half as wide as the launch's tiles takes half-width
+    // tiles (while each CTA's share of B stays whole 32-column boxes)
+    const int bn = (BN / 2 / CG >= 32 && g.N <= BN / 2) ? BN / 2 : BN;
+    const CUtensorMap *tb = kind == 0 ? cached_map(eng, g.B, g.N, g.K, g.ldb, bn / CG, 0, err)
                                       : cached_map(eng, g.B, g.K, g.N, g.ldb, 32, 1, err);
     const CUtensorMap *tc = cached_map(eng, g.C, g.M, g.N, g.ldc, split, 2, err);
     if (!ta || !tb || !tc) return ZRL_CUDA_ERROR;
@@ -1204,7 +1218,8 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
     pr.splits = split;
     pr.tiles_m = (g.M + BM * CG - 1) / (BM * CG);
     pr.div_m = fast_div((uint32_t)pr.tiles_m);
-    pr.tiles_n = (g.N + BN - 1) / BN;
+    pr.bn = bn;
+    pr.tiles_n = (g.N + bn - 1) / bn;
     pr.div_n = fast_div((uint32_t)pr.tiles_n);
     pr.tile0 = tiles;
     pr.bias = g.bias;
