@@ -13,6 +13,32 @@ namespace zrl {
 
 namespace {
 
+// Programmatic dependent launch.  A kernel launched with launch_pdl may
+// start while the previous kernel in the stream is still running: it must
+// call pdl_wait() before touching global memory, after which that kernel
+// has completed and its writes are visible.  pdl_trigger() lets the next
+// kernel begin its own launch early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... K, typename... A>
+void launch_pdl(void (*kfn)(K...), unsigned grid, unsigned block, cudaStream_t s, A... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kfn, args...);
+}
+
+
 constexpr float kLogSqrt2Pi = 0.9189385f;  // ppo.rs:18
 
 // tf32 with round-to-nearest (ties away): the tensor-core GEMMs then read
@@ -196,6 +222,8 @@ __global__ void adv_finalize_kernel(const double *moments, int64_t n_global,
 // applying Normalizer::normalize (ppo.rs:198-205) to the two observation
 // rows and the advantage normalization (ppo.rs:346-348) to adv.
 __global__ void gather_kernel(GatherArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -300,6 +328,8 @@ constexpr int kLossMaxA = 128;  // 4 action dims per lane
 // last block to finish adds the partials in block order (deterministic).
 __global__ void __launch_bounds__(kLossThreads)
 loss_kernel(LossArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int nwb = blockDim.x >> 5;
   const int64_t gw = (int64_t)blockIdx.x * nwb + wid;
@@ -482,6 +512,8 @@ __host__ __device__ __forceinline__ int64_t rs_blocks(int64_t count, int splits)
 }
 
 __global__ void __launch_bounds__(kRsThreads, 2) reduce_segments_kernel(ReduceSegs segs) {
+  pdl_wait();
+  pdl_trigger();
   int si = 0;
   while (si + 1 < segs.n && (int)blockIdx.x >= segs.first_block[si + 1]) ++si;
   const int b = (int)blockIdx.x - segs.first_block[si];
@@ -550,6 +582,8 @@ constexpr int kPrestepThreads = 256;
 
 __global__ void __launch_bounds__(kPrestepThreads)
 prestep_kernel(PrestepArgs a, double *partials, unsigned int *ticket) {
+  pdl_wait();
+  pdl_trigger();
   double sa = 0.0, sc = 0.0;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
 #pragma unroll 4
@@ -655,6 +689,8 @@ __device__ __forceinline__ void adam_one(float &p, float &m, float &v, float g,
 }
 
 __global__ void adam_kernel(AdamArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const DevState *st = a.st;
   const float lr = st->step_lr;
   const int64_t n4 = a.n / 4;
@@ -843,7 +879,7 @@ void launch_adv_finalize(const double *moments, int64_t n_global, DevState *st,
 
 void launch_gather(const GatherArgs &a, cudaStream_t s) {
   const int threads = 256;
-  gather_kernel<<<grid_for(a.n_used * 32, threads), threads, 0, s>>>(a);
+  launch_pdl(gather_kernel, grid_for(a.n_used * 32, threads), threads, s, a);
 }
 
 void launch_norm_prepare(const float *m2, float count, int dim, float *sd,
@@ -869,7 +905,7 @@ void launch_loss(const LossArgs &a, cudaStream_t s) {
   // sample's loads in flight; the block rows are summed by the segment
   // reduce that follows the backward pass
   const int blocks = loss_blocks(a.mb);
-  loss_kernel<<<blocks, kLossThreads, 0, s>>>(a);
+  launch_pdl(loss_kernel, blocks, kLossThreads, s, a);
 }
 
 void launch_colsum(const float *x, int64_t rows, int cols, int ld,
@@ -896,18 +932,18 @@ void launch_reduce_segments(const ReduceSegs &segs_in, cudaStream_t s) {
   }
   segs.first_block[segs.n] = (int)blocks;
   if (blocks == 0) return;
-  reduce_segments_kernel<<<(unsigned)blocks, kRsThreads, 0, s>>>(segs);
+  launch_pdl(reduce_segments_kernel, (unsigned)blocks, kRsThreads, s, segs);
 }
 
 void launch_prestep(const PrestepArgs &a, ReduceScratch &rs, cudaStream_t s) {
   const int64_t work = (a.actor_end - a.actor_begin);
   int blocks = grid_for(work, kPrestepThreads, 148);
   if (blocks > rs.max_blocks) blocks = rs.max_blocks;
-  prestep_kernel<<<blocks, kPrestepThreads, 0, s>>>(a, rs.dpart, rs.ticket + 1);
+  launch_pdl(prestep_kernel, blocks, kPrestepThreads, s, a, rs.dpart, rs.ticket + 1);
 }
 
 void launch_adam(const AdamArgs &a, cudaStream_t s) {
-  adam_kernel<<<grid_for(a.n / 4, 256, 148 * 8), 256, 0, s>>>(a);
+  launch_pdl(adam_kernel, grid_for(a.n / 4, 256, 148 * 8), 256, s, a);
 }
 
 void launch_unpad_rows(const float *src, int64_t rows, int pitch, int cols,
