@@ -42,7 +42,14 @@ def round_tf32(x):
     return b.view(np.float32)
 
 
-def run(ctx, torch, lhs, rhs, lt, rt, split=1):
+def round_bf16(x):
+    """fp32 -> bf16 -> fp32, round to nearest even (the conversion torch and
+    the epilogue use)."""
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(torch.bfloat16).float().numpy()
+
+
+def run(ctx, torch, lhs, rhs, lt, rt, split=1, bf16=False):
     """C = lhs @ rhs with the stored operands transposed as the flags say."""
     m, k = lhs.shape
     n = rhs.shape[1]
@@ -55,9 +62,10 @@ def run(ctx, torch, lhs, rhs, lt, rt, split=1):
 
     def up(x):
         r, c = x.shape
-        ld = (c + 3) // 4 * 4
-        t = torch.zeros((r, ld), dtype=torch.float32, device=dev)
-        t[:, :c] = torch.from_numpy(np.ascontiguousarray(x))
+        al = 8 if bf16 else 4  # 16-byte row pitch
+        ld = (c + al - 1) // al * al
+        t = torch.zeros((r, ld), dtype=torch.bfloat16 if bf16 else torch.float32, device=dev)
+        t[:, :c] = torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(t.dtype)
         return t, ld
 
     ta, lda = up(a)
@@ -75,13 +83,21 @@ def torch():
     return torch
 
 
-@pytest.mark.parametrize("precision", ["fp32", "tf32"])
+@pytest.mark.parametrize("precision", ["fp32", "tf32", "bf16"])
 @pytest.mark.parametrize("ci", range(len(CASES)))
 def test_cutile_selftest_cases(torch, precision, ci):
     m, n, k, lt, rt = CASES[ci]
     lhs = fixture(m, k, ci)
     rhs = fixture(k, n, ci + 7)
     ctx = Z.Context((4, 4), (4, 1), precision=precision)
+    if precision == "bf16":
+        # bf16 operands: exact products, only the fp32 accumulation remains
+        lb, rb = round_bf16(lhs), round_bf16(rhs)
+        ref = lb.astype(np.float64) @ rb.astype(np.float64)
+        got = run(ctx, torch, lb, rb, lt, rt, bf16=True)
+        err = np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-6)
+        assert err < 1e-5, err
+        return
     ref = lhs.astype(np.float64) @ rhs.astype(np.float64)
     got = run(ctx, torch, lhs, rhs, lt, rt)
     err = np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-6)
@@ -96,7 +112,7 @@ def test_cutile_selftest_cases(torch, precision, ci):
         assert err < 1e-5, err
 
 
-@pytest.mark.parametrize("precision", ["fp32", "tf32"])
+@pytest.mark.parametrize("precision", ["fp32", "tf32", "bf16"])
 @pytest.mark.parametrize("shape", PPO)
 @pytest.mark.parametrize("split", [1, 8])
 def test_ppo_shapes(torch, precision, shape, split):
@@ -104,13 +120,14 @@ def test_ppo_shapes(torch, precision, shape, split):
     if split > 1 and not lt:
         pytest.skip("split-K is used for the weight gradient only")
     rng = np.random.default_rng(m + n + k)
-    lhs = round_tf32(rng.standard_normal((m, k), dtype=np.float32))
-    rhs = round_tf32(rng.standard_normal((k, n), dtype=np.float32))
+    rnd = round_bf16 if precision == "bf16" else round_tf32
+    lhs = rnd(rng.standard_normal((m, k), dtype=np.float32))
+    rhs = rnd(rng.standard_normal((k, n), dtype=np.float32))
     ctx = Z.Context((4, 4), (4, 1), precision=precision)
-    got = run(ctx, torch, lhs, rhs, lt, rt, split=split)
+    got = run(ctx, torch, lhs, rhs, lt, rt, split=split, bf16=precision == "bf16")
     ref = lhs.astype(np.float64) @ rhs.astype(np.float64)
     err = np.abs(got - ref).max() / np.abs(ref).max()
     # operands are tf32-exact, so only accumulation error remains; the
     # tensor core's fp32 accumulation over K = 24,576 measures ~6e-5, still
     # 30x inside the 2e-3 tf32 bar
-    assert err < (1e-5 if precision == "fp32" else 2e-4), err
+    assert err < (1e-5 if precision == "fp32" else 2e-4), err  # tf32, bf16: exact operands

@@ -240,6 +240,12 @@ __device__ __forceinline__ uint64_t desc_kmajor(uint32_t addr) {
 __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t addr) {
   return make_desc(addr, 4096, 512, kLayoutSw128Base32);
 }
+//  MN-major bf16 (layout 2, the plain 128-byte swizzle): 64 elements of
+//    M/N per K-row, 8 K-rows per 1 KB atom (sbo); 64-element M/N atom
+//    columns (one TMA box of 64 K-rows each) every 8 KB (lbo).
+__device__ __forceinline__ uint64_t desc_mnmajor_bf16(uint32_t addr) {
+  return make_desc(addr, 8192, 1024, kLayoutSw128);
+}
 
 // Instruction descriptor for kind::tf32 with an f32 accumulator.
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn, bool b_mn) {
@@ -250,6 +256,28 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn, bool 
          | ((b_mn ? 1u : 0u) << 16)     // B major
          | ((uint32_t)(N >> 3) << 17)   // N / 8
          | ((uint32_t)(M >> 4) << 24);  // M / 16
+}
+
+// Instruction descriptor for kind::f16 with bf16 inputs and an f32
+// accumulator.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool b_mn) {
+  return (1u << 4)                      // D format f32
+         | (1u << 7)                    // A format bf16
+         | (1u << 10)                   // B format bf16
+         | ((a_mn ? 1u : 0u) << 15)     // A major
+         | ((b_mn ? 1u : 0u) << 16)     // B major
+         | ((uint32_t)(N >> 3) << 17)   // N / 8
+         | ((uint32_t)(M >> 4) << 24);  // M / 16
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 
 __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b,
@@ -290,6 +318,15 @@ __device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *m
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
       "l"((uint64_t)map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void mma_bf16_pair(uint32_t tmem_d, uint64_t a, uint64_t b,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 __device__ __forceinline__ void mma_tf32_pair(uint32_t tmem_d, uint64_t a, uint64_t b,
@@ -428,7 +465,7 @@ struct Tile {
 
 // Flat tile t -> problem, then m fastest, n, split.  Tiles are BM * CG
 // rows (the CTA pair's tile: 256 rows).
-template <int BN, int CG>
+template <int BN, int CG, int KE>
 __device__ __forceinline__ Tile decode_tile(int t, const TcGroup &g) {
   Tile tl;
   int p = 0;
@@ -445,7 +482,7 @@ __device__ __forceinline__ Tile decode_tile(int t, const TcGroup &g) {
   tl.z = z;
   tl.kbeg = tl.z * pr.kc;
   const int kend = min(pr.K, tl.kbeg + pr.kc);
-  tl.nk = kend > tl.kbeg ? (kend - tl.kbeg + 31) / 32 : 0;
+  tl.nk = kend > tl.kbeg ? (kend - tl.kbeg + KE - 1) / KE : 0;
   return tl;
 }
 
@@ -543,9 +580,15 @@ __device__ __forceinline__ void epi_chunk(const EpiChunk &e, int lane, bool last
     st_shared4(e.slot + ((q ^ e.sw) << 4), v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, int STAGES, int CG>
+template <int BN, bool A_MN, bool B_MN, int EPI, int STAGES, int CG, bool BF>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGroup g) {
+  // K elements of one 128-byte k-block, and the M/N width of one MN-major
+  // TMA box (one 128-byte row): 32 tf32 or 64 bf16
+  constexpr int KE = BF ? 64 : 32;
+  constexpr int MNB = BF ? 64 : 32;   // MN-major box width (elements)
+  constexpr int MNBB = BF ? 8192 : 4096;  // bytes of one MN-major box
+  static_assert(!BF || !B_MN || BN / CG >= 64, "bf16 MN-major B needs 64-column boxes");
   static_assert(BN == 32 || BN == 64 || BN == 128 || BN == 256, "BN");
   static_assert(CG == 1 || (CG == 2 && BN >= 64), "a CTA pair splits B in 32-column boxes");
   using S = Smem<BN, STAGES, EPI, CG>;
@@ -621,7 +664,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
       int kbg = 0;
       bool ok = true;
       for (int t = unit; t < tiles && ok; t += units) {
-        const Tile tl = decode_tile<BN, CG>(t, g);
+        const Tile tl = decode_tile<BN, CG, KE>(t, g);
         // this CTA's rows of A and columns of B
         const int am = tl.m0 + BM * (int)rank;
         const int bn = tl.n0 + tl.bn / CG * (int)rank;
@@ -634,40 +677,40 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
           if (kbg >= STAGES && !(ok = mbar_spin(&empty[s], ph ^ 1u, g.err, 1))) break;
           uint8_t *a_s = smem + s * S::kStage;
           uint8_t *b_s = a_s + S::kA;
-          const int k0 = tl.kbeg + kb * 32;
+          const int k0 = tl.kbeg + kb * KE;
           if (CG == 2) {
             // both CTAs' boxes count on the even CTA's full barrier
             const uint32_t fb = peer_addr(smem_u32(&full[s]), 0);
             if (rank == 0) mbar_expect_tx(&full[s], 2 * stage_bytes);
             if (A_MN) {
 #pragma unroll
-              for (int c = 0; c < BM / 32; ++c)
-                tma_load_2d_pair(a_s + c * 4096, &maps.a[tl.p], fb, am + 32 * c, k0);
+              for (int c = 0; c < BM / MNB; ++c)
+                tma_load_2d_pair(a_s + c * MNBB, &maps.a[tl.p], fb, am + MNB * c, k0);
             } else {
               tma_load_2d_pair(a_s, &maps.a[tl.p], fb, k0, am);
             }
             if (B_MN) {
 #pragma unroll
-              for (int c = 0; c < BN / CG / 32; ++c)
-                if (c < tl.bn / CG / 32)
-                  tma_load_2d_pair(b_s + c * 4096, &maps.b[tl.p], fb, bn + 32 * c, k0);
+              for (int c = 0; c < BN / CG / MNB; ++c)
+                if (c < tl.bn / CG / MNB)
+                  tma_load_2d_pair(b_s + c * MNBB, &maps.b[tl.p], fb, bn + MNB * c, k0);
             } else {
               tma_load_2d_pair(b_s, &maps.b[tl.p], fb, k0, bn);
             }
           } else {
             mbar_expect_tx(&full[s], stage_bytes);
-            if (A_MN) {  // Delta [K rows, M cols]: four 32-column boxes of 32 rows
+            if (A_MN) {  // Delta [K rows, M cols]: MN-major boxes of one k-block
 #pragma unroll
-              for (int c = 0; c < BM / 32; ++c)
-                tma_load_2d(a_s + c * 4096, &maps.a[tl.p], &full[s], am + 32 * c, k0);
+              for (int c = 0; c < BM / MNB; ++c)
+                tma_load_2d(a_s + c * MNBB, &maps.a[tl.p], &full[s], am + MNB * c, k0);
             } else {     // [M rows, K cols]: one box of 128 rows x 32
               tma_load_2d(a_s, &maps.a[tl.p], &full[s], k0, am);
             }
             if (B_MN) {
 #pragma unroll
-              for (int c = 0; c < BN / 32; ++c)
-                if (c < tl.bn / 32)
-                  tma_load_2d(b_s + c * 4096, &maps.b[tl.p], &full[s], bn + 32 * c, k0);
+              for (int c = 0; c < BN / MNB; ++c)
+                if (c < tl.bn / MNB)
+                  tma_load_2d(b_s + c * MNBB, &maps.b[tl.p], &full[s], bn + MNB * c, k0);
             } else {
               tma_load_2d(b_s, &maps.b[tl.p], &full[s], k0, bn);
             }
@@ -678,12 +721,14 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
   } else if (warp == 1) {
     // ---------------------------------------------------- MMA issuer
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc_full = idesc_tf32(BM * CG, BN, A_MN, B_MN);
-      constexpr uint32_t idesc_half = idesc_tf32(BM * CG, BN / 2, A_MN, B_MN);
+      constexpr uint32_t idesc_full = BF ? idesc_bf16(BM * CG, BN, A_MN, B_MN)
+                                         : idesc_tf32(BM * CG, BN, A_MN, B_MN);
+      constexpr uint32_t idesc_half = BF ? idesc_bf16(BM * CG, BN / 2, A_MN, B_MN)
+                                         : idesc_tf32(BM * CG, BN / 2, A_MN, B_MN);
       int kbg = 0, it = 0;
       bool ok = true;
       for (int t = unit; t < tiles && ok; t += units, ++it) {
-        const Tile tl = decode_tile<BN, CG>(t, g);
+        const Tile tl = decode_tile<BN, CG, KE>(t, g);
         const int ab = it & 1;
         const uint32_t aph = (uint32_t)(it >> 1) & 1u;
         // the epilogue must have drained this accumulator (tile it-2)
@@ -700,14 +745,27 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
           const uint32_t b_s = a_s + S::kA;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            // K-major: 32 bytes further in the swizzle row; MN-major: 8
-            // K-rows (1024 bytes) further
-            const uint64_t da = A_MN ? desc_mnmajor(a_s + 1024 * j) : desc_kmajor(a_s + 32 * j);
-            const uint64_t db = B_MN ? desc_mnmajor(b_s + 1024 * j) : desc_kmajor(b_s + 32 * j);
-            if (CG == 2)
-              mma_tf32_pair(d, da, db, idesc, (kb > 0 || j > 0) ? 1u : 0u);
-            else
-              mma_tf32(d, da, db, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+            // one MMA takes 32 bytes of K: K-major, 32 bytes further in the
+            // swizzle row; MN-major, 8 (tf32) or 16 (bf16) K-rows further
+            const uint32_t step = BF ? 2048 : 1024;
+            const uint64_t da = A_MN ? (BF ? desc_mnmajor_bf16(a_s + step * j)
+                                           : desc_mnmajor(a_s + step * j))
+                                     : desc_kmajor(a_s + 32 * j);
+            const uint64_t db = B_MN ? (BF ? desc_mnmajor_bf16(b_s + step * j)
+                                           : desc_mnmajor(b_s + step * j))
+                                     : desc_kmajor(b_s + 32 * j);
+            const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
+            if (CG == 2) {
+              if (BF)
+                mma_bf16_pair(d, da, db, idesc, acc);
+              else
+                mma_tf32_pair(d, da, db, idesc, acc);
+            } else {
+              if (BF)
+                mma_bf16(d, da, db, idesc, acc);
+              else
+                mma_tf32(d, da, db, idesc, acc);
+            }
           }
           if (CG == 2)
             mma_commit_pair(&empty[s]);
@@ -745,7 +803,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
     auto issue_aux = [&](int j) {
       const int t = unit + (j / CPT) * units;
       if (idle || t >= tiles) return;
-      const Tile tl = decode_tile<BN, CG>(t, g);
+      const Tile tl = decode_tile<BN, CG, KE>(t, g);
       const TcProb &pr = g.p[tl.p];
       const int c = half + 2 * (j % CPT);
       const int n = tl.n0 + c * 32;
@@ -764,7 +822,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
     const uint32_t acce_pair = peer_addr(smem_u32(acce), 0);
     const uint32_t wbias = smem_u32(bias_sh + ew * (S::kCptMax * 32));
     for (int t = unit; t < tiles; t += units, ++it) {
-      const Tile tl = decode_tile<BN, CG>(t, g);
+      const Tile tl = decode_tile<BN, CG, KE>(t, g);
       const TcProb &pr = g.p[tl.p];
       const int ab = it & 1;
       const uint32_t aph = (uint32_t)(it >> 1) & 1u;
@@ -784,7 +842,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
       }
       if (EPI == EPI_ELU_GRAD && lane == 0 && !idle && t + units < tiles) {
         // the next tile's post-activation boxes of this warp into L2
-        const Tile nt = decode_tile<BN, CG>(t + units, g);
+        const Tile nt = decode_tile<BN, CG, KE>(t + units, g);
         const TcProb &np = g.p[nt.p];
         const int r0 = nt.m0 + BM * (int)rank + quarter * 32;
 #pragma unroll
@@ -928,15 +986,19 @@ int g_sms = 148;
 // boxes of [box_rows, 32].  K-major operands use the 128-byte swizzle of
 // 16-byte chunks; MN-major ones the 128-byte swizzle of 32-byte chunks
 // (the layout the MN-major tf32 descriptor expects).
+//
+// bf16 operands: boxes of [box_rows, 64] elements (still 128-byte rows),
+// the plain 128-byte swizzle for both majors.
 bool make_map(CUtensorMap *m, const float *base, int64_t rows, int64_t cols, int64_t ld,
-              int box_rows, bool mn_major, std::string *err) {
+              int box_rows, bool mn_major, std::string *err, bool bf16 = false) {
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * (bf16 ? 2 : 4)};
+  cuuint32_t box[2] = {bf16 ? 64u : 32u, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  const CUtensorMapSwizzle sw =
-      mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
-  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box,
+  const CUtensorMapSwizzle sw = (mn_major && !bf16) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                                    : CU_TENSOR_MAP_SWIZZLE_128B;
+  CUresult r = g_encode(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                        2, (void *)base, dims, strides, box,
                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -1003,13 +1065,13 @@ int max_pairs(K kfn, int smem) {
   return n;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, int CG>
+template <int BN, bool A_MN, bool B_MN, int EPI, int CG, bool BF>
 cudaError_t launch_one(const TcMaps &maps, const TcGroup &grp, cudaStream_t s) {
   constexpr int ST = stages_for<BN, EPI, CG>();
   static_assert(ST >= 2, "stage ring");
   using S = Smem<BN, ST, EPI, CG>;
   static_assert(S::kBytes <= 227 * 1024, "shared memory");
-  auto kfn = tc_gemm_kernel<BN, A_MN, B_MN, EPI, ST, CG>;
+  auto kfn = tc_gemm_kernel<BN, A_MN, B_MN, EPI, ST, CG, BF>;
   static bool attr = false;  // set once per instantiation (same value on every device)
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1037,19 +1099,36 @@ cudaError_t launch_one(const TcMaps &maps, const TcGroup &grp, cudaStream_t s) {
   return cudaLaunchKernelEx(&cfg, kfn, maps, grp);
 }
 
-template <int BN, int CG>
+template <int BN, int CG, bool BF>
 cudaError_t dispatch_bn(int kind, int epi, const TcMaps &maps, const TcGroup &grp,
                         cudaStream_t s) {
   if (kind == 0) {  // forward
-    if (epi == EPI_BIAS_ELU) return launch_one<BN, false, false, EPI_BIAS_ELU, CG>(maps, grp, s);
-    if (epi == EPI_BIAS) return launch_one<BN, false, false, EPI_BIAS, CG>(maps, grp, s);
-    return launch_one<BN, false, false, EPI_STORE, CG>(maps, grp, s);
+    if (epi == EPI_BIAS_ELU) return launch_one<BN, false, false, EPI_BIAS_ELU, CG, BF>(maps, grp, s);
+    if (epi == EPI_BIAS) return launch_one<BN, false, false, EPI_BIAS, CG, BF>(maps, grp, s);
+    return launch_one<BN, false, false, EPI_STORE, CG, BF>(maps, grp, s);
   }
-  if (kind == 1) {  // dgrad
-    if (epi == EPI_ELU_GRAD) return launch_one<BN, false, true, EPI_ELU_GRAD, CG>(maps, grp, s);
-    return launch_one<BN, false, true, EPI_STORE, CG>(maps, grp, s);
+  if constexpr (!BF || BN / CG >= 64) {
+    if (kind == 1) {  // dgrad
+      if (epi == EPI_ELU_GRAD)
+        return launch_one<BN, false, true, EPI_ELU_GRAD, CG, BF>(maps, grp, s);
+      return launch_one<BN, false, true, EPI_STORE, CG, BF>(maps, grp, s);
+    }
+    return launch_one<BN, true, true, EPI_STORE, CG, BF>(maps, grp, s);  // wgrad
   }
-  return launch_one<BN, true, true, EPI_STORE, CG>(maps, grp, s);  // wgrad
+  return cudaErrorInvalidValue;
+}
+
+template <bool BF>
+cudaError_t dispatch(int CG, int BN, int kind, int epi, const TcMaps &maps, const TcGroup &grp,
+                     cudaStream_t s) {
+  if (CG == 1) {
+    if (BN == 32) return dispatch_bn<32, 1, BF>(kind, epi, maps, grp, s);
+    if (BN == 64) return dispatch_bn<64, 1, BF>(kind, epi, maps, grp, s);
+    return dispatch_bn<128, 1, BF>(kind, epi, maps, grp, s);
+  }
+  if (BN == 64) return dispatch_bn<64, 2, BF>(kind, epi, maps, grp, s);
+  if (BN == 128) return dispatch_bn<128, 2, BF>(kind, epi, maps, grp, s);
+  return dispatch_bn<256, 2, BF>(kind, epi, maps, grp, s);
 }
 
 }  // namespace
@@ -1058,7 +1137,8 @@ struct TcCache {
   std::map<std::tuple<const void *, int64_t, int64_t, int64_t, int, int>, CUtensorMap> maps;
 };
 
-// kind: 0 K-major operand, 1 MN-major operand, 2 output
+// kind: 0 K-major operand, 1 MN-major operand, 2 output, 3 K-major bf16
+// operand, 4 MN-major bf16 operand
 static const CUtensorMap *cached_map(GemmEngine *eng, const float *base, int64_t rows,
                                      int64_t cols, int64_t ld, int box_or_splits, int kind,
                                      std::string *err) {
@@ -1068,7 +1148,8 @@ static const CUtensorMap *cached_map(GemmEngine *eng, const float *base, int64_t
   if (it != c->maps.end()) return &it->second;
   CUtensorMap m;
   const bool ok = kind == 2 ? make_out_map(&m, (float *)base, rows, cols, ld, box_or_splits, err)
-                            : make_map(&m, base, rows, cols, ld, box_or_splits, kind == 1, err);
+                            : make_map(&m, base, rows, cols, ld, box_or_splits,
+                                       kind == 1 || kind == 4, err, kind >= 3);
   if (!ok) return nullptr;
   if (c->maps.size() > 4096) c->maps.clear();
   return &(c->maps[key] = m);
@@ -1133,10 +1214,11 @@ static int layout_kind(const GemmArgs &g) {
 zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precision,
                          cudaStream_t s, int *launched, std::string *err) {
   *launched = 0;
-  if (precision != ZRL_GEMM_TF32) {
-    *err = "bf16 tensor-core GEMMs are not built in this library";
+  if (precision != ZRL_GEMM_TF32 && precision != ZRL_GEMM_BF16) {
+    *err = "the tensor-core GEMM takes tf32 or bf16 operands";
     return ZRL_NOT_SUPPORTED;
   }
+  const bool bf = precision == ZRL_GEMM_BF16;
   if (n < 1 || n > kMaxProbs) {
     *err = "a grouped tensor-core GEMM takes 1 to 8 problems";
     return ZRL_INVALID_ARG;
@@ -1153,12 +1235,14 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
       *err = "the GEMMs of one group share operand layout and epilogue";
       return ZRL_INVALID_ARG;
     }
-    // TMA needs 16-byte aligned bases and row pitches.  Ragged M, N and K
-    // are handled (out-of-range TMA reads are zero-filled, stores clipped).
+    // TMA needs 16-byte aligned bases and row pitches (operand pitches in
+    // elements: multiples of 4 for fp32, 8 for bf16).  Ragged M, N and K are
+    // handled (out-of-range TMA reads are zero-filled, stores clipped).
     auto a16 = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
-    if (g.lda % 4 || g.ldb % 4 || g.ldc % 4 || (g.aux && g.ldaux % 4) || !a16(g.A) ||
-        !a16(g.B) || !a16(g.C) || (g.aux && !a16(g.aux))) {
-      *err = "tensor-core GEMM needs 16-byte aligned operands and row pitches (multiples of 4)";
+    const int op_align = bf ? 8 : 4;
+    if (g.lda % op_align || g.ldb % op_align || g.ldc % 4 || (g.aux && g.ldaux % 4) ||
+        !a16(g.A) || !a16(g.B) || !a16(g.C) || (g.aux && !a16(g.aux))) {
+      *err = "tensor-core GEMM needs 16-byte aligned operands and row pitches";
       return ZRL_INVALID_ARG;
     }
     if (g.M <= 0 || g.N <= 0 || g.K <= 0) {
@@ -1181,7 +1265,10 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
   // the shared-memory and L2 bytes per flop.  Others run on single CTAs
   // with 128 x BN tiles, BN up to 128.
   const int CG = (minM >= 256 && maxN > 32) ? 2 : 1;
-  const int BN = maxN <= 32 ? 32 : (maxN <= 64 ? 64 : (maxN <= 128 || CG == 1 ? 128 : 256));
+  int BN = maxN <= 32 ? 32 : (maxN <= 64 ? 64 : (maxN <= 128 || CG == 1 ? 128 : 256));
+  // bf16 MN-major B is loaded in 64-column boxes: each CTA's share of a
+  // tile is a whole number of them
+  if (bf && kind != 0 && BN / CG < 64) BN = 64 * CG;
   TcMaps maps;
   memset(&maps, 0, sizeof(maps));
   TcGroup grp;
@@ -1191,14 +1278,17 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
     const GemmArgs &g = gs[i];
     const int split = g.split_k < 1 ? 1 : g.split_k;
     // A: [M rows, K cols] K-major, or [K rows, M cols] MN-major (wgrad)
-    const CUtensorMap *ta = kind == 2 ? cached_map(eng, g.A, g.K, g.M, g.lda, 32, 1, err)
-                                      : cached_map(eng, g.A, g.M, g.K, g.lda, BM, 0, err);
+    const CUtensorMap *ta = kind == 2 ? cached_map(eng, g.A, g.K, g.M, g.lda, bf ? 64 : 32,
+                                                   bf ? 4 : 1, err)
+                                      : cached_map(eng, g.A, g.M, g.K, g.lda, BM, bf ? 3 : 0, err);
     // B: [N rows, K cols] K-major (forward) or [K rows, N cols] MN-major
     // a problem at most half as wide as the launch's tiles takes half-width
     // tiles (while each CTA's share of B stays whole 32-column boxes)
-    const int bn = (BN / 2 / CG >= 32 && g.N <= BN / 2) ? BN / 2 : BN;
-    const CUtensorMap *tb = kind == 0 ? cached_map(eng, g.B, g.N, g.K, g.ldb, bn / CG, 0, err)
-                                      : cached_map(eng, g.B, g.K, g.N, g.ldb, 32, 1, err);
+    const int min_share = (bf && kind != 0) ? 64 : 32;
+    const int bn = (BN / 2 / CG >= min_share && g.N <= BN / 2) ? BN / 2 : BN;
+    const int kmaj = bf ? 3 : 0, mnmaj = bf ? 4 : 1, ke = bf ? 64 : 32;
+    const CUtensorMap *tb = kind == 0 ? cached_map(eng, g.B, g.N, g.K, g.ldb, bn / CG, kmaj, err)
+                                      : cached_map(eng, g.B, g.K, g.N, g.ldb, ke, mnmaj, err);
     const CUtensorMap *tc = cached_map(eng, g.C, g.M, g.N, g.ldc, split, 2, err);
     if (!ta || !tb || !tc) return ZRL_CUDA_ERROR;
     maps.a[i] = *ta;
@@ -1214,7 +1304,7 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
     pr.M = g.M;
     pr.N = g.N;
     pr.K = g.K;
-    pr.kc = ((g.K + split - 1) / split + 31) / 32 * 32;
+    pr.kc = ((g.K + split - 1) / split + ke - 1) / ke * ke;
     pr.splits = split;
     pr.tiles_m = (g.M + BM * CG - 1) / (BM * CG);
     pr.div_m = fast_div((uint32_t)pr.tiles_m);
@@ -1230,16 +1320,8 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
   grp.n = n;
   grp.tiles = tiles;
   grp.err = eng->err_dev;
-  cudaError_t e;
-  if (CG == 1) {
-    if (BN == 32) e = dispatch_bn<32, 1>(kind, gs[0].epi, maps, grp, s);
-    else if (BN == 64) e = dispatch_bn<64, 1>(kind, gs[0].epi, maps, grp, s);
-    else e = dispatch_bn<128, 1>(kind, gs[0].epi, maps, grp, s);
-  } else {
-    if (BN == 64) e = dispatch_bn<64, 2>(kind, gs[0].epi, maps, grp, s);
-    else if (BN == 128) e = dispatch_bn<128, 2>(kind, gs[0].epi, maps, grp, s);
-    else e = dispatch_bn<256, 2>(kind, gs[0].epi, maps, grp, s);
-  }
+  const cudaError_t e = bf ? dispatch<true>(CG, BN, kind, gs[0].epi, maps, grp, s)
+                           : dispatch<false>(CG, BN, kind, gs[0].epi, maps, grp, s);
   if (e != cudaSuccess) {
     *err = std::string("tensor-core GEMM launch: ") + cudaGetErrorString(e);
     return ZRL_CUDA_ERROR;

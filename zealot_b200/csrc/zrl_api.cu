@@ -196,6 +196,12 @@ static zrl_status bad(zrl_ctx *ctx, const char *msg) {
   return ZRL_INVALID_ARG;
 }
 
+// bf16 contexts run the GEMM hook (zrl_gemm) only so far
+static zrl_status bf16_update_unsupported(zrl_ctx *ctx) {
+  ctx->err = "the bf16 update path is not built yet (zrl_gemm takes bf16 operands)";
+  return ZRL_NOT_SUPPORTED;
+}
+
 template <typename T>
 static zrl_status dalloc(zrl_ctx *ctx, T **p, int64_t count) {
   if (*p) cudaFree(*p);
@@ -1374,6 +1380,7 @@ static zrl_status write_back_adv(zrl_ctx *ctx, zrl_batch *b, const float *adv_de
 zrl_status zrl_update(zrl_ctx *ctx, const zrl_ppo_config *cfg, zrl_batch *batch,
                       zrl_stats *out) {
   if (!ctx) return ZRL_INVALID_ARG;
+  if (ctx->precision == ZRL_GEMM_BF16) return bf16_update_unsupported(ctx);
   TRY(check_cfg(ctx, cfg));
   int64_t n_global = 0;
   TRY(check_batch(ctx, batch, &n_global));
@@ -1394,6 +1401,7 @@ zrl_status zrl_update(zrl_ctx *ctx, const zrl_ppo_config *cfg, zrl_batch *batch,
 zrl_status zrl_gae_update(zrl_ctx *ctx, const zrl_ppo_config *cfg,
                           const zrl_rollout *ro, zrl_batch *batch, zrl_stats *out) {
   if (!ctx || !ro) return ZRL_INVALID_ARG;
+  if (ctx->precision == ZRL_GEMM_BF16) return bf16_update_unsupported(ctx);
   TRY(check_cfg(ctx, cfg));
   int64_t n_global = 0;
   TRY(check_batch(ctx, batch, &n_global));
@@ -1447,6 +1455,7 @@ zrl_status zrl_gae_update(zrl_ctx *ctx, const zrl_ppo_config *cfg,
 zrl_status zrl_forward(zrl_ctx *ctx, const float *obs, const float *critic_obs,
                        int64_t n, float *mean_out, float *value_out, int32_t on_device) {
   if (!ctx) return ZRL_INVALID_ARG;
+  if (ctx->precision == ZRL_GEMM_BF16) return bf16_update_unsupported(ctx);
   if (n < 0) return bad(ctx, "negative n");
   if ((mean_out && !obs) || (value_out && !critic_obs)) return bad(ctx, "null input");
   if (n == 0) return ZRL_OK;
@@ -1525,6 +1534,7 @@ zrl_status zrl_minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
                                const zrl_batch *batch, const int64_t *idx,
                                int64_t n_idx, float *grads_out, float *sums3_out) {
   if (!ctx || !idx || !grads_out) return ZRL_INVALID_ARG;
+  if (ctx->precision == ZRL_GEMM_BF16) return bf16_update_unsupported(ctx);
   TRY(check_cfg(ctx, cfg));
   int64_t n_global = 0;
   TRY(check_batch(ctx, batch, &n_global));
@@ -1561,6 +1571,7 @@ zrl_status zrl_minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
 zrl_status zrl_apply_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg, const float *grads,
                            float kl) {
   if (!ctx || !grads) return ZRL_INVALID_ARG;
+  if (ctx->precision == ZRL_GEMM_BF16) return bf16_update_unsupported(ctx);
   TRY(check_cfg(ctx, cfg));
   CK(cudaSetDevice(ctx->device));
   std::vector<float> pad(ctx->grad_len, 0.0f);
@@ -1621,6 +1632,7 @@ zrl_status zrl_policy_step(zrl_ctx *ctx, const float *obs, const float *critic_o
                            int64_t n, uint64_t seed, uint64_t counter, float *action,
                            float *logp, float *mean, float *value, int32_t on_device) {
   if (!ctx || !obs || !action) return ZRL_INVALID_ARG;
+  if (ctx->precision == ZRL_GEMM_BF16) return bf16_update_unsupported(ctx);
   if (value && !critic_obs) return bad(ctx, "value requested without critic_obs");
   if (n < 0) return bad(ctx, "negative n");
   if (n == 0) return ZRL_OK;
