@@ -451,8 +451,8 @@ struct Smem {
   static constexpr int kSlots = slots_for(EPI);
   static constexpr int kStaging = kEpiWarps * kSlots * 4096;
   // the bias of a warp's chunks in the current tile
-  static constexpr int kCptMax = BN >= 64 ? BN / 64 : 1;
-  static constexpr int kBias = kEpiWarps * kCptMax * 32 * 4;
+  static constexpr int kBiasPerWarp = BN / 2 > 64 ? BN / 2 : 64;  // floats
+  static constexpr int kBias = kEpiWarps * kBiasPerWarp * 4;
   static constexpr int kBarOff = kStageBytes + kStaging + kBias;
   // full, empty, acc_full x2, acc_empty x2, one aux barrier per staging slot
   static constexpr int kBars = 2 * STAGES + 4 + kEpiWarps * kSlots;
@@ -578,6 +578,100 @@ __device__ __forceinline__ void epi_chunk(const EpiChunk &e, int lane, bool last
 #pragma unroll
   for (int q = 0; q < 8; ++q)
     st_shared4(e.slot + ((q ^ e.sw) << 4), v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+
+// The 64-column chunk of the bf16-output epilogues (forward hidden layers,
+// dgrad): one row of 64 bf16 is 128 bytes, so the staging slot keeps the
+// 128-byte swizzle.  fp32 math as in epi_chunk; the column sums are taken
+// in two 32-column halves; the stored values are rounded to bf16 (nearest
+// even) by the conversion.
+template <int EPI, bool FULL, typename Release>
+__device__ __forceinline__ void epi_chunk_bf16(const EpiChunk &e, int lane, bool last,
+                                               Release release, bool row_ok, int valid_cols) {
+  float v[64];
+  if (!FULL && e.taddr == 0xFFFFFFFFu) {
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = 0.0f;
+  } else {
+    uint32_t r[32];
+    tmem_ld32(e.taddr, r);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+    tmem_ld32(e.taddr + 32, r);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(r[i]);
+    if (last) release();
+  }
+  if (EPI == EPI_BIAS_ELU) {
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      const float4 b = ld_shared4(e.bias + 16u * q);  // broadcast
+      v[4 * q + 0] += b.x;
+      v[4 * q + 1] += b.y;
+      v[4 * q + 2] += b.z;
+      v[4 * q + 3] += b.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = v[i] > 0.0f ? v[i] : exp_sfu(v[i]) - 1.0f;
+  }
+  if (EPI == EPI_ELU_GRAD) {
+    // the bf16 post-activation row in the slot: 16-byte piece q holds
+    // columns 8q..8q+7
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 raw = ld_shared4(e.slot + ((q ^ e.sw) << 4));
+      const uint32_t w[4] = {__float_as_uint(raw.x), __float_as_uint(raw.y),
+                             __float_as_uint(raw.z), __float_as_uint(raw.w)};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float lo = __uint_as_float(w[i] << 16), hi = __uint_as_float(w[i] & 0xFFFF0000u);
+        v[8 * q + 2 * i] *= fmin_nan(lo + 1.0f, 1.0f);
+        v[8 * q + 2 * i + 1] *= fmin_nan(hi + 1.0f, 1.0f);
+      }
+    }
+  }
+  if (!FULL) {
+#pragma unroll
+    for (int i = 0; i < 64; ++i)
+      if (!row_ok || i >= valid_cols) v[i] = 0.0f;
+  }
+  if (e.colsum) {
+    const uint32_t base = e.slot - (uint32_t)lane * 128u;
+    const uint32_t q = (uint32_t)lane >> 2, wd = ((uint32_t)lane & 3u) * 4u;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      __syncwarp();
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        st_shared4(e.slot + ((k ^ e.sw) << 4), v[32 * h + 4 * k], v[32 * h + 4 * k + 1],
+                   v[32 * h + 4 * k + 2], v[32 * h + 4 * k + 3]);
+      __syncwarp();
+      float cs = 0.0f;
+#pragma unroll
+      for (int r = 0; r < 32; ++r) {
+        float x;
+        asm volatile("ld.shared.f32 %0, [%1];"
+                     : "=f"(x)
+                     : "r"(base + r * 128u + ((q ^ (uint32_t)(r & 7)) << 4) + wd)
+                     : "memory");
+        cs += x;
+      }
+      if (32 * h + lane < valid_cols) e.colsum[32 * h + lane] = cs;
+    }
+    __syncwarp();
+  }
+  // bf16 pairs (round to nearest even), staged for the TMA store
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    uint32_t pk[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;"
+          : "=r"(pk[i])
+          : "f"(v[8 * q + 2 * i + 1]), "f"(v[8 * q + 2 * i]));
+    st_shared4(e.slot + ((q ^ e.sw) << 4), __uint_as_float(pk[0]), __uint_as_float(pk[1]),
+               __uint_as_float(pk[2]), __uint_as_float(pk[3]));
+  }
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI, int STAGES, int CG, bool BF>
@@ -788,11 +882,14 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
     // numbered j = 0, 1, ... over its tiles, cycle through its NS staging
     // slots.
     constexpr int NS = S::kSlots;
-    constexpr int CPT = BN >= 64 ? BN / 64 : 1;
+    // chunk width: 32 fp32 columns, or 64 for bf16 outputs (128-byte rows)
+    constexpr bool OB = BF && (EPI == EPI_BIAS_ELU || EPI == EPI_ELU_GRAD);
+    constexpr int CW = OB ? 64 : 32;
+    constexpr int CPT = BN >= 2 * CW ? BN / (2 * CW) : 1;
     const int ew = warp - 2;       // 0..kEpiWarps-1
     const int quarter = warp & 3;  // TMEM lane quarter = rows of this warp
     const int half = ew >> 2;      // chunks c with c % 2 == half
-    const bool idle = BN < 64 && half == 1;
+    const bool idle = BN < 2 * CW && half == 1;
     const uint32_t slots = smem_u32(smem + S::kStageBytes + ew * (NS * 4096));
     uint64_t *wbar = xbar + ew * NS;
     const uint32_t row_addr = (uint32_t)lane * 128u;  // this lane's row in a slot
@@ -806,9 +903,9 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
       const Tile tl = decode_tile<BN, CG, KE>(t, g);
       const TcProb &pr = g.p[tl.p];
       const int c = half + 2 * (j % CPT);
-      const int n = tl.n0 + c * 32;
+      const int n = tl.n0 + c * CW;
       const int r0 = tl.m0 + BM * (int)rank + quarter * 32;
-      if (c * 32 >= tl.bn || n >= pr.N || r0 >= pr.M) return;
+      if (c * CW >= tl.bn || n >= pr.N || r0 >= pr.M) return;
       const int sl = j % NS;
       mbar_expect_tx(&wbar[sl], 4096);
       tma_load_2d(smem + S::kStageBytes + ew * (NS * 4096) + sl * 4096, &maps.x[tl.p], &wbar[sl],
@@ -820,7 +917,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
     bool ok = true, prev_store = false;
     // the pair's MMA warp waits on the even CTA's acc_empty barriers
     const uint32_t acce_pair = peer_addr(smem_u32(acce), 0);
-    const uint32_t wbias = smem_u32(bias_sh + ew * (S::kCptMax * 32));
+    const uint32_t wbias = smem_u32(bias_sh + ew * S::kBiasPerWarp);
     for (int t = unit; t < tiles; t += units, ++it) {
       const Tile tl = decode_tile<BN, CG, KE>(t, g);
       const TcProb &pr = g.p[tl.p];
@@ -831,13 +928,16 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
         // this tile's bias for the warp's chunks, one coalesced load per
         // chunk before the accumulator wait (0 past N)
 #pragma unroll
-        for (int k = 0; k < CPT; ++k) {
-          const int n = tl.n0 + (half + 2 * k) * 32 + lane;
-          const float b = n < pr.N ? __ldg(pr.bias + n) : 0.0f;
-          asm volatile("st.shared.f32 [%0], %1;" ::"r"(wbias + (uint32_t)(k * 32 + lane) * 4u),
-                       "f"(b)
-                       : "memory");
-        }
+        for (int k = 0; k < CPT; ++k)
+#pragma unroll
+          for (int h = 0; h < CW / 32; ++h) {
+            const int n = tl.n0 + (half + 2 * k) * CW + 32 * h + lane;
+            const float b = n < pr.N ? __ldg(pr.bias + n) : 0.0f;
+            asm volatile("st.shared.f32 [%0], %1;" ::"r"(wbias + (uint32_t)(k * CW + 32 * h + lane) *
+                                                              4u),
+                         "f"(b)
+                         : "memory");
+          }
         __syncwarp();
       }
       if (EPI == EPI_ELU_GRAD && lane == 0 && !idle && t + units < tiles) {
@@ -847,8 +947,8 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
         const int r0 = nt.m0 + BM * (int)rank + quarter * 32;
 #pragma unroll
         for (int k = 0; k < CPT; ++k) {
-          const int n = nt.n0 + (half + 2 * k) * 32;
-          if ((half + 2 * k) * 32 < nt.bn && n < np.N && r0 < np.M)
+          const int n = nt.n0 + (half + 2 * k) * CW;
+          if ((half + 2 * k) * CW < nt.bn && n < np.N && r0 < np.M)
             tma_prefetch_2d(&maps.x[nt.p], n, r0);
         }
       }
@@ -862,10 +962,10 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
 #pragma unroll 1
       for (int k = 0; k < CPT; ++k, ++j) {
         const int c = half + 2 * k;
-        const int n = tl.n0 + c * 32;
+        const int n = tl.n0 + c * CW;
         const int sl = j % NS;
         const uint32_t slot = slots + (uint32_t)sl * 4096u;
-        const bool live = !idle && c * 32 < tl.bn && n < pr.N && row0 < pr.M;  // warp-uniform
+        const bool live = !idle && c * CW < tl.bn && n < pr.N && row0 < pr.M;  // warp-uniform
         if (k == CPT - 1 && !(live && have)) {
           // (no TMEM read in this chunk) hand the accumulator back now
           tc_fence_before();
@@ -894,39 +994,38 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
             __syncwarp();
           }
           EpiChunk ec;
-          ec.taddr = have ? taddr + c * 32 : 0xFFFFFFFFu;
+          ec.taddr = have ? taddr + c * CW : 0xFFFFFFFFu;
           ec.slot = slot + row_addr;
           ec.sw = sw;
-          ec.bias = wbias + (uint32_t)(k * 32) * 4u;
+          ec.bias = wbias + (uint32_t)(k * CW) * 4u;
           ec.round = pr.round_out;
           ec.colsum = pr.colsum
                           ? pr.colsum + ((int64_t)(tl.m0 / BM + rank) * 4 + quarter) * pr.N + n
                           : nullptr;
           // the common case (every row and column valid, accumulator
           // written) has its own code path, free of per-element predicates
-          const int valid_cols = pr.N - n < 32 ? pr.N - n : 32;
-          if (have && rows_full && valid_cols == 32) {
-            epi_chunk<EPI, true>(ec, lane, k == CPT - 1, [&] {
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) {
-                if (CG == 2)
-                  mbar_arrive_cluster(acce_pair + 8u * ab);
-                else
-                  mbar_arrive(&acce[ab]);
-              }
-            }, true, 32);
+          const int valid_cols = pr.N - n < CW ? pr.N - n : CW;
+          auto release = [&] {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              if (CG == 2)
+                mbar_arrive_cluster(acce_pair + 8u * ab);
+              else
+                mbar_arrive(&acce[ab]);
+            }
+          };
+          if (have && rows_full && valid_cols == CW) {
+            if (OB)
+              epi_chunk_bf16<EPI, true>(ec, lane, k == CPT - 1, release, true, CW);
+            else
+              epi_chunk<EPI, true>(ec, lane, k == CPT - 1, release, true, CW);
           } else {
-            epi_chunk<EPI, false>(ec, lane, k == CPT - 1 && have, [&] {
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) {
-                if (CG == 2)
-                  mbar_arrive_cluster(acce_pair + 8u * ab);
-                else
-                  mbar_arrive(&acce[ab]);
-              }
-            }, row_ok, valid_cols);
+            if (OB)
+              epi_chunk_bf16<EPI, false>(ec, lane, k == CPT - 1 && have, release, row_ok,
+                                         valid_cols);
+            else
+              epi_chunk<EPI, false>(ec, lane, k == CPT - 1 && have, release, row_ok, valid_cols);
           }
           fence_proxy_async_smem();
           __syncwarp();
@@ -935,10 +1034,14 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
             bulk_commit();
           }
           stored = true;
-        } else if (!idle && pr.colsum && c * 32 < tl.bn && n < pr.N && n + lane < pr.N &&
+        } else if (!idle && pr.colsum && c * CW < tl.bn && n < pr.N &&
                    tl.m0 + BM * (int)rank < pr.M) {
           // a quarter past the last row: its partial row is 0
-          pr.colsum[((int64_t)(tl.m0 / BM + rank) * 4 + quarter) * pr.N + n + lane] = 0.0f;
+#pragma unroll
+          for (int h = 0; h < CW / 32; ++h)
+            if (n + 32 * h + lane < pr.N)
+              pr.colsum[((int64_t)(tl.m0 / BM + rank) * 4 + quarter) * pr.N + n + 32 * h + lane] =
+                  0.0f;
         }
         if (EPI == EPI_ELU_GRAD && lane == 0) {
           // refill the slot of chunk j-1 with the aux box of chunk j+NS-1
@@ -1012,14 +1115,17 @@ bool make_map(CUtensorMap *m, const float *base, int64_t rows, int64_t cols, int
 // the 128-byte swizzle; the split index is the third coordinate so a box
 // never spills rows into the next split's partial.
 bool make_out_map(CUtensorMap *m, float *base, int64_t rows, int64_t cols, int64_t ld,
-                  int64_t splits, std::string *err) {
+                  int64_t splits, std::string *err, bool bf16 = false) {
+  // bf16 outputs: [32 x 64] boxes, still 128-byte rows
+  const int es = bf16 ? 2 : 4;
   cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)splits};
-  cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)(rows * ld * 4)};
-  cuuint32_t box[3] = {32, 32, 1};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * es, (cuuint64_t)(rows * ld * es)};
+  cuuint32_t box[3] = {bf16 ? 64u : 32u, 32, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)base, dims, strides, box,
-                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = g_encode(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                        3, (void *)base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     *err = "cuTensorMapEncodeTiled (output) failed (" + std::to_string((int)r) + ")";
     return false;
@@ -1033,7 +1139,7 @@ bool make_out_map(CUtensorMap *m, float *base, int64_t rows, int64_t cols, int64
 template <int BN, int EPI, int CG>
 constexpr int stages_for() {
   constexpr int avail = 227 * 1024 - 1024 - kEpiWarps * slots_for(EPI) * 4096 -
-                        kEpiWarps * (BN >= 64 ? BN / 64 : 1) * 32 * 4 -
+                        kEpiWarps * (BN / 2 > 64 ? BN / 2 : 64) * 4 -
                         (8 + kEpiWarps * slots_for(EPI)) * 8 - 64;
   constexpr int st = avail / (BM * BKB + BN / CG * BKB);
   return st > 6 ? 6 : st;
@@ -1138,7 +1244,7 @@ struct TcCache {
 };
 
 // kind: 0 K-major operand, 1 MN-major operand, 2 output, 3 K-major bf16
-// operand, 4 MN-major bf16 operand
+// operand, 4 MN-major bf16 operand, 5 bf16 output
 static const CUtensorMap *cached_map(GemmEngine *eng, const float *base, int64_t rows,
                                      int64_t cols, int64_t ld, int box_or_splits, int kind,
                                      std::string *err) {
@@ -1147,9 +1253,11 @@ static const CUtensorMap *cached_map(GemmEngine *eng, const float *base, int64_t
   auto it = c->maps.find(key);
   if (it != c->maps.end()) return &it->second;
   CUtensorMap m;
-  const bool ok = kind == 2 ? make_out_map(&m, (float *)base, rows, cols, ld, box_or_splits, err)
-                            : make_map(&m, base, rows, cols, ld, box_or_splits,
-                                       kind == 1 || kind == 4, err, kind >= 3);
+  const bool ok = (kind == 2 || kind == 5)
+                      ? make_out_map(&m, (float *)base, rows, cols, ld, box_or_splits, err,
+                                     kind == 5)
+                      : make_map(&m, base, rows, cols, ld, box_or_splits, kind == 1 || kind == 4,
+                                 err, kind >= 3);
   if (!ok) return nullptr;
   if (c->maps.size() > 4096) c->maps.clear();
   return &(c->maps[key] = m);
@@ -1240,7 +1348,8 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
     // handled (out-of-range TMA reads are zero-filled, stores clipped).
     auto a16 = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
     const int op_align = bf ? 8 : 4;
-    if (g.lda % op_align || g.ldb % op_align || g.ldc % 4 || (g.aux && g.ldaux % 4) ||
+    const int out_align = (bf && (g.epi == EPI_BIAS_ELU || g.epi == EPI_ELU_GRAD)) ? 8 : 4;
+    if (g.lda % op_align || g.ldb % op_align || g.ldc % out_align || (g.aux && g.ldaux % op_align) ||
         !a16(g.A) || !a16(g.B) || !a16(g.C) || (g.aux && !a16(g.aux))) {
       *err = "tensor-core GEMM needs 16-byte aligned operands and row pitches";
       return ZRL_INVALID_ARG;
@@ -1289,14 +1398,18 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
     const int kmaj = bf ? 3 : 0, mnmaj = bf ? 4 : 1, ke = bf ? 64 : 32;
     const CUtensorMap *tb = kind == 0 ? cached_map(eng, g.B, g.N, g.K, g.ldb, bn / CG, kmaj, err)
                                       : cached_map(eng, g.B, g.K, g.N, g.ldb, ke, mnmaj, err);
-    const CUtensorMap *tc = cached_map(eng, g.C, g.M, g.N, g.ldc, split, 2, err);
+    // bf16 contexts store the forward hidden activations and the dgrad
+    // deltas in bf16 (the operands of later GEMMs)
+    const bool out_bf = bf && (g.epi == EPI_BIAS_ELU || g.epi == EPI_ELU_GRAD);
+    const CUtensorMap *tc = cached_map(eng, g.C, g.M, g.N, g.ldc, split, out_bf ? 5 : 2, err);
     if (!ta || !tb || !tc) return ZRL_CUDA_ERROR;
     maps.a[i] = *ta;
     maps.b[i] = *tb;
     maps.c[i] = *tc;
     if (kind == 1 && g.epi == EPI_ELU_GRAD) {
       // the post-activation read by the dgrad epilogue in [32 x 32] boxes
-      const CUtensorMap *tx = cached_map(eng, g.aux, g.M, g.N, g.ldaux, 32, 0, err);
+      // ([32 x 64] bf16 boxes in bf16 contexts)
+      const CUtensorMap *tx = cached_map(eng, g.aux, g.M, g.N, g.ldaux, 32, bf ? 3 : 0, err);
       if (!tx) return ZRL_CUDA_ERROR;
       maps.x[i] = *tx;
     }

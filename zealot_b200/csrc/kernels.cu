@@ -5,6 +5,7 @@
 // intrinsics (__fadd_rn, __fmul_rn, ...) so that the compiler cannot fuse a
 // multiply and an add into one FMA.
 #include <cuda_runtime.h>
+#include <cuda_bf16.h>
 #include <stdint.h>
 
 #include "zrl_internal.h"
@@ -43,6 +44,22 @@ constexpr float kLogSqrt2Pi = 0.9189385f;  // ppo.rs:18
 
 // tf32 with round-to-nearest (ties away): the tensor-core GEMMs then read
 // these operands exactly instead of truncating them.
+// GEMM-operand storage modes (OperandMode): 0 fp32 as is, 1 fp32 rounded to
+// tf32 (RN), 2 bf16 (RN-even).  `p` points at element 0 of the row; for
+// bf16 the row holds 2-byte elements.
+__device__ __forceinline__ void store_operand(float *p, int64_t i, float x, int mode) {
+  if (mode == 2) {
+    reinterpret_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(x);
+  } else {
+    uint32_t r;
+    if (mode == 1) {
+      asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+      x = __uint_as_float(r);
+    }
+    p[i] = x;
+  }
+}
+
 __device__ __forceinline__ float rna_tf32(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
@@ -228,7 +245,8 @@ __global__ void gather_kernel(GatherArgs a) {
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const float am = a.st->adv_mean, asd = a.st->adv_sd;
-  const int qa = a.odp / 4, qc = a.cdp / 4;  // float4 per padded row
+  // 16-byte pieces per padded observation row
+  const int qa = a.odp * a.x_bytes / 16, qc = a.cdp * a.x_bytes / 16;
   for (int64_t p = warp; p < a.n_used; p += nwarps) {
     const int64_t r = a.order[p];
     const float4 *xa = reinterpret_cast<const float4 *>(a.xn_a) + r * qa;
@@ -293,28 +311,27 @@ __global__ void norm_prepare_kernel(const float *m2, float count, int dim,
 // i, i+32, ... of the padded row, so the index math has no division.
 __global__ void normalize_rows_kernel(const float *x, int64_t n, int dim,
                                       int pitch, const float *mean,
-                                      const float *sd, float *out, int round) {
+                                      const float *sd, float *out, int mode) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   for (int64_t r = warp; r < n; r += nwarps) {
     const float *xr = x + r * dim;
-    float *o = out + r * pitch;
     for (int i = lane; i < pitch; i += 32) {
       float y = 0.0f;
       if (i < dim) {
         y = __fdiv_rn(__fsub_rn(xr[i], mean[i]), sd[i]);
         y = fminf(fmaxf(y, -5.0f), 5.0f);
       }
-      o[i] = round ? rna_tf32(y) : y;
+      store_operand(out, r * pitch + i, y, mode);
     }
   }
 }
 
-__global__ void round_copy_kernel(const float *src, float *dst, int64_t n) {
+__global__ void round_copy_kernel(const float *src, float *dst, int64_t n, int mode) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
-    dst[i] = rna_tf32(src[i]);
+    store_operand(dst, i, src[i], mode);
 }
 
 // ------------------------------------------------------------ PPO loss
@@ -417,7 +434,7 @@ loss_kernel(LossArgs a) {
         gls[j] += ent_term;
         gmu[j] += g;
       }
-      if (k < a.Ap) a.d_actor[s * a.Ap + k] = a.round_tf32 ? rna_tf32(g) : g;
+      if (k < a.Ap) store_operand(a.d_actor, s * a.Ap + k, g, a.out_mode);
     }
     if (lane == 0) {
       acc_surr += surr * a.scale;
@@ -437,7 +454,7 @@ loss_kernel(LossArgs a) {
       acc_vloss += vloss * a.scale;
       const float gv = a.value_coef * dv * a.scale;
       acc_gv += gv;
-      a.d_critic[s * a.cp] = a.round_tf32 ? rna_tf32(gv) : gv;
+      store_operand(a.d_critic, s * a.cp, gv, a.out_mode);
     }
   }
   // ---- the block's partial row, its warps summed in warp order:
@@ -717,9 +734,16 @@ __global__ void adam_kernel(AdamArgs a) {
     adam_one(p.z, m.z, v.z, g.z, lr, b1c, b2c, cl);
     adam_one(p.w, m.w, v.w, g.w, lr, b1c, b2c, cl);
     p4[q] = p;
-    if (a.p_round)
-      reinterpret_cast<float4 *>(a.p_round)[q] =
-          make_float4(rna_tf32(p.x), rna_tf32(p.y), rna_tf32(p.z), rna_tf32(p.w));
+    if (a.p_round) {
+      if (a.p_mode == 2) {
+        __nv_bfloat162 *o = reinterpret_cast<__nv_bfloat162 *>(a.p_round) + 2 * q;
+        o[0] = __floats2bfloat162_rn(p.x, p.y);
+        o[1] = __floats2bfloat162_rn(p.z, p.w);
+      } else {
+        reinterpret_cast<float4 *>(a.p_round)[q] =
+            make_float4(rna_tf32(p.x), rna_tf32(p.y), rna_tf32(p.z), rna_tf32(p.w));
+      }
+    }
     m4[q] = m;
     v4[q] = v;
   }
@@ -889,13 +913,13 @@ void launch_norm_prepare(const float *m2, float count, int dim, float *sd,
 
 void launch_normalize_rows(const float *x, int64_t n, int dim, int pitch,
                            const float *mean, const float *sd, float *out,
-                           int round_tf32, cudaStream_t s) {
+                           int mode, cudaStream_t s) {
   normalize_rows_kernel<<<grid_for(n * 32, 256), 256, 0, s>>>(x, n, dim, pitch, mean, sd, out,
-                                                               round_tf32);
+                                                               mode);
 }
 
-void launch_round_copy(const float *src, float *dst, int64_t n, cudaStream_t s) {
-  round_copy_kernel<<<grid_for(n, 256), 256, 0, s>>>(src, dst, n);
+void launch_round_copy(const float *src, float *dst, int64_t n, int mode, cudaStream_t s) {
+  round_copy_kernel<<<grid_for(n, 256), 256, 0, s>>>(src, dst, n, mode);
 }
 
 int loss_blocks(int64_t mb) { return grid_for(mb * 32, kLossThreads, 4 * 148); }

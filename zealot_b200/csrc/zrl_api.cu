@@ -108,7 +108,21 @@ struct zrl_ctx {
   // operand copy; P stays the fp32 master copy (bias reads, Adam)
   float *Ptc = nullptr;
   bool tc() const { return precision == ZRL_GEMM_TF32; }
-  const float *Wgemm() const { return tc() ? Ptc : P; }
+  bool bf() const { return precision == ZRL_GEMM_BF16; }
+  // the tensor-core path (tf32 or bf16 operands)
+  bool tcore() const { return precision != ZRL_GEMM_FP32; }
+  // storage of GEMM operands written by the non-GEMM kernels: 0 fp32, 1
+  // tf32-rounded fp32, 2 bf16
+  int opmode() const { return bf() ? 2 : (tc() ? 1 : 0); }
+  int opbytes() const { return bf() ? 2 : 4; }
+  // the weights the GEMMs read: a tf32-rounded or bf16 copy on the tensor
+  // cores, the fp32 master otherwise
+  const float *Wgemm() const { return tcore() ? Ptc : P; }
+  // layer weights at element offset `off` of the GEMM copy
+  const float *Wgemm_at(int64_t off) const {
+    return reinterpret_cast<const float *>(reinterpret_cast<const char *>(Wgemm()) +
+                                           off * (tcore() ? opbytes() : 4));
+  }
   float *sums3 = nullptr;   // = G + dev_params
   DevState *st = nullptr;
   DevState *st_host = nullptr;  // pinned
@@ -196,11 +210,6 @@ static zrl_status bad(zrl_ctx *ctx, const char *msg) {
   return ZRL_INVALID_ARG;
 }
 
-// bf16 contexts run the GEMM hook (zrl_gemm) only so far
-static zrl_status bf16_update_unsupported(zrl_ctx *ctx) {
-  ctx->err = "the bf16 update path is not built yet (zrl_gemm takes bf16 operands)";
-  return ZRL_NOT_SUPPORTED;
-}
 
 template <typename T>
 static zrl_status dalloc(zrl_ctx *ctx, T **p, int64_t count) {
@@ -450,7 +459,7 @@ static GemmArgs fwd_args(zrl_ctx *ctx, int k, int l, const float *in, int64_t ro
   g.A = in;
   g.lda = L.dp[l];
   g.trans_a = false;
-  g.B = ctx->Wgemm() + L.w_off[l];
+  g.B = ctx->Wgemm_at(L.w_off[l]);
   g.ldb = L.dp[l];
   g.trans_b = true;
   g.C = ctx->act[k][l + 1];
@@ -545,7 +554,7 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
       g.A = ctx->dlt[k][l];
       g.lda = L.dp[l + 1];
       g.trans_a = false;
-      g.B = ctx->Wgemm() + L.w_off[l];
+      g.B = ctx->Wgemm_at(L.w_off[l]);
       g.round_out = ctx->tc();
       g.ldb = L.dp[l];
       g.trans_b = false;
@@ -555,7 +564,7 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
       g.aux = ctx->act[k][l];
       g.ldaux = L.dp[l];
       g.split_k = 1;
-      if (ctx->tc()) {
+      if (ctx->tcore()) {
         // db_{l-1}: column sums of delta_{l-1} from the epilogue, one
         // partial row per 32-row quarter of each 128-row block
         g.colsum = *bp;
@@ -568,7 +577,7 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
     TRY(run_group(ctx, d, n));
   }
   const int S = wsplit_for(rows);
-  if (!ctx->tc()) {
+  if (!ctx->tcore()) {
     // db_l = column sums of delta_l for the hidden layers (CUDA-core mode)
     for (int k = 0; k < 2; ++k) {
       const NetLayout &L = ctx->net[k];
@@ -655,7 +664,7 @@ static zrl_status minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
   la.clip = cfg->clip;
   la.entropy_coef = cfg->entropy_coef;
   la.value_coef = cfg->value_coef;
-  la.round_tf32 = ctx->tc();
+  la.out_mode = ctx->opmode();
   la.d_actor = ctx->dlt[0][La.L - 1];
   la.d_critic = ctx->dlt[1][Lc.L - 1];
   la.part = ctx->rs.fpart;
@@ -728,7 +737,8 @@ static zrl_status step(zrl_ctx *ctx, const zrl_ppo_config *cfg, int minibatches,
   a.actor_end = ctx->net[0].dev_end;
   a.critic_end = ctx->net[1].dev_end;
   a.st = ctx->st;
-  a.p_round = ctx->tc() ? ctx->Ptc : nullptr;
+  a.p_round = ctx->tcore() ? ctx->Ptc : nullptr;
+  a.p_mode = ctx->opmode();
   launch_adam(a, ctx->stream);
   ctx->launches++;
   CHECK_LAUNCH();
@@ -782,9 +792,9 @@ static zrl_status normalize_batch(zrl_ctx *ctx, const float *obs, const float *c
                                   int64_t n) {
   if (n <= 0) return ZRL_OK;
   launch_normalize_rows(obs, n, ctx->net[0].d[0], ctx->net[0].dp[0], ctx->obs_mean,
-                        ctx->obs_sd, ctx->n_xa, ctx->tc(), ctx->stream);
+                        ctx->obs_sd, ctx->n_xa, ctx->opmode(), ctx->stream);
   launch_normalize_rows(cobs, n, ctx->net[1].d[0], ctx->net[1].dp[0], ctx->crit_mean,
-                        ctx->crit_sd, ctx->n_xc, ctx->tc(), ctx->stream);
+                        ctx->crit_sd, ctx->n_xc, ctx->opmode(), ctx->stream);
   ctx->launches += 2;
   CHECK_LAUNCH();
   return ZRL_OK;
@@ -806,6 +816,7 @@ static GatherArgs gather_args(zrl_ctx *ctx, const float *act, const float *mo,
   g.A = ctx->A;
   g.odp = ctx->net[0].dp[0];
   g.cdp = ctx->net[1].dp[0];
+  g.x_bytes = ctx->opbytes();
   g.st = ctx->st;
   g.x_a = ctx->e_xa;
   g.x_c = ctx->e_xc;
@@ -820,8 +831,11 @@ static GatherArgs gather_args(zrl_ctx *ctx, const float *act, const float *mo,
 
 static MbView epoch_view(zrl_ctx *ctx, int64_t off, int64_t rows) {
   MbView v{};
-  v.xa = ctx->e_xa + off * ctx->net[0].dp[0];
-  v.xc = ctx->e_xc + off * ctx->net[1].dp[0];
+  // (bf16 rows are half as many bytes: offsets in the operand element size)
+  v.xa = reinterpret_cast<const float *>(reinterpret_cast<const char *>(ctx->e_xa) +
+                                         off * ctx->net[0].dp[0] * ctx->opbytes());
+  v.xc = reinterpret_cast<const float *>(reinterpret_cast<const char *>(ctx->e_xc) +
+                                         off * ctx->net[1].dp[0] * ctx->opbytes());
   v.act = ctx->e_act + off * ctx->A;
   v.mo = ctx->e_mo + off * ctx->A;
   v.lpo = ctx->e_lpo + off;
@@ -1052,7 +1066,7 @@ zrl_status zrl_create(const zrl_model_config *cfg, int device,
   if ((s = dalloc(ctx, &ctx->G, ctx->grad_len)) != ZRL_OK) return fail(s);
   if ((s = dalloc(ctx, &ctx->M, ctx->dev_params)) != ZRL_OK) return fail(s);
   if ((s = dalloc(ctx, &ctx->V, ctx->dev_params)) != ZRL_OK) return fail(s);
-  if (ctx->tc() && (s = dalloc(ctx, &ctx->Ptc, ctx->dev_params)) != ZRL_OK) return fail(s);
+  if (ctx->tcore() && (s = dalloc(ctx, &ctx->Ptc, ctx->dev_params)) != ZRL_OK) return fail(s);
   ctx->sums3 = ctx->G + ctx->dev_params;
   if ((s = dalloc(ctx, &ctx->st, 1)) != ZRL_OK) return fail(s);
   if (cudaMallocHost((void **)&ctx->st_host, sizeof(DevState)) != cudaSuccess)
@@ -1163,8 +1177,8 @@ zrl_status zrl_set_params(zrl_ctx *ctx, const float *flat, int64_t count) {
   flat_to_padded(ctx, flat, pad.data());
   CK(cudaMemcpyAsync(ctx->P, pad.data(), sizeof(float) * ctx->dev_params,
                      cudaMemcpyHostToDevice, ctx->stream));
-  if (ctx->tc()) {
-    launch_round_copy(ctx->P, ctx->Ptc, ctx->dev_params, ctx->stream);
+  if (ctx->tcore()) {
+    launch_round_copy(ctx->P, ctx->Ptc, ctx->dev_params, ctx->opmode(), ctx->stream);
     ctx->launches++;
     CHECK_LAUNCH();
   }
@@ -1380,7 +1394,6 @@ static zrl_status write_back_adv(zrl_ctx *ctx, zrl_batch *b, const float *adv_de
 zrl_status zrl_update(zrl_ctx *ctx, const zrl_ppo_config *cfg, zrl_batch *batch,
                       zrl_stats *out) {
   if (!ctx) return ZRL_INVALID_ARG;
-  if (ctx->precision == ZRL_GEMM_BF16) return bf16_update_unsupported(ctx);
   TRY(check_cfg(ctx, cfg));
   int64_t n_global = 0;
   TRY(check_batch(ctx, batch, &n_global));
@@ -1401,7 +1414,6 @@ zrl_status zrl_update(zrl_ctx *ctx, const zrl_ppo_config *cfg, zrl_batch *batch,
 zrl_status zrl_gae_update(zrl_ctx *ctx, const zrl_ppo_config *cfg,
                           const zrl_rollout *ro, zrl_batch *batch, zrl_stats *out) {
   if (!ctx || !ro) return ZRL_INVALID_ARG;
-  if (ctx->precision == ZRL_GEMM_BF16) return bf16_update_unsupported(ctx);
   TRY(check_cfg(ctx, cfg));
   int64_t n_global = 0;
   TRY(check_batch(ctx, batch, &n_global));
@@ -1455,7 +1467,6 @@ zrl_status zrl_gae_update(zrl_ctx *ctx, const zrl_ppo_config *cfg,
 zrl_status zrl_forward(zrl_ctx *ctx, const float *obs, const float *critic_obs,
                        int64_t n, float *mean_out, float *value_out, int32_t on_device) {
   if (!ctx) return ZRL_INVALID_ARG;
-  if (ctx->precision == ZRL_GEMM_BF16) return bf16_update_unsupported(ctx);
   if (n < 0) return bad(ctx, "negative n");
   if ((mean_out && !obs) || (value_out && !critic_obs)) return bad(ctx, "null input");
   if (n == 0) return ZRL_OK;
@@ -1482,7 +1493,7 @@ zrl_status zrl_forward(zrl_ctx *ctx, const float *obs, const float *critic_obs,
       }
       float *xn = k == 0 ? ctx->e_xa : ctx->e_xc;
       launch_normalize_rows(x, rows, dim, pitch, k == 0 ? ctx->obs_mean : ctx->crit_mean,
-                            k == 0 ? ctx->obs_sd : ctx->crit_sd, xn, ctx->tc(),
+                            k == 0 ? ctx->obs_sd : ctx->crit_sd, xn, ctx->opmode(),
                             ctx->stream);
       ctx->launches++;
       CHECK_LAUNCH();
@@ -1534,7 +1545,6 @@ zrl_status zrl_minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
                                const zrl_batch *batch, const int64_t *idx,
                                int64_t n_idx, float *grads_out, float *sums3_out) {
   if (!ctx || !idx || !grads_out) return ZRL_INVALID_ARG;
-  if (ctx->precision == ZRL_GEMM_BF16) return bf16_update_unsupported(ctx);
   TRY(check_cfg(ctx, cfg));
   int64_t n_global = 0;
   TRY(check_batch(ctx, batch, &n_global));
@@ -1571,7 +1581,6 @@ zrl_status zrl_minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
 zrl_status zrl_apply_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg, const float *grads,
                            float kl) {
   if (!ctx || !grads) return ZRL_INVALID_ARG;
-  if (ctx->precision == ZRL_GEMM_BF16) return bf16_update_unsupported(ctx);
   TRY(check_cfg(ctx, cfg));
   CK(cudaSetDevice(ctx->device));
   std::vector<float> pad(ctx->grad_len, 0.0f);
@@ -1632,7 +1641,6 @@ zrl_status zrl_policy_step(zrl_ctx *ctx, const float *obs, const float *critic_o
                            int64_t n, uint64_t seed, uint64_t counter, float *action,
                            float *logp, float *mean, float *value, int32_t on_device) {
   if (!ctx || !obs || !action) return ZRL_INVALID_ARG;
-  if (ctx->precision == ZRL_GEMM_BF16) return bf16_update_unsupported(ctx);
   if (value && !critic_obs) return bad(ctx, "value requested without critic_obs");
   if (n < 0) return bad(ctx, "negative n");
   if (n == 0) return ZRL_OK;
@@ -1653,7 +1661,7 @@ zrl_status zrl_policy_step(zrl_ctx *ctx, const float *obs, const float *critic_o
       x = ctx->b_obs;
     }
     launch_normalize_rows(x, rows, od, odp, ctx->obs_mean, ctx->obs_sd, ctx->e_xa,
-                          ctx->tc(), ctx->stream);
+                          ctx->opmode(), ctx->stream);
     ctx->launches++;
     TRY(forward_net(ctx, 0, ctx->e_xa, rows));
     float *act_d = on_device ? action + r0 * A : ctx->e_act;
@@ -1672,7 +1680,7 @@ zrl_status zrl_policy_step(zrl_ctx *ctx, const float *obs, const float *critic_o
         c = ctx->b_cobs;
       }
       launch_normalize_rows(c, rows, cd, cdp, ctx->crit_mean, ctx->crit_sd, ctx->e_xc,
-                            ctx->tc(), ctx->stream);
+                            ctx->opmode(), ctx->stream);
       ctx->launches++;
       TRY(forward_net(ctx, 1, ctx->e_xc, rows));
       float *v_d = on_device ? value + r0 : ctx->e_vo;

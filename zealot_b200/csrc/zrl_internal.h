@@ -99,7 +99,8 @@ struct GatherArgs {
   const float *xn_a, *xn_c;  // normalized observation rows, pitch odp / cdp
   const float *action, *mean_old, *logp_old, *value_old, *adv, *ret;
   int A;
-  int odp, cdp;           // padded row pitch (multiples of 32 floats)
+  int odp, cdp;           // padded row pitch (multiples of 32 elements)
+  int x_bytes;            // bytes per observation element (4, or 2 for bf16)
   const DevState *st;   // adv_mean / adv_sd
   float *x_a, *x_c;     // [n_used, odp], [n_used, cdp]
   float *g_action, *g_mean_old;         // [n_used, A]
@@ -112,9 +113,10 @@ void launch_norm_prepare(const float *m2, float count, int dim, float *sd,
                          cudaStream_t s);
 void launch_normalize_rows(const float *x, int64_t n, int dim, int pitch,
                            const float *mean, const float *sd, float *out,
-                           int round_tf32, cudaStream_t s);
+                           int mode, cudaStream_t s);
 // dst = tf32(src) (round to nearest) over n floats.
-void launch_round_copy(const float *src, float *dst, int64_t n, cudaStream_t s);
+// dst[i] = src[i] stored as `mode` says (1 tf32-rounded fp32, 2 bf16).
+void launch_round_copy(const float *src, float *dst, int64_t n, int mode, cudaStream_t s);
 
 // PPO losses (ppo.rs:410-452) over one minibatch.
 struct LossArgs {
@@ -136,7 +138,7 @@ struct LossArgs {
   // deltas, taken in fp32 before any rounding) and the statistic sums
   float *part;
   int width;
-  int round_tf32;         // round the two output deltas to tf32 (RN)
+  int out_mode;           // storage of the two output deltas (OperandMode)
 };
 void launch_loss(const LossArgs &a, cudaStream_t s);
 int loss_blocks(int64_t mb);  // the partial rows launch_loss writes
@@ -191,7 +193,9 @@ struct AdamArgs {
   int64_t n;
   int64_t actor_end, critic_end;  // [0,actor_end) actor, [.., critic_end) critic, rest log_std
   const DevState *st;
-  float *p_round;  // optional: tf32-rounded copy of p for the tensor-core GEMMs
+  float *p_round;  // optional: copy of p for the tensor-core GEMMs, stored
+                   // as p_mode says (1 tf32-rounded fp32, 2 bf16)
+  int p_mode;
 };
 void launch_adam(const AdamArgs &a, cudaStream_t s);
 
