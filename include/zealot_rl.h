@@ -217,7 +217,9 @@ zrl_status zrl_minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
                                int64_t n_idx, float *grads_out,
                                float *sums3_out);
 /* One MLP GEMM through the context's GEMM engine (the precision it was
- * created with), on device pointers, fp32 row-major:
+ * created with), on device pointers, row-major; C is fp32, A and B are fp32
+ * (fp32 and tf32 contexts) or bf16 (bf16 contexts: 2-byte elements, lda and
+ * ldb in elements, multiples of 8):
  *   layout 0: C[M,N] = A[M,K] * B[N,K]^T   (forward:  X W^T)
  *   layout 1: C[M,N] = A[M,K] * B[K,N]     (dgrad:    Delta W)
  *   layout 2: C[M,N] = A[K,M]^T * B[K,N]   (wgrad:    Delta^T X)
