@@ -977,6 +977,14 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
               mbar_arrive(&acce[ab]);
           }
         }
+        if (EPI == EPI_ELU_GRAD && lane == 0 && j >= 1) {
+          // the aux box of chunk j+NS-2 into the slot of chunk j-2, whose
+          // store (issued two chunks back) must be done reading it; the
+          // prologue issued chunks 0..NS-2
+          if (prev_store) bulk_wait_read<1>();
+          else bulk_wait_read<0>();
+          issue_aux(j + NS - 2);
+        }
         bool stored = false;
         if (live) {
           if (EPI == EPI_ELU_GRAD) {
@@ -1042,12 +1050,6 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
             if (n + 32 * h + lane < pr.N)
               pr.colsum[((int64_t)(tl.m0 / BM + rank) * 4 + quarter) * pr.N + n + 32 * h + lane] =
                   0.0f;
-        }
-        if (EPI == EPI_ELU_GRAD && lane == 0) {
-          // refill the slot of chunk j-1 with the aux box of chunk j+NS-1
-          if (stored) bulk_wait_read<1>();
-          else bulk_wait_read<0>();
-          issue_aux(j + NS - 1);
         }
         prev_store = stored;
       }
