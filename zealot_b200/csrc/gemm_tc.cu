@@ -428,6 +428,7 @@ struct TcGroup {
   TcProb p[kMaxProbs];
   int n;       // problems
   int tiles;   // total tiles
+  int reverse; // walk the tiles last to first (L2 reuse of the previous launch's last tiles)
   int *err;
 };
 // Tensor maps per problem: A and B operands, the output C (3-D, split
@@ -468,6 +469,7 @@ struct Tile {
 template <int BN, int CG, int KE>
 __device__ __forceinline__ Tile decode_tile(int t, const TcGroup &g) {
   Tile tl;
+  if (g.reverse) t = g.tiles - 1 - t;
   int p = 0;
   while (p + 1 < g.n && t >= g.p[p + 1].tile0) ++p;
   const TcProb &pr = g.p[p];
@@ -1434,6 +1436,7 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
   }
   grp.n = n;
   grp.tiles = tiles;
+  grp.reverse = gs[0].reverse_tiles;
   grp.err = eng->err_dev;
   const cudaError_t e = bf ? dispatch<true>(CG, BN, kind, gs[0].epi, maps, grp, s)
                            : dispatch<false>(CG, BN, kind, gs[0].epi, maps, grp, s);

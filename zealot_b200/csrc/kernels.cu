@@ -528,7 +528,13 @@ __host__ __device__ __forceinline__ int64_t rs_blocks(int64_t count, int splits)
   return (count / 4 + cols4 - 1) / cols4;
 }
 
-__global__ void __launch_bounds__(kRsThreads, 2) reduce_segments_kernel(ReduceSegs segs) {
+__device__ void prestep_finish(const PrestepArgs &a, double na, double nc);
+template <typename T>
+__device__ T block_sum(T v, T *sh);
+
+__global__ void __launch_bounds__(kRsThreads, 2)
+reduce_segments_kernel(ReduceSegs segs, PrestepArgs pa, double *partials, unsigned int *ticket,
+                       int fuse) {
   pdl_wait();
   pdl_trigger();
   int si = 0;
@@ -567,6 +573,7 @@ __global__ void __launch_bounds__(kRsThreads, 2) reduce_segments_kernel(ReduceSe
   __shared__ float4 part[kRsThreads];
   part[threadIdx.x] = t;
   __syncthreads();
+  double sq = 0.0;
   if (grp == 0 && live) {
     float4 s4 = part[c];
     for (int j = 1; j < G; ++j) {
@@ -577,7 +584,36 @@ __global__ void __launch_bounds__(kRsThreads, 2) reduce_segments_kernel(ReduceSe
       s4.w += x.w;
     }
     reinterpret_cast<float4 *>(dst)[i4] = s4;
+    sq = (double)s4.x * s4.x + (double)s4.y * s4.y + (double)s4.z * s4.z +
+         (double)s4.w * s4.w;
   }
+  if (!fuse) return;
+  // the fused pre-step: squared norms of this block's outputs (one net per
+  // segment), block partials, the last block finishes in block order
+  __shared__ double sh[32];
+  const double tot = block_sum(sq, sh);
+  const int net = segs.net[si];
+  if (threadIdx.x == 0) {
+    partials[2 * blockIdx.x] = net == 0 ? tot : 0.0;
+    partials[2 * blockIdx.x + 1] = net == 1 ? tot : 0.0;
+  }
+  __threadfence();
+  __shared__ bool last;
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  double na = 0.0, nc = 0.0;
+  for (int bb = threadIdx.x; bb < (int)gridDim.x; bb += blockDim.x) {
+    na += __ldcg(&partials[2 * bb]);
+    nc += __ldcg(&partials[2 * bb + 1]);
+  }
+  na = block_sum(na, sh);
+  nc = block_sum(nc, sh);
+  if (threadIdx.x != 0) return;
+  *ticket = 0u;
+  prestep_finish(pa, na, nc);
 }
 
 // ------------------------------------------------------------ pre-step
@@ -595,51 +631,10 @@ __device__ float powi_f(float a, int b) {
   return recip ? __fdiv_rn(1.0f, r) : r;
 }
 
-constexpr int kPrestepThreads = 256;
-
-__global__ void __launch_bounds__(kPrestepThreads)
-prestep_kernel(PrestepArgs a, double *partials, unsigned int *ticket) {
-  pdl_wait();
-  pdl_trigger();
-  double sa = 0.0, sc = 0.0;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-#pragma unroll 4
-  for (int64_t i = a.actor_begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-       i < a.actor_end; i += stride) {
-    const double g = a.grads[i];
-    sa += g * g;
-  }
-#pragma unroll 4
-  for (int64_t i = a.critic_begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-       i < a.critic_end; i += stride) {
-    const double g = a.grads[i];
-    sc += g * g;
-  }
-  __shared__ double sh[32];
-  double ta = block_sum(sa, sh);
-  double tc = block_sum(sc, sh);
-  if (threadIdx.x == 0) {
-    partials[2 * blockIdx.x] = ta;
-    partials[2 * blockIdx.x + 1] = tc;
-  }
-  __threadfence();
-  __shared__ bool last;
-  __syncthreads();
-  if (threadIdx.x == 0) last = atomicAdd(ticket, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  // the whole last block: thread b takes block partials b, b + blockDim,
-  // ..., then the fixed-order block sum
-  double na = 0.0, nc = 0.0;
-  for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) {
-    na += __ldcg(&partials[2 * b]);
-    nc += __ldcg(&partials[2 * b + 1]);
-  }
-  na = block_sum(na, sh);
-  nc = block_sum(nc, sh);
-  if (threadIdx.x != 0) return;
-  *ticket = 0u;
+// The scalar half of the pre-step, given the two squared gradient norms:
+// statistics, adaptive LR, per-net clip scales, Adam step counters and
+// bias corrections (one thread).
+__device__ void prestep_finish(const PrestepArgs &a, double na, double nc) {
   DevState *st = a.st;
   st->sumsq[0] = (float)na;
   st->sumsq[1] = (float)nc;
@@ -687,6 +682,54 @@ prestep_kernel(PrestepArgs a, double *partials, unsigned int *ticket) {
     st->stats[4] = lr;
     for (int j = 0; j < 4; ++j) st->ep_acc[j] = 0.0f;
   }
+}
+
+constexpr int kPrestepThreads = 256;
+
+__global__ void __launch_bounds__(kPrestepThreads)
+prestep_kernel(PrestepArgs a, double *partials, unsigned int *ticket) {
+  pdl_wait();
+  pdl_trigger();
+  double sa = 0.0, sc = 0.0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+#pragma unroll 4
+  for (int64_t i = a.actor_begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+       i < a.actor_end; i += stride) {
+    const double g = a.grads[i];
+    sa += g * g;
+  }
+#pragma unroll 4
+  for (int64_t i = a.critic_begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+       i < a.critic_end; i += stride) {
+    const double g = a.grads[i];
+    sc += g * g;
+  }
+  __shared__ double sh[32];
+  double ta = block_sum(sa, sh);
+  double tc = block_sum(sc, sh);
+  if (threadIdx.x == 0) {
+    partials[2 * blockIdx.x] = ta;
+    partials[2 * blockIdx.x + 1] = tc;
+  }
+  __threadfence();
+  __shared__ bool last;
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // the whole last block: thread b takes block partials b, b + blockDim,
+  // ..., then the fixed-order block sum
+  double na = 0.0, nc = 0.0;
+  for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) {
+    na += __ldcg(&partials[2 * b]);
+    nc += __ldcg(&partials[2 * b + 1]);
+  }
+  na = block_sum(na, sh);
+  nc = block_sum(nc, sh);
+  if (threadIdx.x != 0) return;
+  *ticket = 0u;
+  prestep_finish(a, na, nc);
 }
 
 // ------------------------------------------------------------ Adam
@@ -938,7 +981,8 @@ void launch_colsum(const float *x, int64_t rows, int cols, int ld,
   colsum_kernel<<<grid, 128, 0, s>>>(x, rows, cols, ld, partials, splits);
 }
 
-void launch_reduce_segments(const ReduceSegs &segs_in, cudaStream_t s) {
+int launch_reduce_segments(const ReduceSegs &segs_in, cudaStream_t s, const PrestepArgs *fuse,
+                           ReduceScratch *rs) {
   // segments with the most splits first: their blocks run longest, so they
   // start in the first wave
   ReduceSegs segs = segs_in;
@@ -953,10 +997,22 @@ void launch_reduce_segments(const ReduceSegs &segs_in, cudaStream_t s) {
     segs.first_block[i] = (int)blocks;
     segs.groups[i] = rs_groups(segs.seg[i].splits);
     blocks += rs_blocks(segs.seg[i].count, segs.seg[i].splits);
+    segs.net[i] = -1;
+    if (fuse) {
+      const int64_t off = segs.seg[i].dst - fuse->grads;
+      if (off >= fuse->actor_begin && off < fuse->actor_end) segs.net[i] = 0;
+      else if (off >= fuse->critic_begin && off < fuse->critic_end) segs.net[i] = 1;
+    }
   }
   segs.first_block[segs.n] = (int)blocks;
-  if (blocks == 0) return;
-  launch_pdl(reduce_segments_kernel, (unsigned)blocks, kRsThreads, s, segs);
+  if (blocks == 0) return 0;
+  if (fuse && blocks > rs->max_blocks) fuse = nullptr;  // partials too small: not fused
+  PrestepArgs pa{};
+  if (fuse) pa = *fuse;
+  launch_pdl(reduce_segments_kernel, (unsigned)blocks, kRsThreads, s, segs, pa,
+             fuse ? rs->dpart : (double *)nullptr, fuse ? rs->ticket + 1 : (unsigned int *)nullptr,
+             fuse ? 1 : 0);
+  return fuse ? 1 : 0;
 }
 
 void launch_prestep(const PrestepArgs &a, ReduceScratch &rs, cudaStream_t s) {

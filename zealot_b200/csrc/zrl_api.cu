@@ -495,7 +495,9 @@ static zrl_status run_group(zrl_ctx *ctx, const GemmArgs *gs, int n) {
 
 // Forward of both nets over `rows` rows (inputs xa, xc with pitch dp[0]):
 // layer l of the actor and of the critic run as one grouped launch when
-// they share the epilogue.
+// they share the epilogue.  Odd layers walk their tiles last to first, so
+// each layer first reads the rows the layer before wrote last (still in
+// L2).
 static zrl_status forward_both(zrl_ctx *ctx, const float *xa, const float *xc, int64_t rows) {
   const int maxL = std::max(ctx->net[0].L, ctx->net[1].L);
   for (int l = 0; l < maxL; ++l) {
@@ -504,7 +506,8 @@ static zrl_status forward_both(zrl_ctx *ctx, const float *xa, const float *xc, i
     for (int k = 0; k < 2; ++k) {
       if (l >= ctx->net[k].L) continue;
       const float *in = l == 0 ? (k == 0 ? xa : xc) : ctx->act[k][l];
-      g[n++] = fwd_args(ctx, k, l, in, rows);
+      g[n] = fwd_args(ctx, k, l, in, rows);
+      g[n++].reverse_tiles = l & 1;
     }
     if (n == 2 && g[0].epi != g[1].epi) {
       TRY(run_group(ctx, &g[0], 1));
@@ -529,8 +532,8 @@ static zrl_status forward_net(zrl_ctx *ctx, int k, const float *x, int64_t rows)
 
 // Backward of both nets (net.rs:113-140 batched).  The dgrad chain runs
 // level by level, actor and critic layer l in one launch, each with the
-// ELU' epilogue; then every weight gradient (split-K partials) of both
-// nets runs as grouped launches.  Bias gradients are column sums of the
+// ELU' epilogue; the weight gradients (split-K partials) of both nets run
+// as grouped launches inside the chain.  Bias gradients are column sums of the
 // deltas taken in fp32 where each delta is produced: the output layer's in
 // the loss kernel, a hidden layer's in the epilogue of the tensor-core
 // dgrad that produces it (a separate column-sum pass in the CUDA-core
@@ -539,6 +542,57 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
                                 float **wp, float **bp, ReduceSegs &segs) {
   const int m_tiles = (int)((rows + 127) / 128);
   const int maxL = std::max(ctx->net[0].L, ctx->net[1].L);
+  const int S = wsplit_for(rows);
+  // dW_l = delta_l^T a_l for every layer of both nets, split-K partials.
+  // Tall ones (dp[l+1] >= 256 rows) go to CTA-pair tiles, the rest to
+  // single-CTA tiles: a grouped launch (of at most 8) each, issued right
+  // after the dgrad level that reads the same delta_l and a_l (level 1 for
+  // layer 0), so those reads meet L2.
+  GemmArgs tall[2 * ZRL_MAX_LAYERS], flat[2 * ZRL_MAX_LAYERS];
+  int nt = 0, nf = 0, tall_lvl = 1, flat_lvl = 1;
+  for (int k = 0; k < 2; ++k) {
+    const NetLayout &L = ctx->net[k];
+    for (int l = L.L - 1; l >= 0; --l) {
+      GemmArgs g{};
+      g.M = L.dp[l + 1];
+      g.N = L.dp[l];
+      g.K = (int)rows;
+      g.A = ctx->dlt[k][l];
+      g.lda = L.dp[l + 1];
+      g.trans_a = true;
+      g.B = l == 0 ? (k == 0 ? xa : xc) : ctx->act[k][l];
+      g.ldb = L.dp[l];
+      g.trans_b = false;
+      g.C = *wp;
+      g.ldc = L.dp[l];
+      g.epi = EPI_STORE;
+      g.split_k = S;
+      ReduceSeg sw{ctx->G + L.w_off[l], *wp, (int64_t)L.dp[l + 1] * L.dp[l], S,
+                   (int64_t)L.dp[l + 1] * L.dp[l]};
+      segs.seg[segs.n++] = sw;
+      *wp += (int64_t)S * L.dp[l + 1] * L.dp[l];
+      if (g.M >= 256) {
+        tall[nt++] = g;
+        tall_lvl = nt == 1 ? l : std::min(tall_lvl, l);
+      } else {
+        flat[nf++] = g;
+        flat_lvl = nf == 1 ? l : std::min(flat_lvl, l);
+      }
+    }
+  }
+  tall_lvl = std::max(tall_lvl, 1);
+  flat_lvl = std::max(flat_lvl, 1);
+  // successive launches alternate their tile order, starting opposite to
+  // the forward's last layer (last to first when its index is odd)
+  bool rev = !((maxL - 1) & 1);
+  auto run_w = [&](GemmArgs *w, int nw) -> zrl_status {
+    for (int i = 0; i < nw; i += 8) {
+      for (int j = i; j < std::min(nw, i + 8); ++j) w[j].reverse_tiles = rev;
+      TRY(run_group(ctx, w + i, std::min(8, nw - i)));
+    }
+    rev = !rev;
+    return ZRL_OK;
+  };
   for (int l = maxL - 1; l >= 1; --l) {
     GemmArgs d[2];
     int n = 0;
@@ -564,6 +618,7 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
       g.aux = ctx->act[k][l];
       g.ldaux = L.dp[l];
       g.split_k = 1;
+      g.reverse_tiles = rev;
       if (ctx->tcore()) {
         // db_{l-1}: column sums of delta_{l-1} from the epilogue, one
         // partial row per 32-row quarter of each 128-row block
@@ -575,8 +630,10 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
       }
     }
     TRY(run_group(ctx, d, n));
+    rev = !rev;
+    if (nf && flat_lvl == l) TRY(run_w(flat, nf));
+    if (nt && tall_lvl == l) TRY(run_w(tall, nt));
   }
-  const int S = wsplit_for(rows);
   if (!ctx->tcore()) {
     // db_l = column sums of delta_l for the hidden layers (CUDA-core mode)
     for (int k = 0; k < 2; ++k) {
@@ -591,45 +648,11 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
       }
     }
   }
-  // dW_l = delta_l^T a_l for every layer of both nets
-  GemmArgs w[2 * ZRL_MAX_LAYERS];
-  int nw = 0;
-  for (int k = 0; k < 2; ++k) {
-    const NetLayout &L = ctx->net[k];
-    for (int l = L.L - 1; l >= 0; --l) {
-      GemmArgs &g = w[nw++];
-      g = GemmArgs{};
-      g.M = L.dp[l + 1];
-      g.N = L.dp[l];
-      g.K = (int)rows;
-      g.A = ctx->dlt[k][l];
-      g.lda = L.dp[l + 1];
-      g.trans_a = true;
-      g.B = l == 0 ? (k == 0 ? xa : xc) : ctx->act[k][l];
-      g.ldb = L.dp[l];
-      g.trans_b = false;
-      g.C = *wp;
-      g.ldc = L.dp[l];
-      g.epi = EPI_STORE;
-      g.split_k = S;
-      ReduceSeg sw{ctx->G + L.w_off[l], *wp, (int64_t)L.dp[l + 1] * L.dp[l], S,
-                   (int64_t)L.dp[l + 1] * L.dp[l]};
-      segs.seg[segs.n++] = sw;
-      *wp += (int64_t)S * L.dp[l + 1] * L.dp[l];
-    }
+  // single-layer nets: no dgrad chain, the weight gradients run here
+  if (maxL == 1) {
+    if (nt) TRY(run_w(tall, nt));
+    if (nf) TRY(run_w(flat, nf));
   }
-  // tall weight gradients (dp[l+1] >= 256 rows) go to CTA-pair tiles, the
-  // rest to single-CTA tiles: one grouped launch (of at most 8) each
-  GemmArgs tall[2 * ZRL_MAX_LAYERS], flat[2 * ZRL_MAX_LAYERS];
-  int nt = 0, nf = 0;
-  for (int i = 0; i < nw; ++i) {
-    if (w[i].M >= 256)
-      tall[nt++] = w[i];
-    else
-      flat[nf++] = w[i];
-  }
-  for (int i = 0; i < nt; i += 8) TRY(run_group(ctx, tall + i, std::min(8, nt - i)));
-  for (int i = 0; i < nf; i += 8) TRY(run_group(ctx, flat + i, std::min(8, nf - i)));
   return ZRL_OK;
 }
 
@@ -642,7 +665,9 @@ struct MbView {
 // summed gradient in G (padded layout, log_std included) and the three
 // statistic sums in sums3.
 static zrl_status minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
-                                  const MbView &v, float scale) {
+                                  const MbView &v, float scale,
+                                  const PrestepArgs *fuse = nullptr, bool *fused = nullptr) {
+  if (fused) *fused = false;
   TRY(ensure_mb(ctx, std::max<int64_t>(v.rows, 1)));
   if (v.rows > 0) TRY(forward_both(ctx, v.xa, v.xc, v.rows));
   const NetLayout &La = ctx->net[0], &Lc = ctx->net[1];
@@ -693,7 +718,8 @@ static zrl_status minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
     segs.seg[segs.n++] = ReduceSeg{ctx->G + Lc.b_off[Lc.L - 1], fp + 2 * la.Ap + 4, (int64_t)la.cp, lb, w};
   }
   TRY(backward_both(ctx, v.xa, v.xc, v.rows, &wp, &bp, segs));
-  launch_reduce_segments(segs, ctx->stream);
+  const int f = launch_reduce_segments(segs, ctx->stream, fuse, &ctx->rs);
+  if (fused) *fused = f != 0;
   ctx->launches++;
   CHECK_LAUNCH();
   return ZRL_OK;
@@ -705,8 +731,8 @@ static zrl_status allreduce_grads(zrl_ctx *ctx) {
 }
 
 // Stepping half of minibatch_step (ppo.rs:475-489).
-static zrl_status step(zrl_ctx *ctx, const zrl_ppo_config *cfg, int minibatches,
-                       bool last_of_epoch, bool count_stats) {
+static PrestepArgs prestep_args(zrl_ctx *ctx, const zrl_ppo_config *cfg, int minibatches,
+                                bool last_of_epoch, bool count_stats) {
   PrestepArgs p{};
   p.grads = ctx->G;
   p.actor_begin = ctx->net[0].dev_begin;
@@ -725,9 +751,18 @@ static zrl_status step(zrl_ctx *ctx, const zrl_ppo_config *cfg, int minibatches,
   p.last_of_epoch = last_of_epoch;
   p.count_stats = count_stats;
   p.st = ctx->st;
+  return p;
+}
+
+// prestep_done: the segment reduce already ran the pre-step (one rank).
+static zrl_status step(zrl_ctx *ctx, const zrl_ppo_config *cfg, int minibatches,
+                       bool last_of_epoch, bool count_stats, bool prestep_done = false) {
+  const PrestepArgs p = prestep_args(ctx, cfg, minibatches, last_of_epoch, count_stats);
+  if (!prestep_done) {
   launch_prestep(p, ctx->rs, ctx->stream);
   ctx->launches++;
   CHECK_LAUNCH();
+  }
   AdamArgs a{};
   a.p = ctx->P;
   a.m = ctx->M;
@@ -930,9 +965,12 @@ static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
     }
     for (int64_t m = 0; m < mbs; ++m) {
       MbView v = epoch_view(ctx, P->offs[e * mbs + m], P->counts[e * mbs + m]);
-      TRY(minibatch_grads(ctx, cfg, v, scale));
+      // one rank: the segment reduce also runs the pre-step
+      const PrestepArgs pf = prestep_args(ctx, cfg, (int)mbs, m == mbs - 1, true);
+      bool fused = false;
+      TRY(minibatch_grads(ctx, cfg, v, scale, multi ? nullptr : &pf, &fused));
       TRY(allreduce_grads(ctx));
-      TRY(step(ctx, cfg, (int)mbs, m == mbs - 1, true));
+      TRY(step(ctx, cfg, (int)mbs, m == mbs - 1, true, fused));
     }
   }
   // the next update's orders, computed while this one runs (in the other

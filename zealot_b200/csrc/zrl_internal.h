@@ -164,8 +164,16 @@ struct ReduceSegs {
   // each segment
   int first_block[kMaxSegs + 1];
   int groups[kMaxSegs];
+  int net[kMaxSegs];  // with a fused pre-step: 0 actor, 1 critic, -1 neither
 };
-void launch_reduce_segments(const ReduceSegs &segs, cudaStream_t s);
+struct PrestepArgs;
+struct ReduceScratch;
+// With `fuse` (one rank: no allreduce between the two), the reduce also
+// takes the per-net squared norms of what it writes and its last block
+// runs the pre-step; returns 1 when it did (launch_prestep is then
+// skipped), 0 otherwise.
+int launch_reduce_segments(const ReduceSegs &segs, cudaStream_t s,
+                           const PrestepArgs *fuse = nullptr, ReduceScratch *rs = nullptr);
 
 // Squared norms of the actor/critic gradient segments, then the pre-step
 // scalars (ppo.rs:473-482, net.rs:197-202, net.rs:235-238, ppo.rs:497-500)
@@ -239,6 +247,10 @@ struct GemmArgs {
   // tensor-core dgrad: column sums of the (unrounded) outputs, one row of N
   // partials per 128-row tile: colsum[tile_m * N + n]
   float *colsum;
+  // tensor-core launches: walk the output tiles last to first (a launch
+  // that reads what the previous one wrote meets its most recent tiles
+  // first, while they are still in L2); no effect on the results
+  int reverse_tiles;
 };
 void gemm_simt(const GemmArgs &g, cudaStream_t s);
 
