@@ -475,12 +475,14 @@ __device__ __forceinline__ Tile decode_tile(int t, const TcGroup &g) {
   const TcProb &pr = g.p[p];
   const int lt = t - pr.tile0;
   tl.p = p;
-  const int rest = fdiv(lt, pr.div_m);
-  const int mt = lt - rest * pr.tiles_m;
-  const int z = fdiv(rest, pr.div_n);
-  tl.m0 = mt * BM * CG;
+  // n fastest: the tiles of one row block run side by side and share its
+  // A rows through L2
+  const int rest = fdiv(lt, pr.div_n);
+  const int nt = lt - rest * pr.tiles_n;
+  const int z = fdiv(rest, pr.div_m);
+  tl.m0 = (rest - z * pr.tiles_m) * BM * CG;
   tl.bn = pr.bn;
-  tl.n0 = (rest - z * pr.tiles_n) * pr.bn;
+  tl.n0 = nt * pr.bn;
   tl.z = z;
   tl.kbeg = tl.z * pr.kc;
   const int kend = min(pr.K, tl.kbeg + pr.kc);
@@ -1175,8 +1177,10 @@ int max_pairs(K kfn, int smem) {
   return n;
 }
 
+// With units_out set, only reports the persistent grid's size in tiles
+// processed at once (CTA pairs or CTAs) and launches nothing.
 template <int BN, bool A_MN, bool B_MN, int EPI, int CG, bool BF>
-cudaError_t launch_one(const TcMaps &maps, const TcGroup &grp, cudaStream_t s) {
+cudaError_t launch_one(const TcMaps &maps, const TcGroup &grp, cudaStream_t s, int *units_out) {
   constexpr int ST = stages_for<BN, EPI, CG>();
   static_assert(ST >= 2, "stage ring");
   using S = Smem<BN, ST, EPI, CG>;
@@ -1189,8 +1193,12 @@ cudaError_t launch_one(const TcMaps &maps, const TcGroup &grp, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  cudaLaunchConfig_t cfg = {};
   int units = CG == 2 ? max_pairs(kfn, S::kBytes) : g_sms;
+  if (units_out) {
+    *units_out = units;
+    return cudaSuccess;
+  }
+  cudaLaunchConfig_t cfg = {};
   if (grp.tiles < units) units = grp.tiles;
   cfg.gridDim = dim3(CG * units);
   cfg.blockDim = dim3(kThreads);
@@ -1211,34 +1219,35 @@ cudaError_t launch_one(const TcMaps &maps, const TcGroup &grp, cudaStream_t s) {
 
 template <int BN, int CG, bool BF>
 cudaError_t dispatch_bn(int kind, int epi, const TcMaps &maps, const TcGroup &grp,
-                        cudaStream_t s) {
+                        cudaStream_t s, int *u) {
   if (kind == 0) {  // forward
-    if (epi == EPI_BIAS_ELU) return launch_one<BN, false, false, EPI_BIAS_ELU, CG, BF>(maps, grp, s);
-    if (epi == EPI_BIAS) return launch_one<BN, false, false, EPI_BIAS, CG, BF>(maps, grp, s);
-    return launch_one<BN, false, false, EPI_STORE, CG, BF>(maps, grp, s);
+    if (epi == EPI_BIAS_ELU)
+      return launch_one<BN, false, false, EPI_BIAS_ELU, CG, BF>(maps, grp, s, u);
+    if (epi == EPI_BIAS) return launch_one<BN, false, false, EPI_BIAS, CG, BF>(maps, grp, s, u);
+    return launch_one<BN, false, false, EPI_STORE, CG, BF>(maps, grp, s, u);
   }
   if constexpr (!BF || BN / CG >= 64) {
     if (kind == 1) {  // dgrad
       if (epi == EPI_ELU_GRAD)
-        return launch_one<BN, false, true, EPI_ELU_GRAD, CG, BF>(maps, grp, s);
-      return launch_one<BN, false, true, EPI_STORE, CG, BF>(maps, grp, s);
+        return launch_one<BN, false, true, EPI_ELU_GRAD, CG, BF>(maps, grp, s, u);
+      return launch_one<BN, false, true, EPI_STORE, CG, BF>(maps, grp, s, u);
     }
-    return launch_one<BN, true, true, EPI_STORE, CG, BF>(maps, grp, s);  // wgrad
+    return launch_one<BN, true, true, EPI_STORE, CG, BF>(maps, grp, s, u);  // wgrad
   }
   return cudaErrorInvalidValue;
 }
 
 template <bool BF>
 cudaError_t dispatch(int CG, int BN, int kind, int epi, const TcMaps &maps, const TcGroup &grp,
-                     cudaStream_t s) {
+                     cudaStream_t s, int *units_out = nullptr) {
   if (CG == 1) {
-    if (BN == 32) return dispatch_bn<32, 1, BF>(kind, epi, maps, grp, s);
-    if (BN == 64) return dispatch_bn<64, 1, BF>(kind, epi, maps, grp, s);
-    return dispatch_bn<128, 1, BF>(kind, epi, maps, grp, s);
+    if (BN == 32) return dispatch_bn<32, 1, BF>(kind, epi, maps, grp, s, units_out);
+    if (BN == 64) return dispatch_bn<64, 1, BF>(kind, epi, maps, grp, s, units_out);
+    return dispatch_bn<128, 1, BF>(kind, epi, maps, grp, s, units_out);
   }
-  if (BN == 64) return dispatch_bn<64, 2, BF>(kind, epi, maps, grp, s);
-  if (BN == 128) return dispatch_bn<128, 2, BF>(kind, epi, maps, grp, s);
-  return dispatch_bn<256, 2, BF>(kind, epi, maps, grp, s);
+  if (BN == 64) return dispatch_bn<64, 2, BF>(kind, epi, maps, grp, s, units_out);
+  if (BN == 128) return dispatch_bn<128, 2, BF>(kind, epi, maps, grp, s, units_out);
+  return dispatch_bn<256, 2, BF>(kind, epi, maps, grp, s, units_out);
 }
 
 }  // namespace
@@ -1323,6 +1332,66 @@ static int layout_kind(const GemmArgs &g) {
   return -1;
 }
 
+// Tall GEMMs (every M >= 256) run on CTA pairs with 256 x BN tiles, BN up
+// to 256: each SM then stages half of the B tile, which halves the
+// shared-memory and L2 bytes per flop.  Others run on single CTAs with
+// 128 x BN tiles, BN up to 128.  bf16 MN-major B is loaded in 64-column
+// boxes: each CTA's share of a tile is a whole number of them.
+static void tile_shape(int minM, int maxN, bool bf, int kind, int *CG, int *BN) {
+  *CG = (minM >= 256 && maxN > 32) ? 2 : 1;
+  *BN = maxN <= 32 ? 32 : (maxN <= 64 ? 64 : (maxN <= 128 || *CG == 1 ? 128 : 256));
+  if (bf && kind != 0 && *BN / *CG < 64) *BN = 64 * *CG;
+}
+
+// A problem at most half as wide as the launch's tiles takes half-width
+// tiles (while each CTA's share of B stays whole 32-column boxes, 64 for
+// bf16 MN-major).
+static int tile_width(int N, int BN, int CG, bool bf, int kind) {
+  const int min_share = (bf && kind != 0) ? 64 : 32;
+  return (BN / 2 / CG >= min_share && N <= BN / 2) ? BN / 2 : BN;
+}
+
+int gemm_tc_split(GemmEngine *eng, const GemmArgs *gs, int n, int precision, int max_split) {
+  (void)eng;
+  const bool bf = precision == ZRL_GEMM_BF16;
+  if (n < 1 || max_split < 1) return 1;
+  const int kind = layout_kind(gs[0]);
+  if (kind < 0) return 1;
+  int maxN = 0, minM = INT32_MAX;
+  for (int i = 0; i < n; ++i) {
+    maxN = std::max(maxN, gs[i].N);
+    minM = std::min(minM, gs[i].M);
+  }
+  int CG, BN;
+  tile_shape(minM, maxN, bf, kind, &CG, &BN);
+  int64_t per_split = 0;  // output tiles of one split
+  for (int i = 0; i < n; ++i) {
+    const int bn = tile_width(gs[i].N, BN, CG, bf, kind);
+    per_split += (int64_t)((gs[i].M + BM * CG - 1) / (BM * CG)) * ((gs[i].N + bn - 1) / bn);
+  }
+  int units = 0;
+  TcMaps maps;
+  TcGroup grp;
+  const cudaError_t e = bf ? dispatch<true>(CG, BN, kind, gs[0].epi, maps, grp, nullptr, &units)
+                           : dispatch<false>(CG, BN, kind, gs[0].epi, maps, grp, nullptr, &units);
+  if (e != cudaSuccess || units < 1) return 1;
+  // estimated time: rounds of the persistent grid x k-blocks per split;
+  // the fewest splits (partial bytes) within 3 % of the best
+  const int ke = bf ? 64 : 32;
+  int64_t K = 0;
+  for (int i = 0; i < n; ++i) K = std::max<int64_t>(K, gs[i].K);
+  auto cost = [&](int S) {
+    const int64_t kc = ((K + S - 1) / S + ke - 1) / ke;
+    const int64_t rounds = (per_split * S + units - 1) / units;
+    return rounds * kc;
+  };
+  int64_t best = INT64_MAX;
+  for (int S = 1; S <= max_split; ++S) best = std::min(best, cost(S));
+  for (int S = 1; S <= max_split; ++S)
+    if (cost(S) * 100 <= best * 103) return S;
+  return 1;
+}
+
 zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precision,
                          cudaStream_t s, int *launched, std::string *err) {
   *launched = 0;
@@ -1373,15 +1442,8 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
     maxN = std::max(maxN, g.N);
     minM = std::min(minM, g.M);
   }
-  // Tall GEMMs (every M >= 256) run on CTA pairs with 256 x BN tiles,
-  // BN up to 256: each SM then stages half of the B tile, which halves
-  // the shared-memory and L2 bytes per flop.  Others run on single CTAs
-  // with 128 x BN tiles, BN up to 128.
-  const int CG = (minM >= 256 && maxN > 32) ? 2 : 1;
-  int BN = maxN <= 32 ? 32 : (maxN <= 64 ? 64 : (maxN <= 128 || CG == 1 ? 128 : 256));
-  // bf16 MN-major B is loaded in 64-column boxes: each CTA's share of a
-  // tile is a whole number of them
-  if (bf && kind != 0 && BN / CG < 64) BN = 64 * CG;
+  int CG, BN;
+  tile_shape(minM, maxN, bf, kind, &CG, &BN);
   TcMaps maps;
   memset(&maps, 0, sizeof(maps));
   TcGroup grp;
@@ -1397,8 +1459,7 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
     // B: [N rows, K cols] K-major (forward) or [K rows, N cols] MN-major
     // a problem at most half as wide as the launch's tiles takes half-width
     // tiles (while each CTA's share of B stays whole 32-column boxes)
-    const int min_share = (bf && kind != 0) ? 64 : 32;
-    const int bn = (BN / 2 / CG >= min_share && g.N <= BN / 2) ? BN / 2 : BN;
+    const int bn = tile_width(g.N, BN, CG, bf, kind);
     const int kmaj = bf ? 3 : 0, mnmaj = bf ? 4 : 1, ke = bf ? 64 : 32;
     const CUtensorMap *tb = kind == 0 ? cached_map(eng, g.B, g.N, g.K, g.ldb, bn / CG, kmaj, err)
                                       : cached_map(eng, g.B, g.K, g.N, g.ldb, ke, mnmaj, err);

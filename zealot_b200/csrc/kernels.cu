@@ -491,6 +491,192 @@ loss_kernel(LossArgs a) {
   }
 }
 
+// Quad-per-sample form of the same loss for A <= 32 and Ap == 32 (the
+// per-sample arithmetic of loss_kernel).  Four lanes take one sample, lane
+// q of the quad dimensions 8q .. 8q+7, so a warp covers 8 samples: their
+// mean rows load as two float4 per lane (coalesced), the log-prob and KL
+// sums are two shuffle steps inside the quad, and each lane keeps the
+// per-dimension sums of its 8 dimensions across the samples it visits.
+// At the end the warp folds its 8 sample slots (3 shuffle steps), and the
+// block's warps are summed in warp order into the block's partial row
+// (the layout of loss_kernel's).
+constexpr int kLossQuadThreads = 256;
+
+__global__ void __launch_bounds__(kLossQuadThreads)
+loss_quad_kernel(LossArgs a) {
+  constexpr int NW = kLossQuadThreads / 32;
+  __shared__ float wrow[NW][2 * 32 + 4];
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int q = lane & 3, slot = lane >> 2;
+  const int A = a.A;
+  float ls[8], sd[8], inv_sd[8], inv_var[8], gl[8], gm[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int k = 8 * q + i;
+    ls[i] = k < A ? a.log_std[k] : 0.0f;
+    sd[i] = expf(ls[i]);
+    inv_var[i] = expf(-2.0f * ls[i]);
+    inv_sd[i] = expf(-ls[i]);
+    gl[i] = gm[i] = 0.0f;
+  }
+  const float lo = 1.0f - a.clip, hi = 1.0f + a.clip;
+  const float ent_term = -a.entropy_coef * a.scale;
+  float acc_surr = 0.0f, acc_vloss = 0.0f, acc_kl = 0.0f, acc_gv = 0.0f;
+  // the warp walks groups of 8 samples; every lane runs every iteration
+  // (the quad shuffles take the full warp), lanes past the end as dead
+  const int64_t stride = (int64_t)gridDim.x * kLossQuadThreads / 4;
+  for (int64_t s8 = ((int64_t)blockIdx.x * kLossQuadThreads + wid * 32) / 4; s8 < a.mb;
+       s8 += stride) {
+    const int64_t s = s8 + slot;
+    const bool live = s < a.mb;
+    float mu[8], ac[8], mo[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mu[i] = ac[i] = mo[i] = 0.0f;
+    float lpo = 0.0f, adv = 0.0f;
+    if (live) {
+      const float4 *m4 = reinterpret_cast<const float4 *>(a.mean + s * 32 + 8 * q);
+      const float4 x0 = m4[0], x1 = m4[1];
+      mu[0] = x0.x, mu[1] = x0.y, mu[2] = x0.z, mu[3] = x0.w;
+      mu[4] = x1.x, mu[5] = x1.y, mu[6] = x1.z, mu[7] = x1.w;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int k = 8 * q + i;
+        if (k < A) {
+          ac[i] = a.action[s * A + k];
+          mo[i] = a.mean_old[s * A + k];
+        }
+      }
+      lpo = a.logp_old[s];
+      adv = a.adv[s];
+    }
+    float v = 0.0f, vo = 0.0f, R = 0.0f;
+    if (q == 0 && live) {
+      v = a.value[s * a.cp];
+      vo = a.value_old[s];
+      R = a.ret[s];
+    }
+    float d[8], t[8], kl = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      d[i] = t[i] = 0.0f;
+      if (live && 8 * q + i < A) {
+        d[i] = __fsub_rn(ac[i], mu[i]);
+        const float z = __fdiv_rn(d[i], sd[i]);
+        t[i] = __fsub_rn(__fsub_rn(__fmul_rn(__fmul_rn(-0.5f, z), z), ls[i]), kLogSqrt2Pi);
+        const float dk = (mu[i] - mo[i]) * inv_sd[i];
+        kl += 0.5f * (dk * dk);
+      }
+    }
+    // log-prob summed over k = 0, 1, ... in order, as ActorCritic::logp
+    // (ppo.rs:297-305) and the rollout that recorded logp_old do: the
+    // running sum passes through the quad's lanes in turn, so the ratio at
+    // an unchanged policy is exactly 1
+    float lp = 0.0f;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float prev = __shfl_up_sync(0xffffffffu, lp, 1);
+      if (q == r) {
+        if (r > 0) lp = prev;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (8 * q + i < A) lp = __fadd_rn(lp, t[i]);
+      }
+    }
+    lp = __shfl_sync(0xffffffffu, lp, lane | 3);
+    kl += __shfl_xor_sync(0xffffffffu, kl, 1);
+    kl += __shfl_xor_sync(0xffffffffu, kl, 2);
+    const float ratio = expf(lp - lpo);
+    const float rc = fminf(fmaxf(ratio, lo), hi);
+    const bool clipped = (adv >= 0.0f && ratio > hi) || (adv < 0.0f && ratio < lo);
+    float g[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      g[i] = 0.0f;
+      if (live && 8 * q + i < A) {
+        float t = 0.0f;
+        if (!clipped) {
+          g[i] = -(adv * ratio * d[i] * inv_var[i]) * a.scale;
+          const float dls = adv * ratio * ((d[i] * d[i]) * inv_var[i] - 1.0f);
+          t = -dls * a.scale;
+        }
+        gl[i] += t + ent_term;
+        gm[i] += g[i];
+      }
+    }
+    if (live && a.out_mode == 0) {
+      float4 *o = reinterpret_cast<float4 *>(a.d_actor + s * 32 + 8 * q);
+      o[0] = make_float4(g[0], g[1], g[2], g[3]);
+      o[1] = make_float4(g[4], g[5], g[6], g[7]);
+    } else if (live) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) store_operand(a.d_actor, s * 32 + 8 * q + i, g[i], a.out_mode);
+    }
+    if (q == 0 && live) {
+      acc_surr += fminf(ratio * adv, rc * adv) * a.scale;
+      acc_kl += kl * a.scale;
+      // clipped value loss, ppo.rs:439-449
+      const float vc = vo + fminf(fmaxf(v - vo, -a.clip), a.clip);
+      const float eu = v - R, ec = vc - R;
+      const float lu = eu * eu, lc = ec * ec;
+      float vloss, dv;
+      if (lc > lu) {
+        vloss = lc;
+        dv = 2.0f * ec;
+      } else {
+        vloss = lu;
+        dv = 2.0f * eu;
+      }
+      acc_vloss += vloss * a.scale;
+      const float gv = a.value_coef * dv * a.scale;
+      acc_gv += gv;
+      store_operand(a.d_critic, s * a.cp, gv, a.out_mode);
+    }
+  }
+  // fold the warp's 8 sample slots: lane q of slot 0 ends with dimensions
+  // 8q .. 8q+7 summed over the warp
+#pragma unroll
+  for (int off = 4; off < 32; off *= 2)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      gl[i] += __shfl_xor_sync(0xffffffffu, gl[i], off);
+      gm[i] += __shfl_xor_sync(0xffffffffu, gm[i], off);
+    }
+  acc_surr = warp_sum(acc_surr);
+  acc_vloss = warp_sum(acc_vloss);
+  acc_kl = warp_sum(acc_kl);
+  acc_gv = warp_sum(acc_gv);
+  if (slot == 0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      wrow[wid][8 * q + i] = gl[i];
+      wrow[wid][32 + 8 * q + i] = gm[i];
+    }
+  }
+  if (lane == 0) {
+    wrow[wid][64] = acc_surr;
+    wrow[wid][65] = acc_vloss;
+    wrow[wid][66] = acc_kl;
+    wrow[wid][67] = acc_gv;
+  }
+  __syncthreads();
+  // [g_logstd (Ap) | db_actor (Ap) | surr vloss kl 0 | db_critic (cp)]
+  const int Ap = a.Ap;
+  float *row = a.part + (int64_t)blockIdx.x * a.width;
+  for (int c = threadIdx.x; c < a.width; c += blockDim.x) {
+    int src = -1;
+    if (c < Ap) src = c < A ? c : -1;
+    else if (c < 2 * Ap) src = c - Ap < A ? 32 + (c - Ap) : -1;
+    else if (c < 2 * Ap + 4) src = c - 2 * Ap < 3 ? 64 + (c - 2 * Ap) : -1;
+    else src = c == 2 * Ap + 4 ? 67 : -1;
+    float t = 0.0f;
+    if (src >= 0)
+      for (int w = 0; w < NW; ++w) t += wrow[w][src];
+    row[c] = t;
+  }
+}
+
 // ------------------------------------------------------------ colsum
 
 __global__ void colsum_kernel(const float *x, int64_t rows, int cols, int ld,
@@ -508,19 +694,19 @@ __global__ void colsum_kernel(const float *x, int64_t rows, int cols, int ld,
 // ------------------------------------------------------ segment reduce
 
 // Sum of split partials.  A segment with `splits` partial rows is cut into
-// G = clamp(splits / 8, 1, 16) split groups (a power of two); a block of
+// G = clamp(splits / 8, 1, 64) split groups (a power of two); a block of
 // 512 threads covers 512 / G float4 columns x G groups, consecutive threads
 // on consecutive columns (coalesced).  Group j sums splits j, j+G, j+2G,
 // ... in split order, loading eight rows at a time before adding them, and
-// the G group sums are then added in group order -- a fixed order, so every
-// run gives the same bits.  Every segment count and stride is a multiple of
+// the G group sums are then added pairwise in a fixed tree -- a fixed
+// order, so every run gives the same bits.  Every segment count and stride is a multiple of
 // 4 floats and every pointer 16-byte aligned (the padded layout guarantees
 // both).
 constexpr int kRsThreads = 512;
 
 __host__ __device__ __forceinline__ int rs_groups(int splits) {
   int g = 1;
-  while (g < 16 && g * 8 < splits) g *= 2;
+  while (g < 64 && g * 8 < splits) g *= 2;
   return g;
 }
 __host__ __device__ __forceinline__ int64_t rs_blocks(int64_t count, int splits) {
@@ -570,19 +756,24 @@ reduce_segments_kernel(ReduceSegs segs, PrestepArgs pa, double *partials, unsign
       }
     }
   }
+  // the G group sums of each column, pairwise in a fixed tree
   __shared__ float4 part[kRsThreads];
   part[threadIdx.x] = t;
   __syncthreads();
+  for (int h = G >> 1; h >= 1; h >>= 1) {
+    if (grp < h) {
+      const float4 x = part[threadIdx.x + h * cols4];
+      t.x += x.x;
+      t.y += x.y;
+      t.z += x.z;
+      t.w += x.w;
+      part[threadIdx.x] = t;
+    }
+    __syncthreads();
+  }
   double sq = 0.0;
   if (grp == 0 && live) {
-    float4 s4 = part[c];
-    for (int j = 1; j < G; ++j) {
-      const float4 x = part[j * cols4 + c];
-      s4.x += x.x;
-      s4.y += x.y;
-      s4.z += x.z;
-      s4.w += x.w;
-    }
+    const float4 s4 = t;
     reinterpret_cast<float4 *>(dst)[i4] = s4;
     sq = (double)s4.x * s4.x + (double)s4.y * s4.y + (double)s4.z * s4.z +
          (double)s4.w * s4.w;
@@ -965,14 +1156,26 @@ void launch_round_copy(const float *src, float *dst, int64_t n, int mode, cudaSt
   round_copy_kernel<<<grid_for(n, 256), 256, 0, s>>>(src, dst, n, mode);
 }
 
-int loss_blocks(int64_t mb) { return grid_for(mb * 32, kLossThreads, 4 * 148); }
+// the quad form needs 16-byte aligned 32-float mean rows
+static bool loss_by_quads(const LossArgs &a) {
+  return a.A <= 32 && a.Ap == 32 && ((uintptr_t)a.mean & 15) == 0 &&
+         ((uintptr_t)a.d_actor & 15) == 0;
+}
+
+int loss_blocks(const LossArgs &a) {
+  if (loss_by_quads(a))  // a sample per quad, at most 4 blocks per SM
+    return grid_for(a.mb * 4, kLossQuadThreads, 4 * 148);
+  return grid_for(a.mb * 32, kLossThreads, 4 * 148);
+}
 
 void launch_loss(const LossArgs &a, cudaStream_t s) {
-  // four blocks per SM, each warp walking its samples with the next
-  // sample's loads in flight; the block rows are summed by the segment
-  // reduce that follows the backward pass
-  const int blocks = loss_blocks(a.mb);
-  launch_pdl(loss_kernel, blocks, kLossThreads, s, a);
+  // the block rows are summed by the segment reduce that follows the
+  // backward pass
+  const int blocks = loss_blocks(a);
+  if (loss_by_quads(a))
+    launch_pdl(loss_quad_kernel, blocks, kLossQuadThreads, s, a);
+  else  // four blocks per SM, a warp per sample with the next sample's loads in flight
+    launch_pdl(loss_kernel, blocks, kLossThreads, s, a);
 }
 
 void launch_colsum(const float *x, int64_t rows, int cols, int ld,

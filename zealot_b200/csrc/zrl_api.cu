@@ -384,6 +384,8 @@ static zrl_status start_plan(zrl_ctx *ctx, OrderPlan &P, uint64_t seed0, int64_t
   return ZRL_OK;
 }
 
+constexpr int kMaxWSplit = 32;  // split-K partial rows the scratch holds per weight
+
 static int wsplit_for(int64_t mb) {
   // enough row chunks to fill the machine on the small output tiles, each
   // chunk at least 512 rows
@@ -398,7 +400,7 @@ static zrl_status ensure_mb(zrl_ctx *ctx, int64_t mb) {
     for (int l = 1; l <= L.L; ++l) TRY(dalloc(ctx, &ctx->act[k][l], mb * L.dp[l]));
     for (int l = 0; l < L.L; ++l) TRY(dalloc(ctx, &ctx->dlt[k][l], mb * L.dp[l + 1]));
   }
-  const int S = std::max(wsplit_for(mb), 32);
+  const int S = std::max(wsplit_for(mb), kMaxWSplit);
   int64_t wp = 0, bp = 0;
   for (int k = 0; k < 2; ++k) {
     const NetLayout &L = ctx->net[k];
@@ -547,8 +549,10 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
   // Tall ones (dp[l+1] >= 256 rows) go to CTA-pair tiles, the rest to
   // single-CTA tiles: a grouped launch (of at most 8) each, issued right
   // after the dgrad level that reads the same delta_l and a_l (level 1 for
-  // layer 0), so those reads meet L2.
+  // layer 0), so those reads meet L2.  Each group takes the split count
+  // that fills the grid with the fewest partial rows.
   GemmArgs tall[2 * ZRL_MAX_LAYERS], flat[2 * ZRL_MAX_LAYERS];
+  int64_t tall_dst[2 * ZRL_MAX_LAYERS], flat_dst[2 * ZRL_MAX_LAYERS];
   int nt = 0, nf = 0, tall_lvl = 1, flat_lvl = 1;
   for (int k = 0; k < 2; ++k) {
     const NetLayout &L = ctx->net[k];
@@ -563,23 +567,32 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
       g.B = l == 0 ? (k == 0 ? xa : xc) : ctx->act[k][l];
       g.ldb = L.dp[l];
       g.trans_b = false;
-      g.C = *wp;
       g.ldc = L.dp[l];
       g.epi = EPI_STORE;
-      g.split_k = S;
-      ReduceSeg sw{ctx->G + L.w_off[l], *wp, (int64_t)L.dp[l + 1] * L.dp[l], S,
-                   (int64_t)L.dp[l + 1] * L.dp[l]};
-      segs.seg[segs.n++] = sw;
-      *wp += (int64_t)S * L.dp[l + 1] * L.dp[l];
       if (g.M >= 256) {
+        tall_dst[nt] = L.w_off[l];
         tall[nt++] = g;
         tall_lvl = nt == 1 ? l : std::min(tall_lvl, l);
       } else {
+        flat_dst[nf] = L.w_off[l];
         flat[nf++] = g;
         flat_lvl = nf == 1 ? l : std::min(flat_lvl, l);
       }
     }
   }
+  auto place = [&](GemmArgs *w, const int64_t *dst, int nw) {
+    int sg = ctx->gemm.split_for(w, std::min(nw, 8), ctx->precision, kMaxWSplit, &ctx->err);
+    if (sg < 1) sg = S;
+    for (int i = 0; i < nw; ++i) {
+      w[i].split_k = sg;
+      w[i].C = *wp;
+      const int64_t sz = (int64_t)w[i].M * w[i].N;
+      segs.seg[segs.n++] = ReduceSeg{ctx->G + dst[i], *wp, sz, sg, sz};
+      *wp += (int64_t)sg * sz;
+    }
+  };
+  place(tall, tall_dst, nt);
+  place(flat, flat_dst, nf);
   tall_lvl = std::max(tall_lvl, 1);
   flat_lvl = std::max(flat_lvl, 1);
   // successive launches alternate their tile order, starting opposite to
@@ -700,7 +713,7 @@ static zrl_status minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
     CK(cudaMemsetAsync(ctx->G, 0, sizeof(float) * ctx->grad_len, ctx->stream));
     return ZRL_OK;
   }
-  const int lb = loss_blocks(v.rows);
+  const int lb = loss_blocks(la);
   if (la.width > ctx->rs.fwidth || lb > ctx->rs.max_blocks) return bad(ctx, "loss scratch too small");
   launch_loss(la, ctx->stream);
   ctx->launches++;

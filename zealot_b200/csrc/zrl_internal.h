@@ -141,7 +141,7 @@ struct LossArgs {
   int out_mode;           // storage of the two output deltas (OperandMode)
 };
 void launch_loss(const LossArgs &a, cudaStream_t s);
-int loss_blocks(int64_t mb);  // the partial rows launch_loss writes
+int loss_blocks(const LossArgs &a);  // the partial rows launch_loss writes
 
 // Column sums of a [rows, cols] matrix, split over row chunks into
 // partials [splits, cols].
