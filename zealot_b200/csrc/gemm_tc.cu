@@ -178,13 +178,61 @@ __device__ __forceinline__ void st_shared4(uint32_t addr, float a, float b, floa
                "f"(d)
                : "memory");
 }
-__device__ __forceinline__ float4 ld_shared4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
+// Eight 16-byte shared loads in one statement: all eight are in flight
+// before the first result is used (separate volatile loads would each be
+// waited for in turn).
+__device__ __forceinline__ void ld_shared4x8(const uint32_t (&a)[8], float (&v)[32]) {
+  asm volatile(
+      "ld.shared.v4.f32 {%0, %1, %2, %3}, [%32];\n\t"
+      "ld.shared.v4.f32 {%4, %5, %6, %7}, [%33];\n\t"
+      "ld.shared.v4.f32 {%8, %9, %10, %11}, [%34];\n\t"
+      "ld.shared.v4.f32 {%12, %13, %14, %15}, [%35];\n\t"
+      "ld.shared.v4.f32 {%16, %17, %18, %19}, [%36];\n\t"
+      "ld.shared.v4.f32 {%20, %21, %22, %23}, [%37];\n\t"
+      "ld.shared.v4.f32 {%24, %25, %26, %27}, [%38];\n\t"
+      "ld.shared.v4.f32 {%28, %29, %30, %31}, [%39];"
+      : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]),
+        "=f"(v[7]), "=f"(v[8]), "=f"(v[9]), "=f"(v[10]), "=f"(v[11]), "=f"(v[12]), "=f"(v[13]),
+        "=f"(v[14]), "=f"(v[15]), "=f"(v[16]), "=f"(v[17]), "=f"(v[18]), "=f"(v[19]),
+        "=f"(v[20]), "=f"(v[21]), "=f"(v[22]), "=f"(v[23]), "=f"(v[24]), "=f"(v[25]),
+        "=f"(v[26]), "=f"(v[27]), "=f"(v[28]), "=f"(v[29]), "=f"(v[30]), "=f"(v[31])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]), "r"(a[7])
+      : "memory");
+}
+// Eight 4-byte shared loads in one statement.
+__device__ __forceinline__ void ld_shared1x8(const uint32_t (&a)[8], float (&v)[8]) {
+  asm volatile(
+      "ld.shared.f32 %0, [%8];\n\t"
+      "ld.shared.f32 %1, [%9];\n\t"
+      "ld.shared.f32 %2, [%10];\n\t"
+      "ld.shared.f32 %3, [%11];\n\t"
+      "ld.shared.f32 %4, [%12];\n\t"
+      "ld.shared.f32 %5, [%13];\n\t"
+      "ld.shared.f32 %6, [%14];\n\t"
+      "ld.shared.f32 %7, [%15];"
+      : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]),
+        "=f"(v[7])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]), "r"(a[7])
+      : "memory");
+}
+// Column sum of one 32 x 32 fp32 chunk staged with the 128-byte swizzle
+// (row r's 16-byte piece q at q ^ (r & 7)): lane j adds column j over the
+// rows in row order, the loads batched eight rows at a time.
+__device__ __forceinline__ float colsum_staged(uint32_t base, int lane) {
+  const uint32_t q = (uint32_t)lane >> 2, w = ((uint32_t)lane & 3u) * 4u;
+  float cs = 0.0f;
+#pragma unroll
+  for (int r0 = 0; r0 < 32; r0 += 8) {
+    uint32_t a[8];
+    float x[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      a[i] = base + (uint32_t)(r0 + i) * 128u + ((q ^ (uint32_t)i) << 4) + w;
+    ld_shared1x8(a, x);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) cs += x[i];
+  }
+  return cs;
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -518,32 +566,34 @@ __device__ __forceinline__ void epi_chunk(const EpiChunk &e, int lane, bool last
     if (last) release();
   }
   if (EPI == EPI_BIAS || EPI == EPI_BIAS_ELU) {
+    uint32_t a[8];
+    float b[32];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 b = ld_shared4(e.bias + 16u * q);  // broadcast
-      v[4 * q + 0] += b.x;
-      v[4 * q + 1] += b.y;
-      v[4 * q + 2] += b.z;
-      v[4 * q + 3] += b.w;
-    }
+    for (int q = 0; q < 8; ++q) a[q] = e.bias + 16u * q;  // broadcast
+    ld_shared4x8(a, b);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] += b[i];
   }
   if (EPI == EPI_BIAS_ELU) {
     // ELU (net.rs:13-16); exp on the special-function unit, whose error is
-    // far below the tf32 rounding applied next
+    // far below the tf32 rounding applied next.  Both sides are computed
+    // and selected (no per-element branch).
+    float ex[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = v[i] > 0.0f ? v[i] : exp_sfu(v[i]) - 1.0f;
+    for (int i = 0; i < 32; ++i) ex[i] = exp_sfu(v[i]);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = v[i] > 0.0f ? v[i] : ex[i] - 1.0f;
   }
   if (EPI == EPI_ELU_GRAD) {
     // ELU' from the stored post-activation y in the slot (net.rs:19-22):
     // 1 for y > 0, else y + 1 = min(y + 1, 1) (NaN kept)
+    uint32_t a[8];
+    float y[32];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 y = ld_shared4(e.slot + ((q ^ e.sw) << 4));
-      v[4 * q + 0] *= fmin_nan(y.x + 1.0f, 1.0f);
-      v[4 * q + 1] *= fmin_nan(y.y + 1.0f, 1.0f);
-      v[4 * q + 2] *= fmin_nan(y.z + 1.0f, 1.0f);
-      v[4 * q + 3] *= fmin_nan(y.w + 1.0f, 1.0f);
-    }
+    for (int q = 0; q < 8; ++q) a[q] = e.slot + ((q ^ e.sw) << 4);
+    ld_shared4x8(a, y);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] *= fmin_nan(y[i] + 1.0f, 1.0f);
   }
   if (!FULL) {
     // invalid rows and columns hold 0 (column sums; the store clips them)
@@ -559,18 +609,7 @@ __device__ __forceinline__ void epi_chunk(const EpiChunk &e, int lane, bool last
     for (int q = 0; q < 8; ++q)
       st_shared4(e.slot + ((q ^ e.sw) << 4), v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
     __syncwarp();
-    const uint32_t base = e.slot - (uint32_t)lane * 128u;
-    const uint32_t q = (uint32_t)lane >> 2, w = ((uint32_t)lane & 3u) * 4u;
-    float cs = 0.0f;
-#pragma unroll
-    for (int r = 0; r < 32; ++r) {
-      float x;
-      asm volatile("ld.shared.f32 %0, [%1];"
-                   : "=f"(x)
-                   : "r"(base + r * 128u + (((q ^ (uint32_t)(r & 7))) << 4) + w)
-                   : "memory");
-      cs += x;
-    }
+    const float cs = colsum_staged(e.slot - (uint32_t)lane * 128u, lane);
     if (lane < valid_cols) e.colsum[lane] = cs;
     __syncwarp();
   }
@@ -608,30 +647,35 @@ __device__ __forceinline__ void epi_chunk_bf16(const EpiChunk &e, int lane, bool
   }
   if (EPI == EPI_BIAS_ELU) {
 #pragma unroll
-    for (int q = 0; q < 16; ++q) {
-      const float4 b = ld_shared4(e.bias + 16u * q);  // broadcast
-      v[4 * q + 0] += b.x;
-      v[4 * q + 1] += b.y;
-      v[4 * q + 2] += b.z;
-      v[4 * q + 3] += b.w;
-    }
+    for (int h = 0; h < 2; ++h) {
+      uint32_t a[8];
+      float b[32];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) v[i] = v[i] > 0.0f ? v[i] : exp_sfu(v[i]) - 1.0f;
+      for (int q = 0; q < 8; ++q) a[q] = e.bias + 128u * h + 16u * q;  // broadcast
+      ld_shared4x8(a, b);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[32 * h + i] += b[i];
+    }
+    float ex[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) ex[i] = exp_sfu(v[i]);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = v[i] > 0.0f ? v[i] : ex[i] - 1.0f;
   }
   if (EPI == EPI_ELU_GRAD) {
     // the bf16 post-activation row in the slot: 16-byte piece q holds
     // columns 8q..8q+7
+    uint32_t a[8];
+    float raw[32];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 raw = ld_shared4(e.slot + ((q ^ e.sw) << 4));
-      const uint32_t w[4] = {__float_as_uint(raw.x), __float_as_uint(raw.y),
-                             __float_as_uint(raw.z), __float_as_uint(raw.w)};
+    for (int q = 0; q < 8; ++q) a[q] = e.slot + ((q ^ e.sw) << 4);
+    ld_shared4x8(a, raw);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float lo = __uint_as_float(w[i] << 16), hi = __uint_as_float(w[i] & 0xFFFF0000u);
-        v[8 * q + 2 * i] *= fmin_nan(lo + 1.0f, 1.0f);
-        v[8 * q + 2 * i + 1] *= fmin_nan(hi + 1.0f, 1.0f);
-      }
+    for (int i = 0; i < 32; ++i) {
+      const uint32_t w = __float_as_uint(raw[i]);
+      const float lo = __uint_as_float(w << 16), hi = __uint_as_float(w & 0xFFFF0000u);
+      v[2 * i] *= fmin_nan(lo + 1.0f, 1.0f);
+      v[2 * i + 1] *= fmin_nan(hi + 1.0f, 1.0f);
     }
   }
   if (!FULL) {
@@ -641,7 +685,6 @@ __device__ __forceinline__ void epi_chunk_bf16(const EpiChunk &e, int lane, bool
   }
   if (e.colsum) {
     const uint32_t base = e.slot - (uint32_t)lane * 128u;
-    const uint32_t q = (uint32_t)lane >> 2, wd = ((uint32_t)lane & 3u) * 4u;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       __syncwarp();
@@ -650,16 +693,7 @@ __device__ __forceinline__ void epi_chunk_bf16(const EpiChunk &e, int lane, bool
         st_shared4(e.slot + ((k ^ e.sw) << 4), v[32 * h + 4 * k], v[32 * h + 4 * k + 1],
                    v[32 * h + 4 * k + 2], v[32 * h + 4 * k + 3]);
       __syncwarp();
-      float cs = 0.0f;
-#pragma unroll
-      for (int r = 0; r < 32; ++r) {
-        float x;
-        asm volatile("ld.shared.f32 %0, [%1];"
-                     : "=f"(x)
-                     : "r"(base + r * 128u + ((q ^ (uint32_t)(r & 7)) << 4) + wd)
-                     : "memory");
-        cs += x;
-      }
+      const float cs = colsum_staged(base, lane);
       if (32 * h + lane < valid_cols) e.colsum[32 * h + lane] = cs;
     }
     __syncwarp();
@@ -714,7 +748,9 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], CG * kEpiWarps);  // the pair's epilogue warps
+      // this CTA's epilogue warps, and on the even CTA of a pair one more
+      // arrival: the odd CTA's, forwarded once all its warps arrived
+      mbar_init(&acce[b], kEpiWarps + (CG == 2 && rank == 0 ? 1 : 0));
     }
     for (int b = 0; b < kEpiWarps * S::kSlots; ++b) mbar_init(&xbar[b], 1);
     fence_barrier_init();
@@ -877,6 +913,19 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
         else
           mma_commit(&accf[ab]);
       }
+    } else if (CG == 2 && lane == 0) {
+      // the odd CTA of a pair: forward its epilogue's release of each
+      // accumulator to the even CTA's barrier, where the MMA issuer waits
+      // (one cluster-scope arrival per tile instead of one per warp, off
+      // the epilogue warps' path)
+      const uint32_t acce_peer = peer_addr(smem_u32(acce), 0);
+      int it = 0;
+      for (int t = unit; t < tiles; t += units, ++it) {
+        const int ab = it & 1;
+        const uint32_t aph = (uint32_t)(it >> 1) & 1u;
+        if (!mbar_spin(&acce[ab], aph, g.err, 6)) break;
+        mbar_arrive_cluster(acce_peer + 8u * ab);
+      }
     }
   } else {
     // ---------------------------------------------------- epilogue
@@ -920,7 +969,6 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
     int it = 0, j = 0;
     bool ok = true, prev_store = false;
     // the pair's MMA warp waits on the even CTA's acc_empty barriers
-    const uint32_t acce_pair = peer_addr(smem_u32(acce), 0);
     const uint32_t wbias = smem_u32(bias_sh + ew * S::kBiasPerWarp);
     for (int t = unit; t < tiles; t += units, ++it) {
       const Tile tl = decode_tile<BN, CG, KE>(t, g);
@@ -974,12 +1022,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
           // (no TMEM read in this chunk) hand the accumulator back now
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) {
-            if (CG == 2)
-              mbar_arrive_cluster(acce_pair + 8u * ab);
-            else
-              mbar_arrive(&acce[ab]);
-          }
+          if (lane == 0) mbar_arrive(&acce[ab]);
         }
         if (EPI == EPI_ELU_GRAD && lane == 0 && j >= 1) {
           // the aux box of chunk j+NS-2 into the slot of chunk j-2, whose
@@ -1020,12 +1063,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
           auto release = [&] {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) {
-              if (CG == 2)
-                mbar_arrive_cluster(acce_pair + 8u * ab);
-              else
-                mbar_arrive(&acce[ab]);
-            }
+            if (lane == 0) mbar_arrive(&acce[ab]);
           };
           if (have && rows_full && valid_cols == CW) {
             if (OB)
