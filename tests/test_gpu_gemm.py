@@ -72,6 +72,7 @@ def run(ctx, torch, lhs, rhs, lt, rt, split=1, bf16=False):
     tb, ldb = up(b)
     ldc = (n + 3) // 4 * 4
     tc = torch.full((split, m, ldc), 7.7, dtype=torch.float32, device=dev)
+    torch.cuda.synchronize()  # the library's stream does not wait on torch's
     ctx.call("zrl_gemm", layout, m, n, k, ta.data_ptr(), lda, tb.data_ptr(), ldb,
              tc.data_ptr(), ldc, split)
     return tc.sum(0)[:, :n].cpu().numpy()
@@ -131,3 +132,27 @@ def test_ppo_shapes(torch, precision, shape, split):
     # tensor core's fp32 accumulation over K = 24,576 measures ~6e-5, still
     # 30x inside the 2e-3 tf32 bar
     assert err < (1e-5 if precision == "fp32" else 2e-4), err  # tf32, bf16: exact operands
+
+
+def test_tensor_map_cache_turnover(torch):
+    """Over 4,096 distinct shapes (each rank's share of a minibatch changes
+    from call to call in a multi-GPU update) the tensor-map cache empties
+    itself in the middle of a launch's set-up; every result must stay
+    exact across that point."""
+    ctx = Z.Context((4, 4), (4, 1), precision="tf32")
+    dev = torch.device("cuda")
+    mmax, n, k = 2300, 64, 32
+    g = torch.Generator(device="cpu").manual_seed(5)
+    a = torch.randn(mmax, k, generator=g)
+    b = torch.randn(n, k, generator=g)
+    a = torch.from_numpy(round_tf32(a.numpy())).to(dev)
+    b = torch.from_numpy(round_tf32(b.numpy())).to(dev)
+    ref = (a.double() @ b.double().T).float()
+    c = torch.empty(mmax, n, device=dev)
+    worst = 0.0
+    for m in range(1, mmax + 1):   # two new maps per call (A and C rows)
+        c.fill_(7.7)
+        torch.cuda.synchronize()
+        ctx.call("zrl_gemm", 0, m, n, k, a.data_ptr(), k, b.data_ptr(), k, c.data_ptr(), n, 1)
+        worst = max(worst, float((c[:m] - ref[:m]).abs().max()) / float(ref[:m].abs().max()))
+    assert worst < 1e-5, worst

@@ -1295,23 +1295,30 @@ struct TcCache {
 };
 
 // kind: 0 K-major operand, 1 MN-major operand, 2 output, 3 K-major bf16
-// operand, 4 MN-major bf16 operand, 5 bf16 output
-static const CUtensorMap *cached_map(GemmEngine *eng, const float *base, int64_t rows,
-                                     int64_t cols, int64_t ld, int box_or_splits, int kind,
-                                     std::string *err) {
+// operand, 4 MN-major bf16 operand, 5 bf16 output.  The map is copied out:
+// the cache may be emptied by a later call (shapes that change from call
+// to call, e.g. each rank's share of a minibatch, keep adding keys), so no
+// pointer into it may be held across calls.
+static bool cached_map(GemmEngine *eng, CUtensorMap *out, const float *base, int64_t rows,
+                       int64_t cols, int64_t ld, int box_or_splits, int kind, std::string *err) {
   TcCache *c = static_cast<TcCache *>(eng->cache);
   auto key = std::make_tuple((const void *)base, rows, cols, ld, box_or_splits, kind);
   auto it = c->maps.find(key);
-  if (it != c->maps.end()) return &it->second;
+  if (it != c->maps.end()) {
+    *out = it->second;
+    return true;
+  }
   CUtensorMap m;
   const bool ok = (kind == 2 || kind == 5)
                       ? make_out_map(&m, (float *)base, rows, cols, ld, box_or_splits, err,
                                      kind == 5)
                       : make_map(&m, base, rows, cols, ld, box_or_splits, kind == 1 || kind == 4,
                                  err, kind >= 3);
-  if (!ok) return nullptr;
+  if (!ok) return false;
   if (c->maps.size() > 4096) c->maps.clear();
-  return &(c->maps[key] = m);
+  c->maps[key] = m;
+  *out = m;
+  return true;
 }
 
 zrl_status gemm_tc_init(int device, std::string *err) {
@@ -1491,30 +1498,29 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
     const GemmArgs &g = gs[i];
     const int split = g.split_k < 1 ? 1 : g.split_k;
     // A: [M rows, K cols] K-major, or [K rows, M cols] MN-major (wgrad)
-    const CUtensorMap *ta = kind == 2 ? cached_map(eng, g.A, g.K, g.M, g.lda, bf ? 64 : 32,
-                                                   bf ? 4 : 1, err)
-                                      : cached_map(eng, g.A, g.M, g.K, g.lda, BM, bf ? 3 : 0, err);
+    const bool ta = kind == 2 ? cached_map(eng, &maps.a[i], g.A, g.K, g.M, g.lda, bf ? 64 : 32,
+                                           bf ? 4 : 1, err)
+                              : cached_map(eng, &maps.a[i], g.A, g.M, g.K, g.lda, BM, bf ? 3 : 0,
+                                           err);
     // B: [N rows, K cols] K-major (forward) or [K rows, N cols] MN-major
     // a problem at most half as wide as the launch's tiles takes half-width
     // tiles (while each CTA's share of B stays whole 32-column boxes)
     const int bn = tile_width(g.N, BN, CG, bf, kind);
     const int kmaj = bf ? 3 : 0, mnmaj = bf ? 4 : 1, ke = bf ? 64 : 32;
-    const CUtensorMap *tb = kind == 0 ? cached_map(eng, g.B, g.N, g.K, g.ldb, bn / CG, kmaj, err)
-                                      : cached_map(eng, g.B, g.K, g.N, g.ldb, ke, mnmaj, err);
+    const bool tb = kind == 0
+                        ? cached_map(eng, &maps.b[i], g.B, g.N, g.K, g.ldb, bn / CG, kmaj, err)
+                        : cached_map(eng, &maps.b[i], g.B, g.K, g.N, g.ldb, ke, mnmaj, err);
     // bf16 contexts store the forward hidden activations and the dgrad
     // deltas in bf16 (the operands of later GEMMs)
     const bool out_bf = bf && (g.epi == EPI_BIAS_ELU || g.epi == EPI_ELU_GRAD);
-    const CUtensorMap *tc = cached_map(eng, g.C, g.M, g.N, g.ldc, split, out_bf ? 5 : 2, err);
+    const bool tc =
+        cached_map(eng, &maps.c[i], g.C, g.M, g.N, g.ldc, split, out_bf ? 5 : 2, err);
     if (!ta || !tb || !tc) return ZRL_CUDA_ERROR;
-    maps.a[i] = *ta;
-    maps.b[i] = *tb;
-    maps.c[i] = *tc;
     if (kind == 1 && g.epi == EPI_ELU_GRAD) {
       // the post-activation read by the dgrad epilogue in [32 x 32] boxes
       // ([32 x 64] bf16 boxes in bf16 contexts)
-      const CUtensorMap *tx = cached_map(eng, g.aux, g.M, g.N, g.ldaux, 32, bf ? 3 : 0, err);
-      if (!tx) return ZRL_CUDA_ERROR;
-      maps.x[i] = *tx;
+      if (!cached_map(eng, &maps.x[i], g.aux, g.M, g.N, g.ldaux, 32, bf ? 3 : 0, err))
+        return ZRL_CUDA_ERROR;
     }
     TcProb &pr = grp.p[i];
     pr.M = g.M;
