@@ -51,6 +51,7 @@ struct OrderPlan {
   int64_t n_global = 0, n_local = 0, row_offset = 0;
   int epochs = 0, mbs = 0, world = 1;
   std::vector<int64_t> counts, offs, rows;  // [epochs * mbs], [epochs * mbs], [epochs]
+  std::vector<std::vector<int32_t>> perm;   // [epochs][n_global] (several ranks), reused
   std::vector<std::future<void>> jobs;
 
   bool matches(uint64_t s0, int64_t ng, int64_t nl, int64_t ro, int ep, int mb, int w) const {
@@ -75,13 +76,14 @@ struct OrderPlan {
       }
       return;
     }
-    std::vector<int32_t> perm(n_global);
-    zrl::shuffle_i32(seed, n_global, perm.data());
+    std::vector<int32_t> &pe = perm[e];
+    if ((int64_t)pe.size() < n_global) pe.resize(n_global);
+    zrl::shuffle_i32(seed, n_global, pe.data());
     int64_t n = 0;
     for (int m = 0; m < mbs; ++m) {
       offs[e * mbs + m] = n;
       for (int64_t p = (int64_t)m * mb; p < (int64_t)(m + 1) * mb; ++p) {
-        const int64_t r = perm[p] - row_offset;
+        const int64_t r = pe[p] - row_offset;
         if (r >= 0 && r < n_local) ord[n++] = (int32_t)r;
       }
       counts[e * mbs + m] = n - offs[e * mbs + m];
@@ -378,6 +380,7 @@ static zrl_status start_plan(zrl_ctx *ctx, OrderPlan &P, uint64_t seed0, int64_t
   P.counts.assign((size_t)epochs * mbs, 0);
   P.offs.assign((size_t)epochs * mbs, 0);
   P.rows.assign((size_t)epochs, 0);
+  if (P.world > 1 && (int)P.perm.size() < epochs) P.perm.resize(epochs);
   for (int e = 0; e < epochs; ++e)
     P.jobs.push_back(std::async(std::launch::async, [&P, e] { P.compute(e); }));
   P.valid = true;
@@ -962,6 +965,13 @@ static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
     P = &ctx->plan[0];
     TRY(start_plan(ctx, *P, seed0, n_global, n_local, row_offset, epochs, (int)mbs));
   }
+  // the next update's orders, computed while this one runs (in the other
+  // plan, which the previous update -- complete by now -- used); started
+  // here so the workers have the whole update to finish
+  OrderPlan &Q = P == &ctx->plan[0] ? ctx->plan[1] : ctx->plan[0];
+  if (epochs > 0)
+    TRY(start_plan(ctx, Q, seed0 + (uint64_t)epochs * (uint64_t)mbs, n_global, n_local,
+                   row_offset, epochs, (int)mbs));
   if (epochs > 0) TRY(normalize_batch(ctx, d.obs, d.cobs, n_local));
   for (int e = 0; e < epochs; ++e) {
     P->jobs[e].wait();
@@ -986,12 +996,6 @@ static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
       TRY(step(ctx, cfg, (int)mbs, m == mbs - 1, true, fused));
     }
   }
-  // the next update's orders, computed while this one runs (in the other
-  // plan: this plan's pinned orders may still be in flight to the device)
-  OrderPlan &Q = P == &ctx->plan[0] ? ctx->plan[1] : ctx->plan[0];
-  if (epochs > 0)
-    TRY(start_plan(ctx, Q, seed0 + (uint64_t)epochs * (uint64_t)mbs, n_global, n_local,
-                   row_offset, epochs, (int)mbs));
   ctx->t_logstd_host += cfg->epochs * (int32_t)mbs;
   return ZRL_OK;
 }
