@@ -76,6 +76,22 @@ def flops_per_sample_pass(adims, cdims):
     return f
 
 
+def bytes_per_sample_pass(adims, cdims, elem):
+    """Algorithmic HBM bytes of the GEMMs per sample per epoch: every
+    activation and delta row read or written once per GEMM that uses it --
+    forward (read a_l, write a_l+1), input gradient (read delta_l and the
+    stored a_l for ELU', write delta_l-1; every layer but the first) and
+    weight gradient (read delta_l and a_l).  Weights (L2-resident) and
+    split-K partials are left out."""
+    f = 0
+    for d in (adims, cdims):
+        L = len(d) - 1
+        f += sum(d[l] + d[l + 1] for l in range(L))            # forward
+        f += sum(d[l + 1] + 2 * d[l] for l in range(1, L))     # dgrad
+        f += sum(d[l + 1] + d[l] for l in range(L))            # wgrad
+    return f * elem
+
+
 class Clocks:
     """nvidia-smi sampling during the timed region."""
 
@@ -438,10 +454,26 @@ def main():
     else:
         peak, peak_src = 75.0, "nominal fp32 CUDA-core peak (no measured figure)"
     achieved = fl / (g_ms.value * 1e-3) / 1e12 if g_ms.value > 0 else None
-    roof = {"bound": "tensor", "kernel": "mlp gemm (all GEMM launches of one update)",
-            "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-            "frac": (achieved / peak) if achieved else None,
-            "traffic": profile_traffic(), "peak_source": peak_src,
+    # The MLP GEMMs are skinny (K, N <= 512 against M = 24,576 rows): at
+    # ~50 FLOP per byte they sit left of the ridge (measured tf32 peak /
+    # measured HBM bandwidth, ~115), so the binding roof is HBM.
+    by = bytes_per_sample_pass(w.actor_dims, w.critic_dims,
+                               2 if precision == "bf16" else 4) * n_local * w.epochs
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    ach_gbs = by / (g_ms.value * 1e-3) / 1e9 if g_ms.value > 0 else None
+    roof = {"bound": "hbm", "kernel": "mlp gemm (all GEMM launches of one update)",
+            "achieved": ach_gbs, "peak": hbm, "unit": "GB/s",
+            "frac": (ach_gbs / hbm) if ach_gbs else None,
+            "traffic": profile_traffic(),
+            "peak_source": "MEASURED_PEAKS.json hbm_gbs (copy)" if "hbm_gbs" in peaks
+                           else "fallback 6.65 TB/s",
+            "algorithmic_bytes_per_launch": by / g_n.value if g_n.value else None,
+            "algorithmic_gb_per_update": by / 1e9,
+            "intensity_flop_per_byte": fl / by,
+            "ridge_flop_per_byte": peak * 1e12 / (hbm * 1e9),
+            "tensor_view": {"achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                            "frac": (achieved / peak) if achieved else None,
+                            "peak_source": peak_src},
             "gemm_ms_per_update": g_ms.value, "gemm_launches_per_update": g_n.value,
             "gemm_share_of_update": g_ms.value / u_ms.value if u_ms.value else None,
             "algorithmic_gflop_per_update": fl / 1e9}
