@@ -502,25 +502,32 @@ loss_kernel(LossArgs a) {
 // (the layout of loss_kernel's).
 constexpr int kLossQuadThreads = 256;
 
-__global__ void __launch_bounds__(kLossQuadThreads)
+// three blocks per SM (registers kept under 85): the sample groups of a
+// C2 minibatch then run in one wave
+__global__ void __launch_bounds__(kLossQuadThreads, 3)
 loss_quad_kernel(LossArgs a) {
   constexpr int NW = kLossQuadThreads / 32;
   __shared__ float wrow[NW][2 * 32 + 4];
+  __shared__ float kp[4][32];  // per dimension: log_std, sd, 1 / sd, 1 / var
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int q = lane & 3, slot = lane >> 2;
   const int A = a.A;
-  float ls[8], sd[8], inv_sd[8], inv_var[8], gl[8], gm[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int k = 8 * q + i;
-    ls[i] = k < A ? a.log_std[k] : 0.0f;
-    sd[i] = expf(ls[i]);
-    inv_var[i] = expf(-2.0f * ls[i]);
-    inv_sd[i] = expf(-ls[i]);
-    gl[i] = gm[i] = 0.0f;
+  if (threadIdx.x < 32) {
+    const int k = threadIdx.x;
+    const float l = k < A ? a.log_std[k] : 0.0f;
+    kp[0][k] = l;
+    kp[1][k] = expf(l);
+    kp[2][k] = expf(-l);
+    kp[3][k] = expf(-2.0f * l);
   }
+  __syncthreads();
+  const float *ls = kp[0] + 8 * q, *sd = kp[1] + 8 * q, *inv_sd = kp[2] + 8 * q,
+              *inv_var = kp[3] + 8 * q;
+  float gl[8], gm[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) gl[i] = gm[i] = 0.0f;
   const float lo = 1.0f - a.clip, hi = 1.0f + a.clip;
   const float ent_term = -a.entropy_coef * a.scale;
   float acc_surr = 0.0f, acc_vloss = 0.0f, acc_kl = 0.0f, acc_gv = 0.0f;
