@@ -43,7 +43,7 @@ def parse():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--config", default=None, choices=["c1", "c2", "c4", "c5"])
+    p.add_argument("--config", default=None, choices=["c1", "c2", "c3", "c4", "c5"])
     p.add_argument("--precision", default=None, choices=["tf32", "fp32", "bf16"])
     p.add_argument("--envs-per-gpu", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -289,10 +289,75 @@ def run_reference(args):
 
 # ------------------------------------------------------------- GPU leg
 
+def bench_c3(args):
+    """BASELINE configs[2] (C3): the rollout step -- batch 4096 x obs 96
+    through the actor and critic, Gaussian action sampling with seeded
+    Philox draws and the log-prob (zrl_policy_step on device buffers),
+    repeated for the T = 24 steps of a rollout.  Latency per step and
+    samples/s; one GPU (other ranks exit)."""
+    import torch
+    from zealot_b200 import native as N
+    from zealot_b200 import synth
+    from zealot_b200 import zealot_rl as Z
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    n, T = 4096, 24
+    adims, cdims = synth.WORKLOADS["c2"].actor_dims, synth.WORKLOADS["c2"].critic_dims
+    ac = Z.ActorCritic(adims, cdims, precision=args.precision or "tf32", device=local)
+    ac.params = synth.xavier_params(np.random.default_rng(1234), adims, cdims)
+    g = torch.Generator(device="cpu").manual_seed(7)
+    obs = torch.randn(T, n, adims[0], generator=g).to(dev)
+    cobs = torch.randn(T, n, cdims[0], generator=g).to(dev)
+    act = torch.empty(n, adims[-1], device=dev)
+    mean = torch.empty(n, adims[-1], device=dev)
+    lp = torch.empty(n, device=dev)
+    val = torch.empty(n, device=dev)
+    stream = torch.cuda.ExternalStream(N.lib().zrl_stream(ac.ctx.h), device=dev)
+    torch.cuda.synchronize()
+
+    def rollout(seed):
+        for t in range(T):
+            ac.ctx.call("zrl_policy_step", obs[t].data_ptr(), cobs[t].data_ptr(), n, seed, t,
+                        act.data_ptr(), lp.data_ptr(), mean.data_ptr(), val.data_ptr(), 1)
+
+    for i in range(args.warmup):
+        rollout(i)
+    times = []
+    l0 = ac.kernel_launches()
+    for i in range(args.steps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        rollout(100 + i)
+        e1.record(stream)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = sum(times) / len(times)
+    launches = (ac.kernel_launches() - l0) // args.steps
+    line = {"metric": "rollout-step samples/s (policy forward + Gaussian sampling + logp)",
+            "value": n * T / (ms * 1e-3), "unit": "samples/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "ms_per_rollout_step": ms / T, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": args.precision or "tf32",
+            "data": "synthetic obs ~N(0,1), Xavier-uniform init",
+            "config": {"workload": "c3", "batch": n, "T": T, "actor": list(adims),
+                       "critic": list(cdims),
+                       "note": "one step = a T-step rollout of policy steps; each policy "
+                               "step returns when its outputs are on the device"},
+            "gpu_launches": int(launches)}
+    print(json.dumps(line), flush=True)
+    ac.close()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.config == "c3":
+        return bench_c3(args)
 
     import torch
     import torch.distributed as dist

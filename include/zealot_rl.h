@@ -216,6 +216,13 @@ zrl_status zrl_minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
                                const zrl_batch *batch, const int64_t *idx,
                                int64_t n_idx, float *grads_out,
                                float *sums3_out);
+/* The epoch permutation of ppo.rs:357-363 (the same indices as zrl_shuffle)
+ * computed on the context's device into order[n] (device pointer, int32,
+ * n < 2^31): the Lcg draws by jump-ahead, then each position's value from
+ * the chain of steps that last wrote it.  Replaces the host loop of
+ * ppo.rs:357-363 for callers that want the order on the device. */
+zrl_status zrl_shuffle_device(zrl_ctx *ctx, uint64_t seed, int64_t n,
+                              int32_t *order);
 /* One MLP GEMM through the context's GEMM engine (the precision it was
  * created with), on device pointers, row-major; C is fp32, A and B are fp32
  * (fp32 and tf32 contexts) or bf16 (bf16 contexts: 2-byte elements, lda and

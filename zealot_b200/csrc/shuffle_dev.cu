@@ -1,0 +1,93 @@
+// shuffle_dev.cu -- the epoch permutation of ppo.rs:357-363 computed on the
+// device, equal index for index to the sequential Fisher-Yates loop
+// (host_rng.cpp zrl_shuffle).
+//
+// Step i (i = n-1 down to 1) swaps positions i and j_i = min(trunc(u_d *
+// (i + 1)), i), where u_d is the d-th Lcg draw and d = n - i.  The draws
+// depend on the seed alone, so every j_i is computed at once: the Lcg step
+// is the affine map s -> a s + c (mod 2^64), and the state after d draws is
+// the d-th power of that map applied to Lcg::new(seed), built by squaring.
+//
+// Position i is final after step i and receives what position j_i held
+// just before step i.  Just before step t, a position p holds what the most
+// recent earlier step that targeted it wrote there -- that is the step with
+// the smallest k > t and j_k = p, which wrote what position k held just
+// before step k -- or p itself when no such step exists.  Every output
+// element walks that chain (each hop strictly increases k, so it ends) over
+// per-position lists of the steps that targeted the position.
+#include <cstdint>
+
+#include "zrl_internal.h"
+
+namespace zrl {
+namespace {
+
+constexpr uint64_t kLcgA = 6364136223846793005ull;  // rng.rs:21
+constexpr uint64_t kLcgC = 1442695040888963407ull;
+
+// The Lcg state after d steps from s0.
+__device__ __forceinline__ uint64_t lcg_jump(uint64_t s0, uint64_t d) {
+  uint64_t a = 1, c = 0;              // the composed map so far (identity)
+  uint64_t pa = kLcgA, pc = kLcgC;    // the map of 2^b steps
+  while (d) {
+    if (d & 1) {
+      c = pa * c + pc;
+      a = pa * a;
+    }
+    pc = pa * pc + pc;
+    pa = pa * pa;
+    d >>= 1;
+  }
+  return a * s0 + c;
+}
+
+// j_i for every step, and the per-position lists of the steps that
+// targeted it (head[p] -> next[k] -> ... -> -1, in any order).
+__global__ void fy_link_kernel(uint64_t s0, int32_t n, int32_t *jt, int32_t *head,
+                               int32_t *next) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x + 1; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t s = lcg_jump(s0, (uint64_t)(n - i));
+    // Lcg::unit (rng.rs:19-26): the top 24 bits over 2^24 (exact)
+    const float u = __fmul_rn((float)(s >> 40), 5.9604644775390625e-08f);
+    const float prod = __fmul_rn(u, (float)(i + 1));
+    int64_t j = (int64_t)prod;
+    if (j > i) j = i;
+    jt[i] = (int32_t)j;
+    next[i] = atomicExch(&head[j], (int32_t)i);
+  }
+}
+
+__global__ void fy_walk_kernel(int32_t n, const int32_t *jt, const int32_t *head,
+                               const int32_t *next, int32_t *order) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int32_t p = i == 0 ? 0 : jt[i];
+    int32_t t = (int32_t)i;
+    for (;;) {
+      int32_t best = INT32_MAX;
+      for (int32_t e = head[p]; e >= 0; e = next[e])
+        if (e > t && e < best) best = e;
+      if (best == INT32_MAX) break;
+      p = best;
+      t = best;
+    }
+    order[i] = p;
+  }
+}
+
+}  // namespace
+
+void launch_shuffle_device(uint64_t seed, int32_t n, int32_t *order, int32_t *scratch,
+                           cudaStream_t s) {
+  if (n <= 0) return;
+  int32_t *jt = scratch, *head = scratch + n, *next = scratch + 2 * (int64_t)n;
+  cudaMemsetAsync(head, 0xFF, sizeof(int32_t) * (size_t)n, s);  // -1: empty lists
+  const int threads = 256;
+  const int blocks = (int)std::min<int64_t>(((int64_t)n + threads - 1) / threads, 148 * 16);
+  const uint64_t s0 = seed | 1ull;  // Lcg::new (rng.rs:14-16)
+  fy_link_kernel<<<blocks, threads, 0, s>>>(s0, n, jt, head, next);
+  fy_walk_kernel<<<blocks, threads, 0, s>>>(n, jt, head, next, order);
+}
+
+}  // namespace zrl

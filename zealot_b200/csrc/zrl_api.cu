@@ -1570,6 +1570,24 @@ zrl_status zrl_forward(zrl_ctx *ctx, const float *obs, const float *critic_obs,
   return check_device_error(ctx);
 }
 
+zrl_status zrl_shuffle_device(zrl_ctx *ctx, uint64_t seed, int64_t n, int32_t *order) {
+  if (!ctx || n < 0 || n > INT32_MAX || (n > 0 && !order)) return ZRL_INVALID_ARG;
+  if (n == 0) return ZRL_OK;
+  CK(cudaSetDevice(ctx->device));
+  int32_t *scratch = nullptr;
+  CK(cudaMallocAsync((void **)&scratch, sizeof(int32_t) * 3 * (size_t)n, ctx->stream));
+  launch_shuffle_device(seed, (int32_t)n, order, scratch, ctx->stream);
+  ctx->launches += 2;
+  const cudaError_t e = cudaGetLastError();
+  cudaFreeAsync(scratch, ctx->stream);
+  if (e != cudaSuccess) {
+    ctx->err = std::string("zrl_shuffle_device: ") + cudaGetErrorString(e);
+    return ZRL_CUDA_ERROR;
+  }
+  CK(cudaStreamSynchronize(ctx->stream));
+  return ZRL_OK;
+}
+
 zrl_status zrl_gemm(zrl_ctx *ctx, int32_t layout, int32_t M, int32_t N, int32_t K,
                     const float *A, int32_t lda, const float *B, int32_t ldb, float *C,
                     int32_t ldc, int32_t split_k) {

@@ -117,6 +117,11 @@ void launch_normalize_rows(const float *x, int64_t n, int dim, int pitch,
 // dst = tf32(src) (round to nearest) over n floats.
 // dst[i] = src[i] stored as `mode` says (1 tf32-rounded fp32, 2 bf16).
 void launch_round_copy(const float *src, float *dst, int64_t n, int mode, cudaStream_t s);
+// The epoch permutation of ppo.rs:357-363 (Fisher-Yates driven by
+// Lcg::new(seed)) into order[n] on the device (shuffle_dev.cu); scratch
+// holds 3 n int32.
+void launch_shuffle_device(uint64_t seed, int32_t n, int32_t *order, int32_t *scratch,
+                           cudaStream_t s);
 
 // PPO losses (ppo.rs:410-452) over one minibatch.
 struct LossArgs {
