@@ -775,9 +775,9 @@ static zrl_status step(zrl_ctx *ctx, const zrl_ppo_config *cfg, int minibatches,
                        bool last_of_epoch, bool count_stats, bool prestep_done = false) {
   const PrestepArgs p = prestep_args(ctx, cfg, minibatches, last_of_epoch, count_stats);
   if (!prestep_done) {
-  launch_prestep(p, ctx->rs, ctx->stream);
-  ctx->launches++;
-  CHECK_LAUNCH();
+    launch_prestep(p, ctx->rs, ctx->stream);
+    ctx->launches++;
+    CHECK_LAUNCH();
   }
   AdamArgs a{};
   a.p = ctx->P;
