@@ -602,13 +602,13 @@ loss_quad_kernel(LossArgs a) {
     for (int i = 0; i < 8; ++i) {
       g[i] = 0.0f;
       if (live && 8 * q + i < A) {
-        float t = 0.0f;
+        float gls = 0.0f;  // this sample's log_std gradient term
         if (!clipped) {
           g[i] = -(adv * ratio * d[i] * inv_var[i]) * a.scale;
           const float dls = adv * ratio * ((d[i] * d[i]) * inv_var[i] - 1.0f);
-          t = -dls * a.scale;
+          gls = -dls * a.scale;
         }
-        gl[i] += t + ent_term;
+        gl[i] += gls + ent_term;
         gm[i] += g[i];
       }
     }
