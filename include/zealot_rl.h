@@ -280,6 +280,16 @@ float zrl_lcg_gauss(uint64_t *state);
 /* The epoch permutation of ppo.rs:357-363: Fisher-Yates over n driven by
  * Lcg::new(seed).  order receives n indices. */
 void zrl_shuffle(uint64_t seed, int64_t n, int64_t *order);
+/* One rank's share of the epoch permutation (data parallel over rows): the
+ * permutation of n_global samples (zrl_shuffle(seed)) cut into minibatches
+ * slices of n_global / minibatches positions; per slice, the positions
+ * whose sample lies in [row_offset, row_offset + n_local), as local rows, in
+ * permutation order.  order receives them (at most n_local), counts[m] the
+ * number in slice m; returns the total, or -1 on invalid arguments.  The
+ * host logic the several-rank update runs. */
+int64_t zrl_rank_orders(uint64_t seed, int64_t n_global, int64_t n_local,
+                        int64_t row_offset, int32_t minibatches, int32_t *order,
+                        int64_t *counts);
 
 /* ---- instrumentation ---------------------------------------------------- */
 

@@ -10,6 +10,12 @@
 
 #include "../../include/zealot_rl.h"
 
+namespace zrl {
+void shuffle_i32(uint64_t seed, int64_t n, int32_t *order);
+int64_t rank_slices(const int32_t *perm, int64_t n_global, int64_t n_local, int64_t row_offset,
+                    int minibatches, int32_t *order, int64_t *counts, int64_t *offs);
+}  // namespace zrl
+
 extern "C" {
 
 // rng.rs:14-16
@@ -29,6 +35,20 @@ float zrl_lcg_gauss(uint64_t *s) {
   float r = sqrtf(-2.0f * logf(u1));
   float ang = 6.28318548202514648f * zrl_lcg_unit(s);
   return r * cosf(ang);
+}
+
+int64_t zrl_rank_orders(uint64_t seed, int64_t n_global, int64_t n_local,
+                        int64_t row_offset, int32_t minibatches, int32_t *order,
+                        int64_t *counts) {
+  if (n_global <= 0 || minibatches <= 0 || n_local < 0 || !order || !counts) return -1;
+  int32_t *perm = new int32_t[(size_t)n_global];
+  int64_t *offs = new int64_t[(size_t)minibatches];
+  zrl::shuffle_i32(seed, n_global, perm);
+  const int64_t n = zrl::rank_slices(perm, n_global, n_local, row_offset, minibatches, order,
+                                     counts, offs);
+  delete[] perm;
+  delete[] offs;
+  return n;
 }
 
 void zrl_shuffle(uint64_t seed, int64_t n, int64_t *order) {
@@ -62,6 +82,27 @@ void shuffle_i32(uint64_t seed, int64_t n, int32_t *order) {
     order[i] = order[j];
     order[j] = t;
   }
+}
+
+// One rank's share of an epoch (data parallel over rows): the global
+// permutation perm[n_global] cut into `minibatches` slices of
+// n_global / minibatches positions (ppo.rs:364-367); per slice, the
+// positions whose sample lies in [row_offset, row_offset + n_local), as
+// local rows, in permutation order.  Writes order[] (at most n_local
+// entries) and the per-minibatch counts and offsets; returns the total.
+int64_t rank_slices(const int32_t *perm, int64_t n_global, int64_t n_local, int64_t row_offset,
+                    int minibatches, int32_t *order, int64_t *counts, int64_t *offs) {
+  const int64_t mb = n_global / minibatches;
+  int64_t n = 0;
+  for (int m = 0; m < minibatches; ++m) {
+    offs[m] = n;
+    for (int64_t p = (int64_t)m * mb; p < (int64_t)(m + 1) * mb; ++p) {
+      const int64_t r = perm[p] - row_offset;
+      if (r >= 0 && r < n_local) order[n++] = (int32_t)r;
+    }
+    counts[m] = n - offs[m];
+  }
+  return n;
 }
 
 // Mlp::new (net.rs:61-78) into a flat [w_0, b_0, ...] buffer.

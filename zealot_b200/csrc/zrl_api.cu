@@ -32,6 +32,8 @@ std::vector<uint8_t> st_serialize(const std::map<std::string, StTensor> &ts);
 bool st_parse(const uint8_t *buf, size_t len, std::map<std::string, StTensor> *out,
               std::string *err);
 void shuffle_i32(uint64_t seed, int64_t n, int32_t *order);
+int64_t rank_slices(const int32_t *perm, int64_t n_global, int64_t n_local, int64_t row_offset,
+                    int minibatches, int32_t *order, int64_t *counts, int64_t *offs);
 void mlp_init_reference(const int32_t *dims, int n_dims, float out_scale,
                         uint64_t *rng, float *params);
 }
@@ -79,16 +81,8 @@ struct OrderPlan {
     std::vector<int32_t> &pe = perm[e];
     if ((int64_t)pe.size() < n_global) pe.resize(n_global);
     zrl::shuffle_i32(seed, n_global, pe.data());
-    int64_t n = 0;
-    for (int m = 0; m < mbs; ++m) {
-      offs[e * mbs + m] = n;
-      for (int64_t p = (int64_t)m * mb; p < (int64_t)(m + 1) * mb; ++p) {
-        const int64_t r = pe[p] - row_offset;
-        if (r >= 0 && r < n_local) ord[n++] = (int32_t)r;
-      }
-      counts[e * mbs + m] = n - offs[e * mbs + m];
-    }
-    rows[e] = n;
+    rows[e] = zrl::rank_slices(pe.data(), n_global, n_local, row_offset, mbs, ord,
+                               counts.data() + (int64_t)e * mbs, offs.data() + (int64_t)e * mbs);
   }
 };
 
