@@ -10,6 +10,9 @@
 #include <cuda_runtime.h>
 #include <stdio.h>
 #include <string.h>
+#include <sys/resource.h>
+#include <sys/syscall.h>
+#include <unistd.h>
 
 #include <algorithm>
 #include <future>
@@ -376,7 +379,14 @@ static zrl_status start_plan(zrl_ctx *ctx, OrderPlan &P, uint64_t seed0, int64_t
   P.rows.assign((size_t)epochs, 0);
   if (P.world > 1 && (int)P.perm.size() < epochs) P.perm.resize(epochs);
   for (int e = 0; e < epochs; ++e)
-    P.jobs.push_back(std::async(std::launch::async, [&P, e] { P.compute(e); }));
+    P.jobs.push_back(std::async(std::launch::async, [&P, e] {
+      // below the submitting thread: with several ranks on one host these
+      // workers (the global Fisher-Yates per rank and epoch) can outnumber
+      // the cores, and a rank whose submitting thread waits for a core
+      // delays every rank at the next allreduce
+      setpriority(PRIO_PROCESS, (id_t)syscall(SYS_gettid), 10);
+      P.compute(e);
+    }));
   P.valid = true;
   return ZRL_OK;
 }
