@@ -223,6 +223,15 @@ zrl_status zrl_minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
  * ppo.rs:357-363 for callers that want the order on the device. */
 zrl_status zrl_shuffle_device(zrl_ctx *ctx, uint64_t seed, int64_t n,
                               int32_t *order);
+/* zrl_rank_orders computed on the context's device (the permutation by
+ * zrl_shuffle_device, then an order-keeping compaction of the rank's rows):
+ * order is a device pointer (at most n_local int32), counts a host array of
+ * minibatches entries.  Returns the total, or -1 (zrl_last_error says
+ * why). */
+int64_t zrl_rank_orders_device(zrl_ctx *ctx, uint64_t seed, int64_t n_global,
+                               int64_t n_local, int64_t row_offset,
+                               int32_t minibatches, int32_t *order,
+                               int64_t *counts);
 /* One MLP GEMM through the context's GEMM engine (the precision it was
  * created with), on device pointers, row-major; C is fp32, A and B are fp32
  * (fp32 and tf32 contexts) or bf16 (bf16 contexts: 2-byte elements, lda and

@@ -91,3 +91,115 @@ void launch_shuffle_device(uint64_t seed, int32_t n, int32_t *order, int32_t *sc
 }
 
 }  // namespace zrl
+
+// ------------------------------------------------- one rank's share, on device
+
+namespace zrl {
+namespace {
+
+constexpr int kScanThreads = 1024;
+
+// flag of permutation position p: inside the used slices (p < used) and
+// holding one of this rank's rows
+__device__ __forceinline__ int rank_flag(const int32_t *perm, int64_t p, int64_t used,
+                                         int64_t row_offset, int64_t n_local) {
+  if (p >= used) return 0;
+  const int64_t r = (int64_t)perm[p] - row_offset;
+  return r >= 0 && r < n_local;
+}
+
+// exclusive prefix of v over the block (kScanThreads threads, every thread
+// calls it), and the block's total
+__device__ __forceinline__ int block_excl_scan(int v, int *total) {
+  __shared__ int warp_tot[kScanThreads / 32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_tot[wid] = x;
+  __syncthreads();
+  if (wid == 0) {
+    int w = warp_tot[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    warp_tot[lane] = w;  // inclusive over warps
+  }
+  __syncthreads();
+  const int before = wid > 0 ? warp_tot[wid - 1] : 0;
+  *total = warp_tot[kScanThreads / 32 - 1];
+  __syncthreads();  // warp_tot is reused by the next call
+  return before + x - v;
+}
+
+// pass 1: the number of flagged positions of each block
+__global__ void rank_count_kernel(const int32_t *perm, int64_t used, int64_t row_offset,
+                                  int64_t n_local, int32_t *block_sums) {
+  const int64_t p = (int64_t)blockIdx.x * kScanThreads + threadIdx.x;
+  int total;
+  block_excl_scan(rank_flag(perm, p, used, row_offset, n_local), &total);
+  if (threadIdx.x == 0) block_sums[blockIdx.x] = total;
+}
+
+// pass 2 (one block): exclusive prefix of the block sums, in place
+__global__ void rank_offsets_kernel(int32_t *block_sums, int nblk) {
+  int carry = 0;
+  for (int b0 = 0; b0 < nblk; b0 += kScanThreads) {
+    const int b = b0 + threadIdx.x;
+    const int v = b < nblk ? block_sums[b] : 0;
+    int total;
+    const int e = block_excl_scan(v, &total);
+    if (b < nblk) block_sums[b] = carry + e;
+    carry += total;
+  }
+}
+
+// pass 3: scatter this rank's rows in permutation order; the prefix at
+// every slice boundary gives the per-slice counts: counts[m] receives
+// -prefix(start of slice m), counts[mbs] the prefix at the end
+__global__ void rank_scatter_kernel(const int32_t *perm, int64_t used, int64_t row_offset,
+                                    int64_t n_local, const int32_t *block_offs, int64_t mb,
+                                    int mbs, int32_t *order, int64_t *counts) {
+  const int64_t p = (int64_t)blockIdx.x * kScanThreads + threadIdx.x;
+  const int f = rank_flag(perm, p, used, row_offset, n_local);
+  int total;
+  const int64_t pos = block_offs[blockIdx.x] + block_excl_scan(f, &total);
+  if (f) order[pos] = (int32_t)((int64_t)perm[p] - row_offset);
+  if (p < used && p % mb == 0) counts[p / mb] = -pos;
+  if (p == used - 1) counts[mbs] = pos + f;
+}
+
+// counts[m] = prefix(start of m+1) - prefix(start of m)
+__global__ void rank_counts_kernel(int64_t *counts, int mbs) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int64_t end = counts[mbs];
+  for (int m = mbs - 1; m >= 0; --m) {
+    const int64_t start = -counts[m];
+    counts[m] = end - start;
+    end = start;
+  }
+}
+
+}  // namespace
+
+void launch_rank_orders(const int32_t *perm, int64_t n_global, int64_t n_local,
+                        int64_t row_offset, int mbs, int32_t *order, int64_t *counts,
+                        int32_t *scratch, cudaStream_t s) {
+  const int64_t mb = n_global / mbs;
+  const int64_t used = mb * mbs;
+  const int nblk = (int)((n_global + kScanThreads - 1) / kScanThreads);
+  cudaMemsetAsync(counts, 0, sizeof(int64_t) * (size_t)(mbs + 1), s);
+  if (used <= 0 || nblk <= 0) return;
+  rank_count_kernel<<<nblk, kScanThreads, 0, s>>>(perm, used, row_offset, n_local, scratch);
+  rank_offsets_kernel<<<1, kScanThreads, 0, s>>>(scratch, nblk);
+  rank_scatter_kernel<<<nblk, kScanThreads, 0, s>>>(perm, used, row_offset, n_local, scratch,
+                                                    mb, mbs, order, counts);
+  rank_counts_kernel<<<1, 32, 0, s>>>(counts, mbs);
+}
+
+}  // namespace zrl

@@ -1592,6 +1592,44 @@ zrl_status zrl_shuffle_device(zrl_ctx *ctx, uint64_t seed, int64_t n, int32_t *o
   return ZRL_OK;
 }
 
+int64_t zrl_rank_orders_device(zrl_ctx *ctx, uint64_t seed, int64_t n_global, int64_t n_local,
+                               int64_t row_offset, int32_t minibatches, int32_t *order,
+                               int64_t *counts) {
+  if (!ctx || n_global <= 0 || n_global > INT32_MAX || minibatches <= 0 || n_local < 0 ||
+      !order || !counts)
+    return -1;
+  if (cudaSetDevice(ctx->device) != cudaSuccess) return -1;
+  const size_t nblk = (size_t)(n_global + 1023) / 1024;
+  // perm [n_global] | shuffle scratch [3 n_global] | block sums [nblk + 1],
+  // then the counts [minibatches + 1] on the next 8-byte boundary
+  const size_t ints = (size_t)n_global * 4 + nblk + 1;
+  int32_t *buf = nullptr;
+  if (cudaMallocAsync((void **)&buf,
+                      sizeof(int32_t) * ints + sizeof(int64_t) * (minibatches + 1) + 8,
+                      ctx->stream) != cudaSuccess) {
+    ctx->err = "zrl_rank_orders_device: allocation failed";
+    return -1;
+  }
+  int32_t *perm = buf, *sh = buf + n_global, *bs = buf + 4 * (size_t)n_global;
+  int64_t *cnt = reinterpret_cast<int64_t *>(
+      (reinterpret_cast<uintptr_t>(buf + ints) + 7) & ~(uintptr_t)7);
+  launch_shuffle_device(seed, (int32_t)n_global, perm, sh, ctx->stream);
+  launch_rank_orders(perm, n_global, n_local, row_offset, minibatches, order, cnt, bs,
+                     ctx->stream);
+  ctx->launches += 6;
+  cudaMemcpyAsync(counts, cnt, sizeof(int64_t) * minibatches, cudaMemcpyDeviceToHost,
+                  ctx->stream);
+  cudaFreeAsync(buf, ctx->stream);
+  const cudaError_t e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) {
+    ctx->err = std::string("zrl_rank_orders_device: ") + cudaGetErrorString(e);
+    return -1;
+  }
+  int64_t n = 0;
+  for (int m = 0; m < minibatches; ++m) n += counts[m];
+  return n;
+}
+
 zrl_status zrl_gemm(zrl_ctx *ctx, int32_t layout, int32_t M, int32_t N, int32_t K,
                     const float *A, int32_t lda, const float *B, int32_t ldb, float *C,
                     int32_t ldc, int32_t split_k) {

@@ -122,6 +122,15 @@ void launch_round_copy(const float *src, float *dst, int64_t n, int mode, cudaSt
 // holds 3 n int32.
 void launch_shuffle_device(uint64_t seed, int32_t n, int32_t *order, int32_t *scratch,
                            cudaStream_t s);
+// One rank's share of a device permutation perm[n_global] (shuffle_dev.cu):
+// per slice of n_global / mbs positions, the positions whose sample lies in
+// [row_offset, row_offset + n_local), as local rows, in permutation order,
+// into order[]; counts[0..mbs] (device, mbs + 1 entries) ends with the
+// per-slice counts in counts[0..mbs-1].  scratch holds n_global / 1024 + 1
+// int32.
+void launch_rank_orders(const int32_t *perm, int64_t n_global, int64_t n_local,
+                        int64_t row_offset, int mbs, int32_t *order, int64_t *counts,
+                        int32_t *scratch, cudaStream_t s);
 
 // PPO losses (ppo.rs:410-452) over one minibatch.
 struct LossArgs {

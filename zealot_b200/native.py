@@ -117,6 +117,8 @@ _SIGS = {
     "zrl_shuffle_device": (C.c_int, [_P, C.c_uint64, C.c_int64, _P]),
     "zrl_rank_orders": (C.c_int64, [C.c_uint64, C.c_int64, C.c_int64, C.c_int64, C.c_int32,
                                     _P, _P]),
+    "zrl_rank_orders_device": (C.c_int64, [_P, C.c_uint64, C.c_int64, C.c_int64, C.c_int64,
+                                           C.c_int32, _P, _P]),
     "zrl_kernel_launches": (C.c_int64, [_P]),
     "zrl_set_profiling": (C.c_int, [_P, C.c_int32]),
     "zrl_get_profile": (C.c_int, [_P, C.POINTER(C.c_float), C.POINTER(C.c_float),
