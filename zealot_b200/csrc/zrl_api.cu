@@ -89,6 +89,27 @@ struct OrderPlan {
   }
 };
 
+// Several ranks: every epoch's orders computed on the device (the global
+// permutation by zrl_shuffle_device's kernels, then the compaction of the
+// rank's rows), the per-minibatch counts copied to pinned host memory.  The
+// next update's orders are computed at the end of an update, so the stream
+// synchronization that ends it also delivers the counts.
+struct DevPlan {
+  bool valid = false;
+  uint64_t seed0 = 0;
+  int64_t n_global = 0, n_local = 0, row_offset = 0;
+  int epochs = 0, mbs = 0;
+  int32_t *order = nullptr;   // device [epochs][n_local]
+  int32_t *scratch = nullptr; // device: perm [n_global] | shuffle [3 n_global] | block sums
+  int64_t *cnt = nullptr;     // device [epochs][mbs + 1]
+  int64_t *cnt_host = nullptr;  // pinned [epochs][mbs]
+  int64_t cap_order = 0, cap_scratch = 0, cap_cnt = 0;
+  bool matches(uint64_t s0, int64_t ng, int64_t nl, int64_t ro, int ep, int mb) const {
+    return valid && seed0 == s0 && n_global == ng && n_local == nl && row_offset == ro &&
+           epochs == ep && mbs == mb;
+  }
+};
+
 struct zrl_ctx {
   int device = 0;
   cudaStream_t stream = nullptr;
@@ -147,6 +168,7 @@ struct zrl_ctx {
   int32_t *order_pinned = nullptr;
   int64_t order_pinned_cap = 0;
   OrderPlan plan[2];  // this update's and (speculatively) the next one's
+  DevPlan dplan;      // several ranks: orders on the device
 
   // minibatch activations / deltas
   int64_t mb_cap = 0;
@@ -945,6 +967,65 @@ static zrl_status check_cfg(zrl_ctx *ctx, const zrl_ppo_config *cfg) {
 
 // The epoch/minibatch loop of ActorCritic::update (ppo.rs:350-383) once the
 // batch is on the device and the advantage moments are in ctx->st.
+// Queue the device orders of an update (several ranks) on the context's
+// stream: per epoch the global permutation (seed0 + e * mbs + 1, the seed
+// order of ppo.rs:360) and this rank's compacted rows; the counts reach
+// cnt_host once the stream has passed this point.
+static zrl_status queue_device_orders(zrl_ctx *ctx, uint64_t seed0, int64_t n_global,
+                                      int64_t n_local, int64_t row_offset, int epochs,
+                                      int mbs) {
+  DevPlan &D = ctx->dplan;
+  D.valid = false;
+  if (n_global > INT32_MAX) return bad(ctx, "n_global beyond 2^31 samples");
+  const int64_t nblk = (n_global + 1023) / 1024;
+  const int64_t need_order = std::max<int64_t>((int64_t)epochs * n_local, 1);
+  const int64_t need_scratch = 4 * n_global + nblk + 1;
+  const int64_t need_cnt = (int64_t)epochs * (mbs + 1);
+  if (need_order > D.cap_order) {
+    if (D.order) cudaFree(D.order);
+    D.order = nullptr;
+    D.cap_order = 0;
+    CK(cudaMalloc((void **)&D.order, sizeof(int32_t) * (size_t)need_order));
+    D.cap_order = need_order;
+  }
+  if (need_scratch > D.cap_scratch) {
+    if (D.scratch) cudaFree(D.scratch);
+    D.scratch = nullptr;
+    D.cap_scratch = 0;
+    CK(cudaMalloc((void **)&D.scratch, sizeof(int32_t) * (size_t)need_scratch));
+    D.cap_scratch = need_scratch;
+  }
+  if (need_cnt > D.cap_cnt) {
+    if (D.cnt) cudaFree(D.cnt);
+    if (D.cnt_host) cudaFreeHost(D.cnt_host);
+    D.cnt = nullptr;
+    D.cnt_host = nullptr;
+    D.cap_cnt = 0;
+    CK(cudaMalloc((void **)&D.cnt, sizeof(int64_t) * (size_t)need_cnt));
+    CK(cudaMallocHost((void **)&D.cnt_host, sizeof(int64_t) * (size_t)need_cnt));
+    D.cap_cnt = need_cnt;
+  }
+  int32_t *perm = D.scratch, *sh = D.scratch + n_global, *bs = D.scratch + 4 * n_global;
+  for (int e = 0; e < epochs; ++e) {
+    const uint64_t seed = seed0 + (uint64_t)e * (uint64_t)mbs + 1ull;
+    launch_shuffle_device(seed, (int32_t)n_global, perm, sh, ctx->stream);
+    launch_rank_orders(perm, n_global, n_local, row_offset, mbs, D.order + e * n_local,
+                       D.cnt + (int64_t)e * (mbs + 1), bs, ctx->stream);
+    ctx->launches += 6;
+    CK(cudaMemcpyAsync(D.cnt_host + (int64_t)e * mbs, D.cnt + (int64_t)e * (mbs + 1),
+                       sizeof(int64_t) * mbs, cudaMemcpyDeviceToHost, ctx->stream));
+  }
+  CHECK_LAUNCH();
+  D.seed0 = seed0;
+  D.n_global = n_global;
+  D.n_local = n_local;
+  D.row_offset = row_offset;
+  D.epochs = epochs;
+  D.mbs = mbs;
+  D.valid = true;
+  return ZRL_OK;
+}
+
 static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
                              const DevBatch &d, int64_t n_local,
                              int64_t n_global, int64_t row_offset) {
@@ -961,29 +1042,57 @@ static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
   TRY(ensure_mb(ctx, std::max<int64_t>(multi ? std::min<int64_t>(mb, n_local) : mb, 1)));
   const uint64_t seed0 = (uint64_t)ctx->t_logstd_host;
   const int epochs = std::max(cfg->epochs, 0);
-  // this update's orders: a speculative plan that matches, or start now
   OrderPlan *P = nullptr;
-  for (auto &q : ctx->plan)
-    if (q.matches(seed0, n_global, n_local, row_offset, epochs, (int)mbs, ctx->comm.world)) P = &q;
-  if (!P) {
-    P = &ctx->plan[0];
-    TRY(start_plan(ctx, *P, seed0, n_global, n_local, row_offset, epochs, (int)mbs));
+  // several ranks: per epoch and minibatch, the rank's row count and offset
+  std::vector<int64_t> dcounts, doffs, drows;
+  if (multi) {
+    // this update's orders on the device: queued at the end of the previous
+    // update (its closing synchronization delivered the counts), or now
+    DevPlan &D = ctx->dplan;
+    if (epochs > 0 && !D.matches(seed0, n_global, n_local, row_offset, epochs, (int)mbs)) {
+      TRY(queue_device_orders(ctx, seed0, n_global, n_local, row_offset, epochs, (int)mbs));
+      CK(cudaStreamSynchronize(ctx->stream));  // the counts size this update's launches
+    }
+    dcounts.assign(D.cnt_host, D.cnt_host + (int64_t)epochs * mbs);
+    doffs.assign((size_t)epochs * mbs, 0);
+    drows.assign((size_t)epochs, 0);
+    for (int e = 0; e < epochs; ++e) {
+      int64_t o = 0;
+      for (int64_t m = 0; m < mbs; ++m) {
+        doffs[e * mbs + m] = o;
+        o += dcounts[e * mbs + m];
+      }
+      drows[e] = o;
+    }
+  } else {
+    // this update's orders: a speculative plan that matches, or start now
+    for (auto &q : ctx->plan)
+      if (q.matches(seed0, n_global, n_local, row_offset, epochs, (int)mbs, ctx->comm.world))
+        P = &q;
+    if (!P) {
+      P = &ctx->plan[0];
+      TRY(start_plan(ctx, *P, seed0, n_global, n_local, row_offset, epochs, (int)mbs));
+    }
+    // the next update's orders, computed while this one runs (in the other
+    // plan, which the previous update -- complete by now -- used); started
+    // here so the workers have the whole update to finish
+    OrderPlan &Q = P == &ctx->plan[0] ? ctx->plan[1] : ctx->plan[0];
+    if (epochs > 0)
+      TRY(start_plan(ctx, Q, seed0 + (uint64_t)epochs * (uint64_t)mbs, n_global, n_local,
+                     row_offset, epochs, (int)mbs));
   }
-  // the next update's orders, computed while this one runs (in the other
-  // plan, which the previous update -- complete by now -- used); started
-  // here so the workers have the whole update to finish
-  OrderPlan &Q = P == &ctx->plan[0] ? ctx->plan[1] : ctx->plan[0];
-  if (epochs > 0)
-    TRY(start_plan(ctx, Q, seed0 + (uint64_t)epochs * (uint64_t)mbs, n_global, n_local,
-                   row_offset, epochs, (int)mbs));
   if (epochs > 0) TRY(normalize_batch(ctx, d.obs, d.cobs, n_local));
   for (int e = 0; e < epochs; ++e) {
-    P->jobs[e].wait();
-    const int64_t n_rows = P->rows[e];
+    if (!multi) P->jobs[e].wait();
+    const int64_t n_rows = multi ? drows[e] : P->rows[e];
     if (n_rows > 0) {
-      CK(cudaMemcpyAsync(ctx->order_dev, P->buf + (int64_t)e * n_global,
-                         sizeof(int32_t) * n_rows, cudaMemcpyHostToDevice, ctx->stream));
       GatherArgs g = gather_args(ctx, d.act, d.mo, d.lpo, d.vo, d.adv, d.ret);
+      if (multi) {
+        g.order = ctx->dplan.order + (int64_t)e * n_local;
+      } else {
+        CK(cudaMemcpyAsync(ctx->order_dev, P->buf + (int64_t)e * n_global,
+                           sizeof(int32_t) * n_rows, cudaMemcpyHostToDevice, ctx->stream));
+      }
       g.n_used = n_rows;
       g.apply_adv_norm = 1;
       launch_gather(g, ctx->stream);
@@ -991,7 +1100,9 @@ static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
       CHECK_LAUNCH();
     }
     for (int64_t m = 0; m < mbs; ++m) {
-      MbView v = epoch_view(ctx, P->offs[e * mbs + m], P->counts[e * mbs + m]);
+      const int64_t off = multi ? doffs[e * mbs + m] : P->offs[e * mbs + m];
+      const int64_t cnt = multi ? dcounts[e * mbs + m] : P->counts[e * mbs + m];
+      MbView v = epoch_view(ctx, off, cnt);
       // one rank: the segment reduce also runs the pre-step
       const PrestepArgs pf = prestep_args(ctx, cfg, (int)mbs, m == mbs - 1, true);
       bool fused = false;
@@ -1000,6 +1111,11 @@ static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
       TRY(step(ctx, cfg, (int)mbs, m == mbs - 1, true, fused));
     }
   }
+  // several ranks: the next update's orders, behind this update's work (its
+  // gathers have read the current ones)
+  if (multi && epochs > 0)
+    TRY(queue_device_orders(ctx, seed0 + (uint64_t)epochs * (uint64_t)mbs, n_global, n_local,
+                            row_offset, epochs, (int)mbs));
   ctx->t_logstd_host += cfg->epochs * (int32_t)mbs;
   return ZRL_OK;
 }
@@ -1196,6 +1312,10 @@ zrl_status zrl_destroy(zrl_ctx *ctx) {
   if (ctx->rs.dpart) cudaFree(ctx->rs.dpart);
   if (ctx->rs.ticket) cudaFree(ctx->rs.ticket);
   if (ctx->st_host) cudaFreeHost(ctx->st_host);
+  if (ctx->dplan.order) cudaFree(ctx->dplan.order);
+  if (ctx->dplan.scratch) cudaFree(ctx->dplan.scratch);
+  if (ctx->dplan.cnt) cudaFree(ctx->dplan.cnt);
+  if (ctx->dplan.cnt_host) cudaFreeHost(ctx->dplan.cnt_host);
   for (auto &q : ctx->plan) {
     q.wait_all();
     if (q.buf) cudaFreeHost(q.buf);
