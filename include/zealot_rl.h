@@ -253,15 +253,16 @@ zrl_status zrl_apply_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
 /* GAE for n_envs env-major trajectories plus the normalized advantages,
  * allocating nothing: for callers that cannot call cudaMalloc where they
  * need advantages (GPU memory owned by another runtime's pool, a real-time
- * loop that forbids allocation, work recorded under stream capture).  All
+ * loop that forbids allocation).  All
  * pointers are caller-owned device buffers; `stream` is a cudaStream_t (NULL
  * for the legacy default stream).  Outputs: adv_out/ret_out as zrl_gae,
  * adv_norm_out = (adv - mean) / max(population sd, 1e-6).  Reduction
  * scratch is a fixed array inside the library (about 67 KB on every GPU
  * that loads it), so n_envs is limited to 262,144 (ZRL_INVALID_ARG above)
  * and T to 4096; the first call on a device looks up that array and should
- * come before any stream capture; calls that overlap on the GPU race on the
- * shared array.  It has no counterpart in the reference, which computes
+ * come before any stream capture, and the address it caches does not
+ * survive a cudaDeviceReset of that device; calls that overlap on the GPU
+ * race on the shared array.  It has no counterpart in the reference, which computes
  * GAE on the host. */
 zrl_status zrl_gae_normalize_noalloc(const float *rewards, const float *values,
                                      const uint8_t *dones,

@@ -110,6 +110,7 @@ def lib():
         L.orc_ac_set_normalizers.argtypes = [C.c_void_p, _f32p, _f32p, C.c_float,
                                              _f32p, _f32p, C.c_float]
         L.orc_ac_set_lr.argtypes = [C.c_void_p, C.c_float]
+        L.orc_ac_set_operand_rounding.argtypes = [C.c_void_p, C.c_int32]
         L.orc_ac_get_lr.restype = C.c_float
         L.orc_ac_get_lr.argtypes = [C.c_void_p]
         L.orc_ac_get_adam.argtypes = [C.c_void_p, _i32p, _f32p, _f32p]
@@ -335,6 +336,12 @@ class ActorCritic:
     @lr.setter
     def lr(self, v):
         lib().orc_ac_set_lr(self.h, v)
+
+    def set_tf32_operands(self, on: bool = True):
+        """Emulate a tf32 tensor-core backend's operand rounding (inputs,
+        weights, hidden activations and deltas rounded to tf32, f32
+        accumulation) on top of the reference arithmetic."""
+        lib().orc_ac_set_operand_rounding(self.h, 1 if on else 0)
 
     def adam_state(self):
         t3 = np.zeros(3, np.int32)

@@ -129,11 +129,27 @@ void orc_mlp_init(const int32_t *dims, int32_t n_dims, float out_scale,
   }
 }
 
-/* net.rs:88-108 */
-void orc_mlp_forward(const int32_t *dims, int32_t n_dims, const float *params,
-                     const float *x, float *acts) {
+/* Operand rounding of a tf32 tensor-core GEMM, emulated: the value on the
+ * tf32 grid (10 mantissa bits), nearest, ties away from zero.  The product
+ * of two tf32 values is exact in f32, so a GEMM on rounded operands with
+ * f32 accumulation differs from this emulation only in summation order. */
+static inline float rtf32(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  if ((u & 0x7F800000u) != 0x7F800000u) u = (u + 0x1000u) & 0xFFFFE000u;
+  memcpy(&x, &u, 4);
+  return x;
+}
+
+/* net.rs:88-108.  rnd = 1 rounds every GEMM operand to tf32 where a
+ * tensor-core backend stores it: the input row, the weights and each hidden
+ * activation (after ELU); the output layer stays f32. */
+static void mlp_forward_r(const int32_t *dims, int32_t n_dims, const float *params,
+                          const float *x, float *acts, int rnd) {
   int32_t layers = n_dims - 1;
   memcpy(acts, x, sizeof(float) * (size_t)dims[0]);
+  if (rnd)
+    for (int32_t i = 0; i < dims[0]; ++i) acts[i] = rtf32(acts[i]);
   const float *prev = acts;
   float *out = acts + dims[0];
   const float *p = params;
@@ -145,8 +161,11 @@ void orc_mlp_forward(const int32_t *dims, int32_t n_dims, const float *params,
     for (int32_t o = 0; o < fan_out; ++o) {
       float z = b[o];
       const float *row = w + (int64_t)o * fan_in;
-      for (int32_t i = 0; i < fan_in; ++i) z += row[i] * prev[i];
-      out[o] = last ? z : elu(z);
+      if (rnd)
+        for (int32_t i = 0; i < fan_in; ++i) z += rtf32(row[i]) * prev[i];
+      else
+        for (int32_t i = 0; i < fan_in; ++i) z += row[i] * prev[i];
+      out[o] = last ? z : (rnd ? rtf32(elu(z)) : elu(z));
     }
     p += (int64_t)fan_out * fan_in + fan_out;
     prev = out;
@@ -154,10 +173,28 @@ void orc_mlp_forward(const int32_t *dims, int32_t n_dims, const float *params,
   }
 }
 
-/* net.rs:113-140 */
+void orc_mlp_forward(const int32_t *dims, int32_t n_dims, const float *params,
+                     const float *x, float *acts) {
+  mlp_forward_r(dims, n_dims, params, x, acts, 0);
+}
+
+/* net.rs:113-140.  rnd = 1: each layer's delta enters the weight- and
+ * input-gradient products rounded to tf32 (as a tensor-core backend stores
+ * it), the bias gradient sums the unrounded delta, the weights are read
+ * rounded; acts are the (rounded) activations of mlp_forward_r. */
+static void mlp_backward_r(const int32_t *dims, int32_t n_dims, const float *params,
+                           const float *acts, const float *g_out, float *grads,
+                           float *g_in, int rnd);
+
 void orc_mlp_backward(const int32_t *dims, int32_t n_dims, const float *params,
                       const float *acts, const float *g_out, float *grads,
                       float *g_in) {
+  mlp_backward_r(dims, n_dims, params, acts, g_out, grads, g_in, 0);
+}
+
+static void mlp_backward_r(const int32_t *dims, int32_t n_dims, const float *params,
+                           const float *acts, const float *g_out, float *grads,
+                           float *g_in, int rnd) {
   int32_t layers = n_dims - 1;
   int32_t maxd = 0;
   for (int32_t l = 0; l < n_dims; ++l)
@@ -187,9 +224,17 @@ void orc_mlp_backward(const int32_t *dims, int32_t n_dims, const float *params,
       gb[o] += d;
       const float *wrow = w + (int64_t)o * fan_in;
       float *grow = gw + (int64_t)o * fan_in;
-      for (int32_t i = 0; i < fan_in; ++i) {
-        grow[i] += d * prev[i];
-        g_prev[i] += d * wrow[i];
+      if (rnd) {
+        d = rtf32(d);
+        for (int32_t i = 0; i < fan_in; ++i) {
+          grow[i] += d * prev[i];
+          g_prev[i] += d * rtf32(wrow[i]);
+        }
+      } else {
+        for (int32_t i = 0; i < fan_in; ++i) {
+          grow[i] += d * prev[i];
+          g_prev[i] += d * wrow[i];
+        }
       }
     }
     float *t = delta;
@@ -314,6 +359,7 @@ struct orc_ac {
   float *obs_mean, *obs_m2, obs_count;
   float *crit_mean, *crit_m2, crit_count;
   float lr;
+  int32_t rnd; /* 1: tf32 operand rounding emulated (mlp_forward_r) */
 };
 
 orc_ac *orc_ac_new(const int32_t *adims, int32_t an, const int32_t *cdims,
@@ -397,6 +443,7 @@ void orc_ac_set_normalizers(orc_ac *ac, const float *obs_mean,
 }
 
 void orc_ac_set_lr(orc_ac *ac, float lr) { ac->lr = lr; }
+void orc_ac_set_operand_rounding(orc_ac *ac, int32_t mode) { ac->rnd = mode == 1; }
 float orc_ac_get_lr(const orc_ac *ac) { return ac->lr; }
 
 void orc_ac_get_adam(const orc_ac *ac, int32_t *t3, float *m, float *v) {
@@ -466,14 +513,14 @@ void orc_ac_forward(const orc_ac *ac, const float *obs, const float *cobs,
     if (mean_out) {
       orc_norm_normalize(ac->obs_mean, ac->obs_m2, ac->obs_count,
                          obs + r * ac->obs_dim, ac->obs_dim, xa);
-      orc_mlp_forward(ac->adims, ac->an, ac->params, xa, acts);
+      mlp_forward_r(ac->adims, ac->an, ac->params, xa, acts, ac->rnd);
       memcpy(mean_out + r * ac->act_dim, acts + na - ac->act_dim,
              sizeof(float) * (size_t)ac->act_dim);
     }
     if (value_out) {
       orc_norm_normalize(ac->crit_mean, ac->crit_m2, ac->crit_count,
                          cobs + r * ac->cobs_dim, ac->cobs_dim, xc);
-      orc_mlp_forward(ac->cdims, ac->cn, ac->params + ac->np_a, xc, acts);
+      mlp_forward_r(ac->cdims, ac->cn, ac->params + ac->np_a, xc, acts, ac->rnd);
       value_out[r] = acts[nc - 1];
     }
   }
@@ -503,7 +550,7 @@ static void ac_sample_accumulate(const orc_ac *ac, const orc_batch *b,
   /* --- actor (normalized obs), ppo.rs:410-433 --- */
   orc_norm_normalize(ac->obs_mean, ac->obs_m2, ac->obs_count,
                      b->obs + i * ac->obs_dim, ac->obs_dim, x);
-  orc_mlp_forward(ac->adims, ac->an, ac->params, x, acts);
+  mlp_forward_r(ac->adims, ac->an, ac->params, x, acts, ac->rnd);
   const float *mean = acts + na - A;
   const float *action = b->action + i * A;
   float logp = orc_ac_logp(ac, action, mean);
@@ -527,13 +574,13 @@ static void ac_sample_accumulate(const orc_ac *ac, const orc_batch *b,
     }
     g_logstd[k] += -cfg->entropy_coef * scale;
   }
-  orc_mlp_backward(ac->adims, ac->an, ac->params, acts, g_mean, g_actor, NULL);
+  mlp_backward_r(ac->adims, ac->an, ac->params, acts, g_mean, g_actor, NULL, ac->rnd);
 
   /* --- critic (clipped value loss), ppo.rs:435-450 --- */
   orc_norm_normalize(ac->crit_mean, ac->crit_m2, ac->crit_count,
                      b->critic_obs + i * ac->cobs_dim, ac->cobs_dim, x);
   const float *cparams = ac->params + ac->np_a;
-  orc_mlp_forward(ac->cdims, ac->cn, cparams, x, cacts);
+  mlp_forward_r(ac->cdims, ac->cn, cparams, x, cacts, ac->rnd);
   float v = cacts[nc - 1];
   float vo = b->value_old[i];
   float dvc = v - vo;
@@ -552,7 +599,7 @@ static void ac_sample_accumulate(const orc_ac *ac, const orc_batch *b,
   }
   sums[1] += vloss * scale;
   float gv = cfg->value_coef * dv * scale;
-  orc_mlp_backward(ac->cdims, ac->cn, cparams, cacts, &gv, g_critic, NULL);
+  mlp_backward_r(ac->cdims, ac->cn, cparams, cacts, &gv, g_critic, NULL, ac->rnd);
 
   /* ppo.rs:452 */
   sums[2] += ac_kl(ac, mean, b->mean_old + i * A) * scale;

@@ -126,6 +126,12 @@ void orc_ac_set_normalizers(orc_ac *ac, const float *obs_mean,
                             float crit_count);
 void orc_ac_set_lr(orc_ac *ac, float lr);
 float orc_ac_get_lr(const orc_ac *ac);
+/* 0 (default): the reference's f32 arithmetic.  1: additionally round every
+ * GEMM operand to tf32 where a tensor-core backend stores it (inputs,
+ * weights, hidden activations, the deltas entering the weight- and
+ * input-gradient products), which isolates the tf32 rounding a tf32 GEMM
+ * backend adds from everything else. */
+void orc_ac_set_operand_rounding(orc_ac *ac, int32_t mode);
 /* Adam state: t values for actor, critic, log_std; m/v flat in param order. */
 void orc_ac_get_adam(const orc_ac *ac, int32_t *t3, float *m, float *v);
 void orc_ac_set_adam(orc_ac *ac, const int32_t *t3, const float *m,

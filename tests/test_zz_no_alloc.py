@@ -2,8 +2,7 @@
 
 The no-allocation entry point exists for callers that cannot call cudaMalloc
 where they need advantages (their GPU memory belongs to another runtime's
-pool, their loop forbids allocation, or they record work under stream
-capture).  It must give what the allocating path gives: GAE advantages and
+pool, or their loop forbids allocation).  It must give what the allocating path gives: GAE advantages and
 returns bit-identical to zrl_gae's, and normalized advantages within 1e-5
 (the tolerance of the advantage tests) of those zrl_update writes back.
 Two calls in a row with different sizes check that the scratch array it

@@ -2,9 +2,8 @@
 //
 // Some callers cannot allocate device memory at the point where they need
 // advantages: a trainer whose GPU memory is owned by another runtime's
-// pooled allocator, a host that forbids allocation inside its real-time
-// loop, or work recorded while a CUDA graph is being captured (where
-// cudaMalloc is not allowed).  zrl_gae_normalize_noalloc serves them: it
+// pooled allocator, or a host that forbids allocation inside its real-time
+// loop.  zrl_gae_normalize_noalloc serves them: it
 // takes only caller-owned device buffers and keeps its reduction scratch
 // (per-block partial sums, the two advantage moments, mean and standard
 // deviation) in the file-scope array below.
@@ -16,7 +15,10 @@
 //    envs); larger calls are rejected with ZRL_INVALID_ARG.
 //  * The first call on a device looks up the array's device address
 //    (cudaGetSymbolAddress, with that device current) and caches it; make
-//    that first call before any stream capture.
+//    that first call before any stream capture.  The cached address belongs
+//    to the device's current context: after cudaDeviceReset on that device
+//    it is stale, so a process that resets a device must not call this entry
+//    point on it again.
 //  * All calls share the one array.  Every slot a call reads is written
 //    earlier in the same call, so nothing has to start at zero, but two
 //    calls that overlap on the GPU (different streams, or different host

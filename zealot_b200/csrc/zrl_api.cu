@@ -96,6 +96,10 @@ struct OrderPlan {
 // synchronization that ends it also delivers the counts.
 struct DevPlan {
   bool valid = false;
+  // the counts have reached cnt_host: set by the successful synchronization
+  // that ends an update (or the one right after queueing), cleared whenever
+  // orders are queued, so a failed update's plan is queued again
+  bool delivered = false;
   uint64_t seed0 = 0;
   int64_t n_global = 0, n_local = 0, row_offset = 0;
   int epochs = 0, mbs = 0;
@@ -105,8 +109,8 @@ struct DevPlan {
   int64_t *cnt_host = nullptr;  // pinned [epochs][mbs]
   int64_t cap_order = 0, cap_scratch = 0, cap_cnt = 0;
   bool matches(uint64_t s0, int64_t ng, int64_t nl, int64_t ro, int ep, int mb) const {
-    return valid && seed0 == s0 && n_global == ng && n_local == nl && row_offset == ro &&
-           epochs == ep && mbs == mb;
+    return valid && delivered && seed0 == s0 && n_global == ng && n_local == nl &&
+           row_offset == ro && epochs == ep && mbs == mb;
   }
 };
 
@@ -976,6 +980,7 @@ static zrl_status queue_device_orders(zrl_ctx *ctx, uint64_t seed0, int64_t n_gl
                                       int mbs) {
   DevPlan &D = ctx->dplan;
   D.valid = false;
+  D.delivered = false;
   if (n_global > INT32_MAX) return bad(ctx, "n_global beyond 2^31 samples");
   const int64_t nblk = (n_global + 1023) / 1024;
   const int64_t need_order = std::max<int64_t>((int64_t)epochs * n_local, 1);
@@ -1051,7 +1056,11 @@ static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
     DevPlan &D = ctx->dplan;
     if (epochs > 0 && !D.matches(seed0, n_global, n_local, row_offset, epochs, (int)mbs)) {
       TRY(queue_device_orders(ctx, seed0, n_global, n_local, row_offset, epochs, (int)mbs));
-      CK(cudaStreamSynchronize(ctx->stream));  // the counts size this update's launches
+      // the counts size this update's launches; the stream also holds the
+      // advantage-moment allreduces, so the wait is the bounded one that
+      // aborts the communicator when a peer is gone
+      TRY(ctx->comm.wait(ctx->stream, &ctx->err));
+      D.delivered = true;
     }
     dcounts.assign(D.cnt_host, D.cnt_host + (int64_t)epochs * mbs);
     doffs.assign((size_t)epochs * mbs, 0);
@@ -1140,6 +1149,9 @@ static zrl_status finish_update(zrl_ctx *ctx, zrl_stats *out) {
   if (ctx->comm.world > 1)
     TRY(ctx->comm.wait(ctx->stream, &ctx->err));  // bounded: peers may be gone
   CK(cudaStreamSynchronize(ctx->stream));
+  // the next update's device orders (queued at the end of this one) and
+  // their counts are now in place
+  if (ctx->dplan.valid) ctx->dplan.delivered = true;
   TRY(check_device_error(ctx));
   ctx->lr_host = ctx->st_host->lr;
   if (ctx->st_host->t[2] != ctx->t_logstd_host) {
@@ -1174,11 +1186,16 @@ static void prof_begin(zrl_ctx *ctx, cudaEvent_t *u0) {
   cudaEventRecord(*u0, ctx->stream);
 }
 
-static void prof_end(zrl_ctx *ctx, cudaEvent_t u0) {
-  if (!ctx->profiling) return;
+static zrl_status prof_end(zrl_ctx *ctx, cudaEvent_t u0) {
+  if (!ctx->profiling) return ZRL_OK;
   cudaEvent_t u1 = next_event(ctx);
   cudaEventRecord(u1, ctx->stream);
-  cudaEventSynchronize(u1);
+  // with several ranks the stream holds collectives: wait with the bounded
+  // poll that aborts the communicator when a peer is gone
+  if (ctx->comm.world > 1)
+    TRY(ctx->comm.wait(ctx->stream, &ctx->err));
+  else
+    CK(cudaEventSynchronize(u1));
   float ms = 0.0f;
   cudaEventElapsedTime(&ms, u0, u1);
   ctx->prof_update_ms = ms;
@@ -1190,6 +1207,7 @@ static void prof_end(zrl_ctx *ctx, cudaEvent_t u0) {
     g += t;
   }
   ctx->prof_gemm_ms = g;
+  return ZRL_OK;
 }
 
 // =================================================================== ABI
@@ -1585,7 +1603,7 @@ zrl_status zrl_update(zrl_ctx *ctx, const zrl_ppo_config *cfg, zrl_batch *batch,
   TRY(stage_batch(ctx, batch, &d, true));
   TRY(adv_moments(ctx, d.adv, batch->n, n_global, false, 0));
   TRY(run_epochs(ctx, cfg, d, batch->n, n_global, batch->row_offset));
-  prof_end(ctx, u0);
+  TRY(prof_end(ctx, u0));
   TRY(write_back_adv(ctx, batch, d.adv));
   return finish_update(ctx, out);
 }
@@ -1639,7 +1657,7 @@ zrl_status zrl_gae_update(zrl_ctx *ctx, const zrl_ppo_config *cfg,
   d.ret = ctx->b_ret;
   TRY(adv_moments(ctx, d.adv, n, n_global, n > 0, n > 0 ? gb : 0));
   TRY(run_epochs(ctx, cfg, d, n, n_global, batch->row_offset));
-  prof_end(ctx, u0);
+  TRY(prof_end(ctx, u0));
   return finish_update(ctx, out);
 }
 
