@@ -316,3 +316,56 @@ def test_update_is_deterministic_and_moves_params():
     assert outs[0][1] == outs[1][1]
     assert outs[0][2].tolist() == [6, 6, 6]
     assert not np.array_equal(outs[0][0], ro.params)
+
+
+def _tf32(x):
+    """Round f32 to the tf32 grid, nearest, ties away from zero."""
+    u = np.asarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    u = ((u + 0x1000) & 0xFFFFE000).astype(np.uint32)
+    return u.view(np.float32)
+
+
+def test_tf32_operand_mode_matches_a_python_restatement():
+    """The oracle's tf32 operand-rounding mode (the checker for the tensor-core
+    path): input, weights and hidden activations rounded to tf32, products
+    summed in f32 in the reference's order, output layer kept f32."""
+    assert _tf32(np.float32(1.0 + 2 ** -11)) == np.float32(1.0 + 2 ** -10)  # tie: away
+    assert _tf32(np.float32(1.0 + 2 ** -12)) == np.float32(1.0)
+    assert _tf32(np.float32(-(1.0 + 2 ** -11))) == np.float32(-(1.0 + 2 ** -10))
+    adims, cdims = (5, 7, 3), (4, 6, 1)
+    rng = np.random.default_rng(0)
+    ac = O.ActorCritic(adims, cdims)
+    params = rng.standard_normal(ac.np).astype(np.float32)
+    ac.params = params
+    obs = rng.standard_normal((3, 5)).astype(np.float32)
+    cobs = rng.standard_normal((3, 4)).astype(np.float32)
+    m32, _ = ac.forward(obs, cobs)
+    ac.set_tf32_operands()
+    mt, vt = ac.forward(obs, cobs)
+    assert not np.array_equal(m32, mt)
+
+    def fwd(dims, p, x):
+        a = _tf32(x)
+        off = 0
+        for l in range(len(dims) - 1):
+            fi, fo = dims[l], dims[l + 1]
+            w = p[off:off + fo * fi].reshape(fo, fi)
+            b = p[off + fo * fi:off + fo * fi + fo]
+            off += fo * fi + fo
+            out = np.empty(fo, np.float32)
+            for o in range(fo):
+                z = np.float32(b[o])
+                for i in range(fi):
+                    z = np.float32(z + np.float32(_tf32(w[o, i]) * a[i]))
+                if l < len(dims) - 2:
+                    z = np.float32(z if z > 0 else np.float32(np.exp(z)) - np.float32(1))
+                    z = _tf32(z)
+                out[o] = z
+            a = out
+        return a
+
+    npa = sum(adims[l + 1] * adims[l] + adims[l + 1] for l in range(len(adims) - 1))
+    for r in range(3):
+        np.testing.assert_allclose(fwd(adims, params, obs[r]), mt[r], rtol=2e-7, atol=0)
+        np.testing.assert_allclose(fwd(cdims, params[npa:], cobs[r]), vt[r:r + 1],
+                                   rtol=2e-7, atol=0)
