@@ -49,6 +49,9 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--profile-only", action="store_true",
                    help="run warmup+steps without clocks/baselines (for ncu)")
+    p.add_argument("--traffic-csv", default=None,
+                   help="ncu raw CSV with dram__bytes_{read,write}.sum of the GEMM launches "
+                        "(roofline.traffic); without it traffic is null")
     return p.parse_args()
 
 
@@ -193,95 +196,152 @@ def tf32_peak(torch, dev):
     return 2 * 8192 ** 3 / (best * 1e-3) / 1e12
 
 
-def profile_traffic():
-    """DRAM bytes per launch of the dominant kernel from the committed ncu
-    summary (a `traffic_bytes_per_launch:` line), else None."""
-    d = os.path.join(ROOT, "profiles")
-    if not os.path.isdir(d):
+def ncu_traffic(path):
+    """Mean DRAM bytes (read + write) per launch of the tensor-core GEMM
+    kernel from an ncu raw CSV (``--metrics dram__bytes_read.sum,
+    dram__bytes_write.sum --csv``), or None without one."""
+    if not path or not os.path.exists(path):
         return None
-    for fn in sorted(os.listdir(d)):
-        if not fn.endswith((".md", ".txt")):
+    import csv
+    per = {}
+    with open(path) as f:
+        rows = [r for r in csv.reader(ln for ln in f if not ln.startswith("=="))]
+    if not rows:
+        return None
+    h = rows[0]
+    try:
+        iid, ik, im, iv = (h.index("ID"), h.index("Kernel Name"), h.index("Metric Name"),
+                           h.index("Metric Value"))
+    except ValueError:
+        return None
+    for r in rows[1:]:
+        if len(r) <= iv or "tc_gemm_kernel" not in r[ik]:
             continue
-        for ln in open(os.path.join(d, fn)):
-            if ln.strip().startswith("traffic_bytes_per_launch:"):
-                try:
-                    return float(ln.split(":", 1)[1].split()[0])
-                except ValueError:
-                    return None
-    return None
+        if r[im] in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
+            unit = r[h.index("Metric Unit")] if "Metric Unit" in h else "byte"
+            scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}.get(unit, 1)
+            per[r[iid]] = per.get(r[iid], 0.0) + float(r[iv].replace(",", "")) * scale
+    return sum(per.values()) / len(per) if per else None
 
 
 # ------------------------------------------------------------- CPU legs
 
-def cpu_minibatch_sample(w, seed=0):
-    """Oracle (C restatement of zealot-rl) timing of one minibatch step on
-    all host cores.  Returns (seconds per minibatch step, threads, rows)."""
+def cpu_model():
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_rollout(w, seed=0, n_envs=None):
+    """A synthetic rollout with the workload's shapes and value
+    distributions for the CPU legs (the oracle port of zealot-rl's CPU
+    update): obs / critic obs ~ N(0,1), actions around a zero mean with
+    log_std 0, rewards ~ N(0, 0.1^2), dones ~ Bernoulli(0.005), values ~ N(0,1)."""
     import oracle as O
     from zealot_b200 import synth
-
-    mb = w.n // w.minibatches
-    # a bounded sample: the minibatch rows, drawn as a full rollout would be
-    n_envs = max(1, (mb + w.T - 1) // w.T)
+    n_envs = n_envs or w.n_envs
     rng = np.random.default_rng(seed)
     params = synth.xavier_params(rng, w.actor_dims, w.critic_dims)
     n = n_envs * w.T
     od, cd, A = w.actor_dims[0], w.critic_dims[0], w.actor_dims[-1]
+    action = rng.standard_normal((n, A), dtype=np.float32)
     b = O.SoaBatch(obs=rng.standard_normal((n, od), dtype=np.float32),
                    critic_obs=rng.standard_normal((n, cd), dtype=np.float32),
-                   action=rng.standard_normal((n, A), dtype=np.float32) * 0.1,
-                   mean_old=np.zeros((n, A), np.float32),
-                   logp_old=np.full(n, -26.0, np.float32),
-                   value_old=np.zeros(n, np.float32),
-                   adv=rng.standard_normal(n, dtype=np.float32),
-                   ret=rng.standard_normal(n, dtype=np.float32) * 0.1)
+                   action=action, mean_old=np.zeros((n, A), np.float32),
+                   logp_old=synth.logp_rows(action, np.zeros((n, A), np.float32),
+                                            np.zeros(A, np.float32)),
+                   value_old=rng.standard_normal(n, dtype=np.float32),
+                   adv=np.zeros(n, np.float32), ret=np.zeros(n, np.float32))
+    rew = (0.1 * rng.standard_normal((n_envs, w.T))).astype(np.float32)
+    dones = (rng.random((n_envs, w.T)) < 0.005).astype(np.uint8)
+    lv = rng.standard_normal(n_envs).astype(np.float32)
+    return params, b, rew, dones, lv
+
+
+def cpu_update(w, params, b, rew, dones, lv, epochs, threads):
+    """GAE + ActorCritic::update (the oracle port, ppo.rs:338-510) over the
+    rollout: `epochs` epochs of w.minibatches minibatch steps.  Seconds."""
+    import oracle as O
+    n_envs = rew.shape[0]
     ac = O.ActorCritic(w.actor_dims, w.critic_dims)
     ac.params = params
-    threads = os.cpu_count() or 1
-    idx = np.arange(mb, dtype=np.int64)
-    cfg = O.PpoConfig()
+    ac.lr = w.lr
+    cfg = O.PpoConfig(epochs=epochs, minibatches=w.minibatches)
     t0 = time.perf_counter()
-    g, sums = ac.minibatch_grads(b, idx, cfg, n_threads=threads)
-    ac.apply(cfg, g, float(sums[2]))
-    dt = time.perf_counter() - t0
-    return dt, threads, mb
+    adv, ret = O.gae_batch(rew, b.value_old.reshape(n_envs, w.T), dones, lv, 0.99, 0.95)
+    b.adv[:] = adv.reshape(-1)
+    b.ret[:] = ret.reshape(-1)
+    ac.update(b, cfg, n_threads=threads)
+    return time.perf_counter() - t0
 
 
 def cpu_baseline(w):
-    dt, threads, mb = cpu_minibatch_sample(w)
-    steps = w.epochs * w.minibatches
-    value = w.n / (dt * steps)
+    """The reference's CPU update (oracle port) timed on this host: one whole
+    update of the workload on every core, and one thread on a bounded
+    sample (one minibatch step of an eighth of the rows)."""
+    import oracle as O
+    threads = os.cpu_count() or 1
+    params, b, rew, dones, lv = cpu_rollout(w)
+    dt = cpu_update(w, params, b, rew, dones, lv, w.epochs, threads)
+    value = w.n / dt
+    # one thread: a minibatch step of n/8 rows (the per-sample cost is what
+    # the single thread measures), scaled to the update's sample passes
+    rows = max(1, w.n // w.minibatches // 8)
+    ac = O.ActorCritic(w.actor_dims, w.critic_dims)
+    ac.params = params
+    idx = np.arange(rows, dtype=np.int64)
+    t0 = time.perf_counter()
+    ac.minibatch_grads(b, idx, O.PpoConfig(), n_threads=1)
+    t1 = time.perf_counter() - t0
+    one = w.n / (t1 * (w.n * w.epochs / rows))
     return {"value": value, "unit": "samples/s", "cores": threads, "kind": "port",
-            "sample": f"1 of {steps} minibatch steps ({mb} samples fwd+bwd+clip+Adam) "
-                      f"of {w.name}, {dt:.2f} s, scaled x{steps}; GAE/adv-norm omitted (<1%)"}
+            "cpu_model": cpu_model(),
+            "sample": f"one whole {w.name} update (GAE + {w.epochs} epochs x {w.minibatches} "
+                      f"minibatch steps over {w.n} samples: forward, backward, clip, Adam) "
+                      f"on {threads} threads, {dt:.2f} s",
+            "one_thread": {"value": one, "unit": "samples/s", "cores": 1,
+                           "sample": f"the forward/backward of {rows} rows ({t1:.2f} s), "
+                                     f"scaled to the update's {w.n * w.epochs} sample passes"}}
 
 
 def run_reference(args):
-    """The reference's CPU path (zealot-rl restated in C, the oracle port):
-    each step is a bounded sample of the update (one minibatch step), scaled
-    to the whole update's samples/s."""
+    """The reference's CPU path (zealot-rl's update restated in C, the oracle
+    port) on every host core: each step is one epoch of the update (its
+    minibatch steps over every sample; the epochs of an update do identical
+    work), and samples/s is the update's samples over epochs x that time."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     w, _, precision, scaling = workload(args, 1)
+    threads = os.cpu_count() or 1
+    params, b, rew, dones, lv = cpu_rollout(w)
     vals = []
     for i in range(args.warmup + args.steps):
-        dt, threads, mb = cpu_minibatch_sample(w, seed=i)
+        dt = cpu_update(w, params, b, rew, dones, lv, 1, threads)
         if i >= args.warmup:
             vals.append(dt)
     dt = statistics.median(vals)
-    steps = w.epochs * w.minibatches
-    value = w.n / (dt * steps)
+    value = w.n / (dt * w.epochs)
     line = {"metric": METRIC, "value": value, "unit": "samples/s", "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": dt * steps * 1e3, "higher_is_better": True, "scaling": scaling,
+            "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": w.name, "n_envs": w.n_envs, "T": w.T,
-                       "epochs": w.epochs, "minibatches": w.minibatches,
-                       "actor": list(w.actor_dims), "critic": list(w.critic_dims)},
+            "config": {"workload": w.name, "n_envs_per_gpu": w.n_envs, "n_envs_total": w.n_envs,
+                       "T": w.T, "samples_per_update": w.n, "epochs": w.epochs,
+                       "minibatches": w.minibatches,
+                       "minibatch_size": w.n // w.minibatches,
+                       "actor": list(w.actor_dims), "critic": list(w.critic_dims),
+                       "parallelism": "cpu"},
             "cpu_baseline": {"value": value, "unit": "samples/s", "cores": threads,
-                             "kind": "port",
-                             "sample": f"per step 1 of {steps} minibatch steps "
-                                       f"({mb} samples), scaled x{steps}"},
+                             "kind": "port", "cpu_model": cpu_model(),
+                             "sample": f"per step one epoch of the {w.name} update (GAE + "
+                                       f"{w.minibatches} minibatch steps over all {w.n} "
+                                       f"samples), {dt:.2f} s median; update = "
+                                       f"{w.epochs} epochs"},
             "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -497,6 +557,14 @@ def main():
     import ctypes as C
     g_ms, u_ms, g_n = C.c_float(), C.c_float(), C.c_int64()
     N.lib().zrl_get_profile(ac.ctx.h, C.byref(g_ms), C.byref(u_ms), C.byref(g_n))
+    breakdown = {}
+    i = 0
+    while True:
+        nm, t, k = C.c_char_p(), C.c_float(), C.c_int64()
+        if not N.lib().zrl_profile_site(ac.ctx.h, i, C.byref(nm), C.byref(t), C.byref(k)):
+            break
+        breakdown[nm.value.decode()] = {"ms": round(t.value, 4), "launches": int(k.value)}
+        i += 1
     N.lib().zrl_set_profiling(ac.ctx.h, 0)
 
     if world > 1:
@@ -513,35 +581,65 @@ def main():
     peaks = measured_peaks()
     fl = flops_per_sample_pass(w.actor_dims, w.critic_dims) * n_local * w.epochs
     if precision == "bf16":
-        peak, peak_src = peaks.get("bf16_tflops", 1590.0), "MEASURED_PEAKS bf16_tflops (burst)"
+        peak, peak_src = peaks.get("bf16_tflops", 1590.0), (
+            "MEASURED_PEAKS bf16_tflops (burst)" if "bf16_tflops" in peaks else "fallback 1.59 PF")
     elif precision == "tf32":
         peak, peak_src = tf32_peak(torch, dev), "cuBLAS tf32 8192^3 measured in this run (burst)"
     else:
         peak, peak_src = 75.0, "nominal fp32 CUDA-core peak (no measured figure)"
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    hbm_src = "MEASURED_PEAKS.json hbm_gbs (copy)" if "hbm_gbs" in peaks else "fallback 6.65 TB/s"
+    # The MLP GEMMs are the update's one dense contraction: tensor-core
+    # bound by the workload's own arithmetic (algorithmic FLOPs: forward,
+    # weight and input gradients of both nets).  achieved = FLOPs of one
+    # launch on average / its average duration (CUDA events around every
+    # GEMM launch in a profiled update) = FLOPs of the update's GEMMs / their
+    # summed time.
     achieved = fl / (g_ms.value * 1e-3) / 1e12 if g_ms.value > 0 else None
-    # The MLP GEMMs are skinny (K, N <= 512 against M = 24,576 rows): at
-    # ~50 FLOP per byte they sit left of the ridge (measured tf32 peak /
-    # measured HBM bandwidth, ~115), so the binding roof is HBM.
+    # the layer-by-layer design's own bytes: every activation and delta row
+    # once per GEMM that reads or writes it (what the GEMMs cannot avoid
+    # moving as designed); weights (L2-resident) and split-K partials left out
     by = bytes_per_sample_pass(w.actor_dims, w.critic_dims,
                                2 if precision == "bf16" else 4) * n_local * w.epochs
-    hbm = peaks.get("hbm_gbs", 6650.0)
     ach_gbs = by / (g_ms.value * 1e-3) / 1e9 if g_ms.value > 0 else None
-    roof = {"bound": "hbm", "kernel": "mlp gemm (all GEMM launches of one update)",
-            "achieved": ach_gbs, "peak": hbm, "unit": "GB/s",
-            "frac": (ach_gbs / hbm) if ach_gbs else None,
-            "traffic": profile_traffic(),
-            "peak_source": "MEASURED_PEAKS.json hbm_gbs (copy)" if "hbm_gbs" in peaks
-                           else "fallback 6.65 TB/s",
-            "algorithmic_bytes_per_launch": by / g_n.value if g_n.value else None,
-            "algorithmic_gb_per_update": by / 1e9,
-            "intensity_flop_per_byte": fl / by,
-            "ridge_flop_per_byte": peak * 1e12 / (hbm * 1e9),
-            "tensor_view": {"achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                            "frac": (achieved / peak) if achieved else None,
-                            "peak_source": peak_src},
+    # the whole update against its floor: algorithmic GEMM FLOPs at the
+    # tensor peak plus the update's algorithmic HBM bytes at the copy
+    # bandwidth (per sample pass: obs, critic obs, action, mean_old and four
+    # scalars of the epoch's minibatch, 1016 B; per parameter and minibatch
+    # step: 28 B of Adam and 12 B of weight/gradient traffic; GAE and the
+    # advantage moments), all on n_local samples of this rank
+    A = w.actor_dims[-1]
+    row_bytes = 4 * (w.actor_dims[0] + w.critic_dims[0] + 2 * A + 4)
+    n_par = sum(d[l] * d[l + 1] + d[l + 1] for d in (w.actor_dims, w.critic_dims)
+                for l in range(len(d) - 1)) + A
+    steps = w.epochs * w.minibatches
+    upd_bytes = row_bytes * n_local * w.epochs + 40 * n_par * steps + 17 * n_local + \
+        12 * n_local
+    floor_ms = (fl / (peak * 1e12) + upd_bytes / (hbm * 1e9)) * 1e3
+    gn = max(int(g_n.value), 1)
+    roof = {"bound": "tensor", "kernel": "tc_gemm_kernel (every MLP GEMM launch of one update)",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": (achieved / peak) if achieved else None,
+            "traffic": ncu_traffic(args.traffic_csv),
+            "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum per GEMM "
+                               f"launch, {args.traffic_csv}") if args.traffic_csv else
+                              "null: no ncu capture passed (--traffic-csv)",
+            "peak_source": peak_src + "; MEASURED_PEAKS has no tf32 figure" if precision == "tf32"
+                           else peak_src,
+            "algorithmic_flop_per_launch": fl / gn,
+            "algorithmic_gflop_per_update": fl / 1e9,
             "gemm_ms_per_update": g_ms.value, "gemm_launches_per_update": g_n.value,
+            "avg_launch_us": 1e3 * g_ms.value / gn,
             "gemm_share_of_update": g_ms.value / u_ms.value if u_ms.value else None,
-            "algorithmic_gflop_per_update": fl / 1e9}
+            "profiled_update_ms": u_ms.value, "breakdown_ms_per_update": breakdown,
+            "hbm_view": {"achieved": ach_gbs, "peak": hbm, "unit": "GB/s",
+                         "frac": (ach_gbs / hbm) if ach_gbs else None, "peak_source": hbm_src,
+                         "bytes": "every activation/delta row once per GEMM that uses it",
+                         "gb_per_update": by / 1e9},
+            "update_floor": {"floor_ms": floor_ms, "measured_ms": ms,
+                             "frac": floor_ms / ms,
+                             "algorithmic_gb_per_update": upd_bytes / 1e9,
+                             "how": "GEMM FLOPs / tensor peak + update bytes / HBM copy bandwidth"}}
     cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline(w)
     line = {"metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,

@@ -310,6 +310,15 @@ int64_t zrl_kernel_launches(const zrl_ctx *ctx);
 zrl_status zrl_set_profiling(zrl_ctx *ctx, int32_t enabled);
 zrl_status zrl_get_profile(zrl_ctx *ctx, float *gemm_ms, float *update_ms,
                            int64_t *gemm_launches);
+/* Per launch site of the last profiled update (forward layer, input-
+ * gradient level, weight-gradient group, loss, segment reduce, Adam,
+ * gather, ...): entry i's name, summed device time (ms) and number of
+ * bracketed launches.  Returns 0 past the last entry.  Instrumentation with
+ * no counterpart in the reference; the events that bracket each site keep
+ * consecutive kernels from overlapping, so the sum exceeds an unprofiled
+ * update's time slightly. */
+int32_t zrl_profile_site(const zrl_ctx *ctx, int32_t i, const char **name, float *ms,
+                         int64_t *spans);
 
 #ifdef __cplusplus
 }

@@ -199,6 +199,15 @@ struct zrl_ctx {
   size_t ev_used = 0;
   float prof_gemm_ms = 0.0f, prof_update_ms = 0.0f;
   int64_t prof_gemm_launches = 0;
+  // profiling: (site, start event, stop event, is a GEMM) per launch site
+  // of the last update, and their per-site sums
+  struct Span {
+    const char *site;
+    cudaEvent_t e0, e1;
+    bool gemm;
+  };
+  std::vector<Span> spans;
+  std::vector<std::pair<std::string, std::pair<float, int64_t>>> sites;
 
   Comm comm;
   GemmEngine gemm;
@@ -464,23 +473,38 @@ static cudaEvent_t next_event(zrl_ctx *ctx) {
   return ctx->ev_pool[ctx->ev_used++];
 }
 
-// ------------------------------------------------------------------ GEMM
-
-static zrl_status run_gemm(zrl_ctx *ctx, const GemmArgs &g) {
-  cudaEvent_t e0 = nullptr, e1 = nullptr;
-  if (ctx->profiling) {
+// Profiling (zrl_set_profiling): events on the stream around one launch
+// site.  They separate the kernels they bracket (programmatic dependent
+// launch cannot overlap across an event), so the profiled update runs a
+// little slower than an unprofiled one; the per-site times say where the
+// time goes.
+struct ProfSpan {
+  zrl_ctx *ctx;
+  const char *site;
+  cudaEvent_t e0 = nullptr;
+  bool gemm;
+  ProfSpan(zrl_ctx *c, const char *s, bool is_gemm = false) : ctx(c), site(s), gemm(is_gemm) {
+    if (!ctx->profiling) return;
     e0 = next_event(ctx);
     cudaEventRecord(e0, ctx->stream);
   }
+  ~ProfSpan() {
+    if (!ctx->profiling || !e0) return;
+    cudaEvent_t e1 = next_event(ctx);
+    cudaEventRecord(e1, ctx->stream);
+    ctx->spans.push_back(zrl_ctx::Span{site, e0, e1, gemm});
+  }
+};
+
+// ------------------------------------------------------------------ GEMM
+
+static zrl_status run_gemm(zrl_ctx *ctx, const GemmArgs &g, const char *site = "gemm") {
+  ProfSpan ps(ctx, site, true);
   int launched = 0;
   zrl_status s = ctx->gemm.run(g, ctx->precision, ctx->stream, &launched, &ctx->err);
   if (s != ZRL_OK) return s;
   ctx->launches += launched;
-  if (ctx->profiling) {
-    e1 = next_event(ctx);
-    cudaEventRecord(e1, ctx->stream);
-    ctx->prof_gemm_launches += launched;
-  }
+  if (ctx->profiling) ctx->prof_gemm_launches += launched;
   CHECK_LAUNCH();
   return ZRL_OK;
 }
@@ -508,22 +532,15 @@ static GemmArgs fwd_args(zrl_ctx *ctx, int k, int l, const float *in, int64_t ro
   return g;
 }
 
-static zrl_status run_group(zrl_ctx *ctx, const GemmArgs *gs, int n) {
+static zrl_status run_group(zrl_ctx *ctx, const GemmArgs *gs, int n,
+                            const char *site = "gemm") {
   if (n <= 0) return ZRL_OK;
-  cudaEvent_t e0 = nullptr, e1 = nullptr;
-  if (ctx->profiling) {
-    e0 = next_event(ctx);
-    cudaEventRecord(e0, ctx->stream);
-  }
+  ProfSpan ps(ctx, site, true);
   int launched = 0;
   zrl_status s = ctx->gemm.run_group(gs, n, ctx->precision, ctx->stream, &launched, &ctx->err);
   if (s != ZRL_OK) return s;
   ctx->launches += launched;
-  if (ctx->profiling) {
-    e1 = next_event(ctx);
-    cudaEventRecord(e1, ctx->stream);
-    ctx->prof_gemm_launches += launched;
-  }
+  if (ctx->profiling) ctx->prof_gemm_launches += launched;
   CHECK_LAUNCH();
   return ZRL_OK;
 }
@@ -544,11 +561,15 @@ static zrl_status forward_both(zrl_ctx *ctx, const float *xa, const float *xc, i
       g[n] = fwd_args(ctx, k, l, in, rows);
       g[n++].reverse_tiles = l & 1;
     }
+    static const char *kFwd[ZRL_MAX_LAYERS] = {"gemm fwd L0", "gemm fwd L1", "gemm fwd L2",
+                                                "gemm fwd L3", "gemm fwd L4", "gemm fwd L5",
+                                                "gemm fwd L6", "gemm fwd L7"};
+    const char *site = kFwd[std::min(l, ZRL_MAX_LAYERS - 1)];
     if (n == 2 && g[0].epi != g[1].epi) {
-      TRY(run_group(ctx, &g[0], 1));
-      TRY(run_group(ctx, &g[1], 1));
+      TRY(run_group(ctx, &g[0], 1, site));
+      TRY(run_group(ctx, &g[1], 1, site));
     } else {
-      TRY(run_group(ctx, g, n));
+      TRY(run_group(ctx, g, n, site));
     }
   }
   return ZRL_OK;
@@ -631,10 +652,10 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
   // successive launches alternate their tile order, starting opposite to
   // the forward's last layer (last to first when its index is odd)
   bool rev = !((maxL - 1) & 1);
-  auto run_w = [&](GemmArgs *w, int nw) -> zrl_status {
+  auto run_w = [&](GemmArgs *w, int nw, const char *site) -> zrl_status {
     for (int i = 0; i < nw; i += 8) {
       for (int j = i; j < std::min(nw, i + 8); ++j) w[j].reverse_tiles = rev;
-      TRY(run_group(ctx, w + i, std::min(8, nw - i)));
+      TRY(run_group(ctx, w + i, std::min(8, nw - i), site));
     }
     rev = !rev;
     return ZRL_OK;
@@ -675,10 +696,14 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
         *bp += (int64_t)4 * m_tiles * L.dp[l];
       }
     }
-    TRY(run_group(ctx, d, n));
+    static const char *kDgrad[ZRL_MAX_LAYERS] = {"gemm dgrad L0", "gemm dgrad L1",
+                                                  "gemm dgrad L2", "gemm dgrad L3",
+                                                  "gemm dgrad L4", "gemm dgrad L5",
+                                                  "gemm dgrad L6", "gemm dgrad L7"};
+    TRY(run_group(ctx, d, n, kDgrad[std::min(l, ZRL_MAX_LAYERS - 1)]));
     rev = !rev;
-    if (nf && flat_lvl == l) TRY(run_w(flat, nf));
-    if (nt && tall_lvl == l) TRY(run_w(tall, nt));
+    if (nf && flat_lvl == l) TRY(run_w(flat, nf, "gemm wgrad flat"));
+    if (nt && tall_lvl == l) TRY(run_w(tall, nt, "gemm wgrad tall"));
   }
   if (!ctx->tcore()) {
     // db_l = column sums of delta_l for the hidden layers (CUDA-core mode)
@@ -696,8 +721,8 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
   }
   // single-layer nets: no dgrad chain, the weight gradients run here
   if (maxL == 1) {
-    if (nt) TRY(run_w(tall, nt));
-    if (nf) TRY(run_w(flat, nf));
+    if (nt) TRY(run_w(tall, nt, "gemm wgrad tall"));
+    if (nf) TRY(run_w(flat, nf, "gemm wgrad flat"));
   }
   return ZRL_OK;
 }
@@ -748,9 +773,12 @@ static zrl_status minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
   }
   const int lb = loss_blocks(la);
   if (la.width > ctx->rs.fwidth || lb > ctx->rs.max_blocks) return bad(ctx, "loss scratch too small");
-  launch_loss(la, ctx->stream);
-  ctx->launches++;
-  CHECK_LAUNCH();
+  {
+    ProfSpan ps(ctx, "loss");
+    launch_loss(la, ctx->stream);
+    ctx->launches++;
+    CHECK_LAUNCH();
+  }
   float *wp = ctx->wpart, *bp = ctx->bpart;
   ReduceSegs segs{};
   {
@@ -764,6 +792,7 @@ static zrl_status minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
     segs.seg[segs.n++] = ReduceSeg{ctx->G + Lc.b_off[Lc.L - 1], fp + 2 * la.Ap + 4, (int64_t)la.cp, lb, w};
   }
   TRY(backward_both(ctx, v.xa, v.xc, v.rows, &wp, &bp, segs));
+  ProfSpan ps(ctx, "segment reduce (+pre-step)");
   const int f = launch_reduce_segments(segs, ctx->stream, fuse, &ctx->rs);
   if (fused) *fused = f != 0;
   ctx->launches++;
@@ -773,6 +802,7 @@ static zrl_status minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
 
 static zrl_status allreduce_grads(zrl_ctx *ctx) {
   if (ctx->comm.world <= 1) return ZRL_OK;
+  ProfSpan ps(ctx, "allreduce");
   return ctx->comm.allreduce_f32(ctx->G, ctx->grad_len, ctx->stream, &ctx->err);
 }
 
@@ -805,6 +835,7 @@ static zrl_status step(zrl_ctx *ctx, const zrl_ppo_config *cfg, int minibatches,
                        bool last_of_epoch, bool count_stats, bool prestep_done = false) {
   const PrestepArgs p = prestep_args(ctx, cfg, minibatches, last_of_epoch, count_stats);
   if (!prestep_done) {
+    ProfSpan ps(ctx, "pre-step");
     launch_prestep(p, ctx->rs, ctx->stream);
     ctx->launches++;
     CHECK_LAUNCH();
@@ -820,6 +851,7 @@ static zrl_status step(zrl_ctx *ctx, const zrl_ppo_config *cfg, int minibatches,
   a.st = ctx->st;
   a.p_round = ctx->tcore() ? ctx->Ptc : nullptr;
   a.p_mode = ctx->opmode();
+  ProfSpan ps(ctx, "adam");
   launch_adam(a, ctx->stream);
   ctx->launches++;
   CHECK_LAUNCH();
@@ -830,6 +862,7 @@ static zrl_status step(zrl_ctx *ctx, const zrl_ppo_config *cfg, int minibatches,
 static zrl_status adv_moments(zrl_ctx *ctx, const float *adv, int64_t n,
                               int64_t n_global, bool partials_ready,
                               int partial_blocks) {
+  ProfSpan ps(ctx, "advantage moments");
   int nb = partial_blocks;
   if (!partials_ready) {
     nb = adv_blocks(n);
@@ -872,6 +905,7 @@ static zrl_status adv_moments(zrl_ctx *ctx, const float *adv, int64_t n,
 static zrl_status normalize_batch(zrl_ctx *ctx, const float *obs, const float *cobs,
                                   int64_t n) {
   if (n <= 0) return ZRL_OK;
+  ProfSpan ps(ctx, "normalize");
   launch_normalize_rows(obs, n, ctx->net[0].d[0], ctx->net[0].dp[0], ctx->obs_mean,
                         ctx->obs_sd, ctx->n_xa, ctx->opmode(), ctx->stream);
   launch_normalize_rows(cobs, n, ctx->net[1].d[0], ctx->net[1].dp[0], ctx->crit_mean,
@@ -1104,6 +1138,7 @@ static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
       }
       g.n_used = n_rows;
       g.apply_adv_norm = 1;
+      ProfSpan ps(ctx, "gather");
       launch_gather(g, ctx->stream);
       ctx->launches++;
       CHECK_LAUNCH();
@@ -1182,6 +1217,7 @@ static void prof_begin(zrl_ctx *ctx, cudaEvent_t *u0) {
   if (!ctx->profiling) return;
   ctx->ev_used = 0;
   ctx->prof_gemm_launches = 0;
+  ctx->spans.clear();
   *u0 = next_event(ctx);
   cudaEventRecord(*u0, ctx->stream);
 }
@@ -1200,11 +1236,20 @@ static zrl_status prof_end(zrl_ctx *ctx, cudaEvent_t u0) {
   cudaEventElapsedTime(&ms, u0, u1);
   ctx->prof_update_ms = ms;
   float g = 0.0f;
-  // events after u0 come in (start, stop) pairs per GEMM, u1 last
-  for (size_t i = 1; i + 1 < ctx->ev_used; i += 2) {
+  ctx->sites.clear();
+  for (const auto &sp : ctx->spans) {
     float t = 0.0f;
-    cudaEventElapsedTime(&t, ctx->ev_pool[i], ctx->ev_pool[i + 1]);
-    g += t;
+    cudaEventElapsedTime(&t, sp.e0, sp.e1);
+    if (sp.gemm) g += t;
+    bool found = false;
+    for (auto &kv : ctx->sites)
+      if (kv.first == sp.site) {
+        kv.second.first += t;
+        kv.second.second += 1;
+        found = true;
+        break;
+      }
+    if (!found) ctx->sites.push_back({std::string(sp.site), {t, 1}});
   }
   ctx->prof_gemm_ms = g;
   return ZRL_OK;
@@ -1852,6 +1897,15 @@ zrl_status zrl_set_profiling(zrl_ctx *ctx, int32_t enabled) {
   if (!ctx) return ZRL_INVALID_ARG;
   ctx->profiling = enabled != 0;
   return ZRL_OK;
+}
+
+int32_t zrl_profile_site(const zrl_ctx *ctx, int32_t i, const char **name, float *ms,
+                         int64_t *spans) {
+  if (!ctx || i < 0 || i >= (int32_t)ctx->sites.size()) return 0;
+  if (name) *name = ctx->sites[i].first.c_str();
+  if (ms) *ms = ctx->sites[i].second.first;
+  if (spans) *spans = ctx->sites[i].second.second;
+  return 1;
 }
 
 zrl_status zrl_get_profile(zrl_ctx *ctx, float *gemm_ms, float *update_ms,

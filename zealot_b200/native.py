@@ -123,6 +123,8 @@ _SIGS = {
     "zrl_set_profiling": (C.c_int, [_P, C.c_int32]),
     "zrl_get_profile": (C.c_int, [_P, C.POINTER(C.c_float), C.POINTER(C.c_float),
                                   C.POINTER(C.c_int64)]),
+    "zrl_profile_site": (C.c_int32, [_P, C.c_int32, C.POINTER(C.c_char_p),
+                                     C.POINTER(C.c_float), C.POINTER(C.c_int64)]),
 }
 
 _lib = None
