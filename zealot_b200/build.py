@@ -43,7 +43,8 @@ def _sources():
 
 def _fingerprint() -> str:
     h = hashlib.sha256()
-    for f in _sources() + sorted(glob.glob(os.path.join(CSRC, "*.h"))) + \
+    for f in _sources() + sorted(glob.glob(os.path.join(CSRC, "*.h")) +
+                                 glob.glob(os.path.join(CSRC, "*.cuh"))) + \
             [os.path.join(ROOT, "include", "zealot_rl.h"), __file__]:
         with open(f, "rb") as fh:
             h.update(f.encode())

@@ -450,7 +450,9 @@ static zrl_status ensure_mb(zrl_ctx *ctx, int64_t mb) {
       wp += (int64_t)S * L.dp[l + 1] * L.dp[l];
       // bias-gradient partials: S row chunks (CUDA-core colsum) or one row
       // per 32-row quarter of each 128-row block (tensor-core dgrad epilogue)
-      bp += (int64_t)std::max<int64_t>(S, 4 * ((mb + 127) / 128)) * L.dp[l + 1];
+      // (or, for the fused head's level, one row per epilogue warp of each
+      // CTA: at most 8 per 128-row block)
+      bp += (int64_t)std::max<int64_t>(S, 8 * ((mb + 127) / 128)) * L.dp[l + 1];
     }
   }
   TRY(dalloc(ctx, &ctx->wpart, wp));
@@ -550,9 +552,11 @@ static zrl_status run_group(zrl_ctx *ctx, const GemmArgs *gs, int n,
 // they share the epilogue.  Odd layers walk their tiles last to first, so
 // each layer first reads the rows the layer before wrote last (still in
 // L2).
-static zrl_status forward_both(zrl_ctx *ctx, const float *xa, const float *xc, int64_t rows) {
+static zrl_status forward_both(zrl_ctx *ctx, const float *xa, const float *xc, int64_t rows,
+                               int layers = -1) {
   const int maxL = std::max(ctx->net[0].L, ctx->net[1].L);
-  for (int l = 0; l < maxL; ++l) {
+  const int lim = layers < 0 ? maxL : std::min(layers, maxL);
+  for (int l = 0; l < lim; ++l) {
     GemmArgs g[2];
     int n = 0;
     for (int k = 0; k < 2; ++k) {
@@ -594,10 +598,13 @@ static zrl_status forward_net(zrl_ctx *ctx, int k, const float *x, int64_t rows)
 // the loss kernel, a hidden layer's in the epilogue of the tensor-core
 // dgrad that produces it (a separate column-sum pass in the CUDA-core
 // mode).
+// top: the highest input-gradient level to run (maxL - 1 by default; the
+// fused head computes that level itself and passes maxL - 2).
 static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, int64_t rows,
-                                float **wp, float **bp, ReduceSegs &segs) {
+                                float **wp, float **bp, ReduceSegs &segs, int top = -1) {
   const int m_tiles = (int)((rows + 127) / 128);
   const int maxL = std::max(ctx->net[0].L, ctx->net[1].L);
+  if (top < 0) top = maxL - 1;
   const int S = wsplit_for(rows);
   // dW_l = delta_l^T a_l for every layer of both nets, split-K partials.
   // Tall ones (dp[l+1] >= 256 rows) go to CTA-pair tiles, the rest to
@@ -660,7 +667,7 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
     rev = !rev;
     return ZRL_OK;
   };
-  for (int l = maxL - 1; l >= 1; --l) {
+  for (int l = top; l >= 1; --l) {
     GemmArgs d[2];
     int n = 0;
     for (int k = 0; k < 2; ++k) {
@@ -732,6 +739,88 @@ struct MbView {
   int64_t rows;
 };
 
+// The fused output head (head_tc.cu) takes the tf32 update whenever both
+// nets have the same depth (at least two layers), 32-wide (padded) output
+// layers fed by hidden layers at most 128 wide, and at most 32 actions --
+// the MLPs of the C1-C4 workloads.  Other shapes keep the separate
+// output-layer forward, loss and input-gradient launches.
+static bool head_applies(const zrl_ctx *ctx) {
+  const NetLayout &La = ctx->net[0], &Lc = ctx->net[1];
+  if (!ctx->tc() || La.L != Lc.L || La.L < 2 || ctx->A > 32) return false;
+  for (int k = 0; k < 2; ++k) {
+    const NetLayout &L = ctx->net[k];
+    if (L.dp[L.L] != 32 || L.dp[L.L - 1] > 128) return false;
+  }
+  return true;
+}
+
+// minibatch_grads with the fused head: forward of the hidden layers, the
+// head (output layers, losses, last hidden layer's delta), then the rest of
+// the backward and the segment reduce.
+static zrl_status minibatch_grads_head(zrl_ctx *ctx, const zrl_ppo_config *cfg,
+                                       const MbView &v, float scale, const PrestepArgs *fuse,
+                                       bool *fused) {
+  const NetLayout &La = ctx->net[0], &Lc = ctx->net[1];
+  const int L = La.L;
+  TRY(forward_both(ctx, v.xa, v.xc, v.rows, L - 1));
+  HeadArgs h{};
+  float *wp = ctx->wpart, *bp = ctx->bpart;
+  const int hr = head_partial_rows(v.rows);
+  if (hr > ctx->rs.max_blocks || kHeadWidth > ctx->rs.fwidth) return bad(ctx, "head scratch too small");
+  ReduceSegs segs{};
+  for (int k = 0; k < 2; ++k) {
+    const NetLayout &N = ctx->net[k];
+    HeadNet &n = h.net[k];
+    n.a = ctx->act[k][L - 1];
+    n.k = N.dp[L - 1];
+    n.w = ctx->Wgemm_at(N.w_off[L - 1]);
+    n.b = ctx->P + N.b_off[L - 1];
+    n.d_out = ctx->dlt[k][L - 1];
+    n.d_in = ctx->dlt[k][L - 2];
+    n.colsum = bp;
+    segs.seg[segs.n++] = ReduceSeg{ctx->G + N.b_off[L - 2], bp, (int64_t)n.k, hr, (int64_t)n.k};
+    bp += (int64_t)hr * n.k;
+  }
+  h.action = v.act;
+  h.mean_old = v.mo;
+  h.logp_old = v.lpo;
+  h.value_old = v.vo;
+  h.adv = v.adv;
+  h.ret = v.ret;
+  h.log_std = ctx->P + ctx->ls_off;
+  h.A = ctx->A;
+  h.rows = v.rows;
+  h.scale = scale;
+  h.clip = cfg->clip;
+  h.entropy_coef = cfg->entropy_coef;
+  h.value_coef = cfg->value_coef;
+  h.part = ctx->rs.fpart;
+  h.err = ctx->gemm.err_dev;
+  {
+    // its partial rows: log_std gradient, output-layer bias gradients of
+    // both nets, statistic sums (the loss kernel's layout, 32-wide)
+    const int64_t w = kHeadWidth;
+    float *fp = ctx->rs.fpart;
+    segs.seg[segs.n++] = ReduceSeg{ctx->G + ctx->ls_off, fp, 32, hr, w};
+    segs.seg[segs.n++] = ReduceSeg{ctx->G + La.b_off[L - 1], fp + 32, 32, hr, w};
+    segs.seg[segs.n++] = ReduceSeg{ctx->sums3, fp + 64, 4, hr, w};
+    segs.seg[segs.n++] = ReduceSeg{ctx->G + Lc.b_off[L - 1], fp + 68, 32, hr, w};
+  }
+  {
+    ProfSpan ps(ctx, "head (fwd out + loss + dgrad out)", true);
+    TRY(ctx->gemm.head(h, ctx->stream, &ctx->err));
+    ctx->launches++;
+    CHECK_LAUNCH();
+  }
+  TRY(backward_both(ctx, v.xa, v.xc, v.rows, &wp, &bp, segs, L - 2));
+  ProfSpan ps(ctx, "segment reduce (+pre-step)");
+  const int f = launch_reduce_segments(segs, ctx->stream, fuse, &ctx->rs);
+  if (fused) *fused = f != 0;
+  ctx->launches++;
+  CHECK_LAUNCH();
+  return ZRL_OK;
+}
+
 // Gradient accumulation of one minibatch (ppo.rs:388-462): leaves the
 // summed gradient in G (padded layout, log_std included) and the three
 // statistic sums in sums3.
@@ -740,8 +829,9 @@ static zrl_status minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
                                   const PrestepArgs *fuse = nullptr, bool *fused = nullptr) {
   if (fused) *fused = false;
   TRY(ensure_mb(ctx, std::max<int64_t>(v.rows, 1)));
-  if (v.rows > 0) TRY(forward_both(ctx, v.xa, v.xc, v.rows));
   const NetLayout &La = ctx->net[0], &Lc = ctx->net[1];
+  if (v.rows > 0 && head_applies(ctx)) return minibatch_grads_head(ctx, cfg, v, scale, fuse, fused);
+  if (v.rows > 0) TRY(forward_both(ctx, v.xa, v.xc, v.rows));
   LossArgs la{};
   la.mean = ctx->act[0][La.L];
   la.value = ctx->act[1][Lc.L];

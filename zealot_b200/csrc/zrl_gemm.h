@@ -6,6 +6,8 @@
 // not a fallback.
 #pragma once
 
+#include <cuda.h>
+
 #include <string>
 
 #include "zrl_internal.h"
@@ -13,6 +15,50 @@
 namespace zrl {
 
 struct GemmEngine;
+
+// A TMA tensor map from the engine's cache (gemm_tc.cu): kind 0 a K-major
+// fp32 operand [rows, cols] (pitch ld) in boxes of 32 columns x box rows,
+// 128-byte swizzle; kind 1 the MN-major form (32-byte-atom swizzle); kind 2
+// an fp32 output [splits][rows][cols] written in 32 x 32 boxes.
+bool tc_tensor_map(GemmEngine *eng, CUtensorMap *out, const float *base, int64_t rows,
+                   int64_t cols, int64_t ld, int box_or_splits, int kind, std::string *err);
+// SMs of the device the tensor-core kernels were initialised on.
+int tc_sm_count();
+
+// The fused output head (head_tc.cu) of both nets over one minibatch: the
+// output layer's forward Z = A W^T + b on the tensor cores, the PPO losses
+// of each row (ppo.rs:410-452) giving the output-layer delta D (the loss
+// kernel's math), and the last hidden layer's input gradient
+// D' = (D W) * ELU'(A) on the tensor cores with its bias-gradient column
+// sums -- one launch in place of the output-layer forward, the loss and the
+// output-layer input-gradient launches.  tf32 operands; both nets' output
+// layers 32 wide (padded), their inputs 32..128 wide.
+struct HeadNet {
+  const float *a;   // [rows, k] the last hidden activation (tf32-rounded)
+  int k;            // its padded width (32..128, a multiple of 32)
+  const float *w;   // output-layer weights [32, k] (tf32 copy)
+  const float *b;   // output-layer bias [32] (fp32 master)
+  float *d_out;     // out: the output-layer delta [rows, 32] (tf32-rounded)
+  float *d_in;      // out: the last hidden layer's delta [rows, k] (tf32-rounded)
+  float *colsum;    // out: [head_partial_rows, k] partial column sums of d_in (fp32)
+};
+struct HeadArgs {
+  HeadNet net[2];  // actor, critic
+  const float *action, *mean_old;                 // [rows, A]
+  const float *logp_old, *value_old, *adv, *ret;  // [rows]
+  const float *log_std;                           // [A]
+  int A;
+  int64_t rows;
+  float scale, clip, entropy_coef, value_coef;
+  // [head_partial_rows, 100]: [g_logstd (32) | db_actor (32) | surr vloss kl 0 |
+  // db_critic (32)], the layout of the loss kernel's rows (LossArgs)
+  float *part;
+  int *err;
+};
+constexpr int kHeadWidth = 2 * 32 + 4 + 32;
+// Partial rows the head writes for `rows` rows (four per CTA).
+int head_partial_rows(int64_t rows);
+zrl_status head_tc(GemmEngine *eng, const HeadArgs &a, cudaStream_t s, std::string *err);
 
 // Tensor-core GEMM (gemm_tc.cu).  *launched receives the kernel count.
 zrl_status gemm_tc(GemmEngine *eng, const GemmArgs &g, int precision, cudaStream_t s,
@@ -60,6 +106,16 @@ struct GemmEngine {
       tc_ready = true;
     }
     return gemm_tc_split(this, gs, n, precision, max_split);
+  }
+
+  // The fused output head (tensor cores only).
+  zrl_status head(const HeadArgs &a, cudaStream_t s, std::string *err) {
+    if (!tc_ready) {
+      zrl_status st = gemm_tc_init(0, err);
+      if (st != ZRL_OK) return st;
+      tc_ready = true;
+    }
+    return head_tc(this, a, s, err);
   }
 
   // Several GEMMs of one layout and epilogue: one grouped launch on the
