@@ -165,6 +165,26 @@ zrl_status zrl_get_normalizers(zrl_ctx *ctx, float *obs_mean, float *obs_m2,
  * record_obs, ppo.rs:276-279), rows folded in order. */
 zrl_status zrl_record_obs(zrl_ctx *ctx, const float *obs,
                           const float *critic_obs, int64_t n);
+/* zrl_record_obs with device rows (on_device = 1) and a choice of fold:
+ * mode 0 folds the rows in order (bit-identical to the reference), mode 1
+ * folds chunks of 256 rows in parallel and merges them pairwise with
+ * Normalizer::commit's formula (ppo.rs:185-191): the same statistics up to
+ * f32 rounding, for large row counts. */
+zrl_status zrl_record_obs_ex(zrl_ctx *ctx, const float *obs, const float *critic_obs,
+                             int64_t n, int32_t on_device, int32_t mode);
+/* PendingNorm::push (ppo.rs:126-136) of n rows into the context's pending
+ * statistics of each normalizer (the trainer's pn_obs / pn_cobs pair,
+ * biped_train_gpu.rs:800-801, 904-905); modes as zrl_record_obs_ex. */
+zrl_status zrl_pending_push(zrl_ctx *ctx, const float *obs, const float *critic_obs,
+                            int64_t n, int32_t on_device, int32_t mode);
+/* Normalizer::commit (ppo.rs:179-195) of both pending states into the live
+ * normalizers (biped_train_gpu.rs:1050-1051), which resets them; an empty
+ * pending state leaves its normalizer as it is. */
+zrl_status zrl_commit_pending(zrl_ctx *ctx);
+/* The pending statistics (counts on the host). */
+zrl_status zrl_get_pending(zrl_ctx *ctx, float *obs_mean, float *obs_m2,
+                           float *obs_count, float *crit_mean, float *crit_m2,
+                           float *crit_count);
 /* ActorCritic::lr (ppo.rs:228). */
 zrl_status zrl_set_lr(zrl_ctx *ctx, float lr);
 zrl_status zrl_get_lr(zrl_ctx *ctx, float *lr);

@@ -98,6 +98,8 @@ def lib():
                                          C.c_int64, _f32p]
         L.orc_norm_update.argtypes = [_f32p, _f32p, C.POINTER(C.c_float),
                                       _f32p, C.c_int64]
+        L.orc_norm_commit.argtypes = [_f32p, _f32p, C.POINTER(C.c_float), _f32p, _f32p,
+                                      C.POINTER(C.c_float), C.c_int64]
         L.orc_ac_new.restype = C.c_void_p
         L.orc_ac_new.argtypes = [_i32p, C.c_int32, _i32p, C.c_int32]
         L.orc_ac_free.argtypes = [C.c_void_p]

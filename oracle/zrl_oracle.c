@@ -346,6 +346,28 @@ void orc_norm_update(float *mean, float *m2, float *count, const float *x,
   }
 }
 
+/* ppo.rs:126-136: PendingNorm::push is the same recurrence as
+ * Normalizer::update (orc_norm_update) on a state that starts at count 0,
+ * mean 0, m2 0. */
+
+/* ppo.rs:179-195: Normalizer::commit, the Chan et al. parallel-Welford
+ * merge of a pending state into the live one, then the pending state is
+ * reset.  A pending count of 0 leaves both untouched. */
+void orc_norm_commit(float *mean, float *m2, float *count, float *p_mean,
+                     float *p_m2, float *p_count, int64_t dim) {
+  if (*p_count == 0.0f) return;
+  float n1 = *count, n2 = *p_count;
+  float tot = n1 + n2;
+  for (int64_t i = 0; i < dim; ++i) {
+    float d = p_mean[i] - mean[i];
+    mean[i] += d * n2 / tot;
+    m2[i] += p_m2[i] + d * d * n1 * n2 / tot;
+  }
+  *count = tot;
+  *p_count = 0.0f;
+  for (int64_t i = 0; i < dim; ++i) p_mean[i] = p_m2[i] = 0.0f;
+}
+
 /* ------------------------------------------------------- ActorCritic */
 
 struct orc_ac {

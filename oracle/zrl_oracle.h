@@ -83,6 +83,10 @@ void orc_norm_normalize(const float *mean, const float *m2, float count,
                         const float *x, int64_t dim, float *out);
 void orc_norm_update(float *mean, float *m2, float *count, const float *x,
                      int64_t dim);
+/* ppo.rs:179-195 Normalizer::commit of a PendingNorm (ppo.rs:126-136, whose
+ * push is orc_norm_update from count 0): Chan merge, then pending reset. */
+void orc_norm_commit(float *mean, float *m2, float *count, float *p_mean,
+                     float *p_m2, float *p_count, int64_t dim);
 
 /* ---- ppo.rs ActorCritic ---- */
 typedef struct {

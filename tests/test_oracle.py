@@ -369,3 +369,33 @@ def test_tf32_operand_mode_matches_a_python_restatement():
         np.testing.assert_allclose(fwd(adims, params, obs[r]), mt[r], rtol=2e-7, atol=0)
         np.testing.assert_allclose(fwd(cdims, params[npa:], cobs[r]), vt[r:r + 1],
                                    rtol=2e-7, atol=0)
+
+
+def test_norm_commit_matches_python_restatement():
+    """orc_norm_commit against ppo.rs:179-195 restated with numpy float32
+    scalars (every operation rounded to f32, left to right)."""
+    import ctypes as C
+    rng = np.random.default_rng(3)
+    dim = 7
+    mean = rng.standard_normal(dim).astype(np.float32)
+    m2 = (rng.random(dim) * 9 + 1).astype(np.float32)
+    pm = rng.standard_normal(dim).astype(np.float32)
+    pm2 = (rng.random(dim) * 5).astype(np.float32)
+    n1, n2 = np.float32(1234.0), np.float32(77.0)
+    tot = np.float32(n1 + n2)
+    want_m, want_s = mean.copy(), m2.copy()
+    for i in range(dim):
+        d = np.float32(pm[i] - mean[i])
+        want_m[i] = np.float32(want_m[i] + np.float32(np.float32(d * n2) / tot))
+        t = np.float32(np.float32(np.float32(np.float32(d * d) * n1) * n2) / tot)
+        want_s[i] = np.float32(want_s[i] + np.float32(pm2[i] + t))
+    c, pc = C.c_float(float(n1)), C.c_float(float(n2))
+    m, s, p, ps = mean.copy(), m2.copy(), pm.copy(), pm2.copy()
+    O.lib().orc_norm_commit(m, s, C.byref(c), p, ps, C.byref(pc), dim)
+    assert np.array_equal(m, want_m) and np.array_equal(s, want_s)
+    assert c.value == tot and pc.value == 0.0 and not p.any() and not ps.any()
+    # an empty pending state leaves everything as it is
+    c2, pc2 = C.c_float(5.0), C.c_float(0.0)
+    m3 = mean.copy()
+    O.lib().orc_norm_commit(m3, m2.copy(), C.byref(c2), pm.copy(), pm2.copy(), C.byref(pc2), dim)
+    assert np.array_equal(m3, mean) and c2.value == 5.0

@@ -155,6 +155,13 @@ struct zrl_ctx {
   float *obs_mean = nullptr, *obs_m2 = nullptr, *obs_sd = nullptr;
   float *crit_mean = nullptr, *crit_m2 = nullptr, *crit_sd = nullptr;
   float obs_count = 1.0f, crit_count = 1.0f;
+  // PendingNorm (ppo.rs:118-136) of each normalizer: folded by
+  // zrl_pending_push, merged into the live statistics by zrl_commit_pending
+  float *pend_obs_mean = nullptr, *pend_obs_m2 = nullptr;
+  float *pend_crit_mean = nullptr, *pend_crit_m2 = nullptr;
+  float pend_obs_count = 0.0f, pend_crit_count = 0.0f;
+  float *welford_scratch = nullptr;  // chunk partials of the parallel fold
+  int64_t welford_cap = 0;
 
   // batch capacity
   int64_t n_cap = 0;
@@ -1407,6 +1414,10 @@ zrl_status zrl_create(const zrl_model_config *cfg, int device,
   if ((s = dalloc(ctx, &ctx->crit_mean, cd)) != ZRL_OK) return fail(s);
   if ((s = dalloc(ctx, &ctx->crit_m2, cd)) != ZRL_OK) return fail(s);
   if ((s = dalloc(ctx, &ctx->crit_sd, cd)) != ZRL_OK) return fail(s);
+  if ((s = dalloc(ctx, &ctx->pend_obs_mean, od)) != ZRL_OK) return fail(s);
+  if ((s = dalloc(ctx, &ctx->pend_obs_m2, od)) != ZRL_OK) return fail(s);
+  if ((s = dalloc(ctx, &ctx->pend_crit_mean, cd)) != ZRL_OK) return fail(s);
+  if ((s = dalloc(ctx, &ctx->pend_crit_m2, cd)) != ZRL_OK) return fail(s);
   if ((s = dalloc(ctx, &ctx->moments, 2)) != ZRL_OK) return fail(s);
   ctx->rs.max_blocks = 148 * 16;
   ctx->rs.fwidth = 2 * 128 + 4 + 128;  // loss-kernel partial row for Ap, cp <= 128
@@ -1448,7 +1459,9 @@ zrl_status zrl_destroy(zrl_ctx *ctx) {
                     &ctx->b_vo, &ctx->b_adv, &ctx->b_ret, &ctx->r_rew, &ctx->r_val,
                     &ctx->r_lv, &ctx->n_xa, &ctx->n_xc, &ctx->e_xa, &ctx->e_xc, &ctx->e_act, &ctx->e_mo,
                     &ctx->e_lpo, &ctx->e_vo, &ctx->e_adv, &ctx->e_ret, &ctx->wpart,
-                    &ctx->bpart, &ctx->rs.fpart, &ctx->Ptc};
+                    &ctx->bpart, &ctx->rs.fpart, &ctx->Ptc, &ctx->pend_obs_mean,
+                    &ctx->pend_obs_m2, &ctx->pend_crit_mean, &ctx->pend_crit_m2,
+                    &ctx->welford_scratch};
   for (float **b : bufs)
     if (*b) cudaFree(*b);
   for (int k = 0; k < 2; ++k) {
@@ -2007,30 +2020,128 @@ zrl_status zrl_get_profile(zrl_ctx *ctx, float *gemm_ms, float *update_ms,
   return ZRL_OK;
 }
 
-zrl_status zrl_record_obs(zrl_ctx *ctx, const float *obs, const float *critic_obs,
-                          int64_t n) {
-  if (!ctx || (n > 0 && (!obs || !critic_obs))) return ZRL_INVALID_ARG;
-  if (n < 0) return bad(ctx, "negative n");
-  if (n == 0) return ZRL_OK;
-  CK(cudaSetDevice(ctx->device));
+// Rows of both observation kinds on the device (host rows are copied to
+// the batch staging buffers).
+static zrl_status stage_obs(zrl_ctx *ctx, const float *obs, const float *critic_obs, int64_t n,
+                            int32_t on_device, const float **xo, const float **xc) {
+  if (on_device) {
+    *xo = obs;
+    *xc = critic_obs;
+    return ZRL_OK;
+  }
   const int od = ctx->net[0].d[0], cd = ctx->net[1].d[0];
   TRY(ensure_batch(ctx, n));
   CK(cudaMemcpyAsync(ctx->b_obs, obs, sizeof(float) * n * od, cudaMemcpyHostToDevice,
                      ctx->stream));
-  CK(cudaMemcpyAsync(ctx->b_cobs, critic_obs, sizeof(float) * n * cd,
-                     cudaMemcpyHostToDevice, ctx->stream));
-  launch_record_obs(ctx->b_obs, n, od, ctx->obs_mean, ctx->obs_m2, ctx->obs_count,
-                    ctx->stream);
-  launch_record_obs(ctx->b_cobs, n, cd, ctx->crit_mean, ctx->crit_m2, ctx->crit_count,
-                    ctx->stream);
-  ctx->launches += 2;
-  CHECK_LAUNCH();
-  for (int64_t r = 0; r < n; ++r) {  // the same f32 count recurrence
-    ctx->obs_count += 1.0f;
-    ctx->crit_count += 1.0f;
+  CK(cudaMemcpyAsync(ctx->b_cobs, critic_obs, sizeof(float) * n * cd, cudaMemcpyHostToDevice,
+                     ctx->stream));
+  *xo = ctx->b_obs;
+  *xc = ctx->b_cobs;
+  return ZRL_OK;
+}
+
+// n rows folded into (count, mean, m2) of one normalizer: in order, one
+// row at a time (mode 0, the reference's arithmetic), or in row chunks
+// merged pairwise (mode 1, the parallel fold of welford.cu).
+static zrl_status fold_rows(zrl_ctx *ctx, const float *x, int64_t n, int dim, float *count,
+                            float *mean, float *m2, int32_t mode) {
+  if (mode == 1) {
+    const int64_t need = welford_partial_floats(n, dim);
+    if (need > ctx->welford_cap) {
+      TRY(dalloc(ctx, &ctx->welford_scratch, need));
+      ctx->welford_cap = need;
+    }
+    launch_welford_parallel(x, n, dim, *count, mean, m2, ctx->welford_scratch, ctx->stream);
+    ctx->launches += 2;
+  } else {
+    launch_record_obs(x, n, dim, mean, m2, *count, ctx->stream);
+    ctx->launches++;
   }
+  CHECK_LAUNCH();
+  for (int64_t r = 0; r < n; ++r) *count += 1.0f;  // the f32 count recurrence
+  return ZRL_OK;
+}
+
+static zrl_status record_obs_impl(zrl_ctx *ctx, const float *obs, const float *critic_obs,
+                                  int64_t n, int32_t on_device, int32_t mode) {
+  if (!ctx || (n > 0 && (!obs || !critic_obs))) return ZRL_INVALID_ARG;
+  if (n < 0) return bad(ctx, "negative n");
+  if (mode != 0 && mode != 1) return bad(ctx, "mode must be 0 (sequential) or 1 (parallel)");
+  if (n == 0) return ZRL_OK;
+  CK(cudaSetDevice(ctx->device));
+  const float *xo = nullptr, *xc = nullptr;
+  TRY(stage_obs(ctx, obs, critic_obs, n, on_device, &xo, &xc));
+  TRY(fold_rows(ctx, xo, n, ctx->net[0].d[0], &ctx->obs_count, ctx->obs_mean, ctx->obs_m2, mode));
+  TRY(fold_rows(ctx, xc, n, ctx->net[1].d[0], &ctx->crit_count, ctx->crit_mean, ctx->crit_m2,
+                mode));
   TRY(refresh_norm(ctx));
   CK(cudaStreamSynchronize(ctx->stream));
+  return ZRL_OK;
+}
+
+zrl_status zrl_record_obs(zrl_ctx *ctx, const float *obs, const float *critic_obs,
+                          int64_t n) {
+  return record_obs_impl(ctx, obs, critic_obs, n, 0, 0);
+}
+
+zrl_status zrl_record_obs_ex(zrl_ctx *ctx, const float *obs, const float *critic_obs,
+                             int64_t n, int32_t on_device, int32_t mode) {
+  return record_obs_impl(ctx, obs, critic_obs, n, on_device, mode);
+}
+
+zrl_status zrl_pending_push(zrl_ctx *ctx, const float *obs, const float *critic_obs, int64_t n,
+                            int32_t on_device, int32_t mode) {
+  if (!ctx || (n > 0 && (!obs || !critic_obs))) return ZRL_INVALID_ARG;
+  if (n < 0) return bad(ctx, "negative n");
+  if (mode != 0 && mode != 1) return bad(ctx, "mode must be 0 (sequential) or 1 (parallel)");
+  if (n == 0) return ZRL_OK;
+  CK(cudaSetDevice(ctx->device));
+  const float *xo = nullptr, *xc = nullptr;
+  TRY(stage_obs(ctx, obs, critic_obs, n, on_device, &xo, &xc));
+  TRY(fold_rows(ctx, xo, n, ctx->net[0].d[0], &ctx->pend_obs_count, ctx->pend_obs_mean,
+                ctx->pend_obs_m2, mode));
+  TRY(fold_rows(ctx, xc, n, ctx->net[1].d[0], &ctx->pend_crit_count, ctx->pend_crit_mean,
+                ctx->pend_crit_m2, mode));
+  CK(cudaStreamSynchronize(ctx->stream));
+  return ZRL_OK;
+}
+
+zrl_status zrl_commit_pending(zrl_ctx *ctx) {
+  if (!ctx) return ZRL_INVALID_ARG;
+  CK(cudaSetDevice(ctx->device));
+  // a normalizer whose pending state is empty is left as it is (ppo.rs:180)
+  if (ctx->pend_obs_count != 0.0f) {
+    launch_norm_commit(ctx->obs_mean, ctx->obs_m2, ctx->obs_count, ctx->pend_obs_mean,
+                       ctx->pend_obs_m2, ctx->pend_obs_count, ctx->net[0].d[0], ctx->stream);
+    ctx->launches++;
+    ctx->obs_count = ctx->obs_count + ctx->pend_obs_count;
+    ctx->pend_obs_count = 0.0f;
+  }
+  if (ctx->pend_crit_count != 0.0f) {
+    launch_norm_commit(ctx->crit_mean, ctx->crit_m2, ctx->crit_count, ctx->pend_crit_mean,
+                       ctx->pend_crit_m2, ctx->pend_crit_count, ctx->net[1].d[0], ctx->stream);
+    ctx->launches++;
+    ctx->crit_count = ctx->crit_count + ctx->pend_crit_count;
+    ctx->pend_crit_count = 0.0f;
+  }
+  CHECK_LAUNCH();
+  TRY(refresh_norm(ctx));
+  CK(cudaStreamSynchronize(ctx->stream));
+  return ZRL_OK;
+}
+
+zrl_status zrl_get_pending(zrl_ctx *ctx, float *obs_mean, float *obs_m2, float *obs_count,
+                           float *crit_mean, float *crit_m2, float *crit_count) {
+  if (!ctx) return ZRL_INVALID_ARG;
+  CK(cudaSetDevice(ctx->device));
+  CK(cudaStreamSynchronize(ctx->stream));
+  const int od = ctx->net[0].d[0], cd = ctx->net[1].d[0];
+  if (obs_mean) CK(cudaMemcpy(obs_mean, ctx->pend_obs_mean, 4 * od, cudaMemcpyDeviceToHost));
+  if (obs_m2) CK(cudaMemcpy(obs_m2, ctx->pend_obs_m2, 4 * od, cudaMemcpyDeviceToHost));
+  if (crit_mean) CK(cudaMemcpy(crit_mean, ctx->pend_crit_mean, 4 * cd, cudaMemcpyDeviceToHost));
+  if (crit_m2) CK(cudaMemcpy(crit_m2, ctx->pend_crit_m2, 4 * cd, cudaMemcpyDeviceToHost));
+  if (obs_count) *obs_count = ctx->pend_obs_count;
+  if (crit_count) *crit_count = ctx->pend_crit_count;
   return ZRL_OK;
 }
 

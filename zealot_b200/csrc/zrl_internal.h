@@ -234,6 +234,18 @@ void launch_policy_sample(const float *mean, int pitch, const float *log_std,
 // Normalizer::update over n rows in order (bit-exact Welford).
 void launch_record_obs(const float *x, int64_t n, int dim, float *mean,
                        float *m2, float count0, cudaStream_t s);
+// The parallel Welford fold (welford.cu): rows in chunks of
+// kWelfordChunkRows folded from empty states, merged into (count0, mean,
+// m2) in chunk order by Normalizer::commit's formula; scratch holds
+// welford_partial_floats(n, dim) floats.
+constexpr int kWelfordChunkRows = 256;
+int64_t welford_partial_floats(int64_t n, int dim);
+void launch_welford_parallel(const float *x, int64_t n, int dim, float count0, float *mean,
+                             float *m2, float *scratch, cudaStream_t s);
+// Normalizer::commit (ppo.rs:179-195): the pending state merged into the
+// live one, then reset (the counts are kept on the host).
+void launch_norm_commit(float *mean, float *m2, float count, float *p_mean, float *p_m2,
+                        float p_count, int dim, cudaStream_t s);
 
 // ---- GEMMs (gemm_simt.cu / gemm_tc.cu) ---------------------------------
 

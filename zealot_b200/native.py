@@ -90,6 +90,11 @@ _SIGS = {
     "zrl_set_normalizers": (C.c_int, [_P, _P, _P, C.c_float, _P, _P, C.c_float]),
     "zrl_get_normalizers": (C.c_int, [_P, _P, _P, _P, _P, _P, _P]),
     "zrl_record_obs": (C.c_int, [_P, _P, _P, C.c_int64]),
+    "zrl_record_obs_ex": (C.c_int, [_P, _P, _P, C.c_int64, C.c_int32, C.c_int32]),
+    "zrl_pending_push": (C.c_int, [_P, _P, _P, C.c_int64, C.c_int32, C.c_int32]),
+    "zrl_commit_pending": (C.c_int, [_P]),
+    "zrl_get_pending": (C.c_int, [_P, _P, _P, C.POINTER(C.c_float), _P, _P,
+                                  C.POINTER(C.c_float)]),
     "zrl_set_lr": (C.c_int, [_P, C.c_float]),
     "zrl_get_lr": (C.c_int, [_P, C.POINTER(C.c_float)]),
     "zrl_gae": (C.c_int, [_P, _P, _P, _P, _P, C.c_int64, C.c_int64, C.c_float,

@@ -278,6 +278,42 @@ class ActorCritic:
         c = np.ascontiguousarray(critic_obs, np.float32).reshape(-1, self.critic_dims[0])
         self.ctx.call("zrl_record_obs", N.ptr(o), N.ptr(c), o.shape[0])
 
+    def record_obs_rows(self, obs, critic_obs, parallel=False):
+        """record_obs of many rows, numpy or torch CUDA tensors; parallel
+        folds 256-row chunks and merges them with Normalizer::commit's
+        formula (the same statistics up to f32 rounding)."""
+        o, c, n, dev = self._obs_rows(obs, critic_obs)
+        self.ctx.call("zrl_record_obs_ex", N.ptr(o), N.ptr(c), n, dev, 1 if parallel else 0)
+
+    # -- the trainer's frozen-normalizer flow (PendingNorm, ppo.rs:118-195)
+    def pending_push(self, obs, critic_obs, parallel=False):
+        """PendingNorm::push (ppo.rs:126-136) of rows into the pending
+        statistics of both normalizers (pn_obs / pn_cobs)."""
+        o, c, n, dev = self._obs_rows(obs, critic_obs)
+        self.ctx.call("zrl_pending_push", N.ptr(o), N.ptr(c), n, dev, 1 if parallel else 0)
+
+    def commit_pending(self):
+        """Normalizer::commit (ppo.rs:179-195) of both pending states."""
+        self.ctx.call("zrl_commit_pending")
+
+    def pending(self):
+        od, cd = self.actor_dims[0], self.critic_dims[0]
+        om, om2 = np.empty(od, np.float32), np.empty(od, np.float32)
+        cm, cm2 = np.empty(cd, np.float32), np.empty(cd, np.float32)
+        oc, cc = C.c_float(), C.c_float()
+        self.ctx.call("zrl_get_pending", N.ptr(om), N.ptr(om2), C.byref(oc),
+                      N.ptr(cm), N.ptr(cm2), C.byref(cc))
+        return om, om2, oc.value, cm, cm2, cc.value
+
+    def _obs_rows(self, obs, critic_obs):
+        if hasattr(obs, "data_ptr"):
+            o = obs.contiguous()
+            c = critic_obs.contiguous()
+            return o, c, o.shape[0], 1
+        o = np.ascontiguousarray(obs, np.float32).reshape(-1, self.actor_dims[0])
+        c = np.ascontiguousarray(critic_obs, np.float32).reshape(-1, self.critic_dims[0])
+        return o, c, o.shape[0], 0
+
     # -- inference -------------------------------------------------------
     def forward(self, obs=None, critic_obs=None, n=None):
         """Batched ActorCritic::mean / value; either input may be None."""
