@@ -79,7 +79,9 @@ struct HeadSmem {
   static constexpr int kD = kW + 2 * kWNet;            // 192 KB
   static constexpr int kConst = kD + kKBlock;          // 208 KB
   static constexpr int kBias = kConst + 5 * 32 * 4;
-  static constexpr int kBar = kBias + 2 * 32 * 4;
+  // per input-gradient warp: its running column sums [net][chunk][32]
+  static constexpr int kHb = kBias + 2 * 32 * 4;
+  static constexpr int kBar = kHb + kHeadEpi * 2 * (kHeadMaxK / 32) * 32 * 4;
   // w_full, a_full x2, a_empty x2, out_full, out_empty, d_full, din_full, din_empty
   static constexpr int kBars = 10;
   static constexpr int kBytes = 1024 + kBar + kBars * 8 + 16;
@@ -200,15 +202,17 @@ head_kernel(const __grid_constant__ HeadMaps maps, const __grid_constant__ HeadP
     }
   } else if (warp == 1) {
     // ------------------------------------------------------ MMA issuer
+    // (its waits are per tile and long: suspended polls, which leave the
+    // sub-partition's issue slots to the epilogue warp that shares it)
     if (lane == 0) {
-      bool ok = mbar_spin(w_full, 0, p.err, 12);
+      bool ok = mbar_wait(w_full, 0, p.err, 12);
       // the forward of tile i (its A buffer loaded, the previous output read)
       auto fwd = [&](int i, int t) -> bool {
         const int net = t >= p.blocks ? 1 : 0;
         const int nk = p.k[net] / 32;
         const int b = i & 1;
-        if (!mbar_spin(&a_full[b], (i >> 1) & 1, p.err, 13)) return false;
-        if (i >= 1 && !mbar_spin(out_empty, ((uint32_t)i & 1u) ^ 1u, p.err, 14)) return false;
+        if (!mbar_wait(&a_full[b], (i >> 1) & 1, p.err, 13)) return false;
+        if (i >= 1 && !mbar_wait(out_empty, ((uint32_t)i & 1u) ^ 1u, p.err, 14)) return false;
         tc_fence_after();
         // Z[128 x 32] = A[128 x k] W^T
         const uint32_t a_s = smem_u32(smem + HeadSmem::kA0 + b * kABuf);
@@ -231,8 +235,8 @@ head_kernel(const __grid_constant__ HeadMaps maps, const __grid_constant__ HeadP
         // tile's input gradient drains
         if (t + (int)gridDim.x < tiles && !(ok = fwd(i + 1, t + gridDim.x))) break;
         // (D W)[128 x k] = D[128 x 32] W[32 x k]
-        if (!(ok = mbar_spin(d_full, ph, p.err, 15))) break;
-        if (i >= 1 && !(ok = mbar_spin(din_empty, ph ^ 1u, p.err, 16))) break;
+        if (!(ok = mbar_wait(d_full, ph, p.err, 15))) break;
+        if (i >= 1 && !(ok = mbar_wait(din_empty, ph ^ 1u, p.err, 16))) break;
         tc_fence_after();
         const uint32_t d_s = smem_u32(smem + HeadSmem::kD);
         const uint32_t wn = smem_u32(smem + HeadSmem::kW + net * kWNet) + kWNet / 2;
@@ -449,11 +453,11 @@ head_kernel(const __grid_constant__ HeadMaps maps, const __grid_constant__ HeadP
       row[68 + lane] = lane == 0 ? acc_gb1 : 0.0f;
     } else {
       // ------------------------------------------ input-gradient warps
-      // running sums: lane j holds column 32c + j of the last hidden bias
-      // gradient of each net
-      float acc_hb0[kHeadMaxK / 32], acc_hb1[kHeadMaxK / 32];
-#pragma unroll
-      for (int c = 0; c < kHeadMaxK / 32; ++c) acc_hb0[c] = acc_hb1[c] = 0.0f;
+      // running sums in shared memory: lane j holds column 32c + j of the
+      // last hidden bias gradient of each net (the chunk loop stays rolled:
+      // one copy of its code)
+      float *hb = (float *)(smem + HeadSmem::kHb) + q * 2 * (kHeadMaxK / 32) * 32;
+      for (int e = lane; e < 2 * (kHeadMaxK / 32) * 32; e += 32) hb[e] = 0.0f;
       int i = 0;
       for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
         const int net = t >= p.blocks ? 1 : 0;
@@ -467,9 +471,8 @@ head_kernel(const __grid_constant__ HeadMaps maps, const __grid_constant__ HeadP
         if (!ok) break;
         tc_fence_after();
         const uint32_t abuf = smem_u32(smem + HeadSmem::kA0 + b * kABuf) + (uint32_t)(q * 32 * 128);
-#pragma unroll
-        for (int c = 0; c < kHeadMaxK / 32; ++c) {
-          if (c >= nk) break;  // warp-uniform
+#pragma unroll 1
+        for (int c = 0; c < nk; ++c) {
           uint32_t v32[32];
           tmem_ld32(tmem + kColDin + 32u * c + ((uint32_t)(q * 32) << 16), v32);
           if (c == nk - 1) {
@@ -494,13 +497,7 @@ head_kernel(const __grid_constant__ HeadMaps maps, const __grid_constant__ HeadP
           // sum then reads every row)
           stage_row(reg + row_off, sw, v);
           __syncwarp();
-          {
-            const float cs = colsum_staged(reg, lane);
-            if (net == 0)
-              acc_hb0[c] += cs;
-            else
-              acc_hb1[c] += cs;
-          }
+          hb[(net * (kHeadMaxK / 32) + c) * 32 + lane] += colsum_staged(reg, lane);
           __syncwarp();
 #pragma unroll
           for (int k = 0; k < 32; ++k) v[k] = round_tf32(v[k]);
@@ -520,11 +517,10 @@ head_kernel(const __grid_constant__ HeadMaps maps, const __grid_constant__ HeadP
         }
         __syncwarp();
       }
-#pragma unroll
-      for (int c = 0; c < kHeadMaxK / 32; ++c) {
-        if (c < p.k[0] / 32) p.colsum[0][(int64_t)pr * p.k[0] + 32 * c + lane] = acc_hb0[c];
-        if (c < p.k[1] / 32) p.colsum[1][(int64_t)pr * p.k[1] + 32 * c + lane] = acc_hb1[c];
-      }
+      for (int k = 0; k < 2; ++k)
+        for (int c = 0; c < p.k[k] / 32; ++c)
+          p.colsum[k][(int64_t)pr * p.k[k] + 32 * c + lane] =
+              hb[(k * (kHeadMaxK / 32) + c) * 32 + lane];
     }
     if (lane == 0) bulk_wait_all();
   }
