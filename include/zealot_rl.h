@@ -226,6 +226,15 @@ zrl_status zrl_policy_step(zrl_ctx *ctx, const float *obs,
                            const float *critic_obs, int64_t n, uint64_t seed,
                            uint64_t counter, float *action, float *logp,
                            float *mean, float *value, int32_t on_device);
+/* zrl_policy_step with the reference's sampler: the actions of row r draw
+ * Lcg::gauss (rng.rs:28-32) from one sequential stream in (row, k) order, as
+ * ActorCritic::sample (ppo.rs:313-323) and the GPU trainer's host loop
+ * (biped_train_gpu.rs:913-919) do, starting at *lcg_state; on return
+ * *lcg_state has advanced past the 2 n A uniforms used.  The uniforms are
+ * the reference's bit for bit (jump-ahead on the device). */
+zrl_status zrl_policy_step_lcg(zrl_ctx *ctx, const float *obs, const float *critic_obs,
+                               int64_t n, uint64_t *lcg_state, float *action, float *logp,
+                               float *mean, float *value, int32_t on_device);
 
 /* ---- parity hooks ------------------------------------------------------ */
 

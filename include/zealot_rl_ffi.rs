@@ -68,6 +68,9 @@ extern "C" {
     pub fn zrl_policy_step(ctx: *mut ZrlCtx, obs: *const f32, cobs: *const f32, n: i64,
                            seed: u64, counter: u64, action: *mut f32, logp: *mut f32,
                            mean: *mut f32, value: *mut f32, on_device: i32) -> c_int;
+    pub fn zrl_policy_step_lcg(ctx: *mut ZrlCtx, obs: *const f32, cobs: *const f32, n: i64,
+                               lcg_state: *mut u64, action: *mut f32, logp: *mut f32,
+                               mean: *mut f32, value: *mut f32, on_device: i32) -> c_int;
     pub fn zrl_save(ctx: *mut ZrlCtx, path: *const c_char) -> c_int;
     pub fn zrl_load(ctx: *mut ZrlCtx, path: *const c_char) -> c_int;
     pub fn zrl_load_from_bytes(ctx: *mut ZrlCtx, bytes: *const u8, len: usize) -> c_int;

@@ -350,3 +350,32 @@ def test_reference_init_matches_oracle():
     o = O.ActorCritic.new(SMALL_A, SMALL_C, 0.6, 3e-3, O.Lcg(2024))
     assert np.array_equal(g.params, o.params)
     assert g.lr == o.lr
+
+
+def test_policy_step_lcg_stream_matches_sequential_sampling():
+    """zrl_policy_step_lcg against ActorCritic::sample (ppo.rs:313-323) run
+    row after row on one oracle Lcg stream: the same stream state afterwards
+    (bit-exact: 2 n A uniforms), actions within 1e-5 (the uniforms are
+    identical; log, cos and exp may differ by an ulp from the host's libm),
+    logp as the oracle's logp of the GPU's actions."""
+    case = Case(n_envs=5, T=7, seed=15, perturb=0.05)
+    gpu = case.gpu_ac("fp32")
+    rng = Z.Lcg(4242)
+    act, lp, mean, val = gpu.sample_rows(case.ro.obs, case.ro.critic_obs, rng)
+    orc = O.ActorCritic(case.adims, case.cdims)
+    orc.params = gpu.params
+    o_rng = O.Lcg(4242)
+    m2, v2 = gpu.forward(case.ro.obs, case.ro.critic_obs)
+    ls = gpu.log_std.astype(np.float32)
+    for r in range(case.ro.n):
+        for k in range(len(ls)):
+            want = np.float32(m2[r, k] + np.float32(np.exp(ls[k])) * np.float32(o_rng.gauss()))
+            assert abs(act[r, k] - want) <= 1e-5 * max(1.0, abs(want)), (r, k)
+        assert abs(lp[r] - orc.logp(act[r], mean[r])) <= 1e-4 * max(1.0, abs(lp[r]))
+    assert rng.state.value == o_rng.state.value
+    assert np.array_equal(mean, m2) and np.array_equal(val, v2)
+    # the same start state draws the same actions; the advanced state others
+    again, *_ = gpu.sample_rows(case.ro.obs, case.ro.critic_obs, Z.Lcg(4242))
+    assert np.array_equal(again, act)
+    nxt, *_ = gpu.sample_rows(case.ro.obs, case.ro.critic_obs, rng)
+    assert not np.array_equal(nxt, act)

@@ -1259,4 +1259,9 @@ void launch_policy_sample(const float *mean, int pitch, const float *log_std, in
                                                        n, logp);
 }
 
+void launch_logp_rows(const float *action, const float *mean, int pitch, const float *log_std,
+                      int A, int64_t n, float *logp, cudaStream_t s) {
+  logp_rows_kernel<<<grid_for(n, 256), 256, 0, s>>>(action, mean, pitch, log_std, A, n, logp);
+}
+
 }  // namespace zrl

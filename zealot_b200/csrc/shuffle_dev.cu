@@ -41,6 +41,32 @@ __device__ __forceinline__ uint64_t lcg_jump(uint64_t s0, uint64_t d) {
   return a * s0 + c;
 }
 
+// ActorCritic::sample's draws (ppo.rs:313-323; the GPU trainer's host loop,
+// biped_train_gpu.rs:913-919) from one sequential Lcg stream over (row, k):
+// the g-th gauss (g = row * A + k) is Box-Muller (rng.rs:28-32) of the
+// stream's draws 2g and 2g + 1 after s0, reached by jump-ahead -- the
+// uniforms are the reference's bit for bit.
+__global__ void lcg_sample_kernel(const float *mean, int pitch, const float *log_std, int A,
+                                  int64_t n, uint64_t s0, int64_t row0, float *action,
+                                  float *mean_out) {
+  const int64_t total = n * A;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = e / A;
+    const int k = (int)(e - row * A);
+    const uint64_t g = (uint64_t)(row0 + row) * (uint64_t)A + (uint64_t)k;
+    uint64_t st = lcg_jump(s0, 2 * g);
+    st = st * kLcgA + kLcgC;
+    const float u1 = (float)(st >> 40) / 16777216.0f;
+    st = st * kLcgA + kLcgC;
+    const float u2 = (float)(st >> 40) / 16777216.0f;
+    const float z = sqrtf(-2.0f * logf(fmaxf(u1, 1e-7f))) * cosf(6.28318548202514648f * u2);
+    const float mu = mean[row * pitch + k];
+    action[row * A + k] = mu + expf(log_std[k]) * z;
+    if (mean_out) mean_out[row * A + k] = mu;
+  }
+}
+
 // j_i for every step, and the per-position lists of the steps that
 // targeted it (head[p] -> next[k] -> ... -> -1, in any order).
 __global__ void fy_link_kernel(uint64_t s0, int32_t n, int32_t *jt, int32_t *head,
@@ -200,6 +226,15 @@ void launch_rank_orders(const int32_t *perm, int64_t n_global, int64_t n_local,
   rank_scatter_kernel<<<nblk, kScanThreads, 0, s>>>(perm, used, row_offset, n_local, scratch,
                                                     mb, mbs, order, counts);
   rank_counts_kernel<<<1, 32, 0, s>>>(counts, mbs);
+}
+
+void launch_lcg_sample(const float *mean, int pitch, const float *log_std, int A, int64_t n,
+                       uint64_t s0, int64_t row0, float *action, float *mean_out,
+                       cudaStream_t s) {
+  const int64_t work = n * A;
+  const int blocks = (int)std::min<int64_t>((work + 255) / 256, 148 * 16);
+  lcg_sample_kernel<<<blocks, 256, 0, s>>>(mean, pitch, log_std, A, n, s0, row0, action,
+                                            mean_out);
 }
 
 }  // namespace zrl

@@ -2145,9 +2145,28 @@ zrl_status zrl_get_pending(zrl_ctx *ctx, float *obs_mean, float *obs_m2, float *
   return ZRL_OK;
 }
 
-zrl_status zrl_policy_step(zrl_ctx *ctx, const float *obs, const float *critic_obs,
-                           int64_t n, uint64_t seed, uint64_t counter, float *action,
-                           float *logp, float *mean, float *value, int32_t on_device) {
+// The Lcg state after d draws from s (the affine step of rng.rs:21-23
+// raised to the d-th power by squaring).
+static uint64_t lcg_jump_host(uint64_t s, uint64_t d) {
+  uint64_t a = 1, c = 0, pa = 6364136223846793005ull, pc = 1442695040888963407ull;
+  while (d) {
+    if (d & 1) {
+      c = pa * c + pc;
+      a = pa * a;
+    }
+    pc = pa * pc + pc;
+    pa = pa * pa;
+    d >>= 1;
+  }
+  return a * s + c;
+}
+
+// The rollout policy step with either sampler: Philox (seed, counter) or
+// the reference's sequential Lcg stream (*lcg, advanced by 2 n A draws).
+static zrl_status policy_step_impl(zrl_ctx *ctx, const float *obs, const float *critic_obs,
+                                   int64_t n, uint64_t seed, uint64_t counter, uint64_t *lcg,
+                                   float *action, float *logp, float *mean, float *value,
+                                   int32_t on_device) {
   if (!ctx || !obs || !action) return ZRL_INVALID_ARG;
   if (value && !critic_obs) return bad(ctx, "value requested without critic_obs");
   if (n < 0) return bad(ctx, "negative n");
@@ -2176,8 +2195,16 @@ zrl_status zrl_policy_step(zrl_ctx *ctx, const float *obs, const float *critic_o
     float *lp_d = logp ? (on_device ? logp + r0 : ctx->e_lpo) : nullptr;
     float *mean_d = mean ? (on_device ? mean + r0 * A : ctx->e_mo) : nullptr;
     // rows are numbered globally so a chunked call draws the same numbers
-    launch_policy_sample(ctx->act[0][La.L], La.dp[La.L], ctx->P + ctx->ls_off, A, rows,
-                         seed, counter, act_d, lp_d, mean_d, ctx->stream, r0);
+    if (lcg) {
+      launch_lcg_sample(ctx->act[0][La.L], La.dp[La.L], ctx->P + ctx->ls_off, A, rows, *lcg, r0,
+                        act_d, mean_d, ctx->stream);
+      if (lp_d)
+        launch_logp_rows(act_d, ctx->act[0][La.L], La.dp[La.L], ctx->P + ctx->ls_off, A, rows,
+                         lp_d, ctx->stream);
+    } else {
+      launch_policy_sample(ctx->act[0][La.L], La.dp[La.L], ctx->P + ctx->ls_off, A, rows,
+                           seed, counter, act_d, lp_d, mean_d, ctx->stream, r0);
+    }
     ctx->launches += logp ? 2 : 1;
     CHECK_LAUNCH();
     if (value) {
@@ -2212,7 +2239,23 @@ zrl_status zrl_policy_step(zrl_ctx *ctx, const float *obs, const float *critic_o
     // keep the staging buffers alive until the copies drain
     CK(cudaStreamSynchronize(ctx->stream));
   }
+  if (lcg) *lcg = lcg_jump_host(*lcg, 2ull * (uint64_t)n * (uint64_t)A);
   return check_device_error(ctx);
+}
+
+zrl_status zrl_policy_step(zrl_ctx *ctx, const float *obs, const float *critic_obs,
+                           int64_t n, uint64_t seed, uint64_t counter, float *action,
+                           float *logp, float *mean, float *value, int32_t on_device) {
+  return policy_step_impl(ctx, obs, critic_obs, n, seed, counter, nullptr, action, logp, mean,
+                          value, on_device);
+}
+
+zrl_status zrl_policy_step_lcg(zrl_ctx *ctx, const float *obs, const float *critic_obs,
+                               int64_t n, uint64_t *lcg_state, float *action, float *logp,
+                               float *mean, float *value, int32_t on_device) {
+  if (!lcg_state) return bad(ctx, "null Lcg state");
+  return policy_step_impl(ctx, obs, critic_obs, n, 0, 0, lcg_state, action, logp, mean, value,
+                          on_device);
 }
 
 // ---------------------------------------------------------------- I/O

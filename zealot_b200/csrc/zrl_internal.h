@@ -231,6 +231,15 @@ void launch_policy_sample(const float *mean, int pitch, const float *log_std,
                           int A, int64_t n, uint64_t seed, uint64_t counter,
                           float *action, float *logp, float *mean_out,
                           cudaStream_t s, int64_t row0 = 0);
+// The reference's sampling stream (shuffle_dev.cu): action = mean +
+// exp(log_std) * Lcg::gauss() with the gauss of (row, k) the (row * A + k)-th
+// of one Lcg stream that starts at state s0 (rows numbered from row0).
+void launch_lcg_sample(const float *mean, int pitch, const float *log_std, int A, int64_t n,
+                       uint64_t s0, int64_t row0, float *action, float *mean_out,
+                       cudaStream_t s);
+// logp of n action rows (ppo.rs:297-305).
+void launch_logp_rows(const float *action, const float *mean, int pitch, const float *log_std,
+                      int A, int64_t n, float *logp, cudaStream_t s);
 // Normalizer::update over n rows in order (bit-exact Welford).
 void launch_record_obs(const float *x, int64_t n, int dim, float *mean,
                        float *m2, float count0, cudaStream_t s);

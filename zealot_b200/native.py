@@ -105,6 +105,8 @@ _SIGS = {
     "zrl_forward": (C.c_int, [_P, _P, _P, C.c_int64, _P, _P, C.c_int32]),
     "zrl_policy_step": (C.c_int, [_P, _P, _P, C.c_int64, C.c_uint64, C.c_uint64,
                                   _P, _P, _P, _P, C.c_int32]),
+    "zrl_policy_step_lcg": (C.c_int, [_P, _P, _P, C.c_int64, C.POINTER(C.c_uint64), _P, _P,
+                                      _P, _P, C.c_int32]),
     "zrl_minibatch_grads": (C.c_int, [_P, C.POINTER(PpoConfigC), C.POINTER(BatchC), _P,
                                       C.c_int64, _P, _P]),
     "zrl_apply_grads": (C.c_int, [_P, C.POINTER(PpoConfigC), _P, C.c_float]),

@@ -382,6 +382,21 @@ class ActorCritic:
                       N.ptr(act), N.ptr(lp), N.ptr(mean), N.ptr(val), 0)
         return act, lp, mean, val
 
+    def sample_rows(self, obs, critic_obs, rng: "Lcg"):
+        """ActorCritic::sample (ppo.rs:313-323) for every row in order from
+        one Lcg stream, on the GPU: (action, logp, mean, value); rng
+        advances past the draws used, as n sequential sample calls would."""
+        obs = np.ascontiguousarray(obs, np.float32)
+        critic_obs = np.ascontiguousarray(critic_obs, np.float32)
+        n = obs.shape[0]
+        act = np.empty((n, self.action_dim), np.float32)
+        lp = np.empty(n, np.float32)
+        mean = np.empty((n, self.action_dim), np.float32)
+        val = np.empty(n, np.float32)
+        self.ctx.call("zrl_policy_step_lcg", N.ptr(obs), N.ptr(critic_obs), n,
+                      C.byref(rng.state), N.ptr(act), N.ptr(lp), N.ptr(mean), N.ptr(val), 0)
+        return act, lp, mean, val
+
     # -- training --------------------------------------------------------
     def update(self, batch, cfg: PpoConfig, n_global=0, row_offset=0,
                write_back_adv=False) -> PpoStats:
