@@ -330,6 +330,28 @@ int64_t zrl_rank_orders(uint64_t seed, int64_t n_global, int64_t n_local,
                         int64_t row_offset, int32_t minibatches, int32_t *order,
                         int64_t *counts);
 
+/* ---- failure handling ---------------------------------------------------- */
+
+/* Bound (ns, at least 1 ms) of every wait inside the tensor-core kernels'
+ * pipelines (default 20 s): a wait that runs out records a code in the
+ * context's device error flag, every role of the kernel gives up in turn,
+ * and the call that finishes the work returns ZRL_TIMEOUT (the flag is then
+ * cleared, so the context stays usable).  No counterpart in the reference,
+ * which has no device pipelines. */
+zrl_status zrl_set_wait_limit(zrl_ctx *ctx, uint64_t ns);
+/* Test hook: the next tensor-core GEMM launch of this context makes its MMA
+ * issuer wait on a barrier that nothing completes, so the wait runs out
+ * after the wait limit (the failure path above, without a GPU fault). */
+zrl_status zrl_test_stall_next_gemm(zrl_ctx *ctx);
+/* Test hook: the bounded stream wait of the several-rank path (the poll of
+ * the stream and of NCCL's asynchronous error that aborts the communicator
+ * on a timeout or an error) run on fakes, no GPU needed: scenario 0 the
+ * stream completes, 1 it never does (ZRL_TIMEOUT after timeout_ms), 2 the
+ * communicator reports an error (ZRL_NCCL_ERROR), 3 the stream reports a
+ * failed kernel (ZRL_CUDA_ERROR).  *aborted: whether the communicator was
+ * aborted. */
+zrl_status zrl_test_comm_wait(int32_t scenario, int32_t timeout_ms, int32_t *aborted);
+
 /* ---- instrumentation ---------------------------------------------------- */
 
 /* Number of kernels this context launched since it was created. */

@@ -112,6 +112,10 @@ extern "C" {
     pub fn zrl_rank_orders_device(ctx: *mut ZrlCtx, seed: u64, n_global: i64, n_local: i64,
                                   row_offset: i64, minibatches: i32, order: *mut i32,
                                   counts: *mut i64) -> i64;
+    // failure handling
+    pub fn zrl_set_wait_limit(ctx: *mut ZrlCtx, ns: u64) -> c_int;
+    pub fn zrl_test_stall_next_gemm(ctx: *mut ZrlCtx) -> c_int;
+    pub fn zrl_test_comm_wait(scenario: i32, timeout_ms: i32, aborted: *mut i32) -> c_int;
     // instrumentation
     pub fn zrl_kernel_launches(ctx: *const ZrlCtx) -> i64;
     pub fn zrl_set_profiling(ctx: *mut ZrlCtx, enabled: i32) -> c_int;

@@ -85,6 +85,8 @@ struct TcGroup {
   int tiles;   // total tiles
   int reverse; // walk the tiles last to first (L2 reuse of the previous launch's last tiles)
   int *err;
+  uint64_t wait_ns;  // bound of every mbarrier wait
+  int stall;         // test hook: the MMA issuer waits on a barrier nothing completes
 };
 // Tensor maps per problem: A and B operands, the output C (3-D, split
 // index outermost) and the dgrad epilogue's post-activation X.
@@ -110,8 +112,9 @@ struct Smem {
   static constexpr int kBiasPerWarp = BN / 2 > 64 ? BN / 2 : 64;  // floats
   static constexpr int kBias = kEpiWarps * kBiasPerWarp * 4;
   static constexpr int kBarOff = kStageBytes + kStaging + kBias;
-  // full, empty, acc_full x2, acc_empty x2, one aux barrier per staging slot
-  static constexpr int kBars = 2 * STAGES + 4 + kEpiWarps * kSlots;
+  // full, empty, acc_full x2, acc_empty x2, one aux barrier per staging
+  // slot, and one that nothing completes (the stall test hook)
+  static constexpr int kBars = 2 * STAGES + 4 + kEpiWarps * kSlots + 1;
   static constexpr int kBytes = 1024 /*align*/ + kBarOff + kBars * 8 + 16;
 };
 
@@ -338,7 +341,8 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
   uint64_t *accf = empty + STAGES;  // [2]
   uint64_t *acce = accf + 2;        // [2]
   uint64_t *xbar = acce + 2;        // [kEpiWarps][kSlots]
-  uint32_t *tmem_slot = (uint32_t *)(xbar + kEpiWarps * S::kSlots);
+  uint64_t *never = xbar + kEpiWarps * S::kSlots;
+  uint32_t *tmem_slot = (uint32_t *)(never + 1);
   float *bias_sh = (float *)(smem + S::kStageBytes + S::kStaging);  // [kEpiWarps][kCptMax][32]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -360,6 +364,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
       mbar_init(&acce[b], kEpiWarps + (CG == 2 && rank == 0 ? 1 : 0));
     }
     for (int b = 0; b < kEpiWarps * S::kSlots; ++b) mbar_init(&xbar[b], 1);
+    mbar_init(never, 1);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -415,7 +420,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
         for (int kb = 0; kb < tl.nk; ++kb, ++kbg) {
           const int s = kbg % STAGES;
           const uint32_t ph = (uint32_t)(kbg / STAGES) & 1u;
-          if (kbg >= STAGES && !(ok = mbar_spin(&empty[s], ph ^ 1u, g.err, 1))) break;
+          if (kbg >= STAGES && !(ok = mbar_spin(&empty[s], ph ^ 1u, g.err, 1, g.wait_ns))) break;
           uint8_t *a_s = smem + s * S::kStage;
           uint8_t *b_s = a_s + S::kA;
           const int k0 = tl.kbeg + kb * KE;
@@ -467,20 +472,22 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
       constexpr uint32_t idesc_half = BF ? idesc_bf16(BM * CG, BN / 2, A_MN, B_MN)
                                          : idesc_tf32(BM * CG, BN / 2, A_MN, B_MN);
       int kbg = 0, it = 0;
-      bool ok = true;
+      // the stall test hook: a wait that runs out (nothing completes the
+      // barrier), after which every role of the kernel gives up in turn
+      bool ok = !g.stall || mbar_spin(never, 0, g.err, 7, g.wait_ns);
       for (int t = unit; t < tiles && ok; t += units, ++it) {
         const Tile tl = decode_tile<BN, CG, KE>(t, g);
         const int ab = it & 1;
         const uint32_t aph = (uint32_t)(it >> 1) & 1u;
         // the epilogue must have drained this accumulator (tile it-2)
-        if (it >= 2 && !(ok = mbar_spin(&acce[ab], aph ^ 1u, g.err, 4))) break;
+        if (it >= 2 && !(ok = mbar_spin(&acce[ab], aph ^ 1u, g.err, 4, g.wait_ns))) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(ab * BN);
         const uint32_t idesc = tl.bn == BN ? idesc_full : idesc_half;
         for (int kb = 0; kb < tl.nk; ++kb, ++kbg) {
           const int s = kbg % STAGES;
           const uint32_t ph = (uint32_t)(kbg / STAGES) & 1u;
-          if (!(ok = mbar_spin(&full[s], ph, g.err, 2))) break;
+          if (!(ok = mbar_spin(&full[s], ph, g.err, 2, g.wait_ns))) break;
           tc_fence_after();
           const uint32_t a_s = smem_u32(smem + s * S::kStage);
           const uint32_t b_s = a_s + S::kA;
@@ -530,7 +537,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
       for (int t = unit; t < tiles; t += units, ++it) {
         const int ab = it & 1;
         const uint32_t aph = (uint32_t)(it >> 1) & 1u;
-        if (!mbar_spin(&acce[ab], aph, g.err, 6)) break;
+        if (!mbar_spin(&acce[ab], aph, g.err, 6, g.wait_ns)) break;
         mbar_arrive_cluster(acce_peer + 8u * ab);
       }
     }
@@ -611,7 +618,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
             tma_prefetch_2d(&maps.x[nt.p], n, r0);
         }
       }
-      if (ok) ok = mbar_wait(&accf[ab], aph, g.err, 3);
+      if (ok) ok = mbar_wait(&accf[ab], aph, g.err, 3, g.wait_ns);
       ok = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld is collective
       tc_fence_after();
       const bool rows_full = row0 + 32 <= pr.M;  // uniform
@@ -643,7 +650,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
         if (live) {
           if (EPI == EPI_ELU_GRAD) {
             // the post-activation box of this chunk (TMA, one chunk ahead)
-            if (!mbar_wait(&wbar[sl], (xph >> sl) & 1u, g.err, 5)) ok = false;
+            if (!mbar_wait(&wbar[sl], (xph >> sl) & 1u, g.err, 5, g.wait_ns)) ok = false;
             xph ^= 1u << sl;
           }
           if (EPI != EPI_ELU_GRAD) {
@@ -1161,6 +1168,9 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
   grp.tiles = tiles;
   grp.reverse = gs[0].reverse_tiles;
   grp.err = eng->err_dev;
+  grp.wait_ns = eng->wait_ns;
+  grp.stall = eng->stall_next;
+  eng->stall_next = 0;
   const cudaError_t e = bf ? dispatch<true>(CG, BN, kind, gs[0].epi, maps, grp, s)
                            : dispatch<false>(CG, BN, kind, gs[0].epi, maps, grp, s);
   if (e != cudaSuccess) {

@@ -69,6 +69,7 @@ struct HeadParams {
   float scale, clip, entropy_coef, value_coef;
   float *part;
   int *err;
+  uint64_t wait_ns;  // bound of every mbarrier wait
 };
 
 // shared memory: two activation buffers, both nets' weights, the delta
@@ -192,7 +193,7 @@ head_kernel(const __grid_constant__ HeadMaps maps, const __grid_constant__ HeadP
         const int net = t >= p.blocks ? 1 : 0;
         const int m0 = (t - net * p.blocks) * kHeadRows;
         const int b = i & 1;
-        if (i >= 2 && !(ok = mbar_wait(&a_empty[b], ((i >> 1) & 1) ^ 1u, p.err, 11))) break;
+        if (i >= 2 && !(ok = mbar_wait(&a_empty[b], ((i >> 1) & 1) ^ 1u, p.err, 11, p.wait_ns))) break;
         const int nk = p.k[net] / 32;
         mbar_expect_tx(&a_full[b], (uint32_t)(nk * kKBlock));
         uint8_t *abuf = smem + HeadSmem::kA0 + b * kABuf;
@@ -205,14 +206,14 @@ head_kernel(const __grid_constant__ HeadMaps maps, const __grid_constant__ HeadP
     // (its waits are per tile and long: suspended polls, which leave the
     // sub-partition's issue slots to the epilogue warp that shares it)
     if (lane == 0) {
-      bool ok = mbar_wait(w_full, 0, p.err, 12);
+      bool ok = mbar_wait(w_full, 0, p.err, 12, p.wait_ns);
       // the forward of tile i (its A buffer loaded, the previous output read)
       auto fwd = [&](int i, int t) -> bool {
         const int net = t >= p.blocks ? 1 : 0;
         const int nk = p.k[net] / 32;
         const int b = i & 1;
-        if (!mbar_wait(&a_full[b], (i >> 1) & 1, p.err, 13)) return false;
-        if (i >= 1 && !mbar_wait(out_empty, ((uint32_t)i & 1u) ^ 1u, p.err, 14)) return false;
+        if (!mbar_wait(&a_full[b], (i >> 1) & 1, p.err, 13, p.wait_ns)) return false;
+        if (i >= 1 && !mbar_wait(out_empty, ((uint32_t)i & 1u) ^ 1u, p.err, 14, p.wait_ns)) return false;
         tc_fence_after();
         // Z[128 x 32] = A[128 x k] W^T
         const uint32_t a_s = smem_u32(smem + HeadSmem::kA0 + b * kABuf);
@@ -235,8 +236,8 @@ head_kernel(const __grid_constant__ HeadMaps maps, const __grid_constant__ HeadP
         // tile's input gradient drains
         if (t + (int)gridDim.x < tiles && !(ok = fwd(i + 1, t + gridDim.x))) break;
         // (D W)[128 x k] = D[128 x 32] W[32 x k]
-        if (!(ok = mbar_wait(d_full, ph, p.err, 15))) break;
-        if (i >= 1 && !(ok = mbar_wait(din_empty, ph ^ 1u, p.err, 16))) break;
+        if (!(ok = mbar_wait(d_full, ph, p.err, 15, p.wait_ns))) break;
+        if (i >= 1 && !(ok = mbar_wait(din_empty, ph ^ 1u, p.err, 16, p.wait_ns))) break;
         tc_fence_after();
         const uint32_t d_s = smem_u32(smem + HeadSmem::kD);
         const uint32_t wn = smem_u32(smem + HeadSmem::kW + net * kWNet) + kWNet / 2;
@@ -318,7 +319,7 @@ head_kernel(const __grid_constant__ HeadMaps maps, const __grid_constant__ HeadP
         // the delta tile is free once the previous tile's D W has read it
         // and this warp's previous store out of it is done reading
         if (i >= 1) {
-          if (ok) ok = mbar_wait(din_full, ph ^ 1u, p.err, 19);
+          if (ok) ok = mbar_wait(din_full, ph ^ 1u, p.err, 19, p.wait_ns);
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
         }
@@ -343,7 +344,7 @@ head_kernel(const __grid_constant__ HeadMaps maps, const __grid_constant__ HeadP
           __syncwarp();
         }
         // ---- the forward output of the row
-        if (ok) ok = mbar_wait(out_full, ph, p.err, 17);
+        if (ok) ok = mbar_wait(out_full, ph, p.err, 17, p.wait_ns);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
@@ -466,7 +467,7 @@ head_kernel(const __grid_constant__ HeadMaps maps, const __grid_constant__ HeadP
         const int b = i & 1;
         const int row0 = m0 + 32 * q;
         const bool live = (int64_t)row0 + lane < p.rows;
-        if (ok) ok = mbar_wait(din_full, (uint32_t)i & 1u, p.err, 18);
+        if (ok) ok = mbar_wait(din_full, (uint32_t)i & 1u, p.err, 18, p.wait_ns);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
@@ -583,6 +584,7 @@ zrl_status head_tc(GemmEngine *eng, const HeadArgs &a, cudaStream_t s, std::stri
   p.value_coef = a.value_coef;
   p.part = a.part;
   p.err = a.err;
+  p.wait_ns = eng->wait_ns;
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -2,7 +2,7 @@
 // kernels (gemm_tc.cu, head_tc.cu): mbarriers with bounded waits, TMA tile
 // loads and stores, tcgen05 MMA / commit / TMEM loads, shared-memory matrix
 // and instruction descriptors, and the epilogue's small numeric helpers.
-// Every wait is bounded: it gives up after kWaitNs of wall time (or
+// Every wait is bounded: it gives up after a wall-time limit (or
 // kWaitLimit polls), records a code in an error flag and returns false.
 #pragma once
 
@@ -14,7 +14,7 @@ namespace zrl {
 namespace {
 
 // a second bound on a wait, on the number of polls, should the global timer
-// not advance; the wall-time bound (kWaitNs) is the one that normally ends
+// not advance; the wall-time bound (a launch parameter) is the one that normally ends
 // a wait that never completes
 constexpr uint32_t kWaitLimit = 1u << 24;
 
@@ -75,27 +75,29 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 
 // Bounded wait: true when the phase completed, false (and *err set) when
-// kWaitNs of wall time passed without it (however long each poll slept).
-constexpr uint64_t kWaitNs = 20ull * 1000 * 1000 * 1000;
+// limit_ns of wall time passed without it (however long each poll slept).
+// The limit is a launch parameter (the context's wait limit, 20 s unless
+// set otherwise).
 __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, int *err,
-                                          int code) {
+                                          int code, uint64_t limit_ns) {
   if (mbar_try(b, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 0; i < kWaitLimit; ++i) {
     if (mbar_try(b, parity)) return true;
-    if (global_ns() - t0 > kWaitNs) break;
+    if (global_ns() - t0 > limit_ns) break;
   }
   atomicExch(err, code);
   return false;
 }
 
 // Bounded spin for the latency-critical single-thread roles.
-__device__ __forceinline__ bool mbar_spin(uint64_t *b, uint32_t parity, int *err, int code) {
+__device__ __forceinline__ bool mbar_spin(uint64_t *b, uint32_t parity, int *err, int code,
+                                          uint64_t limit_ns) {
   if (mbar_test(b, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 0;; ++i) {
     if (mbar_test(b, parity)) return true;
-    if ((i & 255) == 255 && global_ns() - t0 > kWaitNs) break;
+    if ((i & 255) == 255 && global_ns() - t0 > limit_ns) break;
   }
   atomicExch(err, code);
   return false;

@@ -1996,6 +1996,29 @@ zrl_status zrl_apply_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg, const float 
   return zrl_get_lr(ctx, &lr);
 }
 
+zrl_status zrl_set_wait_limit(zrl_ctx *ctx, uint64_t ns) {
+  if (!ctx) return ZRL_INVALID_ARG;
+  if (ns < 1000000ull) return bad(ctx, "wait limit below 1 ms");
+  ctx->gemm.wait_ns = ns;
+  return ZRL_OK;
+}
+
+zrl_status zrl_test_comm_wait(int32_t scenario, int32_t timeout_ms, int32_t *aborted) {
+  if (!aborted || scenario < 0 || scenario > 3 || timeout_ms < 0) return ZRL_INVALID_ARG;
+  std::string err;
+  int ab = 0;
+  const zrl_status st = comm_wait_fake(scenario, timeout_ms, &ab, &err);
+  *aborted = ab;
+  return st;
+}
+
+zrl_status zrl_test_stall_next_gemm(zrl_ctx *ctx) {
+  if (!ctx) return ZRL_INVALID_ARG;
+  if (!ctx->tcore()) return bad(ctx, "the stall hook is in the tensor-core GEMM");
+  ctx->gemm.stall_next = 1;
+  return ZRL_OK;
+}
+
 zrl_status zrl_set_profiling(zrl_ctx *ctx, int32_t enabled) {
   if (!ctx) return ZRL_INVALID_ARG;
   ctx->profiling = enabled != 0;

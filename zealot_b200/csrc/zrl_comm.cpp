@@ -128,38 +128,74 @@ zrl_status Comm::allreduce_f64(double *buf, int64_t count, cudaStream_t s,
   return do_allreduce(this, buf, count, kNcclFloat64, s, err);
 }
 
-zrl_status Comm::wait(cudaStream_t s, std::string *err) {
+// The bounded wait of Comm::wait over its three effects, so the failure
+// paths can be driven by fakes: query() is cudaStreamQuery of the stream,
+// async_err() the communicator's asynchronous error (0 or in progress:
+// none), abort() aborts the communicator.
+template <typename Query, typename AsyncErr, typename Abort>
+static zrl_status wait_loop(int timeout_ms, Query query, AsyncErr async_err, Abort abort,
+                            std::string *err) {
   const auto t0 = std::chrono::steady_clock::now();
   for (;;) {
-    cudaError_t q = cudaStreamQuery(s);
+    cudaError_t q = query();
     if (q == cudaSuccess) return ZRL_OK;
     if (q != cudaErrorNotReady) {
       *err = std::string("stream: ") + cudaGetErrorString(q);
       return ZRL_CUDA_ERROR;
     }
-    if (world > 1 && comm) {
-      nccl_result_t ae = 0;
-      g_api.async_error(comm, &ae);
-      if (ae != 0 && ae != kNcclInProgress) {
-        *err = nccl_msg("NCCL async", ae);
-        g_api.comm_abort(comm);
-        aborted = true;
-        return ZRL_NCCL_ERROR;
-      }
+    const nccl_result_t ae = async_err();
+    if (ae != 0 && ae != kNcclInProgress) {
+      *err = nccl_msg("NCCL async", ae);
+      abort();
+      return ZRL_NCCL_ERROR;
     }
     const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
                         std::chrono::steady_clock::now() - t0)
                         .count();
     if (ms > timeout_ms) {
       *err = "timed out waiting for the stream (a peer rank may be gone)";
-      if (world > 1 && comm) {
-        g_api.comm_abort(comm);
-        aborted = true;
-      }
+      abort();
       return ZRL_TIMEOUT;
     }
     std::this_thread::sleep_for(std::chrono::microseconds(50));
   }
+}
+
+zrl_status Comm::wait(cudaStream_t s, std::string *err) {
+  return wait_loop(
+      timeout_ms, [&] { return cudaStreamQuery(s); },
+      [&]() -> nccl_result_t {
+        nccl_result_t ae = 0;
+        if (world > 1 && comm) g_api.async_error(comm, &ae);
+        return ae;
+      },
+      [&] {
+        if (world > 1 && comm) {
+          g_api.comm_abort(comm);
+          aborted = true;
+        }
+      },
+      err);
+}
+
+// Comm::wait's failure paths on fakes (no GPU, no NCCL): scenario 0 the
+// stream completes on the fifth poll; 1 it never completes; 2 the
+// communicator reports an asynchronous error on the third poll; 3 the
+// stream reports a failed kernel.  *aborted receives whether the
+// communicator would have been aborted.
+zrl_status comm_wait_fake(int scenario, int timeout_ms, int *aborted, std::string *err) {
+  int polls = 0;
+  *aborted = 0;
+  return wait_loop(
+      timeout_ms,
+      [&]() -> cudaError_t {
+        ++polls;
+        if (scenario == 0 && polls >= 5) return cudaSuccess;
+        if (scenario == 3) return cudaErrorLaunchFailure;
+        return cudaErrorNotReady;
+      },
+      [&]() -> nccl_result_t { return scenario == 2 && polls >= 3 ? 3 /* internal error */ : 0; },
+      [&] { *aborted = 1; }, err);
 }
 
 void Comm::destroy() {

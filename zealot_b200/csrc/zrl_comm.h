@@ -40,4 +40,7 @@ struct Comm {
   void destroy();
 };
 
+// Comm::wait's bounded loop driven by fakes (zrl_comm.cpp), for tests.
+zrl_status comm_wait_fake(int scenario, int timeout_ms, int *aborted, std::string *err);
+
 }  // namespace zrl

@@ -76,6 +76,8 @@ struct GemmEngine {
   bool tc_ready = false;
   void *cache = nullptr;  // tensor-map cache (gemm_tc.cu)
   int *err_dev = nullptr; // device flag set by a timed-out pipeline wait
+  uint64_t wait_ns = 20ull * 1000 * 1000 * 1000;  // bound of every pipeline wait
+  int stall_next = 0;     // test hook: the next tensor-core GEMM launch stalls
 
   zrl_status init(int device, std::string *err);
   void destroy();
