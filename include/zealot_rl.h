@@ -64,7 +64,8 @@ typedef struct {
 } zrl_stats;
 
 /* Network shapes and capacity.  actor_dims[0] = obs dim,
- * actor_dims[n_actor_dims-1] = action dim; critic_dims ends in 1
+ * actor_dims[n_actor_dims-1] = action dim (at most 128); critic_dims ends in
+ * 1; both observation widths at most 256 (ZRL_NOT_SUPPORTED beyond)
  * (ActorCritic::new, ppo.rs:235-247). */
 typedef struct {
   int32_t n_actor_dims;
@@ -329,6 +330,19 @@ void zrl_shuffle(uint64_t seed, int64_t n, int64_t *order);
 int64_t zrl_rank_orders(uint64_t seed, int64_t n_global, int64_t n_local,
                         int64_t row_offset, int32_t minibatches, int32_t *order,
                         int64_t *counts);
+
+/* L/R mirror augmentation of the GPU trainer (biped_train_gpu.rs:89-185,
+ * 988-1003): when set, zrl_update / zrl_gae_update train on 2 n samples,
+ * the n mirrored copies first, then the batch itself.  A mirrored sample
+ * has obs, critic_obs, action and mean_old mapped by signed permutations,
+ * (P x)[i] = sign[i] * x[perm[i]] (each perm a permutation of its space,
+ * each sign +-1), and logp_old, value_old, adv, ret unchanged.  The mirror
+ * is applied to the raw rows as the epoch gather reads them, so the batch
+ * is not copied.  obs_perm = NULL turns it off.  One rank only
+ * (ZRL_NOT_SUPPORTED with several). */
+zrl_status zrl_set_mirror(zrl_ctx *ctx, const int32_t *obs_perm, const float *obs_sign,
+                          const int32_t *cobs_perm, const float *cobs_sign,
+                          const int32_t *act_perm, const float *act_sign);
 
 /* ---- failure handling ---------------------------------------------------- */
 

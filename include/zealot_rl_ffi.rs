@@ -112,6 +112,9 @@ extern "C" {
     pub fn zrl_rank_orders_device(ctx: *mut ZrlCtx, seed: u64, n_global: i64, n_local: i64,
                                   row_offset: i64, minibatches: i32, order: *mut i32,
                                   counts: *mut i64) -> i64;
+    pub fn zrl_set_mirror(ctx: *mut ZrlCtx, obs_perm: *const i32, obs_sign: *const f32,
+                          cobs_perm: *const i32, cobs_sign: *const f32, act_perm: *const i32,
+                          act_sign: *const f32) -> c_int;
     // failure handling
     pub fn zrl_set_wait_limit(ctx: *mut ZrlCtx, ns: u64) -> c_int;
     pub fn zrl_test_stall_next_gemm(ctx: *mut ZrlCtx) -> c_int;

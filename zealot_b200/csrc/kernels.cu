@@ -235,9 +235,12 @@ __global__ void adv_finalize_kernel(const double *moments, int64_t n_global,
 
 // ------------------------------------------------------------ gather
 
-// One warp per output position: copies row order[p] of every batch array,
-// applying Normalizer::normalize (ppo.rs:198-205) to the two observation
-// rows and the advantage normalization (ppo.rs:346-348) to adv.
+// One warp per output position: copies row order[p] of every batch array --
+// the observation rows already normalized (normalize_rows_kernel, once per
+// update) as 16-byte pieces -- and applies the advantage normalization
+// (ppo.rs:346-348) to adv.  With the mirror augmentation a virtual row
+// r < n_base takes base row r's mirrored normalized rows and its action and
+// mean_old through the action space's signed permutation.
 __global__ void gather_kernel(GatherArgs a) {
   pdl_wait();
   pdl_trigger();
@@ -247,51 +250,46 @@ __global__ void gather_kernel(GatherArgs a) {
   const float am = a.st->adv_mean, asd = a.st->adv_sd;
   // 16-byte pieces per padded observation row
   const int qa = a.odp * a.x_bytes / 16, qc = a.cdp * a.x_bytes / 16;
+  const bool al = lane < a.A;
+  const int ai = al && a.n_base > 0 ? a.m_aperm[lane] : lane;
+  const float asg = al && a.n_base > 0 ? a.m_asign[lane] : 1.0f;
   for (int64_t p = warp; p < a.n_used; p += nwarps) {
     const int64_t r = a.order[p];
-    const float4 *xa = reinterpret_cast<const float4 *>(a.xn_a) + r * qa;
-    const float4 *xc = reinterpret_cast<const float4 *>(a.xn_c) + r * qc;
+    const bool mir = a.n_base > 0 && r < a.n_base;
+    const int64_t src = a.n_base > 0 ? (mir ? r : r - a.n_base) : r;
+    const float4 *xa = reinterpret_cast<const float4 *>(mir ? a.xm_a : a.xn_a) + src * qa;
+    const float4 *xc = reinterpret_cast<const float4 *>(mir ? a.xm_c : a.xn_c) + src * qc;
     float4 *ya = reinterpret_cast<float4 *>(a.x_a) + p * qa;
     float4 *yc = reinterpret_cast<float4 *>(a.x_c) + p * qc;
-    if (qa <= 32 && qc <= 32 && a.A <= 32) {
-      // every load of the row first, then every store
+    // every load of the row first, then every store
+    float act = 0.0f, mo = 0.0f, sc = 0.0f;
+    if (al) {
+      const int kk = mir ? ai : lane;
+      act = a.action[src * a.A + kk];
+      mo = a.mean_old[src * a.A + kk];
+    }
+    if (lane == 0) sc = a.logp_old[src];
+    else if (lane == 1) sc = a.value_old[src];
+    else if (lane == 2) sc = a.adv[src];
+    else if (lane == 3) sc = a.ret[src];
+    if (qa <= 32 && qc <= 32) {
       float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vc = va;
-      float act = 0.0f, mo = 0.0f, scal = 0.0f;
       if (lane < qa) va = xa[lane];
       if (lane < qc) vc = xc[lane];
-      if (lane < a.A) {
-        act = a.action[r * a.A + lane];
-        mo = a.mean_old[r * a.A + lane];
-      }
-      if (lane == 0) scal = a.logp_old[r];
-      else if (lane == 1) scal = a.value_old[r];
-      else if (lane == 2) scal = a.adv[r];
-      else if (lane == 3) scal = a.ret[r];
       if (lane < qa) ya[lane] = va;
       if (lane < qc) yc[lane] = vc;
-      if (lane < a.A) {
-        a.g_action[p * a.A + lane] = act;
-        a.g_mean_old[p * a.A + lane] = mo;
-      }
-      if (lane == 0) a.g_logp_old[p] = scal;
-      else if (lane == 1) a.g_value_old[p] = scal;
-      else if (lane == 2) a.g_adv[p] = a.apply_adv_norm ? __fdiv_rn(__fsub_rn(scal, am), asd) : scal;
-      else if (lane == 3) a.g_ret[p] = scal;
     } else {
       for (int i = lane; i < qa; i += 32) ya[i] = xa[i];
       for (int i = lane; i < qc; i += 32) yc[i] = xc[i];
-      for (int k = lane; k < a.A; k += 32) {
-        a.g_action[p * a.A + k] = a.action[r * a.A + k];
-        a.g_mean_old[p * a.A + k] = a.mean_old[r * a.A + k];
-      }
-      if (lane == 0) {
-        a.g_logp_old[p] = a.logp_old[r];
-        a.g_value_old[p] = a.value_old[r];
-        const float ad = a.adv[r];
-        a.g_adv[p] = a.apply_adv_norm ? __fdiv_rn(__fsub_rn(ad, am), asd) : ad;
-        a.g_ret[p] = a.ret[r];
-      }
     }
+    if (al) {
+      a.g_action[p * a.A + lane] = mir ? act * asg : act;
+      a.g_mean_old[p * a.A + lane] = mir ? mo * asg : mo;
+    }
+    if (lane == 0) a.g_logp_old[p] = sc;
+    else if (lane == 1) a.g_value_old[p] = sc;
+    else if (lane == 2) a.g_adv[p] = a.apply_adv_norm ? __fdiv_rn(__fsub_rn(sc, am), asd) : sc;
+    else if (lane == 3) a.g_ret[p] = sc;
   }
 }
 
@@ -309,9 +307,12 @@ __global__ void norm_prepare_kernel(const float *m2, float count, int dim,
 
 // One warp per row (rows strided over the grid): lane i takes columns
 // i, i+32, ... of the padded row, so the index math has no division.
+// With perm/sign (the mirror augmentation) row r is first mapped by the
+// signed permutation: x'[i] = sign[i] * x[perm[i]].
 __global__ void normalize_rows_kernel(const float *x, int64_t n, int dim,
                                       int pitch, const float *mean,
-                                      const float *sd, float *out, int mode) {
+                                      const float *sd, float *out, int mode,
+                                      const int32_t *perm, const float *sign) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -320,7 +321,8 @@ __global__ void normalize_rows_kernel(const float *x, int64_t n, int dim,
     for (int i = lane; i < pitch; i += 32) {
       float y = 0.0f;
       if (i < dim) {
-        y = __fdiv_rn(__fsub_rn(xr[i], mean[i]), sd[i]);
+        const float v = perm ? xr[perm[i]] * sign[i] : xr[i];
+        y = __fdiv_rn(__fsub_rn(v, mean[i]), sd[i]);
         y = fminf(fmaxf(y, -5.0f), 5.0f);
       }
       store_operand(out, r * pitch + i, y, mode);
@@ -1154,9 +1156,9 @@ void launch_norm_prepare(const float *m2, float count, int dim, float *sd,
 
 void launch_normalize_rows(const float *x, int64_t n, int dim, int pitch,
                            const float *mean, const float *sd, float *out,
-                           int mode, cudaStream_t s) {
+                           int mode, cudaStream_t s, const int32_t *perm, const float *sign) {
   normalize_rows_kernel<<<grid_for(n * 32, 256), 256, 0, s>>>(x, n, dim, pitch, mean, sd, out,
-                                                               mode);
+                                                               mode, perm, sign);
 }
 
 void launch_round_copy(const float *src, float *dst, int64_t n, int mode, cudaStream_t s) {

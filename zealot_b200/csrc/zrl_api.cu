@@ -171,8 +171,15 @@ struct zrl_ctx {
   uint8_t *r_done = nullptr;
   int64_t env_cap = 0, r_cap = 0;
   // normalized observations of the whole batch, padded rows (computed once
-  // per update; the epochs permute rows of these)
-  float *n_xa = nullptr, *n_xc = nullptr;
+  // per update; the epochs permute rows of these), and with the mirror
+  // augmentation those of the mirrored rows (xm)
+  float *n_xa = nullptr, *n_xc = nullptr, *n_xma = nullptr, *n_xmc = nullptr;
+  int64_t n_xm_cap = 0;
+  // L/R mirror augmentation (biped_train_gpu.rs:89-185, 988-1003): signed
+  // permutations of the observation, critic observation and action spaces
+  bool mirror = false;
+  int32_t *mir_operm = nullptr, *mir_cperm = nullptr, *mir_aperm = nullptr;
+  float *mir_osign = nullptr, *mir_csign = nullptr, *mir_asign = nullptr;
   float *e_xa = nullptr, *e_xc = nullptr, *e_act = nullptr, *e_mo = nullptr;
   float *e_lpo = nullptr, *e_vo = nullptr, *e_adv = nullptr, *e_ret = nullptr;
   int32_t *order_dev = nullptr;
@@ -995,36 +1002,55 @@ static zrl_status adv_moments(zrl_ctx *ctx, const float *adv, int64_t n,
   return ZRL_OK;
 }
 
+struct DevBatch {
+  const float *obs, *cobs, *act, *mo, *lpo, *vo, *adv, *ret;
+};
+
 // Normalized, clamped (tf32-rounded in the tensor-core modes) observation
 // rows of the whole batch, padded to the GEMM pitch: Normalizer::normalize
 // (ppo.rs:196-205) applied once per update, since the normalizers do not
-// change during it.
+// change during it -- and, with the mirror augmentation, the same of the
+// mirrored rows (the normalizers apply to the mirrored raw observations,
+// as the reference normalizes mirror_sample's output).
 static zrl_status normalize_batch(zrl_ctx *ctx, const float *obs, const float *cobs,
                                   int64_t n) {
   if (n <= 0) return ZRL_OK;
   ProfSpan ps(ctx, "normalize");
-  launch_normalize_rows(obs, n, ctx->net[0].d[0], ctx->net[0].dp[0], ctx->obs_mean,
-                        ctx->obs_sd, ctx->n_xa, ctx->opmode(), ctx->stream);
-  launch_normalize_rows(cobs, n, ctx->net[1].d[0], ctx->net[1].dp[0], ctx->crit_mean,
-                        ctx->crit_sd, ctx->n_xc, ctx->opmode(), ctx->stream);
+  const NetLayout &La = ctx->net[0], &Lc = ctx->net[1];
+  launch_normalize_rows(obs, n, La.d[0], La.dp[0], ctx->obs_mean, ctx->obs_sd, ctx->n_xa,
+                        ctx->opmode(), ctx->stream);
+  launch_normalize_rows(cobs, n, Lc.d[0], Lc.dp[0], ctx->crit_mean, ctx->crit_sd, ctx->n_xc,
+                        ctx->opmode(), ctx->stream);
   ctx->launches += 2;
+  if (ctx->mirror) {
+    if (n > ctx->n_xm_cap) {
+      TRY(dalloc(ctx, &ctx->n_xma, n * La.dp[0]));
+      TRY(dalloc(ctx, &ctx->n_xmc, n * Lc.dp[0]));
+      ctx->n_xm_cap = n;
+    }
+    launch_normalize_rows(obs, n, La.d[0], La.dp[0], ctx->obs_mean, ctx->obs_sd, ctx->n_xma,
+                          ctx->opmode(), ctx->stream, ctx->mir_operm, ctx->mir_osign);
+    launch_normalize_rows(cobs, n, Lc.d[0], Lc.dp[0], ctx->crit_mean, ctx->crit_sd, ctx->n_xmc,
+                          ctx->opmode(), ctx->stream, ctx->mir_cperm, ctx->mir_csign);
+    ctx->launches += 2;
+  }
   CHECK_LAUNCH();
   return ZRL_OK;
 }
 
-static GatherArgs gather_args(zrl_ctx *ctx, const float *act, const float *mo,
-                              const float *lpo, const float *vo, const float *adv,
-                              const float *ret) {
+// The epoch gather's arguments (virtual rows [0, n_base) are the mirrored
+// copies of the n_base base rows when n_base > 0).
+static GatherArgs gather_args(zrl_ctx *ctx, const DevBatch &d, int64_t n_base) {
   GatherArgs g{};
   g.order = ctx->order_dev;
   g.xn_a = ctx->n_xa;
   g.xn_c = ctx->n_xc;
-  g.action = act;
-  g.mean_old = mo;
-  g.logp_old = lpo;
-  g.value_old = vo;
-  g.adv = adv;
-  g.ret = ret;
+  g.action = d.act;
+  g.mean_old = d.mo;
+  g.logp_old = d.lpo;
+  g.value_old = d.vo;
+  g.adv = d.adv;
+  g.ret = d.ret;
   g.A = ctx->A;
   g.odp = ctx->net[0].dp[0];
   g.cdp = ctx->net[1].dp[0];
@@ -1038,6 +1064,13 @@ static GatherArgs gather_args(zrl_ctx *ctx, const float *act, const float *mo,
   g.g_value_old = ctx->e_vo;
   g.g_adv = ctx->e_adv;
   g.g_ret = ctx->e_ret;
+  if (n_base > 0) {
+    g.n_base = n_base;
+    g.xm_a = ctx->n_xma;
+    g.xm_c = ctx->n_xmc;
+    g.m_aperm = ctx->mir_aperm;
+    g.m_asign = ctx->mir_asign;
+  }
   return g;
 }
 
@@ -1057,10 +1090,6 @@ static MbView epoch_view(zrl_ctx *ctx, int64_t off, int64_t rows) {
   v.rows = rows;
   return v;
 }
-
-struct DevBatch {
-  const float *obs, *cobs, *act, *mo, *lpo, *vo, *adv, *ret;
-};
 
 static zrl_status stage_batch(zrl_ctx *ctx, const zrl_batch *b, DevBatch *d,
                               bool need_adv_ret) {
@@ -1165,6 +1194,14 @@ static zrl_status queue_device_orders(zrl_ctx *ctx, uint64_t seed0, int64_t n_gl
 static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
                              const DevBatch &d, int64_t n_local,
                              int64_t n_global, int64_t row_offset) {
+  // the mirror augmentation doubles the batch: virtual rows [0, n) are the
+  // mirrored copies, [n, 2n) the samples themselves (biped_train_gpu.rs:
+  // 988-1003 puts the mirrored copies first); one rank only
+  const int64_t n_base = ctx->mirror ? n_local : 0;
+  if (ctx->mirror) {
+    n_local *= 2;
+    n_global *= 2;
+  }
   const int64_t mbs = cfg->minibatches;
   const int64_t mb = n_global / mbs;
   const float scale = 1.0f / (float)mb;
@@ -1221,12 +1258,12 @@ static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
       TRY(start_plan(ctx, Q, seed0 + (uint64_t)epochs * (uint64_t)mbs, n_global, n_local,
                      row_offset, epochs, (int)mbs));
   }
-  if (epochs > 0) TRY(normalize_batch(ctx, d.obs, d.cobs, n_local));
+  if (epochs > 0) TRY(normalize_batch(ctx, d.obs, d.cobs, n_base > 0 ? n_base : n_local));
   for (int e = 0; e < epochs; ++e) {
     if (!multi) P->jobs[e].wait();
     const int64_t n_rows = multi ? drows[e] : P->rows[e];
     if (n_rows > 0) {
-      GatherArgs g = gather_args(ctx, d.act, d.mo, d.lpo, d.vo, d.adv, d.ret);
+      GatherArgs g = gather_args(ctx, d, n_base);
       if (multi) {
         g.order = ctx->dplan.order + (int64_t)e * n_local;
       } else {
@@ -1383,6 +1420,8 @@ zrl_status zrl_create(const zrl_model_config *cfg, int device,
   for (int i = 0; i < cfg->n_critic_dims; ++i)
     if (cfg->critic_dims[i] < 1) return ZRL_INVALID_ARG;
   if (cfg->actor_dims[cfg->n_actor_dims - 1] > 128) return ZRL_NOT_SUPPORTED;
+  // the epoch gather normalizes observation rows up to 256 wide per warp
+  if (cfg->actor_dims[0] > 256 || cfg->critic_dims[0] > 256) return ZRL_NOT_SUPPORTED;
   if (cfg->precision < 0 || cfg->precision > 2) return ZRL_INVALID_ARG;
   zrl_ctx *ctx = new zrl_ctx();
   ctx->mcfg = *cfg;
@@ -1457,11 +1496,12 @@ zrl_status zrl_destroy(zrl_ctx *ctx) {
                     &ctx->obs_sd, &ctx->crit_mean, &ctx->crit_m2, &ctx->crit_sd,
                     &ctx->b_obs, &ctx->b_cobs, &ctx->b_act, &ctx->b_mo, &ctx->b_lpo,
                     &ctx->b_vo, &ctx->b_adv, &ctx->b_ret, &ctx->r_rew, &ctx->r_val,
-                    &ctx->r_lv, &ctx->n_xa, &ctx->n_xc, &ctx->e_xa, &ctx->e_xc, &ctx->e_act, &ctx->e_mo,
+                    &ctx->r_lv, &ctx->n_xa, &ctx->n_xc, &ctx->n_xma, &ctx->n_xmc, &ctx->e_xa, &ctx->e_xc, &ctx->e_act, &ctx->e_mo,
                     &ctx->e_lpo, &ctx->e_vo, &ctx->e_adv, &ctx->e_ret, &ctx->wpart,
                     &ctx->bpart, &ctx->rs.fpart, &ctx->Ptc, &ctx->pend_obs_mean,
                     &ctx->pend_obs_m2, &ctx->pend_crit_mean, &ctx->pend_crit_m2,
-                    &ctx->welford_scratch};
+                    &ctx->welford_scratch, &ctx->mir_osign, &ctx->mir_csign,
+                    &ctx->mir_asign};
   for (float **b : bufs)
     if (*b) cudaFree(*b);
   for (int k = 0; k < 2; ++k) {
@@ -1472,6 +1512,8 @@ zrl_status zrl_destroy(zrl_ctx *ctx) {
   }
   if (ctx->r_done) cudaFree(ctx->r_done);
   if (ctx->order_dev) cudaFree(ctx->order_dev);
+  for (int32_t *m : {ctx->mir_operm, ctx->mir_cperm, ctx->mir_aperm})
+    if (m) cudaFree(m);
   if (ctx->st) cudaFree(ctx->st);
   if (ctx->adv_part) cudaFree(ctx->adv_part);
   if (ctx->moments) cudaFree(ctx->moments);
@@ -1717,6 +1759,20 @@ static zrl_status check_batch(zrl_ctx *ctx, const zrl_batch *b, int64_t *n_globa
   return ZRL_OK;
 }
 
+// The update's sample count check (ppo.rs:340), on the mirrored batch's
+// doubled count when the augmentation is on (one rank only).
+static zrl_status check_mirror(zrl_ctx *ctx, const zrl_batch *b, const zrl_ppo_config *cfg,
+                               int64_t n_global) {
+  if (ctx->mirror && ctx->comm.world > 1) {
+    ctx->err = "the mirror augmentation runs on one rank";
+    return ZRL_NOT_SUPPORTED;
+  }
+  const int64_t n = ctx->mirror ? 2 * n_global : n_global;
+  if (n < cfg->minibatches) return bad(ctx, "fewer samples than minibatches");
+  (void)b;
+  return ZRL_OK;
+}
+
 static zrl_status write_back_adv(zrl_ctx *ctx, zrl_batch *b, const float *adv_dev) {
   if (!b->write_back_adv || b->n == 0) return ZRL_OK;
   // normalized advantages in the batch's own row order (ppo.rs:346-348):
@@ -1743,10 +1799,11 @@ zrl_status zrl_update(zrl_ctx *ctx, const zrl_ppo_config *cfg, zrl_batch *batch,
   int64_t n_global = 0;
   TRY(check_batch(ctx, batch, &n_global));
   if (batch->n > 0 && (!batch->adv || !batch->ret)) return bad(ctx, "null adv/ret");
-  if (n_global < cfg->minibatches) return bad(ctx, "fewer samples than minibatches");
+  TRY(check_mirror(ctx, batch, cfg, n_global));
   CK(cudaSetDevice(ctx->device));
   cudaEvent_t u0 = nullptr;
   prof_begin(ctx, &u0);
+  TRY(ensure_batch(ctx, ctx->mirror ? 2 * batch->n : batch->n));  // the doubled epoch rows
   DevBatch d{};
   TRY(stage_batch(ctx, batch, &d, true));
   TRY(adv_moments(ctx, d.adv, batch->n, n_global, false, 0));
@@ -1764,10 +1821,11 @@ zrl_status zrl_gae_update(zrl_ctx *ctx, const zrl_ppo_config *cfg,
   TRY(check_batch(ctx, batch, &n_global));
   if (ro->n_envs * ro->T != batch->n) return bad(ctx, "rollout and batch disagree on n");
   if (ro->T > 4096) return bad(ctx, "T larger than 4096 is not supported");
-  if (n_global < cfg->minibatches) return bad(ctx, "fewer samples than minibatches");
+  TRY(check_mirror(ctx, batch, cfg, n_global));
   CK(cudaSetDevice(ctx->device));
   cudaEvent_t u0 = nullptr;
   prof_begin(ctx, &u0);
+  TRY(ensure_batch(ctx, ctx->mirror ? 2 * batch->n : batch->n));  // the doubled epoch rows
   DevBatch d{};
   TRY(stage_batch(ctx, batch, &d, false));
   TRY(ensure_envs(ctx, ro->n_envs, ro->T));
@@ -1962,7 +2020,7 @@ zrl_status zrl_minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
   CK(cudaMemcpyAsync(ctx->order_dev, ctx->order_pinned, sizeof(int32_t) * n_idx,
                      cudaMemcpyHostToDevice, ctx->stream));
   TRY(normalize_batch(ctx, d.obs, d.cobs, batch->n));
-  GatherArgs g = gather_args(ctx, d.act, d.mo, d.lpo, d.vo, d.adv, d.ret);
+  GatherArgs g = gather_args(ctx, d, 0);
   g.n_used = n_idx;
   g.apply_adv_norm = 0;  // the hook takes advantages as given
   launch_gather(g, ctx->stream);
@@ -1994,6 +2052,49 @@ zrl_status zrl_apply_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg, const float 
   ctx->t_logstd_host += 1;
   float lr = 0.0f;
   return zrl_get_lr(ctx, &lr);
+}
+
+zrl_status zrl_set_mirror(zrl_ctx *ctx, const int32_t *obs_perm, const float *obs_sign,
+                          const int32_t *cobs_perm, const float *cobs_sign,
+                          const int32_t *act_perm, const float *act_sign) {
+  if (!ctx) return ZRL_INVALID_ARG;
+  if (!obs_perm) {
+    ctx->mirror = false;
+    return ZRL_OK;
+  }
+  if (!obs_sign || !cobs_perm || !cobs_sign || !act_perm || !act_sign)
+    return bad(ctx, "the mirror needs all six arrays");
+  // each a signed permutation: perm a permutation of 0..d-1, sign +-1
+  auto valid = [](const int32_t *perm, const float *sign, int d) {
+    std::vector<char> seen(d, 0);
+    for (int i = 0; i < d; ++i) {
+      if (perm[i] < 0 || perm[i] >= d || seen[perm[i]]) return false;
+      seen[perm[i]] = 1;
+      if (sign[i] != 1.0f && sign[i] != -1.0f) return false;
+    }
+    return true;
+  };
+  const int od = ctx->net[0].d[0], cd = ctx->net[1].d[0], A = ctx->A;
+  if (!valid(obs_perm, obs_sign, od) || !valid(cobs_perm, cobs_sign, cd) ||
+      !valid(act_perm, act_sign, A))
+    return bad(ctx, "mirror: perm must be a permutation and sign +-1");
+  CK(cudaSetDevice(ctx->device));
+  if (!ctx->mir_operm) {
+    TRY(dalloc(ctx, &ctx->mir_operm, od));
+    TRY(dalloc(ctx, &ctx->mir_cperm, cd));
+    TRY(dalloc(ctx, &ctx->mir_aperm, A));
+    TRY(dalloc(ctx, &ctx->mir_osign, od));
+    TRY(dalloc(ctx, &ctx->mir_csign, cd));
+    TRY(dalloc(ctx, &ctx->mir_asign, A));
+  }
+  CK(cudaMemcpy(ctx->mir_operm, obs_perm, 4 * od, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(ctx->mir_cperm, cobs_perm, 4 * cd, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(ctx->mir_aperm, act_perm, 4 * A, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(ctx->mir_osign, obs_sign, 4 * od, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(ctx->mir_csign, cobs_sign, 4 * cd, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(ctx->mir_asign, act_sign, 4 * A, cudaMemcpyHostToDevice));
+  ctx->mirror = true;
+  return ZRL_OK;
 }
 
 zrl_status zrl_set_wait_limit(zrl_ctx *ctx, uint64_t ns) {

@@ -91,12 +91,19 @@ void launch_adv_sqdev(const float *adv, int64_t n, const double *moments,
 void launch_adv_finalize(const double *moments, int64_t n_global, DevState *st,
                          cudaStream_t s);
 
-// Epoch gather: rows order[p] of the raw batch -> position p, with the
-// observation normalizers and the advantage normalization applied.
+// Epoch gather: rows order[p] of the batch -> position p: the observation
+// rows from their normalized copies (Normalizer::normalize applied once per
+// update, ppo.rs:196-205), the advantage normalization (ppo.rs:346-348)
+// applied to adv.  With the mirror augmentation on (n_base > 0) the batch
+// is 2 n_base virtual rows: row r < n_base is the L/R mirror of base row r
+// (biped_train_gpu.rs:89-185: its observation rows from the normalized
+// mirrored copies xm_a / xm_c, its action and mean_old through the action
+// space's signed permutation), row r >= n_base is base row r - n_base.
 struct GatherArgs {
-  const int32_t *order;  // [n_used] local row indices
+  const int32_t *order;  // [n_used] local (virtual) row indices
   int64_t n_used;
   const float *xn_a, *xn_c;  // normalized observation rows, pitch odp / cdp
+  const float *xm_a, *xm_c;  // the same of the mirrored rows (mirror on)
   const float *action, *mean_old, *logp_old, *value_old, *adv, *ret;
   int A;
   int odp, cdp;           // padded row pitch (multiples of 32 elements)
@@ -106,14 +113,19 @@ struct GatherArgs {
   float *g_action, *g_mean_old;         // [n_used, A]
   float *g_logp_old, *g_value_old, *g_adv, *g_ret;
   int apply_adv_norm;
+  int64_t n_base;       // mirror augmentation: base rows (0 = off)
+  const int32_t *m_aperm;  // action space: (P a)[k] = sign[k] * a[perm[k]]
+  const float *m_asign;
 };
 void launch_gather(const GatherArgs &a, cudaStream_t s);
 // Normalizer divisors: sd = sqrt(max(m2/count, 1e-8)) (ppo.rs:201-202).
 void launch_norm_prepare(const float *m2, float count, int dim, float *sd,
                          cudaStream_t s);
+// perm/sign (optional): rows mapped by a signed permutation first.
 void launch_normalize_rows(const float *x, int64_t n, int dim, int pitch,
                            const float *mean, const float *sd, float *out,
-                           int mode, cudaStream_t s);
+                           int mode, cudaStream_t s, const int32_t *perm = nullptr,
+                           const float *sign = nullptr);
 // dst = tf32(src) (round to nearest) over n floats.
 // dst[i] = src[i] stored as `mode` says (1 tf32-rounded fp32, 2 bf16).
 void launch_round_copy(const float *src, float *dst, int64_t n, int mode, cudaStream_t s);

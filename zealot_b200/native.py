@@ -127,6 +127,7 @@ _SIGS = {
     "zrl_rank_orders_device": (C.c_int64, [_P, C.c_uint64, C.c_int64, C.c_int64, C.c_int64,
                                            C.c_int32, _P, _P]),
     "zrl_kernel_launches": (C.c_int64, [_P]),
+    "zrl_set_mirror": (C.c_int, [_P, _P, _P, _P, _P, _P, _P]),
     "zrl_set_wait_limit": (C.c_int, [_P, C.c_uint64]),
     "zrl_test_stall_next_gemm": (C.c_int, [_P]),
     "zrl_test_comm_wait": (C.c_int, [C.c_int32, C.c_int32, C.POINTER(C.c_int32)]),

@@ -285,6 +285,21 @@ class ActorCritic:
         o, c, n, dev = self._obs_rows(obs, critic_obs)
         self.ctx.call("zrl_record_obs_ex", N.ptr(o), N.ptr(c), n, dev, 1 if parallel else 0)
 
+    def set_mirror(self, obs, critic_obs=None, action=None):
+        """The L/R mirror augmentation (biped_train_gpu.rs:89-185, 988-1003):
+        each argument a (perm, sign) pair of a signed permutation
+        (P x)[i] = sign[i] * x[perm[i]]; obs=None turns it off.  Updates then
+        train on the mirrored copies of the batch followed by the batch."""
+        if obs is None:
+            self.ctx.call("zrl_set_mirror", None, None, None, None, None, None)
+            self._mirror = None
+            return
+        arrs = []
+        for perm, sign in (obs, critic_obs, action):
+            arrs += [np.ascontiguousarray(perm, np.int32), np.ascontiguousarray(sign, np.float32)]
+        self.ctx.call("zrl_set_mirror", *[N.ptr(a) for a in arrs])
+        self._mirror = arrs
+
     # -- the trainer's frozen-normalizer flow (PendingNorm, ppo.rs:118-195)
     def pending_push(self, obs, critic_obs, parallel=False):
         """PendingNorm::push (ppo.rs:126-136) of rows into the pending
