@@ -47,6 +47,8 @@ def parse():
     p.add_argument("--precision", default=None, choices=["tf32", "fp32", "bf16"])
     p.add_argument("--envs-per-gpu", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-other-configs", action="store_true",
+                   help="skip the C3 rollout-step and C5 wide-update measurements")
     p.add_argument("--profile-only", action="store_true",
                    help="run warmup+steps without clocks/baselines (for ncu)")
     p.add_argument("--traffic-csv", default=None,
@@ -356,17 +358,23 @@ def bench_c3(args):
     repeated for the T = 24 steps of a rollout.  Latency per step and
     samples/s; one GPU (other ranks exit)."""
     import torch
-    from zealot_b200 import native as N
-    from zealot_b200 import synth
-    from zealot_b200 import zealot_rl as Z
     if int(os.environ.get("RANK", "0")) != 0:
         return
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
+    line = measure_c3(args.steps, args.warmup, args.precision or "tf32", local)
+    print(json.dumps(line), flush=True)
+
+
+def measure_c3(steps, warmup, precision, local):
+    import torch
+    from zealot_b200 import native as N
+    from zealot_b200 import synth
+    from zealot_b200 import zealot_rl as Z
     dev = torch.device("cuda", local)
     n, T = 4096, 24
     adims, cdims = synth.WORKLOADS["c2"].actor_dims, synth.WORKLOADS["c2"].critic_dims
-    ac = Z.ActorCritic(adims, cdims, precision=args.precision or "tf32", device=local)
+    ac = Z.ActorCritic(adims, cdims, precision=precision, device=local)
     ac.params = synth.xavier_params(np.random.default_rng(1234), adims, cdims)
     g = torch.Generator(device="cpu").manual_seed(7)
     obs = torch.randn(T, n, adims[0], generator=g).to(dev)
@@ -383,11 +391,11 @@ def bench_c3(args):
             ac.ctx.call("zrl_policy_step", obs[t].data_ptr(), cobs[t].data_ptr(), n, seed, t,
                         act.data_ptr(), lp.data_ptr(), mean.data_ptr(), val.data_ptr(), 1)
 
-    for i in range(args.warmup):
+    for i in range(warmup):
         rollout(i)
     times = []
     l0 = ac.kernel_launches()
-    for i in range(args.steps):
+    for i in range(steps):
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -396,20 +404,80 @@ def bench_c3(args):
         e1.synchronize()
         times.append(e0.elapsed_time(e1))
     ms = sum(times) / len(times)
-    launches = (ac.kernel_launches() - l0) // args.steps
+    launches = (ac.kernel_launches() - l0) // steps
     line = {"metric": "rollout-step samples/s (policy forward + Gaussian sampling + logp)",
             "value": n * T / (ms * 1e-3), "unit": "samples/s", "n_gpus": 1,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "steps": steps, "warmup": warmup, "ms_per_step": ms,
             "ms_per_rollout_step": ms / T, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": args.precision or "tf32",
+            "vs_baseline": None, "dtype": precision,
             "data": "synthetic obs ~N(0,1), Xavier-uniform init",
             "config": {"workload": "c3", "batch": n, "T": T, "actor": list(adims),
                        "critic": list(cdims),
                        "note": "one step = a T-step rollout of policy steps; each policy "
                                "step returns when its outputs are on the device"},
             "gpu_launches": int(launches)}
-    print(json.dumps(line), flush=True)
     ac.close()
+    return line
+
+
+def measure_update(name, steps, warmup, local):
+    """Device-resident update throughput of another workload on this GPU
+    (CUDA events on the library's stream, 512 MiB L2 flush between timed
+    updates), with its GEMMs' tensor-core throughput from a profiled
+    update."""
+    import ctypes as C
+
+    import torch
+    from zealot_b200 import native as N
+    from zealot_b200 import synth
+    from zealot_b200 import zealot_rl as Z
+    dev = torch.device("cuda", local)
+    w = synth.WORKLOADS[name]
+    ac = Z.ActorCritic(w.actor_dims, w.critic_dims, precision=w.precision, device=local)
+    params = synth.xavier_params(np.random.default_rng(1234), w.actor_dims, w.critic_dims)
+    ac.params = params
+    ac.lr = w.lr
+    ro = synth.make_rollout(1000, w.n_envs, w.T, w.actor_dims, w.critic_dims,
+                            lambda p, o, c: ac.forward(o, c), params=params)
+
+    def dt_(a, dtype=torch.float32):
+        return torch.from_numpy(np.ascontiguousarray(a)).to(dev, dtype)
+
+    d = {f: dt_(getattr(ro, f)) for f in ("obs", "critic_obs", "action", "mean_old",
+                                          "logp_old", "value_old")}
+    b = Z.SoaBatch(adv=torch.zeros(ro.n, device=dev), ret=torch.zeros(ro.n, device=dev), **d)
+    rew, val = dt_(ro.rewards), dt_(ro.value_old.reshape(ro.n_envs, ro.T))
+    done, lv = dt_(ro.dones, torch.uint8), dt_(ro.last_values)
+    cfg = Z.PpoConfig(epochs=w.epochs, minibatches=w.minibatches, adaptive_lr=True)
+    stream = torch.cuda.ExternalStream(N.lib().zrl_stream(ac.ctx.h), device=dev)
+    flush = torch.empty(512 * 1024 * 1024 // 4, device=dev)
+    for _ in range(warmup):
+        ac.gae_update(rew, val, done, lv, b, cfg, ro.n, 0)
+    times = []
+    for _ in range(steps):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ac.gae_update(rew, val, done, lv, b, cfg, ro.n, 0)
+        e1.record(stream)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = sum(times) / len(times)
+    N.check(N.lib().zrl_set_profiling(ac.ctx.h, 1), ac.ctx.h)
+    ac.gae_update(rew, val, done, lv, b, cfg, ro.n, 0)
+    g_ms, u_ms, g_n = C.c_float(), C.c_float(), C.c_int64()
+    N.lib().zrl_get_profile(ac.ctx.h, C.byref(g_ms), C.byref(u_ms), C.byref(g_n))
+    fl = flops_per_sample_pass(w.actor_dims, w.critic_dims) * ro.n * w.epochs
+    ac.close()
+    del flush
+    return {"workload": name, "samples_per_update": ro.n, "epochs": w.epochs,
+            "minibatches": w.minibatches, "actor": list(w.actor_dims),
+            "critic": list(w.critic_dims), "dtype": w.precision, "steps": steps,
+            "warmup": warmup, "ms_per_update": ms, "samples_per_s": ro.n / (ms * 1e-3),
+            "gemm_ms_per_update": g_ms.value,
+            "gemm_tflops": fl / (g_ms.value * 1e-3) / 1e12 if g_ms.value > 0 else None,
+            "algorithmic_gflop_per_update": fl / 1e9}
 
 
 def main():
@@ -641,6 +709,12 @@ def main():
                              "algorithmic_gb_per_update": upd_bytes / 1e9,
                              "how": "GEMM FLOPs / tensor peak + update bytes / HBM copy bandwidth"}}
     cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline(w)
+    # the other single-GPU configurations, timed on this GPU in the same run
+    # (the rollout step; configs[4]: the wide bf16 pair)
+    others = None
+    if world == 1 and not args.no_other_configs and (args.config or "c2") == "c2":
+        others = {"c3": measure_c3(10, 3, "tf32", local),
+                  "c5": measure_update("c5", 3, 2, local)}
     line = {"metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
@@ -654,7 +728,7 @@ def main():
             "e2e": {"value": n_global / (e2e_ms * 1e-3), "unit": "samples/s",
                     "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes},
             "gpu_launches": int(launches),
-            "roofline": roof, "clocks": clk, "cpu_baseline": cpu,
+            "roofline": roof, "clocks": clk, "cpu_baseline": cpu, "other_configs": others,
             "stats_last": {"kl": st.kl, "surrogate": st.surrogate,
                            "value_loss": st.value_loss, "entropy": st.entropy, "lr": st.lr}}
     print(json.dumps(line), flush=True)
