@@ -137,6 +137,22 @@ def test_update_matches_oracle_fp32(adaptive, epochs, minibatches):
     assert gpu.adam_state()[0].tolist() == [epochs * minibatches] * 3
 
 
+def test_update_wide_action_space_fp32():
+    """An action space wider than a warp (40 dimensions): the epoch gather
+    copies action and mean_old rows with its wide-row loop and the loss runs
+    a warp per sample with lanes holding dims k and k + 32."""
+    case = Case((12, 64, 32, 40), SMALL_C, n_envs=10, T=16, seed=9, perturb=0.03,
+                norm_stats=True)
+    cfg = Z.PpoConfig(epochs=2, minibatches=2)
+    ocfg = O.PpoConfig(epochs=2, minibatches=2)
+    gpu = case.gpu_ac("fp32")
+    st = gpu.update(case.soa(), cfg)
+    dp, st2, orc, drift = oracle_update_with_drift(case, ocfg)
+    assert_update_close(gpu.params - case.params, dp, drift, case.adims, case.cdims)
+    for k in ("kl", "surrogate", "value_loss", "entropy"):
+        assert abs(getattr(st, k) - st2[k]) <= 1e-4 * max(abs(st2[k]), 1e-3), (k, st, st2)
+
+
 def test_update_c1_matches_oracle_fp32():
     # BASELINE configs[0]: N=64 x T=24, 1 epoch x 1 minibatch, lr 1e-3
     # (a fresh rollout: each side records mean_old/logp_old with its own

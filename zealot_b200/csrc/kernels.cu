@@ -244,52 +244,89 @@ __global__ void adv_finalize_kernel(const double *moments, int64_t n_global,
 __global__ void gather_kernel(GatherArgs a) {
   pdl_wait();
   pdl_trigger();
+  constexpr int R = 2;  // rows per warp and pass, their loads all in flight together
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const float am = a.st->adv_mean, asd = a.st->adv_sd;
   // 16-byte pieces per padded observation row
   const int qa = a.odp * a.x_bytes / 16, qc = a.cdp * a.x_bytes / 16;
+  const bool small = qa <= 32 && qc <= 32 && a.A <= 32;
   const bool al = lane < a.A;
   const int ai = al && a.n_base > 0 ? a.m_aperm[lane] : lane;
   const float asg = al && a.n_base > 0 ? a.m_asign[lane] : 1.0f;
-  for (int64_t p = warp; p < a.n_used; p += nwarps) {
-    const int64_t r = a.order[p];
-    const bool mir = a.n_base > 0 && r < a.n_base;
-    const int64_t src = a.n_base > 0 ? (mir ? r : r - a.n_base) : r;
-    const float4 *xa = reinterpret_cast<const float4 *>(mir ? a.xm_a : a.xn_a) + src * qa;
-    const float4 *xc = reinterpret_cast<const float4 *>(mir ? a.xm_c : a.xn_c) + src * qc;
-    float4 *ya = reinterpret_cast<float4 *>(a.x_a) + p * qa;
-    float4 *yc = reinterpret_cast<float4 *>(a.x_c) + p * qc;
-    // every load of the row first, then every store
-    float act = 0.0f, mo = 0.0f, sc = 0.0f;
-    if (al) {
-      const int kk = mir ? ai : lane;
-      act = a.action[src * a.A + kk];
-      mo = a.mean_old[src * a.A + kk];
+  for (int64_t p0 = warp * R; p0 < a.n_used; p0 += nwarps * R) {
+    int64_t src[R];
+    bool mir[R], live[R];
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+      live[u] = p0 + u < a.n_used;
+      const int64_t r = live[u] ? a.order[p0 + u] : 0;
+      mir[u] = a.n_base > 0 && r < a.n_base;
+      src[u] = a.n_base > 0 ? (mir[u] ? r : r - a.n_base) : r;
     }
-    if (lane == 0) sc = a.logp_old[src];
-    else if (lane == 1) sc = a.value_old[src];
-    else if (lane == 2) sc = a.adv[src];
-    else if (lane == 3) sc = a.ret[src];
-    if (qa <= 32 && qc <= 32) {
-      float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vc = va;
-      if (lane < qa) va = xa[lane];
-      if (lane < qc) vc = xc[lane];
-      if (lane < qa) ya[lane] = va;
-      if (lane < qc) yc[lane] = vc;
-    } else {
-      for (int i = lane; i < qa; i += 32) ya[i] = xa[i];
-      for (int i = lane; i < qc; i += 32) yc[i] = xc[i];
+    if (small) {
+      // every load of both rows first, then every store
+      float4 va[R], vc[R];
+      float act[R], mo[R], sc[R];
+#pragma unroll
+      for (int u = 0; u < R; ++u) {
+        const float4 *xa = reinterpret_cast<const float4 *>(mir[u] ? a.xm_a : a.xn_a) + src[u] * qa;
+        const float4 *xc = reinterpret_cast<const float4 *>(mir[u] ? a.xm_c : a.xn_c) + src[u] * qc;
+        va[u] = live[u] && lane < qa ? xa[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+        vc[u] = live[u] && lane < qc ? xc[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+        act[u] = mo[u] = sc[u] = 0.0f;
+        if (live[u] && al) {
+          const int kk = mir[u] ? ai : lane;
+          act[u] = a.action[src[u] * a.A + kk];
+          mo[u] = a.mean_old[src[u] * a.A + kk];
+        }
+        if (live[u] && lane < 4) {
+          const float *col = lane == 0 ? a.logp_old : lane == 1 ? a.value_old
+                           : lane == 2 ? a.adv : a.ret;
+          sc[u] = col[src[u]];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < R; ++u) {
+        if (!live[u]) break;
+        const int64_t p = p0 + u;
+        if (lane < qa) reinterpret_cast<float4 *>(a.x_a)[p * qa + lane] = va[u];
+        if (lane < qc) reinterpret_cast<float4 *>(a.x_c)[p * qc + lane] = vc[u];
+        if (al) {
+          a.g_action[p * a.A + lane] = mir[u] ? act[u] * asg : act[u];
+          a.g_mean_old[p * a.A + lane] = mir[u] ? mo[u] * asg : mo[u];
+        }
+        if (lane == 0) a.g_logp_old[p] = sc[u];
+        else if (lane == 1) a.g_value_old[p] = sc[u];
+        else if (lane == 2)
+          a.g_adv[p] = a.apply_adv_norm ? __fdiv_rn(__fsub_rn(sc[u], am), asd) : sc[u];
+        else if (lane == 3) a.g_ret[p] = sc[u];
+      }
+      continue;
     }
-    if (al) {
-      a.g_action[p * a.A + lane] = mir ? act * asg : act;
-      a.g_mean_old[p * a.A + lane] = mir ? mo * asg : mo;
+    // wide rows (more than 512 bytes, or more than 32 action dimensions)
+    for (int u = 0; u < R; ++u) {
+      if (!live[u]) break;
+      const int64_t p = p0 + u;
+      const float4 *xa = reinterpret_cast<const float4 *>(mir[u] ? a.xm_a : a.xn_a) + src[u] * qa;
+      const float4 *xc = reinterpret_cast<const float4 *>(mir[u] ? a.xm_c : a.xn_c) + src[u] * qc;
+      for (int i = lane; i < qa; i += 32) reinterpret_cast<float4 *>(a.x_a)[p * qa + i] = xa[i];
+      for (int i = lane; i < qc; i += 32) reinterpret_cast<float4 *>(a.x_c)[p * qc + i] = xc[i];
+      for (int k = lane; k < a.A; k += 32) {
+        const int kk = mir[u] ? a.m_aperm[k] : k;
+        const float sg = mir[u] ? a.m_asign[k] : 1.0f;
+        a.g_action[p * a.A + k] = a.action[src[u] * a.A + kk] * sg;
+        a.g_mean_old[p * a.A + k] = a.mean_old[src[u] * a.A + kk] * sg;
+      }
+      if (lane == 0) {
+        a.g_logp_old[p] = a.logp_old[src[u]];
+        a.g_value_old[p] = a.value_old[src[u]];
+        const float v = a.adv[src[u]];
+        a.g_adv[p] = a.apply_adv_norm ? __fdiv_rn(__fsub_rn(v, am), asd) : v;
+        a.g_ret[p] = a.ret[src[u]];
+      }
     }
-    if (lane == 0) a.g_logp_old[p] = sc;
-    else if (lane == 1) a.g_value_old[p] = sc;
-    else if (lane == 2) a.g_adv[p] = a.apply_adv_norm ? __fdiv_rn(__fsub_rn(sc, am), asd) : sc;
-    else if (lane == 3) a.g_ret[p] = sc;
   }
 }
 
@@ -309,23 +346,36 @@ __global__ void norm_prepare_kernel(const float *m2, float count, int dim,
 // i, i+32, ... of the padded row, so the index math has no division.
 // With perm/sign (the mirror augmentation) row r is first mapped by the
 // signed permutation: x'[i] = sign[i] * x[perm[i]].
-__global__ void normalize_rows_kernel(const float *x, int64_t n, int dim,
-                                      int pitch, const float *mean,
-                                      const float *sd, float *out, int mode,
-                                      const int32_t *perm, const float *sign) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t r = warp; r < n; r += nwarps) {
-    const float *xr = x + r * dim;
-    for (int i = lane; i < pitch; i += 32) {
+// One thread per padded column (blockDim = pitch, at most 256), a block per
+// group of kNormRows rows: every row's load is issued before the first
+// division, so each warp keeps kNormRows 128-byte loads in flight.
+constexpr int kNormRows = 8;
+
+__global__ void normalize_rows_kernel(const float *__restrict__ x, int64_t n, int dim,
+                                      int pitch, const float *__restrict__ mean,
+                                      const float *__restrict__ sd, float *__restrict__ out,
+                                      int mode, const int32_t *__restrict__ perm,
+                                      const float *__restrict__ sign) {
+  const int i = threadIdx.x;
+  const bool col = i < dim;
+  const int src = col ? (perm ? perm[i] : i) : 0;
+  const float sg = col && perm ? sign[i] : 1.0f;
+  const float mu = col ? mean[i] : 0.0f, s = col ? sd[i] : 1.0f;
+  for (int64_t r0 = (int64_t)blockIdx.x * kNormRows; r0 < n; r0 += (int64_t)gridDim.x * kNormRows) {
+    float v[kNormRows];
+#pragma unroll
+    for (int u = 0; u < kNormRows; ++u)
+      v[u] = col && r0 + u < n ? x[(r0 + u) * dim + src] : 0.0f;
+#pragma unroll
+    for (int u = 0; u < kNormRows; ++u) {
+      if (r0 + u >= n) break;
       float y = 0.0f;
-      if (i < dim) {
-        const float v = perm ? xr[perm[i]] * sign[i] : xr[i];
-        y = __fdiv_rn(__fsub_rn(v, mean[i]), sd[i]);
+      if (col) {
+        const float vv = perm ? v[u] * sg : v[u];
+        y = __fdiv_rn(__fsub_rn(vv, mu), s);
         y = fminf(fmaxf(y, -5.0f), 5.0f);
       }
-      store_operand(out, r * pitch + i, y, mode);
+      store_operand(out, (r0 + u) * pitch + i, y, mode);
     }
   }
 }
@@ -992,6 +1042,219 @@ __global__ void adam_kernel(AdamArgs a) {
   }
 }
 
+// ------------------------------------------------ reduce + pre-step + Adam
+
+// One rank's whole stepping half of a minibatch (ppo.rs:462-489) in one
+// cooperative launch, every block resident at once:
+//  A. the segment reduce (the work of reduce_segments_kernel's blocks,
+//     taken in turn by this grid's blocks), with each block's squared norms
+//     of what it wrote, per net;
+//  B. a grid barrier, then every block folds the block norms in block
+//     order (the same bits in every block) and computes the pre-step's
+//     scalars from the state it read before the barrier -- block 0 alone
+//     writes them back (statistics, adaptive LR, clip scales, Adam steps);
+//  C. Adam over the parameter buffer with those scalars.
+// The barrier is a counter that only grows: this launch waits for it to
+// reach `target` (the host adds the grid size per launch); its wait is
+// bounded (error code 8 in *err, then the block goes on).
+struct PreScalars {
+  float lr, clip[2], bc1[3], bc2[3];
+  int32_t t[3];
+};
+
+__device__ PreScalars prestep_scalars(const PrestepArgs &a, float lr, const int32_t *t_old,
+                                      float kl, double na, double nc) {
+  PreScalars o;
+  if (a.adaptive_lr) {
+    if (kl > a.desired_kl * 2.0f)
+      lr = fmaxf(__fdiv_rn(lr, 1.5f), a.lr_min);
+    else if (kl > 0.0f && kl < a.desired_kl / 2.0f)
+      lr = fminf(__fmul_rn(lr, 1.5f), a.lr_max);
+  }
+  o.lr = lr;
+  const float norms[2] = {__fsqrt_rn((float)na), __fsqrt_rn((float)nc)};
+  for (int j = 0; j < 2; ++j)
+    o.clip[j] = (norms[j] > a.max_grad_norm && norms[j] > 0.0f)
+                    ? __fdiv_rn(a.max_grad_norm, norms[j]) : 1.0f;
+  for (int j = 0; j < 3; ++j) {
+    o.t[j] = t_old[j] + 1;
+    o.bc1[j] = __fsub_rn(1.0f, powi_f(0.9f, o.t[j]));
+    o.bc2[j] = __fsub_rn(1.0f, powi_f(0.999f, o.t[j]));
+  }
+  return o;
+}
+
+__global__ void __launch_bounds__(kRsThreads, 2)
+reduce_step_kernel(ReduceSegs segs, PrestepArgs pa, AdamArgs aa, double *partials,
+                   unsigned int *bar, unsigned int target, int *err, int items) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ double sh[32];
+  __shared__ float4 part[kRsThreads];
+  DevState *st = pa.st;
+  // the pre-step's inputs, read before the barrier: after it block 0
+  // overwrites the state and every block's Adam writes log_std
+  const float lr_old = st->lr;
+  const int32_t t_old[3] = {st->t[0], st->t[1], st->t[2]};
+  float ent = 0.0f;  // entropy of the pre-step log_std (ppo.rs:308-311, 473)
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    const float c0 = __fadd_rn(0.5f, kLogSqrt2Pi);
+    for (int k = 0; k < pa.A; ++k) ent = __fadd_rn(ent, __fadd_rn(pa.log_std[k], c0));
+  }
+  // ---- A: the reduce
+  double sq[2] = {0.0, 0.0};
+  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    int si = 0;
+    while (si + 1 < segs.n && item >= segs.first_block[si + 1]) ++si;
+    const int b = item - segs.first_block[si];
+    const int64_t count4 = segs.seg[si].count / 4;
+    const int splits = segs.seg[si].splits;
+    const int64_t stride4 = segs.seg[si].stride / 4;
+    const int G = segs.groups[si];
+    const int cols4 = kRsThreads / G;
+    const int c = threadIdx.x & (cols4 - 1), grp = threadIdx.x / cols4;
+    const int64_t i4 = (int64_t)b * cols4 + c;
+    const bool live = i4 < count4;
+    const float4 *src = reinterpret_cast<const float4 *>(segs.seg[si].src) + i4;
+    float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (live) {
+      for (int z0 = grp; z0 < splits; z0 += 8 * G) {
+        float4 x[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int z = z0 + u * G;
+          x[u] = z < splits ? __ldcs(src + (int64_t)z * stride4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          t.x += x[u].x;
+          t.y += x[u].y;
+          t.z += x[u].z;
+          t.w += x[u].w;
+        }
+      }
+    }
+    __syncthreads();  // part[] of the previous item is no longer read
+    part[threadIdx.x] = t;
+    __syncthreads();
+    for (int h = G >> 1; h >= 1; h >>= 1) {
+      if (grp < h) {
+        const float4 x = part[threadIdx.x + h * cols4];
+        t.x += x.x;
+        t.y += x.y;
+        t.z += x.z;
+        t.w += x.w;
+        part[threadIdx.x] = t;
+      }
+      __syncthreads();
+    }
+    if (grp == 0 && live) {
+      reinterpret_cast<float4 *>(segs.seg[si].dst)[i4] = t;
+      const int net = segs.net[si];
+      if (net >= 0)
+        sq[net] += (double)t.x * t.x + (double)t.y * t.y + (double)t.z * t.z + (double)t.w * t.w;
+    }
+  }
+  const double ba = block_sum(sq[0], sh);
+  const double bc = block_sum(sq[1], sh);
+  if (threadIdx.x == 0) {
+    partials[2 * blockIdx.x] = ba;
+    partials[2 * blockIdx.x + 1] = bc;
+  }
+  // ---- B: grid barrier, norms, pre-step scalars
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    atomicAdd(bar, 1u);
+    unsigned int seen = 0;
+    for (uint32_t i = 0;; ++i) {
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(seen) : "l"(bar) : "memory");
+      if ((int)(seen - target) >= 0) break;
+      if (i > (1u << 22)) {  // about a second of 256 ns naps: give up
+        atomicExch(err, 8);
+        break;
+      }
+      __nanosleep(256);
+    }
+  }
+  __syncthreads();
+  double na = 0.0, nc = 0.0;
+  for (int bb = threadIdx.x; bb < (int)gridDim.x; bb += blockDim.x) {
+    na += __ldcg(&partials[2 * bb]);
+    nc += __ldcg(&partials[2 * bb + 1]);
+  }
+  na = block_sum(na, sh);
+  nc = block_sum(nc, sh);
+  __shared__ PreScalars ps;
+  if (threadIdx.x == 0) {
+    const float kl = __ldcg(pa.sums3 + 2);
+    ps = prestep_scalars(pa, lr_old, t_old, kl, na, nc);
+    if (blockIdx.x == 0) {
+      // what prestep_finish writes: statistics, lr, clip scales, steps
+      st->sumsq[0] = (float)na;
+      st->sumsq[1] = (float)nc;
+      if (pa.count_stats) {
+        st->ep_acc[0] += kl;
+        st->ep_acc[1] += __ldcg(pa.sums3 + 0);
+        st->ep_acc[2] += __ldcg(pa.sums3 + 1);
+        st->ep_acc[3] += ent;
+      }
+      st->lr = ps.lr;
+      st->step_lr = ps.lr;
+      for (int j = 0; j < 2; ++j) st->clip_scale[j] = ps.clip[j];
+      for (int j = 0; j < 3; ++j) {
+        st->t[j] = ps.t[j];
+        st->bc1[j] = ps.bc1[j];
+        st->bc2[j] = ps.bc2[j];
+      }
+      if (pa.count_stats && pa.last_of_epoch) {
+        const float inv = __fdiv_rn(1.0f, (float)pa.minibatches);
+        for (int j = 0; j < 4; ++j) st->stats[j] = st->ep_acc[j] * inv;
+        st->stats[4] = ps.lr;
+        for (int j = 0; j < 4; ++j) st->ep_acc[j] = 0.0f;
+      }
+    }
+  }
+  __syncthreads();
+  // ---- C: Adam (adam_kernel's arithmetic, these scalars)
+  const int64_t n4 = aa.n / 4;
+  float4 *p4 = reinterpret_cast<float4 *>(aa.p);
+  float4 *m4 = reinterpret_cast<float4 *>(aa.m);
+  float4 *v4 = reinterpret_cast<float4 *>(aa.v);
+  const float4 *g4 = reinterpret_cast<const float4 *>(aa.g);
+  for (int64_t qd = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; qd < n4;
+       qd += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = qd * 4;
+    const int j = i < aa.actor_end ? 0 : (i < aa.critic_end ? 1 : 2);
+    const float cs = j < 2 ? ps.clip[j] : 1.0f;
+    float4 pp = p4[qd], mm = m4[qd], vv = v4[qd], gg = __ldcg(g4 + qd);
+    if (cs != 1.0f) {
+      gg.x = __fmul_rn(gg.x, cs);
+      gg.y = __fmul_rn(gg.y, cs);
+      gg.z = __fmul_rn(gg.z, cs);
+      gg.w = __fmul_rn(gg.w, cs);
+    }
+    const bool cl = j == 2;
+    adam_one(pp.x, mm.x, vv.x, gg.x, ps.lr, ps.bc1[j], ps.bc2[j], cl);
+    adam_one(pp.y, mm.y, vv.y, gg.y, ps.lr, ps.bc1[j], ps.bc2[j], cl);
+    adam_one(pp.z, mm.z, vv.z, gg.z, ps.lr, ps.bc1[j], ps.bc2[j], cl);
+    adam_one(pp.w, mm.w, vv.w, gg.w, ps.lr, ps.bc1[j], ps.bc2[j], cl);
+    p4[qd] = pp;
+    if (aa.p_round) {
+      if (aa.p_mode == 2) {
+        __nv_bfloat162 *o = reinterpret_cast<__nv_bfloat162 *>(aa.p_round) + 2 * qd;
+        o[0] = __floats2bfloat162_rn(pp.x, pp.y);
+        o[1] = __floats2bfloat162_rn(pp.z, pp.w);
+      } else {
+        reinterpret_cast<float4 *>(aa.p_round)[qd] =
+            make_float4(rna_tf32(pp.x), rna_tf32(pp.y), rna_tf32(pp.z), rna_tf32(pp.w));
+      }
+    }
+    m4[qd] = mm;
+    v4[qd] = vv;
+  }
+}
+
 // ------------------------------------------------------------ misc
 
 __global__ void unpad_rows_kernel(const float *src, int64_t rows, int pitch,
@@ -1157,8 +1420,10 @@ void launch_norm_prepare(const float *m2, float count, int dim, float *sd,
 void launch_normalize_rows(const float *x, int64_t n, int dim, int pitch,
                            const float *mean, const float *sd, float *out,
                            int mode, cudaStream_t s, const int32_t *perm, const float *sign) {
-  normalize_rows_kernel<<<grid_for(n * 32, 256), 256, 0, s>>>(x, n, dim, pitch, mean, sd, out,
-                                                               mode, perm, sign);
+  // pitch is a multiple of 32 and at most 256 (zrl_create's limit)
+  const int blocks = grid_for((n + kNormRows - 1) / kNormRows, 1, 148 * 32);
+  normalize_rows_kernel<<<blocks, pitch, 0, s>>>(x, n, dim, pitch, mean, sd, out, mode, perm,
+                                                 sign);
 }
 
 void launch_round_copy(const float *src, float *dst, int64_t n, int mode, cudaStream_t s) {
@@ -1193,11 +1458,10 @@ void launch_colsum(const float *x, int64_t rows, int cols, int ld,
   colsum_kernel<<<grid, 128, 0, s>>>(x, rows, cols, ld, partials, splits);
 }
 
-int launch_reduce_segments(const ReduceSegs &segs_in, cudaStream_t s, const PrestepArgs *fuse,
-                           ReduceScratch *rs) {
-  // segments with the most splits first: their blocks run longest, so they
-  // start in the first wave
-  ReduceSegs segs = segs_in;
+// Segments with the most splits first (their blocks run longest, so they
+// start in the first wave), then each segment's first block, split groups
+// and net (with `fuse`: 0 actor, 1 critic, -1 neither).
+static bool plan_segments(ReduceSegs &segs, const PrestepArgs *fuse, int *blocks_out) {
   for (int i = 1; i < segs.n; ++i)
     for (int j = i; j > 0 && segs.seg[j].splits > segs.seg[j - 1].splits; --j) {
       const ReduceSeg t = segs.seg[j];
@@ -1217,6 +1481,18 @@ int launch_reduce_segments(const ReduceSegs &segs_in, cudaStream_t s, const Pres
     }
   }
   segs.first_block[segs.n] = (int)blocks;
+  if (blocks > INT32_MAX / 2) return false;
+  *blocks_out = (int)blocks;
+  return true;
+}
+
+int launch_reduce_segments(const ReduceSegs &segs_in, cudaStream_t s, const PrestepArgs *fuse,
+                           ReduceScratch *rs) {
+  // segments with the most splits first: their blocks run longest, so they
+  // start in the first wave
+  ReduceSegs segs = segs_in;
+  int blocks = 0;
+  if (!plan_segments(segs, fuse, &blocks)) return 0;
   if (blocks == 0) return 0;
   if (fuse && blocks > rs->max_blocks) fuse = nullptr;  // partials too small: not fused
   PrestepArgs pa{};
@@ -1225,6 +1501,51 @@ int launch_reduce_segments(const ReduceSegs &segs_in, cudaStream_t s, const Pres
              fuse ? rs->dpart : (double *)nullptr, fuse ? rs->ticket + 1 : (unsigned int *)nullptr,
              fuse ? 1 : 0);
   return fuse ? 1 : 0;
+}
+
+bool launch_reduce_step(const ReduceSegs &segs_in, const PrestepArgs &pa, const AdamArgs &aa,
+                        ReduceScratch &rs, int *err, cudaStream_t s) {
+  if (rs.coop_blocks < 0) return false;
+  if (rs.coop_blocks == 0) {
+    // every block resident at once: the occupancy of this kernel on every SM
+    int dev = 0, sms = 0, per_sm = 0, coop = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, reduce_step_kernel, kRsThreads,
+                                                      0) != cudaSuccess ||
+        !coop || per_sm < 1) {
+      cudaGetLastError();
+      rs.coop_blocks = -1;
+      return false;
+    }
+    rs.coop_blocks = sms * per_sm;
+    if (rs.coop_blocks > rs.max_blocks) rs.coop_blocks = rs.max_blocks;
+  }
+  ReduceSegs segs = segs_in;
+  int items = 0;
+  if (!plan_segments(segs, &pa, &items) || items == 0) return false;
+  unsigned grid = (unsigned)rs.coop_blocks;
+  if (aa.n % 4 != 0) return false;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kRsThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const unsigned int target = rs.bar_count + grid;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, reduce_step_kernel, segs, pa, aa, rs.dpart,
+                                           rs.ticket + 2, target, err, items);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    rs.coop_blocks = -1;  // refused: the separate kernels from now on
+    return false;
+  }
+  rs.bar_count = target;
+  return true;
 }
 
 void launch_prestep(const PrestepArgs &a, ReduceScratch &rs, cudaStream_t s) {

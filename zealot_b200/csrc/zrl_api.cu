@@ -768,12 +768,51 @@ static bool head_applies(const zrl_ctx *ctx) {
   return true;
 }
 
+// Adam over the whole parameter buffer (net.rs:233-251, ppo.rs:496-510).
+static AdamArgs adam_args(zrl_ctx *ctx) {
+  AdamArgs a{};
+  a.p = ctx->P;
+  a.m = ctx->M;
+  a.v = ctx->V;
+  a.g = ctx->G;
+  a.n = ctx->dev_params;
+  a.actor_end = ctx->net[0].dev_end;
+  a.critic_end = ctx->net[1].dev_end;
+  a.st = ctx->st;
+  a.p_round = ctx->tcore() ? ctx->Ptc : nullptr;
+  a.p_mode = ctx->opmode();
+  return a;
+}
+
+// The segment reduce of a minibatch's partial sums.  One rank (`fuse` set):
+// with the pre-step in the same launch (*fused = 1), and where the device
+// takes a cooperative launch with the Adam step as well (*fused = 2).
+static zrl_status reduce_grads(zrl_ctx *ctx, const ReduceSegs &segs, const PrestepArgs *fuse,
+                               int *fused) {
+  if (fuse && ctx->gemm.err_dev && ctx->rs.coop_blocks >= 0) {
+    ProfSpan ps(ctx, "segment reduce + pre-step + adam");
+    if (launch_reduce_step(segs, *fuse, adam_args(ctx), ctx->rs, ctx->gemm.err_dev,
+                           ctx->stream)) {
+      if (fused) *fused = 2;
+      ctx->launches++;
+      CHECK_LAUNCH();
+      return ZRL_OK;
+    }
+  }
+  ProfSpan ps(ctx, "segment reduce (+pre-step)");
+  const int f = launch_reduce_segments(segs, ctx->stream, fuse, &ctx->rs);
+  if (fused) *fused = f;
+  ctx->launches++;
+  CHECK_LAUNCH();
+  return ZRL_OK;
+}
+
 // minibatch_grads with the fused head: forward of the hidden layers, the
 // head (output layers, losses, last hidden layer's delta), then the rest of
 // the backward and the segment reduce.
 static zrl_status minibatch_grads_head(zrl_ctx *ctx, const zrl_ppo_config *cfg,
                                        const MbView &v, float scale, const PrestepArgs *fuse,
-                                       bool *fused) {
+                                       int *fused) {
   const NetLayout &La = ctx->net[0], &Lc = ctx->net[1];
   const int L = La.L;
   TRY(forward_both(ctx, v.xa, v.xc, v.rows, L - 1));
@@ -827,12 +866,7 @@ static zrl_status minibatch_grads_head(zrl_ctx *ctx, const zrl_ppo_config *cfg,
     CHECK_LAUNCH();
   }
   TRY(backward_both(ctx, v.xa, v.xc, v.rows, &wp, &bp, segs, L - 2));
-  ProfSpan ps(ctx, "segment reduce (+pre-step)");
-  const int f = launch_reduce_segments(segs, ctx->stream, fuse, &ctx->rs);
-  if (fused) *fused = f != 0;
-  ctx->launches++;
-  CHECK_LAUNCH();
-  return ZRL_OK;
+  return reduce_grads(ctx, segs, fuse, fused);
 }
 
 // Gradient accumulation of one minibatch (ppo.rs:388-462): leaves the
@@ -840,8 +874,8 @@ static zrl_status minibatch_grads_head(zrl_ctx *ctx, const zrl_ppo_config *cfg,
 // statistic sums in sums3.
 static zrl_status minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
                                   const MbView &v, float scale,
-                                  const PrestepArgs *fuse = nullptr, bool *fused = nullptr) {
-  if (fused) *fused = false;
+                                  const PrestepArgs *fuse = nullptr, int *fused = nullptr) {
+  if (fused) *fused = 0;
   TRY(ensure_mb(ctx, std::max<int64_t>(v.rows, 1)));
   const NetLayout &La = ctx->net[0], &Lc = ctx->net[1];
   if (v.rows > 0 && head_applies(ctx)) return minibatch_grads_head(ctx, cfg, v, scale, fuse, fused);
@@ -896,12 +930,7 @@ static zrl_status minibatch_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
     segs.seg[segs.n++] = ReduceSeg{ctx->G + Lc.b_off[Lc.L - 1], fp + 2 * la.Ap + 4, (int64_t)la.cp, lb, w};
   }
   TRY(backward_both(ctx, v.xa, v.xc, v.rows, &wp, &bp, segs));
-  ProfSpan ps(ctx, "segment reduce (+pre-step)");
-  const int f = launch_reduce_segments(segs, ctx->stream, fuse, &ctx->rs);
-  if (fused) *fused = f != 0;
-  ctx->launches++;
-  CHECK_LAUNCH();
-  return ZRL_OK;
+  return reduce_grads(ctx, segs, fuse, fused);
 }
 
 static zrl_status allreduce_grads(zrl_ctx *ctx) {
@@ -934,29 +963,20 @@ static PrestepArgs prestep_args(zrl_ctx *ctx, const zrl_ppo_config *cfg, int min
   return p;
 }
 
-// prestep_done: the segment reduce already ran the pre-step (one rank).
+// done: what the segment reduce already ran (one rank): 1 the pre-step,
+// 2 the pre-step and Adam.
 static zrl_status step(zrl_ctx *ctx, const zrl_ppo_config *cfg, int minibatches,
-                       bool last_of_epoch, bool count_stats, bool prestep_done = false) {
+                       bool last_of_epoch, bool count_stats, int done = 0) {
+  if (done >= 2) return ZRL_OK;
   const PrestepArgs p = prestep_args(ctx, cfg, minibatches, last_of_epoch, count_stats);
-  if (!prestep_done) {
+  if (!done) {
     ProfSpan ps(ctx, "pre-step");
     launch_prestep(p, ctx->rs, ctx->stream);
     ctx->launches++;
     CHECK_LAUNCH();
   }
-  AdamArgs a{};
-  a.p = ctx->P;
-  a.m = ctx->M;
-  a.v = ctx->V;
-  a.g = ctx->G;
-  a.n = ctx->dev_params;
-  a.actor_end = ctx->net[0].dev_end;
-  a.critic_end = ctx->net[1].dev_end;
-  a.st = ctx->st;
-  a.p_round = ctx->tcore() ? ctx->Ptc : nullptr;
-  a.p_mode = ctx->opmode();
   ProfSpan ps(ctx, "adam");
-  launch_adam(a, ctx->stream);
+  launch_adam(adam_args(ctx), ctx->stream);
   ctx->launches++;
   CHECK_LAUNCH();
   return ZRL_OK;
@@ -1283,7 +1303,7 @@ static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
       MbView v = epoch_view(ctx, off, cnt);
       // one rank: the segment reduce also runs the pre-step
       const PrestepArgs pf = prestep_args(ctx, cfg, (int)mbs, m == mbs - 1, true);
-      bool fused = false;
+      int fused = 0;
       TRY(minibatch_grads(ctx, cfg, v, scale, multi ? nullptr : &pf, &fused));
       TRY(allreduce_grads(ctx));
       TRY(step(ctx, cfg, (int)mbs, m == mbs - 1, true, fused));
@@ -1298,15 +1318,18 @@ static zrl_status run_epochs(zrl_ctx *ctx, const zrl_ppo_config *cfg,
   return ZRL_OK;
 }
 
-// A tensor-core pipeline wait that ran out of polls leaves a code in the
-// engine's device flag (1: producer, 2: MMA issuer, 3: epilogue).
+// A device wait that ran out leaves a code in the engine's device flag
+// (tensor-core pipelines: 1 producer, 2 MMA issuer, 3 epilogue, ...;
+// 8 the grid barrier of the fused reduce + step).
 static zrl_status check_device_error(zrl_ctx *ctx) {
   if (!ctx->gemm.err_dev) return ZRL_OK;
   int code = 0;
   CK(cudaMemcpy(&code, ctx->gemm.err_dev, sizeof(int), cudaMemcpyDeviceToHost));
   if (code != 0) {
     cudaMemset(ctx->gemm.err_dev, 0, sizeof(int));
-    ctx->err = "tensor-core GEMM pipeline wait timed out (code " + std::to_string(code) + ")";
+    ctx->err = code == 8 ? std::string("reduce + step grid barrier wait timed out (code 8)")
+                         : "tensor-core GEMM pipeline wait timed out (code " +
+                               std::to_string(code) + ")";
     return ZRL_TIMEOUT;
   }
   return ZRL_OK;
@@ -1465,6 +1488,8 @@ zrl_status zrl_create(const zrl_model_config *cfg, int device,
   if ((s = dalloc(ctx, &ctx->rs.dpart, (int64_t)ctx->rs.max_blocks * 2)) != ZRL_OK)
     return fail(s);
   if ((s = dalloc(ctx, &ctx->rs.ticket, 4)) != ZRL_OK) return fail(s);
+  ctx->rs.bar_count = 0;
+  ctx->rs.coop_blocks = 0;
   // identity normalizers (Normalizer::new: mean 0, m2 1, count 1)
   {
     std::vector<float> ones(std::max(od, cd), 1.0f);

@@ -57,9 +57,11 @@ struct DevState {
 struct ReduceScratch {
   float *fpart;          // [max_blocks * fwidth]
   double *dpart;         // [max_blocks * 2]
-  unsigned int *ticket;  // [4]
+  unsigned int *ticket;  // [4]: [1] last-block ticket, [2] grid-barrier counter
   int max_blocks;
   int fwidth;
+  unsigned int bar_count;  // the grid-barrier counter's value after the launches so far
+  int coop_blocks;         // reduce_step grid: 0 not yet sized, -1 unavailable
 };
 
 // ---- kernel launch wrappers (kernels.cu) ------------------------------
@@ -232,6 +234,14 @@ struct AdamArgs {
   int p_mode;
 };
 void launch_adam(const AdamArgs &a, cudaStream_t s);
+
+// One rank: the segment reduce, the pre-step and Adam in one cooperative
+// launch (a grid barrier between the reduce and the step).  Returns false,
+// having launched nothing, where the device refuses a cooperative launch;
+// the caller then runs launch_reduce_segments (fused) and launch_adam.  A
+// barrier wait that runs out leaves code 8 in *err.
+bool launch_reduce_step(const ReduceSegs &segs, const PrestepArgs &pa, const AdamArgs &aa,
+                        ReduceScratch &rs, int *err, cudaStream_t s);
 
 // Copy an n-element slice of a padded [rows, pitch] buffer into a dense
 // [rows, cols] one (and back).
