@@ -2,7 +2,8 @@
 24,576 rows, and at that size the update takes code paths that toy sizes
 never reach -- grouped launches of both nets, CTA-pair (256-row) tiles
 running several rounds per persistent CTA, double-buffered accumulators,
-the split-K counts chosen for the weight gradients (9 and 24 at C2) and the
+the split-K counts chosen for the weight gradients (at C2: 10 for layer 1's
+and 8 for layer 0's, whose tiles move 3/4 of the bytes, 24 for the flat group) and the
 column-sum rows the segment reduce folds.  These tests run those paths.
 
 Inputs: a seeded rollout with the C2 dims (96->512->256->128->29 actor,

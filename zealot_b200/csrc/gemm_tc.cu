@@ -1011,6 +1011,11 @@ static void tile_shape(int minM, int maxN, bool bf, int kind, int *CG, int *BN) 
   *CG = (minM >= 256 && maxN > 32) ? 2 : 1;
   *BN = maxN <= 32 ? 32 : (maxN <= 64 ? 64 : (maxN <= 128 || *CG == 1 ? 128 : 256));
   if (bf && kind != 0 && *BN / *CG < 64) *BN = 64 * *CG;
+  // input gradients: 256 x 128 pair tiles (measured at C2: dgrad level 1,
+  // N = 512, 61.9 -> 57.5 us; level 2, N = 256, 36.1 -> 35.3 us), twice
+  // the tiles to even out the persistent grid's last round; the forward
+  // keeps 256-wide tiles (level 1, N = 256, is 24 % slower at 128)
+  if (*CG == 2 && *BN == 256 && kind == 1) *BN = 128;
 }
 
 // A problem at most half as wide as the launch's tiles takes half-width
@@ -1021,12 +1026,13 @@ static int tile_width(int N, int BN, int CG, bool bf, int kind) {
   return (BN / 2 / CG >= min_share && N <= BN / 2) ? BN / 2 : BN;
 }
 
-int gemm_tc_split(GemmEngine *eng, const GemmArgs *gs, int n, int precision, int max_split) {
+int gemm_tc_split(GemmEngine *eng, const GemmArgs *gs, int n, int precision, int max_split,
+                  int *splits) {
   (void)eng;
   const bool bf = precision == ZRL_GEMM_BF16;
-  if (n < 1 || max_split < 1) return 1;
+  if (n < 1 || n > kMaxProbs || max_split < 1) return 0;
   const int kind = layout_kind(gs[0]);
-  if (kind < 0) return 1;
+  if (kind < 0) return 0;
   int maxN = 0, minM = INT32_MAX;
   for (int i = 0; i < n; ++i) {
     maxN = std::max(maxN, gs[i].N);
@@ -1034,32 +1040,55 @@ int gemm_tc_split(GemmEngine *eng, const GemmArgs *gs, int n, int precision, int
   }
   int CG, BN;
   tile_shape(minM, maxN, bf, kind, &CG, &BN);
-  int64_t per_split = 0;  // output tiles of one split
+  int bn[kMaxProbs];
+  int64_t tiles1[kMaxProbs];  // output tiles of one split
   for (int i = 0; i < n; ++i) {
-    const int bn = tile_width(gs[i].N, BN, CG, bf, kind);
-    per_split += (int64_t)((gs[i].M + BM * CG - 1) / (BM * CG)) * ((gs[i].N + bn - 1) / bn);
+    bn[i] = tile_width(gs[i].N, BN, CG, bf, kind);
+    tiles1[i] = (int64_t)((gs[i].M + BM * CG - 1) / (BM * CG)) * ((gs[i].N + bn[i] - 1) / bn[i]);
   }
   int units = 0;
   TcMaps maps;
   TcGroup grp;
   const cudaError_t e = bf ? dispatch<true>(CG, BN, kind, gs[0].epi, maps, grp, nullptr, &units)
                            : dispatch<false>(CG, BN, kind, gs[0].epi, maps, grp, nullptr, &units);
-  if (e != cudaSuccess || units < 1) return 1;
-  // estimated time: rounds of the persistent grid x k-blocks per split;
-  // the fewest splits (partial bytes) within 3 % of the best
+  if (e != cudaSuccess || units < 1) return 0;
+  // These tiles stream both operands (K = samples) and are bound by the
+  // operand bytes of a k-block, which grow with the tile's rows + columns:
+  // a problem with narrower tiles takes proportionally fewer splits, so
+  // every tile of the launch moves about the same bytes (the persistent grid
+  // deals tiles round-robin, so equal tiles keep its units equally busy).
+  // Measured at C2, layer 1 (256 x 256 tiles) and layer 0 (256 x 128): equal
+  // splits 61.5 us, splits in the ratio of the MMA work (2 : 1) 74 us.
+  const int wmax = BM * CG + BN;
+  auto split_of = [&](int S, int i) {
+    const int s = (int)(((int64_t)S * (BM * CG + bn[i]) * 2 + wmax) / (2 * wmax));  // rounded
+    return s < 1 ? 1 : s;
+  };
+  // estimated time: rounds of the persistent grid x the largest tile's
+  // bytes -- its k-blocks of (rows + columns) x 128 B, plus its fp32
+  // partial tile, written here and read back by the segment reduce; the
+  // fewest splits within 3 % of the best
   const int ke = bf ? 64 : 32;
-  int64_t K = 0;
-  for (int i = 0; i < n; ++i) K = std::max<int64_t>(K, gs[i].K);
   auto cost = [&](int S) {
-    const int64_t kc = ((K + S - 1) / S + ke - 1) / ke;
-    const int64_t rounds = (per_split * S + units - 1) / units;
-    return rounds * kc;
+    int64_t tiles = 0, big = 0;
+    for (int i = 0; i < n; ++i) {
+      const int si = split_of(S, i);
+      tiles += tiles1[i] * si;
+      const int64_t kc = ((gs[i].K + si - 1) / si + ke - 1) / ke;
+      big = std::max<int64_t>(big, kc * (BM * CG + bn[i]) + (int64_t)BM * CG * bn[i] / 16);
+    }
+    return (tiles + units - 1) / units * big;
   };
   int64_t best = INT64_MAX;
   for (int S = 1; S <= max_split; ++S) best = std::min(best, cost(S));
+  int pick = 1;
   for (int S = 1; S <= max_split; ++S)
-    if (cost(S) * 100 <= best * 103) return S;
-  return 1;
+    if (cost(S) * 100 <= best * 103) {
+      pick = S;
+      break;
+    }
+  for (int i = 0; i < n; ++i) splits[i] = split_of(pick, i);
+  return pick;
 }
 
 zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precision,

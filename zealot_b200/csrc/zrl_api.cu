@@ -624,8 +624,10 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
   // Tall ones (dp[l+1] >= 256 rows) go to CTA-pair tiles, the rest to
   // single-CTA tiles: a grouped launch (of at most 8) each, issued right
   // after the dgrad level that reads the same delta_l and a_l (level 1 for
-  // layer 0), so those reads meet L2.  Each group takes the split count
-  // that fills the grid with the fewest partial rows.
+  // layer 0), so those reads meet L2.  Each group takes the split counts
+  // that fill the grid with the fewest partial rows (per problem: one with
+  // half-width tiles takes half the splits, so the launch's tiles hold equal
+  // work).
   GemmArgs tall[2 * ZRL_MAX_LAYERS], flat[2 * ZRL_MAX_LAYERS];
   int64_t tall_dst[2 * ZRL_MAX_LAYERS], flat_dst[2 * ZRL_MAX_LAYERS];
   int nt = 0, nf = 0, tall_lvl = 1, flat_lvl = 1;
@@ -656,9 +658,14 @@ static zrl_status backward_both(zrl_ctx *ctx, const float *xa, const float *xc, 
     }
   }
   auto place = [&](GemmArgs *w, const int64_t *dst, int nw) {
-    int sg = ctx->gemm.split_for(w, std::min(nw, 8), ctx->precision, kMaxWSplit, &ctx->err);
-    if (sg < 1) sg = S;
+    int sp[2 * ZRL_MAX_LAYERS];
+    for (int i0 = 0; i0 < nw; i0 += 8) {
+      const int m = std::min(nw - i0, 8);
+      if (ctx->gemm.split_for(w + i0, m, ctx->precision, kMaxWSplit, sp + i0, &ctx->err) < 1)
+        for (int i = i0; i < i0 + m; ++i) sp[i] = S;
+    }
     for (int i = 0; i < nw; ++i) {
+      const int sg = sp[i];
       w[i].split_k = sg;
       w[i].C = *wp;
       const int64_t sz = (int64_t)w[i].M * w[i].N;

@@ -70,7 +70,8 @@ zrl_status gemm_tc_init(int device, std::string *err);
 // Split-K count (1..max_split) for a group of weight-gradient GEMMs sharing
 // K: the fewest splits whose output tiles fill the persistent grid about as
 // well as any (gemm_tc.cu).
-int gemm_tc_split(GemmEngine *eng, const GemmArgs *gs, int n, int precision, int max_split);
+int gemm_tc_split(GemmEngine *eng, const GemmArgs *gs, int n, int precision, int max_split,
+                  int *splits);
 
 struct GemmEngine {
   bool tc_ready = false;
@@ -99,15 +100,17 @@ struct GemmEngine {
     return gemm_tc(this, g, precision, s, launched, err);
   }
 
-  // Split-K count for a weight-gradient group (see gemm_tc_split); 0 on
-  // the CUDA cores, where the caller keeps its own split.
-  int split_for(const GemmArgs *gs, int n, int precision, int max_split, std::string *err) {
+  // Split-K counts for a weight-gradient group, one per problem, into
+  // splits[0..n) (see gemm_tc_split); returns 0 on the CUDA cores, where
+  // the caller keeps its own split.
+  int split_for(const GemmArgs *gs, int n, int precision, int max_split, int *splits,
+                std::string *err) {
     if (precision == ZRL_GEMM_FP32) return 0;
     if (!tc_ready) {
       if (gemm_tc_init(0, err) != ZRL_OK) return 0;
       tc_ready = true;
     }
-    return gemm_tc_split(this, gs, n, precision, max_split);
+    return gemm_tc_split(this, gs, n, precision, max_split, splits);
   }
 
   // The fused output head (tensor cores only).
