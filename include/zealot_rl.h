@@ -337,9 +337,10 @@ int64_t zrl_rank_orders(uint64_t seed, int64_t n_global, int64_t n_local,
  * has obs, critic_obs, action and mean_old mapped by signed permutations,
  * (P x)[i] = sign[i] * x[perm[i]] (each perm a permutation of its space,
  * each sign +-1), and logp_old, value_old, adv, ret unchanged.  The mirror
- * is applied to the raw rows as the epoch gather reads them, so the batch
- * is not copied.  obs_perm = NULL turns it off.  One rank only
- * (ZRL_NOT_SUPPORTED with several). */
+ * is applied once per update, where the observations are normalized (the
+ * mirrored normalized rows are written beside the originals), and to action
+ * and mean_old as the epoch gather copies them.  obs_perm = NULL turns it
+ * off.  One rank only (ZRL_NOT_SUPPORTED with several). */
 zrl_status zrl_set_mirror(zrl_ctx *ctx, const int32_t *obs_perm, const float *obs_sign,
                           const int32_t *cobs_perm, const float *cobs_sign,
                           const int32_t *act_perm, const float *act_sign);
