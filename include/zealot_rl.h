@@ -289,9 +289,9 @@ zrl_status zrl_apply_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
  * adv_norm_out = (adv - mean) / max(population sd, 1e-6).  Reduction
  * scratch is a fixed array inside the library (about 67 KB on every GPU
  * that loads it), so n_envs is limited to 262,144 (ZRL_INVALID_ARG above)
- * and T to 4096; the first call on a device looks up that array and should
- * come before any stream capture, and the address it caches does not
- * survive a cudaDeviceReset of that device; calls that overlap on the GPU
+ * and T to 4096; the first call on a device looks up that array's address
+ * (cudaGetSymbolAddress) and caches it, and that address does not survive a
+ * cudaDeviceReset of that device; calls that overlap on the GPU
  * race on the shared array.  It has no counterpart in the reference, which computes
  * GAE on the host. */
 zrl_status zrl_gae_normalize_noalloc(const float *rewards, const float *values,

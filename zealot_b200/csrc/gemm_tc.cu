@@ -160,12 +160,6 @@ struct EpiChunk {
   float *colsum;     // this quarter's partial row at the chunk's first column
 };
 
-// The chunk's accumulator values v -> the epilogue function, the optional
-// column sums, rounding and the staging.
-template <int EPI, bool FULL>
-__device__ __forceinline__ void epi_math(float (&v)[32], const EpiChunk &e, int lane, bool row_ok,
-                                         int valid_cols);
-
 template <int EPI, bool FULL, typename Release>
 __device__ __forceinline__ void epi_chunk(const EpiChunk &e, int lane, bool last,
                                           Release release, bool row_ok, int valid_cols) {
@@ -181,12 +175,6 @@ __device__ __forceinline__ void epi_chunk(const EpiChunk &e, int lane, bool last
     // last read of this accumulator: hand it back to the MMA warp
     if (last) release();
   }
-  epi_math<EPI, FULL>(v, e, lane, row_ok, valid_cols);
-}
-
-template <int EPI, bool FULL>
-__device__ __forceinline__ void epi_math(float (&v)[32], const EpiChunk &e, int lane, bool row_ok,
-                                         int valid_cols) {
   if (EPI == EPI_BIAS || EPI == EPI_BIAS_ELU) {
     uint32_t a[8];
     float b[32];
@@ -637,77 +625,8 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
       const bool row_ok = row0 + lane < pr.M;
       const uint32_t taddr = tmem + (uint32_t)(ab * BN) + ((uint32_t)(quarter * 32) << 16);
       const bool have = ok && tl.nk > 0;
-      // Full tiles (fp32 outputs): the next chunk's accumulator columns are
-      // loaded from TMEM while this chunk's math runs; the accumulator goes
-      // back to the MMA warp as soon as its last columns are in registers.
-      const bool piped = !OB && !idle && have && rows_full && tl.bn == BN &&
-                         tl.n0 + BN <= pr.N;  // warp-uniform
-      uint32_t cur[32], nxt[32];
-      if (piped) {
-        tmem_ld32_start(taddr + half * CW, cur);
-        tmem_ld_wait(cur);
-        if (CPT == 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acce[ab]);
-        }
-      }
 #pragma unroll 1
       for (int k = 0; k < CPT; ++k, ++j) {
-        if (piped) {
-          if (k + 1 < CPT) tmem_ld32_start(taddr + (half + 2 * (k + 1)) * CW, nxt);
-          const int c = half + 2 * k;
-          const int n = tl.n0 + c * CW;
-          const int sl = j % NS;
-          const uint32_t slot = slots + (uint32_t)sl * 4096u;
-          if (EPI == EPI_ELU_GRAD && lane == 0 && j >= 1) {
-            if (prev_store) bulk_wait_read<1>();
-            else bulk_wait_read<0>();
-            issue_aux(j + NS - 2);
-          }
-          if (EPI == EPI_ELU_GRAD) {
-            if (!mbar_wait(&wbar[sl], (xph >> sl) & 1u, g.err, 5, g.wait_ns)) ok = false;
-            xph ^= 1u << sl;
-          } else {
-            if (lane == 0) {
-              if (prev_store) bulk_wait_read<1>();
-              else bulk_wait_read<0>();
-            }
-            __syncwarp();
-          }
-          EpiChunk ec;
-          ec.taddr = 0;
-          ec.slot = slot + row_addr;
-          ec.sw = sw;
-          ec.bias = wbias + (uint32_t)(k * CW) * 4u;
-          ec.round = pr.round_out;
-          ec.colsum = pr.colsum
-                          ? pr.colsum + ((int64_t)(tl.m0 / BM + rank) * 4 + quarter) * pr.N + n
-                          : nullptr;
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(cur[i]);
-          epi_math<EPI, true>(v, ec, lane, true, CW);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_3d(&maps.c[tl.p], smem + (slot - smem_u32(smem)), n, row0, tl.z);
-            bulk_commit();
-          }
-          prev_store = true;
-          if (k + 1 < CPT) {
-            tmem_ld_wait(nxt);
-            if (k + 2 == CPT) {
-              // the accumulator's last columns are in registers
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&acce[ab]);
-            }
-#pragma unroll
-            for (int i = 0; i < 32; ++i) cur[i] = nxt[i];
-          }
-          continue;
-        }
         const int c = half + 2 * k;
         const int n = tl.n0 + c * CW;
         const int sl = j % NS;

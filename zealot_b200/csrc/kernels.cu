@@ -1044,11 +1044,12 @@ __global__ void adam_kernel(AdamArgs a) {
 
 // ------------------------------------------------ reduce + pre-step + Adam
 
-// One rank's whole stepping half of a minibatch (ppo.rs:462-489) in one
-// cooperative launch, every block resident at once:
-//  A. the segment reduce (the work of reduce_segments_kernel's blocks,
-//     taken in turn by this grid's blocks), with each block's squared norms
-//     of what it wrote, per net;
+// The stepping half of a minibatch (ppo.rs:462-489) in one cooperative
+// launch, every block resident at once:
+//  A. one rank: the segment reduce (the work of reduce_segments_kernel's
+//     blocks, taken in turn by this grid's blocks), with each block's
+//     squared norms of what it wrote, per net; several ranks (from_grads,
+//     no segments): the squared norms of the allreduced gradient;
 //  B. a grid barrier, then every block folds the block norms in block
 //     order (the same bits in every block) and computes the pre-step's
 //     scalars from the state it read before the barrier -- block 0 alone
@@ -1086,7 +1087,7 @@ __device__ PreScalars prestep_scalars(const PrestepArgs &a, float lr, const int3
 
 __global__ void __launch_bounds__(kRsThreads, 2)
 reduce_step_kernel(ReduceSegs segs, PrestepArgs pa, AdamArgs aa, double *partials,
-                   unsigned int *bar, unsigned int target, int *err, int items) {
+                   unsigned int *bar, unsigned int target, int *err, int items, int from_grads) {
   pdl_wait();
   pdl_trigger();
   __shared__ double sh[32];
@@ -1153,6 +1154,21 @@ reduce_step_kernel(ReduceSegs segs, PrestepArgs pa, AdamArgs aa, double *partial
       const int net = segs.net[si];
       if (net >= 0)
         sq[net] += (double)t.x * t.x + (double)t.y * t.y + (double)t.z * t.z + (double)t.w * t.w;
+    }
+  }
+  if (from_grads) {
+    // several ranks: the norms of the allreduced gradient itself (the
+    // per-net ranges start and end on 16-byte boundaries)
+    const float4 *g4 = reinterpret_cast<const float4 *>(pa.grads);
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (int64_t i = pa.actor_begin / 4 + t0; i < pa.actor_end / 4; i += stride) {
+      const float4 x = __ldcg(g4 + i);
+      sq[0] += (double)x.x * x.x + (double)x.y * x.y + (double)x.z * x.z + (double)x.w * x.w;
+    }
+    for (int64_t i = pa.critic_begin / 4 + t0; i < pa.critic_end / 4; i += stride) {
+      const float4 x = __ldcg(g4 + i);
+      sq[1] += (double)x.x * x.x + (double)x.y * x.y + (double)x.z * x.z + (double)x.w * x.w;
     }
   }
   const double ba = block_sum(sq[0], sh);
@@ -1504,7 +1520,7 @@ int launch_reduce_segments(const ReduceSegs &segs_in, cudaStream_t s, const Pres
 }
 
 bool launch_reduce_step(const ReduceSegs &segs_in, const PrestepArgs &pa, const AdamArgs &aa,
-                        ReduceScratch &rs, int *err, cudaStream_t s) {
+                        ReduceScratch &rs, int *err, cudaStream_t s, bool from_grads) {
   if (rs.coop_blocks < 0) return false;
   if (rs.coop_blocks == 0) {
     // every block resident at once: the occupancy of this kernel on every SM
@@ -1524,7 +1540,10 @@ bool launch_reduce_step(const ReduceSegs &segs_in, const PrestepArgs &pa, const 
   }
   ReduceSegs segs = segs_in;
   int items = 0;
-  if (!plan_segments(segs, &pa, &items) || items == 0) return false;
+  if (!plan_segments(segs, from_grads ? nullptr : &pa, &items)) return false;
+  if (items == 0 && !from_grads) return false;
+  if (from_grads && ((pa.actor_begin | pa.actor_end | pa.critic_begin | pa.critic_end) & 3))
+    return false;
   unsigned grid = (unsigned)rs.coop_blocks;
   if (aa.n % 4 != 0) return false;
   cudaLaunchConfig_t cfg{};
@@ -1538,7 +1557,7 @@ bool launch_reduce_step(const ReduceSegs &segs_in, const PrestepArgs &pa, const 
   cfg.numAttrs = 1;
   const unsigned int target = rs.bar_count + grid;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, reduce_step_kernel, segs, pa, aa, rs.dpart,
-                                           rs.ticket + 2, target, err, items);
+                                           rs.ticket + 2, target, err, items, from_grads ? 1 : 0);
   if (e != cudaSuccess) {
     cudaGetLastError();
     rs.coop_blocks = -1;  // refused: the separate kernels from now on

@@ -976,6 +976,17 @@ static zrl_status step(zrl_ctx *ctx, const zrl_ppo_config *cfg, int minibatches,
                        bool last_of_epoch, bool count_stats, int done = 0) {
   if (done >= 2) return ZRL_OK;
   const PrestepArgs p = prestep_args(ctx, cfg, minibatches, last_of_epoch, count_stats);
+  if (!done && ctx->gemm.err_dev && ctx->rs.coop_blocks >= 0) {
+    // the pre-step and Adam in one cooperative launch
+    ProfSpan ps(ctx, "pre-step + adam");
+    const ReduceSegs none{};
+    if (launch_reduce_step(none, p, adam_args(ctx), ctx->rs, ctx->gemm.err_dev, ctx->stream,
+                           true)) {
+      ctx->launches++;
+      CHECK_LAUNCH();
+      return ZRL_OK;
+    }
+  }
   if (!done) {
     ProfSpan ps(ctx, "pre-step");
     launch_prestep(p, ctx->rs, ctx->stream);

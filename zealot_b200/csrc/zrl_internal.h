@@ -236,12 +236,13 @@ struct AdamArgs {
 void launch_adam(const AdamArgs &a, cudaStream_t s);
 
 // One rank: the segment reduce, the pre-step and Adam in one cooperative
-// launch (a grid barrier between the reduce and the step).  Returns false,
-// having launched nothing, where the device refuses a cooperative launch;
-// the caller then runs launch_reduce_segments (fused) and launch_adam.  A
-// barrier wait that runs out leaves code 8 in *err.
+// launch (a grid barrier between the reduce and the step).  Several ranks
+// (from_grads, segs empty): the pre-step's norms of the allreduced gradient
+// and Adam, likewise.  Returns false, having launched nothing, where the
+// device refuses a cooperative launch; the caller then runs the separate
+// kernels.  A barrier wait that runs out leaves code 8 in *err.
 bool launch_reduce_step(const ReduceSegs &segs, const PrestepArgs &pa, const AdamArgs &aa,
-                        ReduceScratch &rs, int *err, cudaStream_t s);
+                        ReduceScratch &rs, int *err, cudaStream_t s, bool from_grads = false);
 
 // Copy an n-element slice of a padded [rows, pitch] buffer into a dense
 // [rows, cols] one (and back).
