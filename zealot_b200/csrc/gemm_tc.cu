@@ -233,6 +233,50 @@ __device__ __forceinline__ void epi_chunk(const EpiChunk &e, int lane, bool last
     st_shared4(e.slot + ((q ^ e.sw) << 4), v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
 }
 
+// Two 32 x 32 chunks of the forward bias + ELU epilogue (fp32 output, every
+// row and column valid, no column sums) in lockstep: the same operations as
+// epi_chunk<EPI_BIAS_ELU, true> on each, as two independent chains the
+// scheduler can interleave.
+__device__ __forceinline__ void epi_pair_bias_elu(float (&va)[32], float (&vb)[32],
+                                                  uint32_t bias_a, uint32_t bias_b,
+                                                  uint32_t slot_a, uint32_t slot_b, uint32_t sw,
+                                                  int round) {
+  {
+    uint32_t a[8], b[8];
+    float x[32], y[32];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      a[q] = bias_a + 16u * q;  // broadcast
+      b[q] = bias_b + 16u * q;
+    }
+    ld_shared4x8(a, x);
+    ld_shared4x8(b, y);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      va[i] += x[i];
+      vb[i] += y[i];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float ea = exp_sfu(va[i]), eb = exp_sfu(vb[i]);
+    va[i] = va[i] > 0.0f ? va[i] : ea - 1.0f;
+    vb[i] = vb[i] > 0.0f ? vb[i] : eb - 1.0f;
+  }
+  if (round) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      va[i] = round_tf32(va[i]);
+      vb[i] = round_tf32(vb[i]);
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    st_shared4(slot_a + ((q ^ sw) << 4), va[4 * q], va[4 * q + 1], va[4 * q + 2], va[4 * q + 3]);
+    st_shared4(slot_b + ((q ^ sw) << 4), vb[4 * q], vb[4 * q + 1], vb[4 * q + 2], vb[4 * q + 3]);
+  }
+}
+
 // The 64-column chunk of the bf16-output epilogues (forward hidden layers,
 // dgrad): one row of 64 bf16 is 128 bytes, so the staging slot keeps the
 // 128-byte swizzle.  fp32 math as in epi_chunk; the column sums are taken
@@ -625,6 +669,55 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
       const bool row_ok = row0 + lane < pr.M;
       const uint32_t taddr = tmem + (uint32_t)(ab * BN) + ((uint32_t)(quarter * 32) << 16);
       const bool have = ok && tl.nk > 0;
+      if constexpr (EPI == EPI_BIAS_ELU && !OB && CPT % 2 == 0 && NS == 2) {
+        // full forward tiles with a short K (at most 4 k-blocks: the
+        // epilogue, not the main loop, sets their pace): the warp's chunks
+        // two at a time -- both accumulator loads, one wait, both chunks'
+        // math, both stores (measured at C2: level 0, K = 96, 36.5 -> 32.5
+        // us; levels 1-2, K = 512 and 256, 4 % slower, so they stay single)
+        if (!idle && have && tl.nk <= 4 && rows_full && tl.bn == BN && tl.n0 + BN <= pr.N &&
+            !pr.colsum) {
+#pragma unroll 1
+          for (int k = 0; k < CPT; k += 2, j += 2) {
+            // both staging slots free: the previous stores have read them
+            if (lane == 0) bulk_wait_read<0>();
+            __syncwarp();
+            uint32_t ra[32], rb[32];
+            tmem_ld32_start(taddr + (half + 2 * k) * CW, ra);
+            tmem_ld32_start(taddr + (half + 2 * k + 2) * CW, rb);
+            tmem_ld_wait(ra);
+            tmem_ld_wait(rb);
+            if (k + 2 == CPT) {
+              // the accumulator's last columns are in registers
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&acce[ab]);
+            }
+            float va[32], vb[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              va[i] = __uint_as_float(ra[i]);
+              vb[i] = __uint_as_float(rb[i]);
+            }
+            const uint32_t sa = slots + (uint32_t)(j % NS) * 4096u;
+            const uint32_t sb = slots + (uint32_t)((j + 1) % NS) * 4096u;
+            epi_pair_bias_elu(va, vb, wbias + (uint32_t)(k * CW) * 4u,
+                              wbias + (uint32_t)((k + 1) * CW) * 4u, sa + row_addr,
+                              sb + row_addr, sw, pr.round_out);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&maps.c[tl.p], smem + (sa - smem_u32(smem)),
+                           tl.n0 + (half + 2 * k) * CW, row0, tl.z);
+              tma_store_3d(&maps.c[tl.p], smem + (sb - smem_u32(smem)),
+                           tl.n0 + (half + 2 * k + 2) * CW, row0, tl.z);
+              bulk_commit();
+            }
+          }
+          prev_store = true;
+          continue;
+        }
+      }
 #pragma unroll 1
       for (int k = 0; k < CPT; ++k, ++j) {
         const int c = half + 2 * k;
