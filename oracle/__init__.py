@@ -345,6 +345,10 @@ class ActorCritic:
         accumulation) on top of the reference arithmetic."""
         lib().orc_ac_set_operand_rounding(self.h, 1 if on else 0)
 
+    def set_bf16_operands(self, on: bool = True):
+        """The same with bf16 operands (nearest, ties to even)."""
+        lib().orc_ac_set_operand_rounding(self.h, 2 if on else 0)
+
     def adam_state(self):
         t3 = np.zeros(3, np.int32)
         m = np.empty(self.np, np.float32)

@@ -141,7 +141,23 @@ static inline float rtf32(float x) {
   return x;
 }
 
-/* net.rs:88-108.  rnd = 1 rounds every GEMM operand to tf32 where a
+/* The same for a bf16 tensor-core GEMM: 8 significant bits, nearest, ties
+ * to even (the conversion the bf16 backend stores with); a product of two
+ * bf16 values is exact in f32 too. */
+static inline float rbf16(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  if ((u & 0x7F800000u) != 0x7F800000u) u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+  memcpy(&x, &u, 4);
+  return x;
+}
+
+/* The operand rounding of mode rnd: 0 none (f32), 1 tf32, 2 bf16. */
+static inline float rop(float x, int rnd) {
+  return rnd == 1 ? rtf32(x) : (rnd == 2 ? rbf16(x) : x);
+}
+
+/* net.rs:88-108.  rnd = 1 (2) rounds every GEMM operand to tf32 (bf16) where a
  * tensor-core backend stores it: the input row, the weights and each hidden
  * activation (after ELU); the output layer stays f32. */
 static void mlp_forward_r(const int32_t *dims, int32_t n_dims, const float *params,
@@ -149,7 +165,7 @@ static void mlp_forward_r(const int32_t *dims, int32_t n_dims, const float *para
   int32_t layers = n_dims - 1;
   memcpy(acts, x, sizeof(float) * (size_t)dims[0]);
   if (rnd)
-    for (int32_t i = 0; i < dims[0]; ++i) acts[i] = rtf32(acts[i]);
+    for (int32_t i = 0; i < dims[0]; ++i) acts[i] = rop(acts[i], rnd);
   const float *prev = acts;
   float *out = acts + dims[0];
   const float *p = params;
@@ -162,10 +178,10 @@ static void mlp_forward_r(const int32_t *dims, int32_t n_dims, const float *para
       float z = b[o];
       const float *row = w + (int64_t)o * fan_in;
       if (rnd)
-        for (int32_t i = 0; i < fan_in; ++i) z += rtf32(row[i]) * prev[i];
+        for (int32_t i = 0; i < fan_in; ++i) z += rop(row[i], rnd) * prev[i];
       else
         for (int32_t i = 0; i < fan_in; ++i) z += row[i] * prev[i];
-      out[o] = last ? z : (rnd ? rtf32(elu(z)) : elu(z));
+      out[o] = last ? z : (rnd ? rop(elu(z), rnd) : elu(z));
     }
     p += (int64_t)fan_out * fan_in + fan_out;
     prev = out;
@@ -225,10 +241,10 @@ static void mlp_backward_r(const int32_t *dims, int32_t n_dims, const float *par
       const float *wrow = w + (int64_t)o * fan_in;
       float *grow = gw + (int64_t)o * fan_in;
       if (rnd) {
-        d = rtf32(d);
+        d = rop(d, rnd);
         for (int32_t i = 0; i < fan_in; ++i) {
           grow[i] += d * prev[i];
-          g_prev[i] += d * rtf32(wrow[i]);
+          g_prev[i] += d * rop(wrow[i], rnd);
         }
       } else {
         for (int32_t i = 0; i < fan_in; ++i) {
@@ -381,7 +397,7 @@ struct orc_ac {
   float *obs_mean, *obs_m2, obs_count;
   float *crit_mean, *crit_m2, crit_count;
   float lr;
-  int32_t rnd; /* 1: tf32 operand rounding emulated (mlp_forward_r) */
+  int32_t rnd; /* operand rounding emulated (mlp_forward_r): 1 tf32, 2 bf16 */
 };
 
 orc_ac *orc_ac_new(const int32_t *adims, int32_t an, const int32_t *cdims,
@@ -465,7 +481,9 @@ void orc_ac_set_normalizers(orc_ac *ac, const float *obs_mean,
 }
 
 void orc_ac_set_lr(orc_ac *ac, float lr) { ac->lr = lr; }
-void orc_ac_set_operand_rounding(orc_ac *ac, int32_t mode) { ac->rnd = mode == 1; }
+void orc_ac_set_operand_rounding(orc_ac *ac, int32_t mode) {
+  ac->rnd = (mode == 1 || mode == 2) ? mode : 0;
+}
 float orc_ac_get_lr(const orc_ac *ac) { return ac->lr; }
 
 void orc_ac_get_adam(const orc_ac *ac, int32_t *t3, float *m, float *v) {

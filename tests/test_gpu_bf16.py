@@ -14,6 +14,17 @@ standardized action residuals (ppo.rs:297-305, 410-433): every actor
 tensor then moves by the same ~3 % (measured 3.0-3.3 % on the C5 dims),
 so the gradient bar is 5e-2 per tensor (norm-wise), and a whole update
 must move the parameters in the oracle's direction (cosine > 0.97).
+
+Those bars measure bf16 itself.  The second oracle rounds every GEMM
+operand to bf16 where this library stores it (O.ActorCritic.
+set_bf16_operands: inputs, weights, hidden activations, deltas; products
+exact in f32), so against it only the summation order and the ELU's
+exponential differ.  Measured on the C5 dims: forward 2.6e-4, gradient
+tensors at most 6.1e-4, loss sums 3e-5, a whole update 9.8e-3 relative L2
+per tensor (the oracle against itself with another thread count: 1.2e-3),
+cosine 0.99997.  Bars: forward and gradient 2e-3 per tensor, loss sums
+1e-3, update 2e-2 per tensor and cosine > 0.999 -- a sign error in any one
+tensor fails them.
 """
 from __future__ import annotations
 
@@ -72,3 +83,50 @@ def test_bf16_update_moves_like_the_oracle(case):
     cos = float(d_gpu @ d_orc / (np.linalg.norm(d_gpu) * np.linalg.norm(d_orc)))
     assert cos > 0.97, cos
     assert abs(st.value_loss - st2["value_loss"]) <= TOL * abs(st2["value_loss"])
+
+
+TOL_BF = 2e-3
+
+
+def _bf16_oracle(case, lr=None):
+    orc = case.oracle_ac() if lr is None else case.oracle_ac(lr=lr)
+    orc.set_bf16_operands()
+    return orc
+
+
+def test_bf16_forward_matches_the_bf16_oracle(case):
+    gpu = case.gpu_ac("bf16")
+    mean, value = gpu.forward(case.ro.obs, case.ro.critic_obs)
+    m2, v2 = _bf16_oracle(case).forward(case.ro.obs, case.ro.critic_obs)
+    em = np.linalg.norm(mean - m2) / np.linalg.norm(m2)
+    ev = np.linalg.norm(value - v2) / np.linalg.norm(v2)
+    assert em < TOL_BF and ev < TOL_BF, (em, ev)
+
+
+def test_bf16_gradient_matches_the_bf16_oracle(case):
+    gpu = case.gpu_ac("bf16")
+    idx = O.shuffle(3, case.ro.n)
+    g, s = gpu.minibatch_grads(case.soa(), idx, Z.PpoConfig())
+    g2, s2 = _bf16_oracle(case).minibatch_grads(case.oracle_batch(), idx, O.PpoConfig(),
+                                                n_threads=8)
+    errs = tensor_l2(g, g2, case.adims, case.cdims)
+    bad = {k: v for k, v in errs.items() if v > TOL_BF}
+    assert not bad, bad
+    np.testing.assert_allclose(s, s2, rtol=1e-3, atol=1e-5)
+
+
+def test_bf16_update_matches_the_bf16_oracle(case):
+    cfg = Z.PpoConfig(epochs=2, minibatches=4, adaptive_lr=False)
+    gpu = case.gpu_ac("bf16", lr=1e-3)
+    st = gpu.update(case.soa(), cfg)
+    orc = _bf16_oracle(case, lr=1e-3)
+    st2 = orc.update(case.oracle_batch(), O.PpoConfig(epochs=2, minibatches=4, adaptive_lr=False))
+    d_gpu = gpu.params - case.params
+    d_orc = orc.params - case.params
+    l2 = tensor_l2(d_gpu, d_orc, case.adims, case.cdims)
+    bad = {k: v for k, v in l2.items() if v > 2e-2}
+    assert not bad, bad
+    cos = float(d_gpu @ d_orc / (np.linalg.norm(d_gpu) * np.linalg.norm(d_orc)))
+    assert cos > 0.999, cos
+    for k in ("kl", "surrogate", "value_loss", "entropy"):
+        assert abs(getattr(st, k) - st2[k]) <= 2e-3 * max(abs(st2[k]), 1e-3), (k, st, st2)

@@ -371,6 +371,56 @@ def test_tf32_operand_mode_matches_a_python_restatement():
                                    rtol=2e-7, atol=0)
 
 
+def _bf16(x):
+    """Round f32 to bf16, nearest, ties to even (kept as f32)."""
+    u = np.asarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
+def test_bf16_operand_mode_matches_a_python_restatement():
+    """The oracle's bf16 operand-rounding mode (the checker for the bf16
+    tensor-core path), against the same restatement as the tf32 mode."""
+    assert _bf16(np.float32(1.0 + 2 ** -8)) == np.float32(1.0)          # tie: even
+    assert _bf16(np.float32(1.0 + 3 * 2 ** -8)) == np.float32(1.0 + 2 ** -6)
+    assert _bf16(np.float32(1.0 + 2 ** -8 + 2 ** -20)) == np.float32(1.0 + 2 ** -7)
+    adims, cdims = (5, 7, 3), (4, 6, 1)
+    rng = np.random.default_rng(1)
+    ac = O.ActorCritic(adims, cdims)
+    params = rng.standard_normal(ac.np).astype(np.float32)
+    ac.params = params
+    obs = rng.standard_normal((3, 5)).astype(np.float32)
+    cobs = rng.standard_normal((3, 4)).astype(np.float32)
+    ac.set_bf16_operands()
+    mb, vb = ac.forward(obs, cobs)
+
+    def fwd(dims, p, x):
+        a = _bf16(x)
+        off = 0
+        for l in range(len(dims) - 1):
+            fi, fo = dims[l], dims[l + 1]
+            w = p[off:off + fo * fi].reshape(fo, fi)
+            b = p[off + fo * fi:off + fo * fi + fo]
+            off += fo * fi + fo
+            out = np.empty(fo, np.float32)
+            for o in range(fo):
+                z = np.float32(b[o])
+                for i in range(fi):
+                    z = np.float32(z + np.float32(_bf16(w[o, i]) * a[i]))
+                if l < len(dims) - 2:
+                    z = np.float32(z if z > 0 else np.float32(np.exp(z)) - np.float32(1))
+                    z = _bf16(z)
+                out[o] = z
+            a = out
+        return a
+
+    npa = sum(adims[l + 1] * adims[l] + adims[l + 1] for l in range(len(adims) - 1))
+    for r in range(3):
+        np.testing.assert_allclose(fwd(adims, params, obs[r]), mb[r], rtol=2e-7, atol=0)
+        np.testing.assert_allclose(fwd(cdims, params[npa:], cobs[r]), vb[r:r + 1],
+                                   rtol=2e-7, atol=0)
+
+
 def test_norm_commit_matches_python_restatement():
     """orc_norm_commit against ppo.rs:179-195 restated with numpy float32
     scalars (every operation rounded to f32, left to right)."""
