@@ -1,10 +1,10 @@
-"""PPO-update benchmark (BASELINE metric: PPO-update samples/s).
+"""PPO-update benchmark (metric: PPO-update samples/s).
 
 One step = one full zealot-rl update of a synthetic rollout: GAE over every
 env, advantage normalization, then epochs x minibatches of shuffled
 minibatch steps (forward and backward of actor and critic, PPO losses,
 per-net gradient clip, adaptive LR, Adam).  At N=1 the workload is
-BASELINE configs[1] (N=4096 envs x T=24, 5 epochs x 4 minibatches, tf32
+The C2 workload (N=4096 envs x T=24, 5 epochs x 4 minibatches, tf32
 GEMMs); with --gpus N every rank runs that per-GPU workload on its own envs
 (weak scaling; the global minibatch is N times larger) and the gradient is
 allreduced over NCCL once per minibatch.
@@ -352,7 +352,7 @@ def run_reference(args):
 # ------------------------------------------------------------- GPU leg
 
 def bench_c3(args):
-    """BASELINE configs[2] (C3): the rollout step -- batch 4096 x obs 96
+    """The C3 workload: the rollout step -- batch 4096 x obs 96
     through the actor and critic, Gaussian action sampling with seeded
     Philox draws and the log-prob (zrl_policy_step on device buffers),
     repeated for the T = 24 steps of a rollout.  Latency per step and
@@ -710,7 +710,7 @@ def main():
                              "how": "GEMM FLOPs / tensor peak + update bytes / HBM copy bandwidth"}}
     cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline(w)
     # the other single-GPU configurations, timed on this GPU in the same run
-    # (the rollout step; configs[4]: the wide bf16 pair)
+    # (C3: the rollout step; C5: the wide bf16 actor-critic)
     others = None
     if world == 1 and not args.no_other_configs and (args.config or "c2") == "c2":
         others = {"c3": measure_c3(10, 3, "tf32", local),

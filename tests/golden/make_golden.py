@@ -1,6 +1,6 @@
 """Generate the C1 golden fixture (tests/golden/c1_golden.npz).
 
-Workload C1: 64 envs x 24 steps, actor
+Workload C1 (the CPU-runnable case): 64 envs x 24 steps, actor
 96-512-256-128-29, critic 96-512-256-128-1, 1 epoch x 1 minibatch, Adam lr
 1e-3, adaptive LR off, seed 0.  Every input comes from the reference Lcg
 (rng.rs), so it is regenerated bit-exactly from the seed:

@@ -1,4 +1,4 @@
-"""The bf16 tensor-core path (C5: bf16 GEMM inputs,
+"""The bf16 tensor-core path (the C5 workload: bf16 GEMM inputs,
 fp32 master weights and Adam) against the fp32 CPU oracle.
 
 In a bf16 context every GEMM operand is stored in bf16 (round to nearest

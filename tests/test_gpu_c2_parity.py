@@ -1,4 +1,4 @@
-"""Parity at the benchmark's size: BASELINE configs[1] (C2) runs minibatches of
+"""Parity at the benchmark's size: the C2 workload runs minibatches of
 24,576 rows, and at that size the update takes code paths that toy sizes
 never reach -- grouped launches of both nets, CTA-pair (256-row) tiles
 running several rounds per persistent CTA, double-buffered accumulators,
@@ -27,7 +27,7 @@ tensor:
   few tf32 ulps (the tensor core's accumulation order, ELU's exp on the
   special-function unit) are magnified relative to the result;
 * the same gradient against the f32 reference: 5e-3 (tf32 rounding plus the
-  above); the three loss sums: 2e-3, the BASELINE bar for tf32 losses;
+  above); the three loss sums: 2e-3, the bar for tf32 losses;
 * the update's Adam step applied by the oracle to the GPU's own gradient:
   parameters within 1e-5 (the composition check of the C1 test);
 * a whole C2 update (5 epochs x 4 minibatches of 24,576): statistics within
@@ -178,7 +178,7 @@ def test_c2_minibatch_update_composition(mb_case, adaptive):
 
 def test_c2_whole_update_matches_oracle():
     """A whole C2 update: 4096 envs x 24, 5 epochs x 4 minibatches of 24,576,
-    adaptive LR on."""
+    adaptive LR on (the C2 workload)."""
     case = BigCase(n_envs=4096, T=24, seed=22)
     cfg = Z.PpoConfig(epochs=5, minibatches=4, adaptive_lr=True)
     ocfg = O.PpoConfig(epochs=5, minibatches=4, adaptive_lr=True)

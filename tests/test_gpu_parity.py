@@ -7,7 +7,7 @@ Tolerances (written in each test):
 * fp32 CUDA-core GEMM mode: the reference's sums in another order,
   1e-4 relative (norm-wise per tensor) for gradients, 1e-5 for forwards;
 * tf32 tensor-core mode: 2e-3 relative for GEMM outputs, gradients and
-  losses (the BASELINE tolerance).
+  losses (the tolerance for tf32 losses).
 """
 import numpy as np
 import pytest
@@ -154,7 +154,7 @@ def test_update_wide_action_space_fp32():
 
 
 def test_update_c1_matches_oracle_fp32():
-    # N=64 x T=24, 1 epoch x 1 minibatch, lr 1e-3
+    # C1: N=64 x T=24, 1 epoch x 1 minibatch, lr 1e-3
     # (a fresh rollout: each side records mean_old/logp_old with its own
     # forward, so KL is exactly 0 on both and the adaptive LR holds)
     case = Case(C_A, C_C, n_envs=64, T=24, seed=0)
@@ -172,7 +172,7 @@ def test_update_c1_matches_oracle_fp32():
 
 @pytest.mark.parametrize("adaptive", [False, True])
 def test_update_c1_matches_oracle_tf32(adaptive):
-    """BASELINE configs[0] in the tensor-core mode, checked as a composition.
+    """C1 in the tensor-core mode, checked as a composition.
 
     1. the update's statistics (taken before the Adam step with one epoch of
        one minibatch) are GEMM outputs of the same inputs: within 2e-3;

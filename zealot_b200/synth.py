@@ -48,7 +48,7 @@ C_ACTOR = (96, 512, 256, 128, 29)
 C_CRITIC = (96, 512, 256, 128, 1)
 
 WORKLOADS = {
-    # CPU-runnable reference update.
+    # C1: the CPU-runnable reference update.
     "c1": Workload("c1", 64, 24, C_ACTOR, C_CRITIC, 1, 1),
     # single-B200 full update.
     "c2": Workload("c2", 4096, 24, C_ACTOR, C_CRITIC, 5, 4),
