@@ -62,10 +62,13 @@ def test_gemm_wait_runs_out_and_the_context_recovers():
     assert time.time() - t0 < 10.0
     # usable again: same starting point, same result as a fresh context
     ac.params = case.params
-    N.check(N.lib().zrl_set_adam_state(ac.ctx.h, np.zeros(3, np.int32).ctypes.data,
-                                       np.zeros(ac.ctx.np, np.float32).ctypes.data,
-                                       np.zeros(ac.ctx.np, np.float32).ctypes.data,
-                                       ac.ctx.np), ac.ctx.h)
+    # (the arrays must outlive the call: an address taken from a temporary
+    # points at freed memory by the time the library reads it)
+    t3 = np.zeros(3, np.int32)
+    m0 = np.zeros(ac.ctx.np, np.float32)
+    v0 = np.zeros(ac.ctx.np, np.float32)
+    N.check(N.lib().zrl_set_adam_state(ac.ctx.h, t3.ctypes.data, m0.ctypes.data,
+                                       v0.ctypes.data, ac.ctx.np), ac.ctx.h)
     ac.lr = ref_lr = 1e-3
     ref2 = case.gpu_ac("tf32", lr=ref_lr)
     ref2.update(case.soa(), cfg)

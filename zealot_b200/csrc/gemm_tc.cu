@@ -897,11 +897,9 @@ constexpr int stages_for() {
 }
 
 // Co-resident CTA pairs of one instantiation (its shared memory and the
-// GPCs decide), cached.
+// GPCs decide).
 template <typename K>
 int max_pairs(K kfn, int smem) {
-  static int cached = 0;
-  if (cached > 0) return cached;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * 64);
   cfg.blockDim = dim3(kThreads);
@@ -918,7 +916,6 @@ int max_pairs(K kfn, int smem) {
     cudaGetLastError();
     n = g_sms / 2;
   }
-  cached = n;
   return n;
 }
 
@@ -938,7 +935,11 @@ cudaError_t launch_one(const TcMaps &maps, const TcGroup &grp, cudaStream_t s, i
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  int units = CG == 2 ? max_pairs(kfn, S::kBytes) : g_sms;
+  // cached per instantiation (every instantiation has the same function
+  // type, so the cache cannot live in max_pairs)
+  static int pairs = 0;
+  if (CG == 2 && pairs == 0) pairs = max_pairs(kfn, S::kBytes);
+  int units = CG == 2 ? pairs : g_sms;
   if (units_out) {
     *units_out = units;
     return cudaSuccess;
