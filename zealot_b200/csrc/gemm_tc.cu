@@ -98,7 +98,12 @@ struct TcMaps {
 // chunk is staged while the previous chunk's store still reads its slot;
 // three in the dgrad epilogue, where a slot first receives the chunk's
 // TMA-loaded post-activation, two chunks ahead.
-constexpr int slots_for(int epi) { return epi == EPI_ELU_GRAD ? 3 : 2; }
+// A plain store epilogue (the weight gradients' split-K partials: about one
+// tile per CTA and launch) takes one slot, which leaves room for one more
+// stage of the operand stream.
+constexpr int slots_for(int epi) {
+  return epi == EPI_ELU_GRAD ? 3 : (epi == EPI_STORE ? 1 : 2);
+}
 
 template <int BN, int STAGES, int EPI, int CG>
 struct Smem {
@@ -747,10 +752,10 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
             xph ^= 1u << sl;
           }
           if (EPI != EPI_ELU_GRAD) {
-            // the store that last used this slot (two chunks back) must be
+            // the store that last used this slot (NS chunks back) must be
             // done reading it
             if (lane == 0) {
-              if (prev_store) bulk_wait_read<1>();
+              if (prev_store && NS > 1) bulk_wait_read<1>();
               else bulk_wait_read<0>();
             }
             __syncwarp();
