@@ -98,6 +98,11 @@ struct TcMaps {
 // chunk is staged while the previous chunk's store still reads its slot;
 // three in the dgrad epilogue, where a slot first receives the chunk's
 // TMA-loaded post-activation, two chunks ahead.
+// The per-warp bias of the current tile (the epilogues that add a bias).
+constexpr int bias_bytes(int bn, int epi) {
+  return (epi == EPI_BIAS || epi == EPI_BIAS_ELU) ? kEpiWarps * (bn / 2 > 64 ? bn / 2 : 64) * 4 : 0;
+}
+
 // A plain store epilogue (the weight gradients' split-K partials: about one
 // tile per CTA and launch) takes one slot, which leaves room for one more
 // stage of the operand stream.
@@ -115,7 +120,7 @@ struct Smem {
   static constexpr int kStaging = kEpiWarps * kSlots * 4096;
   // the bias of a warp's chunks in the current tile
   static constexpr int kBiasPerWarp = BN / 2 > 64 ? BN / 2 : 64;  // floats
-  static constexpr int kBias = kEpiWarps * kBiasPerWarp * 4;
+  static constexpr int kBias = bias_bytes(BN, EPI);
   static constexpr int kBarOff = kStageBytes + kStaging + kBias;
   // full, empty, acc_full x2, acc_empty x2, one aux barrier per staging
   // slot, and one that nothing completes (the stall test hook)
@@ -895,8 +900,7 @@ bool make_out_map(CUtensorMap *m, float *base, int64_t rows, int64_t cols, int64
 template <int BN, int EPI, int CG>
 constexpr int stages_for() {
   constexpr int avail = 227 * 1024 - 1024 - kEpiWarps * slots_for(EPI) * 4096 -
-                        kEpiWarps * (BN / 2 > 64 ? BN / 2 : 64) * 4 -
-                        (8 + kEpiWarps * slots_for(EPI)) * 8 - 64;
+                        bias_bytes(BN, EPI) - (8 + kEpiWarps * slots_for(EPI)) * 8 - 64;
   constexpr int st = avail / (BM * BKB + BN / CG * BKB);
   return st > 6 ? 6 : st;
 }
