@@ -57,6 +57,7 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;
 // or every weight gradient of both nets) as one flat tile space, problem
 // after problem.
 constexpr int kMaxProbs = 8;
+constexpr bool kLongKOneSlot = true;  // see dispatch_bn
 // n / d for 0 <= n < 2^31 as (umulhi(n, mul) + n) >> shift (Granlund and
 // Montgomery's division by invariant integers; the host picks mul, shift).
 struct FastDiv {
@@ -110,13 +111,13 @@ constexpr int slots_for(int epi) {
   return epi == EPI_ELU_GRAD ? 3 : (epi == EPI_STORE ? 1 : 2);
 }
 
-template <int BN, int STAGES, int EPI, int CG>
+template <int BN, int STAGES, int EPI, int CG, int NSL>
 struct Smem {
   static constexpr int kA = BM * BKB;                 // 16 KB
   static constexpr int kB = BN / CG * BKB;            // this CTA's B columns * 128 B
   static constexpr int kStage = kA + kB;
   static constexpr int kStageBytes = STAGES * kStage;
-  static constexpr int kSlots = slots_for(EPI);
+  static constexpr int kSlots = NSL;
   static constexpr int kStaging = kEpiWarps * kSlots * 4096;
   // the bias of a warp's chunks in the current tile
   static constexpr int kBiasPerWarp = BN / 2 > 64 ? BN / 2 : 64;  // floats
@@ -376,7 +377,7 @@ __device__ __forceinline__ void epi_chunk_bf16(const EpiChunk &e, int lane, bool
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, int STAGES, int CG, bool BF>
+template <int BN, bool A_MN, bool B_MN, int EPI, int STAGES, int CG, bool BF, int NSL>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGroup g) {
   // K elements of one 128-byte k-block, and the M/N width of one MN-major
@@ -387,7 +388,7 @@ tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcGr
   static_assert(!BF || !B_MN || BN / CG >= 64, "bf16 MN-major B needs 64-column boxes");
   static_assert(BN == 32 || BN == 64 || BN == 128 || BN == 256, "BN");
   static_assert(CG == 1 || (CG == 2 && BN >= 64), "a CTA pair splits B in 32-column boxes");
-  using S = Smem<BN, STAGES, EPI, CG>;
+  using S = Smem<BN, STAGES, EPI, CG, NSL>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t *full = (uint64_t *)(smem + S::kBarOff);
@@ -897,10 +898,10 @@ bool make_out_map(CUtensorMap *m, float *base, int64_t rows, int64_t cols, int64
 // The deepest stage ring (at most 6) that fits next to the epilogue
 // staging slots: more k-blocks in flight hide the TMA -> MMA -> release
 // round trip.
-template <int BN, int EPI, int CG>
+template <int BN, int EPI, int CG, int NSL>
 constexpr int stages_for() {
-  constexpr int avail = 227 * 1024 - 1024 - kEpiWarps * slots_for(EPI) * 4096 -
-                        bias_bytes(BN, EPI) - (8 + kEpiWarps * slots_for(EPI)) * 8 - 64;
+  constexpr int avail = 227 * 1024 - 1024 - kEpiWarps * NSL * 4096 - bias_bytes(BN, EPI) -
+                        (8 + kEpiWarps * NSL) * 8 - 64;
   constexpr int st = avail / (BM * BKB + BN / CG * BKB);
   return st > 6 ? 6 : st;
 }
@@ -930,13 +931,13 @@ int max_pairs(K kfn, int smem) {
 
 // With units_out set, only reports the persistent grid's size in tiles
 // processed at once (CTA pairs or CTAs) and launches nothing.
-template <int BN, bool A_MN, bool B_MN, int EPI, int CG, bool BF>
+template <int BN, bool A_MN, bool B_MN, int EPI, int CG, bool BF, int NSL = slots_for(EPI)>
 cudaError_t launch_one(const TcMaps &maps, const TcGroup &grp, cudaStream_t s, int *units_out) {
-  constexpr int ST = stages_for<BN, EPI, CG>();
+  constexpr int ST = stages_for<BN, EPI, CG, NSL>();
   static_assert(ST >= 2, "stage ring");
-  using S = Smem<BN, ST, EPI, CG>;
+  using S = Smem<BN, ST, EPI, CG, NSL>;
   static_assert(S::kBytes <= 227 * 1024, "shared memory");
-  auto kfn = tc_gemm_kernel<BN, A_MN, B_MN, EPI, ST, CG, BF>;
+  auto kfn = tc_gemm_kernel<BN, A_MN, B_MN, EPI, ST, CG, BF, NSL>;
   static bool attr = false;  // set once per instantiation (same value on every device)
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -972,10 +973,21 @@ cudaError_t launch_one(const TcMaps &maps, const TcGroup &grp, cudaStream_t s, i
   return cudaLaunchKernelEx(&cfg, kfn, maps, grp);
 }
 
+// epi | kOneSlot: a long-K forward (its main loop, not its epilogue, sets
+// the pace) with one staging slot per epilogue warp, whose room goes to
+// one more operand stage
+constexpr int kOneSlot = 0x100;
+
 template <int BN, int CG, bool BF>
 cudaError_t dispatch_bn(int kind, int epi, const TcMaps &maps, const TcGroup &grp,
                         cudaStream_t s, int *u) {
+  const bool one = (epi & kOneSlot) != 0;
+  epi &= ~kOneSlot;
   if (kind == 0) {  // forward
+    if constexpr (BN == 256) {
+      if (epi == EPI_BIAS_ELU && one)
+        return launch_one<BN, false, false, EPI_BIAS_ELU, CG, BF, 1>(maps, grp, s, u);
+    }
     if (epi == EPI_BIAS_ELU)
       return launch_one<BN, false, false, EPI_BIAS_ELU, CG, BF>(maps, grp, s, u);
     if (epi == EPI_BIAS) return launch_one<BN, false, false, EPI_BIAS, CG, BF>(maps, grp, s, u);
@@ -1303,8 +1315,15 @@ zrl_status gemm_tc_group(GemmEngine *eng, const GemmArgs *gs, int n, int precisi
   grp.wait_ns = eng->wait_ns;
   grp.stall = eng->stall_next;
   eng->stall_next = 0;
-  const cudaError_t e = bf ? dispatch<true>(CG, BN, kind, gs[0].epi, maps, grp, s)
-                           : dispatch<false>(CG, BN, kind, gs[0].epi, maps, grp, s);
+  // a forward whose every problem has K >= 256 (8 k-blocks or more)
+  int minK = INT32_MAX;
+  for (int i = 0; i < n; ++i) minK = std::min(minK, gs[i].K);
+  const int epi_sel =
+      gs[0].epi | ((kLongKOneSlot && kind == 0 && gs[0].epi == EPI_BIAS_ELU && minK >= 256)
+                       ? kOneSlot
+                       : 0);
+  const cudaError_t e = bf ? dispatch<true>(CG, BN, kind, epi_sel, maps, grp, s)
+                           : dispatch<false>(CG, BN, kind, epi_sel, maps, grp, s);
   if (e != cudaSuccess) {
     *err = std::string("tensor-core GEMM launch: ") + cudaGetErrorString(e);
     return ZRL_CUDA_ERROR;
