@@ -58,6 +58,7 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;
 // after problem.
 constexpr int kMaxProbs = 8;
 constexpr bool kLongKOneSlot = true;  // see dispatch_bn
+constexpr int kMaxStages = 8;
 // n / d for 0 <= n < 2^31 as (umulhi(n, mul) + n) >> shift (Granlund and
 // Montgomery's division by invariant integers; the host picks mul, shift).
 struct FastDiv {
@@ -895,7 +896,7 @@ bool make_out_map(CUtensorMap *m, float *base, int64_t rows, int64_t cols, int64
   return true;
 }
 
-// The deepest stage ring (at most 6) that fits next to the epilogue
+// The deepest stage ring (at most kMaxStages) that fits next to the epilogue
 // staging slots: more k-blocks in flight hide the TMA -> MMA -> release
 // round trip.
 template <int BN, int EPI, int CG, int NSL>
@@ -903,7 +904,7 @@ constexpr int stages_for() {
   constexpr int avail = 227 * 1024 - 1024 - kEpiWarps * NSL * 4096 - bias_bytes(BN, EPI) -
                         (8 + kEpiWarps * NSL) * 8 - 64;
   constexpr int st = avail / (BM * BKB + BN / CG * BKB);
-  return st > 6 ? 6 : st;
+  return st > kMaxStages ? kMaxStages : st;
 }
 
 // Co-resident CTA pairs of one instantiation (its shared memory and the
@@ -984,7 +985,7 @@ cudaError_t dispatch_bn(int kind, int epi, const TcMaps &maps, const TcGroup &gr
   const bool one = (epi & kOneSlot) != 0;
   epi &= ~kOneSlot;
   if (kind == 0) {  // forward
-    if constexpr (BN == 256) {
+    if constexpr (BN >= 128 && CG == 2) {
       if (epi == EPI_BIAS_ELU && one)
         return launch_one<BN, false, false, EPI_BIAS_ELU, CG, BF, 1>(maps, grp, s, u);
     }
