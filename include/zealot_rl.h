@@ -290,7 +290,8 @@ zrl_status zrl_apply_grads(zrl_ctx *ctx, const zrl_ppo_config *cfg,
  * scratch is a fixed array inside the library (about 67 KB on every GPU
  * that loads it), so n_envs is limited to 262,144 (ZRL_INVALID_ARG above)
  * and T to 4096; the first call on a device looks up that array's address
- * (cudaGetSymbolAddress) and caches it, and that address does not survive a
+ * (cudaGetSymbolAddress) and caches it, so make that first call before any
+ * stream capture begins on the device; that address does not survive a
  * cudaDeviceReset of that device; calls that overlap on the GPU
  * race on the shared array.  It has no counterpart in the reference, which computes
  * GAE on the host. */

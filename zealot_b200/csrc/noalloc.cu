@@ -14,7 +14,8 @@
 //  * It bounds the problem size: n_envs <= kMaxEnvs (one partial per 32
 //    envs); larger calls are rejected with ZRL_INVALID_ARG.
 //  * The first call on a device looks up the array's device address
-//    (cudaGetSymbolAddress, with that device current) and caches it.  The
+//    (cudaGetSymbolAddress, with that device current) and caches it; make
+//    that first call before any stream capture begins on the device.  The
 //    cached address belongs
 //    to the device's current context: after cudaDeviceReset on that device
 //    it is stale, so a process that resets a device must not call this entry
