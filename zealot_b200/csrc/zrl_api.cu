@@ -1359,10 +1359,11 @@ static zrl_status finish_update(zrl_ctx *ctx, zrl_stats *out) {
   if (ctx->comm.world > 1)
     TRY(ctx->comm.wait(ctx->stream, &ctx->err));  // bounded: peers may be gone
   CK(cudaStreamSynchronize(ctx->stream));
-  // the next update's device orders (queued at the end of this one) and
-  // their counts are now in place
-  if (ctx->dplan.valid) ctx->dplan.delivered = true;
   TRY(check_device_error(ctx));
+  // the next update's device orders (queued at the end of this one) and
+  // their counts are now in place; after a device error they are queued
+  // again by the next update
+  if (ctx->dplan.valid) ctx->dplan.delivered = true;
   ctx->lr_host = ctx->st_host->lr;
   if (ctx->st_host->t[2] != ctx->t_logstd_host) {
     ctx->err = "internal: Adam step counter mismatch";
