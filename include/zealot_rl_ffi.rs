@@ -1,7 +1,8 @@
 // zealot_rl_ffi.rs -- the Rust declarations of include/zealot_rl.h, one per
 // entry point, for the zealot-rl-cuda crate (zealot-rl-cuda/src/ffi.rs).
 // Written against the header; no Rust toolchain builds it here, and
-// tests/test_ffi_decls.py keeps its entry points equal to the header's.
+// tests/test_ffi_decls.py keeps its entry points, argument and return types
+// (pointee constness included) and struct fields equal to the header's.
 use std::os::raw::{c_char, c_int, c_void};
 
 #[repr(C)] pub struct ZrlCtx { _p: [u8; 0] }
