@@ -449,3 +449,79 @@ def test_norm_commit_matches_python_restatement():
     m3 = mean.copy()
     O.lib().orc_norm_commit(m3, m2.copy(), C.byref(c2), pm.copy(), pm2.copy(), C.byref(pc2), dim)
     assert np.array_equal(m3, mean) and c2.value == 5.0
+
+
+def test_gae_random_cases_match_python_restatement():
+    """orc_gae against ppo.rs:681-703 restated with numpy float32 scalars
+    (each operation rounded to f32, left to right, as the Rust expression
+    evaluates), bit for bit: ragged lengths, episode ends anywhere (the
+    first and the last step included), several gamma/lambda pairs."""
+    rng = np.random.default_rng(11)
+    f = np.float32
+    for case in range(40):
+        T = int(rng.integers(1, 60))
+        r = (rng.standard_normal(T) * rng.choice([0.01, 1.0, 100.0])).astype(np.float32)
+        v = rng.standard_normal(T).astype(np.float32)
+        d = rng.random(T) < rng.choice([0.0, 0.1, 0.5])
+        if case % 5 == 0:
+            d[0] = d[-1] = True
+        lv = f(rng.standard_normal())
+        gamma, lam = [(0.99, 0.95), (0.9, 1.0), (1.0, 0.0), (0.5, 0.5)][case % 4]
+        g32, l32 = f(gamma), f(lam)
+        want_a = np.empty(T, np.float32)
+        want_r = np.empty(T, np.float32)
+        acc, nv = f(0.0), lv
+        for i in reversed(range(T)):
+            nt = f(0.0) if d[i] else f(1.0)
+            delta = f(f(r[i] + f(f(g32 * nv) * nt)) - v[i])
+            acc = f(delta + f(f(f(g32 * l32) * nt) * acc))
+            want_a[i] = acc
+            want_r[i] = f(acc + v[i])
+            nv = v[i]
+        adv, ret = O.gae(r, v, d, lv, gamma, lam)
+        assert np.array_equal(adv, want_a), case
+        assert np.array_equal(ret, want_r), case
+
+
+def test_norm_update_and_normalize_match_python_restatement():
+    """orc_norm_update (Normalizer::update, ppo.rs:160-167, and the
+    PendingNorm::push recurrence) and orc_norm_normalize (ppo.rs:197-205)
+    against numpy float32 restatements, bit for bit, from the identity prior
+    (mean 0, m2 1, count 1) through observations of mixed scales; normalize
+    then hits both clamps and the 1e-8 variance floor."""
+    import ctypes as C
+    rng = np.random.default_rng(5)
+    f = np.float32
+    dim = 9
+    mean = np.zeros(dim, np.float32)
+    m2 = np.ones(dim, np.float32)
+    cnt = C.c_float(1.0)
+    w_mean, w_m2, w_cnt = mean.copy(), m2.copy(), f(1.0)
+    for k in range(200):
+        x = (rng.standard_normal(dim) * [1e-3, 0.1, 1, 10, 1e3, 1, 1, 5, 0.5]
+             + [0, 3, -2, 0, 50, 0, 0, 0, 1]).astype(np.float32)
+        x[5] = f(0.25)  # a constant feature: its variance decays toward the floor
+        O.lib().orc_norm_update(mean, m2, C.byref(cnt), x, dim)
+        w_cnt = f(w_cnt + f(1.0))
+        for i in range(dim):
+            dd = f(x[i] - w_mean[i])
+            w_mean[i] = f(w_mean[i] + f(dd / w_cnt))
+            w_m2[i] = f(w_m2[i] + f(dd * f(x[i] - w_mean[i])))
+        assert f(cnt.value) == w_cnt
+        assert np.array_equal(mean, w_mean) and np.array_equal(m2, w_m2), k
+    for scale in (1.0, 100.0):
+        x = (rng.standard_normal(dim) * scale).astype(np.float32)
+        out = np.empty(dim, np.float32)
+        O.lib().orc_norm_normalize(mean, m2, cnt.value, x, dim, out)
+        want = np.empty(dim, np.float32)
+        for i in range(dim):
+            var = max(f(m2[i] / f(cnt.value)), f(1e-8))
+            want[i] = min(max(f(f(x[i] - mean[i]) / np.sqrt(var)), f(-5.0)), f(5.0))
+        assert np.array_equal(out, want), scale
+    # zero variance: the floor, then the clamp
+    z = np.zeros(dim, np.float32)
+    out = np.empty(dim, np.float32)
+    O.lib().orc_norm_normalize(z, z, 7.0, np.full(dim, 1e-5, np.float32), dim, out)
+    assert np.array_equal(out, np.full(dim, f(f(1e-5) / np.sqrt(f(1e-8))), np.float32))
+    O.lib().orc_norm_normalize(z, z, 7.0, np.full(dim, 1.0, np.float32), dim, out)
+    assert np.array_equal(out, np.full(dim, 5.0, np.float32))
