@@ -2,9 +2,11 @@
 
 Each test restates one unit test of zealot-rl (file:line given) and runs it
 on the C restatement, which pins the oracle before it is used as the
-checker for the CUDA library.  Further self-consistency checks (a float64
-finite-difference check of the whole PPO gradient, and the multi-threaded
-fold against the sequential one) follow.
+checker for the CUDA library.  Further checks follow: a float64
+finite-difference check of the whole PPO gradient, the multi-threaded fold
+against the sequential one, and bit-for-bit comparisons of GAE, the Welford
+normalizer, Adam, the gradient clip and the operand roundings with numpy
+float32 restatements in the reference's operation order.
 """
 import math
 
@@ -525,3 +527,48 @@ def test_norm_update_and_normalize_match_python_restatement():
     assert np.array_equal(out, np.full(dim, f(f(1e-5) / np.sqrt(f(1e-8))), np.float32))
     O.lib().orc_norm_normalize(z, z, 7.0, np.full(dim, 1.0, np.float32), dim, out)
     assert np.array_equal(out, np.full(dim, 5.0, np.float32))
+
+
+def test_adam_and_clip_match_python_restatement():
+    """orc_adam_step (Adam::step, net.rs:233-251) and orc_grad_l2_norm /
+    orc_grad_clip (MlpGrad::l2_norm / clip, net.rs:180-202) against numpy
+    float32 restatements in the reference's operation order, bit for bit,
+    over several steps with gradients of mixed scale (zeros included)."""
+    rng = np.random.default_rng(9)
+    f = np.float32
+    n = 257
+    p = rng.standard_normal(n).astype(np.float32)
+    m = np.zeros(n, np.float32)
+    v = np.zeros(n, np.float32)
+    wp, wm, wv = p.copy(), m.copy(), v.copy()
+    b1, b2, eps = f(0.9), f(0.999), f(1e-8)
+    t = 0
+    for step in range(6):
+        g = (rng.standard_normal(n) * rng.choice([1e-6, 1e-2, 1.0, 30.0])).astype(np.float32)
+        g[::17] = 0.0
+        lr = [1e-3, 3e-4, 1e-2][step % 3]
+        t = O.adam_step(p, g, m, v, t, lr)
+        bc1 = f(f(1.0) - f(O.powi(0.9, t)))
+        bc2 = f(f(1.0) - f(O.powi(0.999, t)))
+        for i in range(n):
+            wm[i] = f(f(b1 * wm[i]) + f(f(f(1.0) - b1) * g[i]))
+            wv[i] = f(f(b2 * wv[i]) + f(f(f(f(1.0) - b2) * g[i]) * g[i]))
+            upd = f(f(f(lr) * f(wm[i] / bc1)) / f(np.sqrt(f(wv[i] / bc2)) + eps))
+            wp[i] = f(wp[i] - upd)
+        assert t == step + 1
+        assert np.array_equal(m, wm) and np.array_equal(v, wv), step
+        assert np.array_equal(p, wp), step
+    for scale in (1e-3, 1.0, 1e3):
+        g = (rng.standard_normal(n) * scale).astype(np.float32)
+        s = f(0.0)
+        for x in g:
+            s = f(s + f(x * x))
+        norm = np.sqrt(s)
+        assert f(O.grad_l2_norm(g)) == norm
+        for max_norm in (0.5, 1.0, 1e6):
+            got = g.copy()
+            O.grad_clip(got, max_norm)
+            want = g.copy()
+            if norm > f(max_norm) and norm > 0:
+                want = (want * f(f(max_norm) / norm)).astype(np.float32)
+            assert np.array_equal(got, want), (scale, max_norm)
