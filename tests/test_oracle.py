@@ -572,3 +572,55 @@ def test_adam_and_clip_match_python_restatement():
             if norm > f(max_norm) and norm > 0:
                 want = (want * f(f(max_norm) / norm)).astype(np.float32)
             assert np.array_equal(got, want), (scale, max_norm)
+
+
+def test_minibatch_losses_match_a_float64_restatement():
+    """The oracle's minibatch statistics (surrogate, value loss, KL) and its
+    log_std gradient against ppo.rs:408-452 (with logp and kl,
+    ppo.rs:297-334) restated in float64 on the oracle's own forward outputs:
+    the clipped surrogate and its clip mask, the clipped value loss, the
+    entropy term of the log_std gradient and the KL of shared-std
+    Gaussians.  The finite-difference test checks the gradient against the
+    oracle's loss; this one checks the loss formulas themselves."""
+    from tests.helpers import Case, SMALL_A, SMALL_C
+    case = Case(SMALL_A, SMALL_C, n_envs=8, T=12, seed=4, perturb=0.08, norm_stats=True)
+    ac = O.ActorCritic(case.adims, case.cdims)
+    ac.params = case.params
+    ac.set_normalizers(*case.norm)
+    batch = case.oracle_batch()
+    cfg = O.PpoConfig()
+    idx = np.random.default_rng(2).permutation(batch.n)[:48]
+    g, sums = ac.minibatch_grads(batch, idx, cfg)
+
+    A = case.adims[-1]
+    ls = case.params[-A:].astype(np.float64)
+    mean, value = ac.forward(batch.obs[idx], batch.critic_obs[idx])
+    mean, value = mean.astype(np.float64), value.astype(np.float64)
+    act = batch.action[idx].astype(np.float64)
+    mo = batch.mean_old[idx].astype(np.float64)
+    lpo = batch.logp_old[idx].astype(np.float64)
+    vo = batch.value_old[idx].astype(np.float64)
+    adv = batch.adv[idx].astype(np.float64)
+    ret = batch.ret[idx].astype(np.float64)
+    scale = 1.0 / len(idx)
+    c = cfg.clip
+    log_sqrt_2pi = 0.5 * math.log(2.0 * math.pi)
+    logp = np.sum(-0.5 * ((act - mean) / np.exp(ls)) ** 2 - ls - log_sqrt_2pi, axis=1)
+    ratio = np.exp(logp - lpo)
+    surr = np.minimum(ratio * adv, np.clip(ratio, 1 - c, 1 + c) * adv)
+    clipped = ((adv >= 0) & (ratio > 1 + c)) | ((adv < 0) & (ratio < 1 - c))
+    assert clipped.any() and (~clipped).any()  # both branches exercised
+    d = act - mean
+    inv_var = np.exp(-2.0 * ls)
+    dls = adv[:, None] * ratio[:, None] * (d * d * inv_var - 1.0)
+    g_ls = np.sum(np.where(clipped[:, None], 0.0, -dls), axis=0) * scale
+    g_ls += -cfg.entropy_coef * scale * len(idx)
+    v_cl = vo + np.clip(value - vo, -c, c)
+    l_un, l_cl = (value - ret) ** 2, (v_cl - ret) ** 2
+    vloss = np.where(l_cl > l_un, l_cl, l_un)
+    assert (l_cl > l_un).any()  # the clipped value branch is taken somewhere
+    kl = np.sum(0.5 * ((mean - mo) * np.exp(-ls)) ** 2, axis=1)
+    want = np.array([surr.sum(), vloss.sum(), kl.sum()]) * scale
+    np.testing.assert_allclose(sums, want, rtol=1e-4, atol=1e-7)
+    err = np.max(np.abs(g[-A:] - g_ls)) / np.max(np.abs(g_ls))
+    assert err < 1e-4, err
