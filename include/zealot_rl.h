@@ -338,10 +338,15 @@ int64_t zrl_rank_orders(uint64_t seed, int64_t n_global, int64_t n_local,
  * has obs, critic_obs, action and mean_old mapped by signed permutations,
  * (P x)[i] = sign[i] * x[perm[i]] (each perm a permutation of its space,
  * each sign +-1), and logp_old, value_old, adv, ret unchanged.  The mirror
- * is applied once per update, where the observations are normalized (the
- * mirrored normalized rows are written beside the originals), and to action
- * and mean_old as the epoch gather copies them.  obs_perm = NULL turns it
- * off.  One rank only (ZRL_NOT_SUPPORTED with several). */
+ * is applied once per update, where the observations are normalized: the
+ * mirrored raw observations are normalized with the same statistics, as
+ * the trainer normalizes each mirrored Sample, and written beside the
+ * originals; action and mean_old are mapped as the epoch gather copies
+ * them.  cfg->minibatches counts minibatches of the 2 n samples: the GPU
+ * trainer keeps its minibatch size and doubles the count
+ * (biped_train_gpu.rs:639-643, 1005), so pass twice its minibatches to
+ * train as it does.  obs_perm = NULL turns it off.  One rank only
+ * (ZRL_NOT_SUPPORTED with several). */
 zrl_status zrl_set_mirror(zrl_ctx *ctx, const int32_t *obs_perm, const float *obs_sign,
                           const int32_t *cobs_perm, const float *cobs_sign,
                           const int32_t *act_perm, const float *act_sign);
