@@ -1,0 +1,48 @@
+"""bench.py's reference arm on CPU: the JSON line a benchmark driver parses.
+
+`bench.py --impl reference` times zealot-rl's CPU update (the oracle port)
+on the host cores and prints one JSON line with the same metric, unit and
+config keys as the GPU arm, plus `impl`, `cpu_baseline` and an `e2e` object
+whose copy counts are zero.  Under torchrun only rank 0 prints; the other
+ranks exit 0 without work.  Run here on the small C1 workload."""
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _run(extra_env=None):
+    env = dict(os.environ)
+    env.update(extra_env or {})
+    p = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--config", "c1",
+                        "--steps", "2", "--warmup", "1"], cwd=ROOT, env=env,
+                       capture_output=True, text=True, timeout=300)
+    assert p.returncode == 0, p.stderr[-2000:]
+    return [ln for ln in p.stdout.splitlines() if ln.strip()]
+
+
+def test_reference_arm_prints_one_complete_line():
+    lines = _run()
+    assert len(lines) == 1, lines
+    d = json.loads(lines[0])
+    for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+              "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+              "cpu_baseline", "e2e"):
+        assert k in d, k
+    assert d["impl"] == "reference"
+    assert d["unit"] == "samples/s" and d["higher_is_better"] is True
+    assert d["value"] > 0 and d["ms_per_step"] > 0
+    assert (d["steps"], d["warmup"], d["n_gpus"]) == (2, 1, 1)
+    assert d["config"]["workload"] == "c1"
+    cb = d["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"]
+    assert cb["unit"] == d["unit"] and cb["sample"]
+    e = d["e2e"]
+    assert e["value"] == d["value"] and e["unit"] == d["unit"]
+    assert e["h2d_bytes_per_step"] == 0 and e["d2h_bytes_per_step"] == 0
+
+
+def test_reference_arm_is_silent_on_other_ranks():
+    assert _run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"}) == []
