@@ -10,7 +10,6 @@ tf32-representable, as the library stores them) and fp32 1e-5.
 import numpy as np
 import pytest
 
-from zealot_b200 import native as N
 from zealot_b200 import zealot_rl as Z
 
 pytestmark = pytest.mark.gpu

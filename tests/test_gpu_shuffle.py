@@ -1,8 +1,6 @@
 """The device epoch permutation (zrl_shuffle_device) against the host
 Fisher-Yates loop of ppo.rs:357-363 (zrl_shuffle, itself pinned to the
 oracle's Lcg): bit-exact, from tiny n to the 8-GPU C4 sample count."""
-import ctypes as C
-
 import numpy as np
 import pytest
 

@@ -3,8 +3,6 @@ data-parallel update runs) against a restatement on the oracle's shuffle:
 rank r of a world holds rows [r * n_local, (r + 1) * n_local); per global
 minibatch slice of the epoch permutation (ppo.rs:356-367) it keeps the
 positions it holds, as local rows, in permutation order.  Runs on CPU."""
-import ctypes as C
-
 import numpy as np
 import pytest
 
