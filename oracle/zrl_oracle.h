@@ -6,7 +6,7 @@
  * entry and bench.py's CPU-baseline leg may load it; no product code path
  * links, imports or calls it.
  *
- * Each function restates one piece of zealot-rl (Rust, zealot-rl/src/*.rs)
+ * Each function restates one piece of zealot-rl (Rust, zealot-rl/src/{rng,net,ppo}.rs)
  * in plain C with the same f32 operation order, so the sequential mode
  * reproduces the reference's single-threaded results:
  *

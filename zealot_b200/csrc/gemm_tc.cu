@@ -939,12 +939,18 @@ cudaError_t launch_one(const TcMaps &maps, const TcGroup &grp, cudaStream_t s, i
   using S = Smem<BN, ST, EPI, CG, NSL>;
   static_assert(S::kBytes <= 227 * 1024, "shared memory");
   auto kfn = tc_gemm_kernel<BN, A_MN, B_MN, EPI, ST, CG, BF, NSL>;
-  static bool attr = false;  // set once per instantiation (same value on every device)
-  if (!attr) {
+  // the shared-memory opt-in belongs to the current device's context: set
+  // once per instantiation and device
+  constexpr int kMaxDevices = 64;
+  static bool attr[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return cudaErrorInvalidDevice;
+  if (!attr[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          S::kBytes);
     if (e != cudaSuccess) return e;
-    attr = true;
+    attr[dev] = true;
   }
   // cached per instantiation (every instantiation has the same function
   // type, so the cache cannot live in max_pairs)
@@ -1163,8 +1169,8 @@ int gemm_tc_split(GemmEngine *eng, const GemmArgs *gs, int n, int precision, int
     tiles1[i] = (int64_t)((gs[i].M + BM * CG - 1) / (BM * CG)) * ((gs[i].N + bn[i] - 1) / bn[i]);
   }
   int units = 0;
-  TcMaps maps;
-  TcGroup grp;
+  TcMaps maps{};  // not read: the dispatch only reports the grid's units
+  TcGroup grp{};
   const cudaError_t e = bf ? dispatch<true>(CG, BN, kind, gs[0].epi, maps, grp, nullptr, &units)
                            : dispatch<false>(CG, BN, kind, gs[0].epi, maps, grp, nullptr, &units);
   if (e != cudaSuccess || units < 1) return 0;

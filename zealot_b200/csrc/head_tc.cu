@@ -585,15 +585,23 @@ zrl_status head_tc(GemmEngine *eng, const HeadArgs &a, cudaStream_t s, std::stri
   p.part = a.part;
   p.err = a.err;
   p.wait_ns = eng->wait_ns;
-  static bool attr = false;
-  if (!attr) {
+  // the shared-memory opt-in belongs to the current device's context: set
+  // once per device
+  constexpr int kMaxDevices = 64;
+  static bool attr[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    *err = "head: no usable current device";
+    return ZRL_CUDA_ERROR;
+  }
+  if (!attr[dev]) {
     cudaError_t e = cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          HeadSmem::kBytes);
     if (e != cudaSuccess) {
       *err = std::string("head: ") + cudaGetErrorString(e);
       return ZRL_CUDA_ERROR;
     }
-    attr = true;
+    attr[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(head_grid(a.rows));
