@@ -8,7 +8,9 @@ sums per-rank gradients scaled by 1 / (global minibatch size) with one
 allreduce per minibatch.  These tests run that decomposition with the CPU
 oracle as the per-rank gradient and torch.distributed (gloo, world size 2)
 as the allreduce, and check it against the single-process gradient of each
-global minibatch -- the property the multi-GPU path relies on.
+global minibatch -- the property the multi-GPU path relies on -- with two,
+three and four ranks (rank shares of a global minibatch are uneven and may
+be empty).
 """
 from __future__ import annotations
 
@@ -21,7 +23,6 @@ import pytest
 import oracle as O
 from tests.helpers import Case, SMALL_A, SMALL_C
 
-WORLD = 2
 MINIBATCHES = 4
 
 
@@ -49,16 +50,16 @@ def _local_batch(case, lo, hi):
                                    "value_old", "adv", "ret")})
 
 
-def _worker(rank, port, step, q):
+def _worker(rank, world, port, step, q):
     import torch
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         case = _case()
         n = case.ro.n
-        n_local = n // WORLD
+        n_local = n // world
         row_off = rank * n_local
         mb = n // MINIBATCHES
         ac = O.ActorCritic(case.adims, case.cdims)
@@ -86,16 +87,16 @@ def _worker(rank, port, step, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("step", [0, 13])
-def test_two_rank_gradients_sum_to_global_minibatch(step):
+@pytest.mark.parametrize("world,step", [(2, 0), (2, 13), (3, 5), (4, 13)])
+def test_rank_gradients_sum_to_global_minibatch(world, step):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, port, step, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, step, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=300) for _ in range(WORLD))
+    res = dict(q.get(timeout=300) for _ in range(world))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -115,9 +116,10 @@ def test_two_rank_gradients_sum_to_global_minibatch(step):
             g, s = ac.minibatch_grads(full, perm[m * mb:(m + 1) * mb], cfg)
             want = np.concatenate([g, s])
             # every global position went to exactly one rank
-            assert res[0][i][0] + res[1][i][0] == mb
-            # both ranks hold the same allreduced sum
-            np.testing.assert_array_equal(res[0][i][1], res[1][i][1])
+            assert sum(res[r][i][0] for r in range(world)) == mb
+            # every rank holds the same allreduced sum
+            for r in range(1, world):
+                np.testing.assert_array_equal(res[0][i][1], res[r][i][1])
             got = res[0][i][1]
             err = np.abs(got - want).max() / max(np.abs(want).max(), 1e-30)
             assert err < 1e-5, (e, m, err)
