@@ -81,6 +81,8 @@ void orc_gae(const float *rewards, const float *values, const uint8_t *dones,
   }
 }
 
+/* gae per env of an env-major [n_envs, T] rollout, as the GPU trainer calls
+ * it per env (biped_train_gpu.rs:974-981). */
 void orc_gae_batch(const float *rewards, const float *values,
                    const uint8_t *dones, const float *last_values,
                    int64_t n_envs, int64_t T, float gamma, float lam,
@@ -99,6 +101,8 @@ static inline float elu_grad_from_act(float a) {
   return a > 0.0f ? 1.0f : a + 1.0f;
 }
 
+/* Parameters of Mlp::new(dims) (net.rs:61-78): w [out, in] and b [out] per
+ * layer. */
 int64_t orc_mlp_param_count(const int32_t *dims, int32_t n_dims) {
   int64_t c = 0;
   for (int32_t l = 0; l + 1 < n_dims; ++l)
@@ -189,6 +193,7 @@ static void mlp_forward_r(const int32_t *dims, int32_t n_dims, const float *para
   }
 }
 
+/* Mlp::forward (net.rs:88-108) with the reference's f32 arithmetic. */
 void orc_mlp_forward(const int32_t *dims, int32_t n_dims, const float *params,
                      const float *x, float *acts) {
   mlp_forward_r(dims, n_dims, params, x, acts, 0);
@@ -202,6 +207,7 @@ static void mlp_backward_r(const int32_t *dims, int32_t n_dims, const float *par
                            const float *acts, const float *g_out, float *grads,
                            float *g_in, int rnd);
 
+/* Mlp::backward (net.rs:113-140) with the reference's f32 arithmetic. */
 void orc_mlp_backward(const int32_t *dims, int32_t n_dims, const float *params,
                       const float *acts, const float *g_out, float *grads,
                       float *g_in) {
@@ -400,6 +406,9 @@ struct orc_ac {
   int32_t rnd; /* operand rounding emulated (mlp_forward_r): 1 tf32, 2 bf16 */
 };
 
+/* The ActorCritic state (ppo.rs:208-229, 235-266): two Mlps, log_std, one
+ * Adam per net plus log_std's Adam state, both normalizers (identity
+ * prior, ppo.rs:142-148). */
 orc_ac *orc_ac_new(const int32_t *adims, int32_t an, const int32_t *cdims,
                    int32_t cn) {
   if (an < 2 || cn < 2 || an > ORC_MAX_LAYERS + 1 || cn > ORC_MAX_LAYERS + 1)
