@@ -27,9 +27,10 @@ _u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
 
 
 def build(force: bool = False) -> str:
-    """Compile liboracle.so from the C restatement (make -C oracle)."""
-    if force or not os.path.exists(_LIB_PATH):
-        subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    """Compile liboracle.so from the C restatement (make -C oracle): make
+    rebuilds it whenever the C sources are newer than the library, and
+    force rebuilds it unconditionally."""
+    subprocess.run(["make", "-s", "-C", _HERE] + (["-B"] if force else []), check=True)
     return _LIB_PATH
 
 
