@@ -13,6 +13,7 @@ from __future__ import annotations
 import ctypes as C
 import os
 import subprocess
+import warnings
 from dataclasses import dataclass
 
 import numpy as np
@@ -29,8 +30,15 @@ _u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
 def build(force: bool = False) -> str:
     """Compile liboracle.so from the C restatement (make -C oracle): make
     rebuilds it whenever the C sources are newer than the library, and
-    force rebuilds it unconditionally."""
-    subprocess.run(["make", "-s", "-C", _HERE] + (["-B"] if force else []), check=True)
+    force rebuilds it unconditionally.  Where make or the compiler cannot
+    run and a library is already there (a copy of the tree on another
+    machine), that library is used, with a warning."""
+    try:
+        subprocess.run(["make", "-s", "-C", _HERE] + (["-B"] if force else []), check=True)
+    except (OSError, subprocess.CalledProcessError) as e:
+        if force or not os.path.exists(_LIB_PATH):
+            raise
+        warnings.warn(f"oracle: make failed ({e}); using the existing {_LIB_PATH}")
     return _LIB_PATH
 
 
