@@ -120,7 +120,8 @@ typedef struct {
 typedef struct zrl_ctx zrl_ctx;
 
 /* Fills out[128] with a fresh ncclUniqueId (rank 0 calls it, the caller
- * distributes the bytes to the other ranks' zrl_comm.nccl_id). */
+ * distributes the bytes to the other ranks' zrl_comm.nccl_id).  No
+ * counterpart in the reference, which trains on one device. */
 zrl_status zrl_nccl_unique_id(uint8_t *out);
 
 /* ---- lifetime ------------------------------------------------------- */
@@ -130,16 +131,24 @@ zrl_status zrl_nccl_unique_id(uint8_t *out);
  * initialisation half is zrl_init_reference / zrl_set_params. */
 zrl_status zrl_create(const zrl_model_config *cfg, int device,
                       const zrl_comm *comm, zrl_ctx **out);
+/* Frees the context (the reference's ActorCritic is freed by Drop). */
 zrl_status zrl_destroy(zrl_ctx *ctx);
+/* The message of the last failure on ctx (where the reference panics, this
+ * library returns a status and keeps the message here). */
 const char *zrl_last_error(const zrl_ctx *ctx);
+/* ZRL_ABI_VERSION of the loaded library.  No counterpart in the reference. */
 int32_t zrl_abi_version(void);
-/* Blocks until the context's stream is idle. */
+/* Blocks until the context's stream is idle.  No counterpart in the
+ * reference (its update returns when the work is done). */
 zrl_status zrl_synchronize(zrl_ctx *ctx);
-/* The context's cudaStream_t, for callers that order their own work. */
+/* The context's cudaStream_t, for callers that order their own work.  No
+ * counterpart in the reference. */
 void *zrl_stream(zrl_ctx *ctx);
 
 /* ---- parameters and state -------------------------------------------- */
 
+/* Length of the flat parameter vector: the element count of the tensors
+ * ActorCritic::save writes (ppo.rs:539-571). */
 int64_t zrl_param_count(const zrl_ctx *ctx);
 /* ActorCritic::new initialisation (ppo.rs:235-266, net.rs:61-78) from an
  * Lcg state (rng.rs); *lcg_state is advanced exactly as the reference. */
@@ -149,7 +158,10 @@ zrl_status zrl_init_reference(zrl_ctx *ctx, float init_noise_std,
  * resets the Adam state, as ActorCritic::load does (ppo.rs:633-647). */
 zrl_status zrl_set_params(zrl_ctx *ctx, const float *flat, int64_t count);
 zrl_status zrl_get_params(zrl_ctx *ctx, float *flat, int64_t count);
-/* Adam state (t for actor, critic, log_std; m and v flat in param order). */
+/* Adam state (t for actor, critic, log_std; m and v flat in param order):
+ * the reference's private opt_actor / opt_critic / m_logstd, v_logstd,
+ * t_logstd fields (ppo.rs:221-226, net.rs:207-216), which it neither
+ * exposes nor saves; here for checkpoints that keep them and for tests. */
 zrl_status zrl_set_adam_state(zrl_ctx *ctx, const int32_t *t3,
                               const float *m, const float *v, int64_t count);
 zrl_status zrl_get_adam_state(zrl_ctx *ctx, int32_t *t3, float *m, float *v,
@@ -182,7 +194,8 @@ zrl_status zrl_pending_push(zrl_ctx *ctx, const float *obs, const float *critic_
  * normalizers (biped_train_gpu.rs:1050-1051), which resets them; an empty
  * pending state leaves its normalizer as it is. */
 zrl_status zrl_commit_pending(zrl_ctx *ctx);
-/* The pending statistics (counts on the host). */
+/* The pending statistics (counts on the host): the fields of the two
+ * PendingNorm values (ppo.rs:118-122). */
 zrl_status zrl_get_pending(zrl_ctx *ctx, float *obs_mean, float *obs_m2,
                            float *obs_count, float *crit_mean, float *crit_m2,
                            float *crit_count);
@@ -362,7 +375,8 @@ zrl_status zrl_set_mirror(zrl_ctx *ctx, const int32_t *obs_perm, const float *ob
 zrl_status zrl_set_wait_limit(zrl_ctx *ctx, uint64_t ns);
 /* Test hook: the next tensor-core GEMM launch of this context makes its MMA
  * issuer wait on a barrier that nothing completes, so the wait runs out
- * after the wait limit (the failure path above, without a GPU fault). */
+ * after the wait limit (the failure path above, without a GPU fault).  No
+ * counterpart in the reference. */
 zrl_status zrl_test_stall_next_gemm(zrl_ctx *ctx);
 /* Test hook: the bounded stream wait of the several-rank path (the poll of
  * the stream and of NCCL's asynchronous error that aborts the communicator
@@ -370,15 +384,17 @@ zrl_status zrl_test_stall_next_gemm(zrl_ctx *ctx);
  * stream completes, 1 it never does (ZRL_TIMEOUT after timeout_ms), 2 the
  * communicator reports an error (ZRL_NCCL_ERROR), 3 the stream reports a
  * failed kernel (ZRL_CUDA_ERROR).  *aborted: whether the communicator was
- * aborted. */
+ * aborted.  No counterpart in the reference. */
 zrl_status zrl_test_comm_wait(int32_t scenario, int32_t timeout_ms, int32_t *aborted);
 
 /* ---- instrumentation ---------------------------------------------------- */
 
-/* Number of kernels this context launched since it was created. */
+/* Number of kernels this context launched since it was created.  No
+ * counterpart in the reference (instrumentation). */
 int64_t zrl_kernel_launches(const zrl_ctx *ctx);
 /* Device time (ms) of the GEMM kernels of the last update, measured with
- * CUDA events on the context's stream when profiling is enabled. */
+ * CUDA events on the context's stream when profiling is enabled.  No
+ * counterpart in the reference (instrumentation). */
 zrl_status zrl_set_profiling(zrl_ctx *ctx, int32_t enabled);
 zrl_status zrl_get_profile(zrl_ctx *ctx, float *gemm_ms, float *update_ms,
                            int64_t *gemm_launches);
