@@ -4,7 +4,8 @@
 on the host cores and prints one JSON line with the same metric, unit and
 config keys as the GPU arm, plus `impl`, `cpu_baseline` and an `e2e` object
 whose copy counts are zero.  Under torchrun only rank 0 prints; the other
-ranks exit 0 without work.  Run here on the small C1 workload."""
+ranks exit 0 without work.  Run here on the small C1 workload; the parser
+that fills roofline.traffic from an ncu CSV is checked on a synthetic one."""
 import json
 import os
 import subprocess
@@ -46,3 +47,35 @@ def test_reference_arm_prints_one_complete_line():
 
 def test_reference_arm_is_silent_on_other_ranks():
     assert _run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"}) == []
+
+
+def test_traffic_is_read_from_an_ncu_csv(tmp_path):
+    """roofline.traffic from `--traffic-csv`: the mean over the captured
+    tc_gemm_kernel launches of dram__bytes_read.sum + dram__bytes_write.sum,
+    whatever unit ncu printed, other kernels ignored; None without a usable
+    capture."""
+    sys.path.insert(0, ROOT)
+    import bench
+    hdr = ('"ID","Process ID","Process Name","Host Name","Kernel Name","Context","Stream",'
+           '"Block Size","Grid Size","Device","CC","Section Name","Metric Name",'
+           '"Metric Unit","Metric Value"\n')
+
+    def row(i, kernel, metric, unit, value):
+        return (f'"{i}","1","python","h","{kernel}","1","7","(320, 1, 1)","(148, 1, 1)",'
+                f'"0","10.0","Command line profiler metrics","{metric}","{unit}","{value}"\n')
+
+    k = "void zrl::tc_gemm_kernel<256, false, false, 2, 5, 2, false, 1>(TcMaps, TcGroup)"
+    csv = tmp_path / "gemm.csv"
+    csv.write_text("==PROF== Connected to process 1\n" + hdr
+                   + row(0, k, "dram__bytes_read.sum", "Mbyte", "101.80")
+                   + row(0, k, "dram__bytes_write.sum", "Kbyte", "6,500.00")
+                   + row(0, k, "gpu__time_duration.sum", "usecond", "34.8")
+                   + row(1, "head_kernel(HeadParams)", "dram__bytes_read.sum", "Mbyte", "31.4")
+                   + row(2, k, "dram__bytes_read.sum", "Gbyte", "0.2")
+                   + row(2, k, "dram__bytes_write.sum", "byte", "100000000"))
+    want = ((101.8e6 + 6.5e6) + (0.2e9 + 1e8)) / 2
+    assert abs(bench.ncu_traffic(str(csv)) - want) < 1.0
+    assert bench.ncu_traffic(str(tmp_path / "missing.csv")) is None
+    bad = tmp_path / "bad.csv"
+    bad.write_text('"a","b"\n"1","2"\n')
+    assert bench.ncu_traffic(str(bad)) is None
