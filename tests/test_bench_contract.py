@@ -79,3 +79,17 @@ def test_traffic_is_read_from_an_ncu_csv(tmp_path):
     bad = tmp_path / "bad.csv"
     bad.write_text('"a","b"\n"1","2"\n')
     assert bench.ncu_traffic(str(bad)) is None
+
+
+def test_roofline_flop_count_is_the_documented_one():
+    """The numerator of roofline.achieved: GEMM FLOPs per sample pass of the
+    C1-C4 nets (actor 96-512-256-128-29, critic 96-512-256-128-1): forward
+    859,648, weight gradient 859,648, input gradient 663,040 -- 2,382,336 in
+    all, so a C2 update (98,304 samples x 5 epochs) is 1.171 TFLOP."""
+    sys.path.insert(0, ROOT)
+    import bench
+    a, c = (96, 512, 256, 128, 29), (96, 512, 256, 128, 1)
+    assert bench.flops_per_sample_pass(a, c) == 2_382_336
+    fwd = sum(2 * d[i] * d[i + 1] for d in (a, c) for i in range(4))
+    assert fwd == 859_648
+    assert abs(bench.flops_per_sample_pass(a, c) * 98_304 * 5 / 1e12 - 1.171) < 5e-4
